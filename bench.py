@@ -1,0 +1,402 @@
+"""Benchmark of the flat multi-token verify path on B200 (one JSON line on rank 0).
+
+Workload: every fused 4-bit projection of one synthetic 32-layer hybrid
+decoder step at M=8 tokens: 129 qmm launches, 2,024,755,200 packed weight bytes per step.
+A step is one pass over all 129 projections, replayed from a CUDA graph with programmatic
+dependent launch between kernels.  Weights total 2.0 GB, far above the 126 MB L2, so no L2
+flush is needed between steps.
+
+metric: qmm HBM GB/s over the step (algorithmic bytes = packed weights + bf16 activations in
+and out, per step, divided by the device time of the step).  Extra keys report the config-1
+per-M sweep (40 rotated copies of the 9728 x 2560 matrix per M), the M=1 stack cost (cost of
+M=8 vs M=1) and the CPU baseline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl skinny|reference]
+
+With N > 1 (torchrun) every rank runs an independent replica of the stack (the path has no
+exchange step at this configuration): value = bytes of all ranks / max-over-ranks time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+FALLBACK_HBM_GBS = 6650.0
+M_STACK = 8
+
+
+# ------------------------------------------------------------------------------------------------
+# helpers
+# ------------------------------------------------------------------------------------------------
+def measured_hbm_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def init_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------------------------
+# workload
+# ------------------------------------------------------------------------------------------------
+def build_weights(shapes, dev, seed=0):
+    from skinny_mlx_b200.qmm import quantize, repack_for_skinny
+
+    ws = []
+    gen = torch.Generator(device=dev)
+    for idx, (_, n, k) in enumerate(shapes):
+        gen.manual_seed(seed * 100003 + idx)
+        w = torch.randn(n, k, device=dev, generator=gen, dtype=torch.float32).mul_(0.02)
+        packed, s, b = quantize(w)
+        del w
+        ws.append(repack_for_skinny(packed, s, b))
+        del packed, s, b
+    torch.cuda.synchronize()
+    return ws
+
+
+class StackRunner:
+    """All projections of the stack at a fixed token count, captured in one CUDA graph."""
+
+    def __init__(self, shapes, weights, m, dev, seed=1):
+        from skinny_mlx_b200.qmm import skinny_qmm
+
+        self.shapes, self.weights, self.m = shapes, weights, m
+        ks = sorted({k for _, _, k in shapes})
+        self.koff, off = {}, 0
+        for k in ks:
+            self.koff[k] = off
+            off += m * k
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        self.x_all = torch.randn(off, device=dev, generator=gen).to(torch.bfloat16)
+        self.xs = {k: self.x_all[self.koff[k]: self.koff[k] + m * k].view(m, k) for k in ks}
+        self.outs = [torch.empty(m, n, dtype=torch.bfloat16, device=dev) for _, n, _ in shapes]
+        self.stream = torch.cuda.Stream(dev)
+        self._qmm = skinny_qmm
+        with torch.cuda.stream(self.stream):
+            for _ in range(2):
+                self.run_eager()
+        self.stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self.run_eager()
+        self.stream.synchronize()
+
+    def run_eager(self):
+        for (_, _, k), w, o in zip(self.shapes, self.weights, self.outs):
+            self._qmm(self.xs[k], w, out=o)
+
+    def replay(self):
+        self.graph.replay()
+
+    def algorithmic_bytes(self) -> int:
+        from skinny_mlx_b200.configs import packed_bytes
+
+        return sum(packed_bytes(n, k) + 2 * self.m * (n + k) for _, n, k in self.shapes)
+
+
+def time_replays(runner: StackRunner, steps: int, warmup: int, world: int, sampler=None):
+    s = runner.stream
+    for _ in range(warmup):
+        with torch.cuda.stream(s):
+            runner.replay()
+    s.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(steps):
+            runner.replay()
+        e1.record(s)
+    e1.synchronize()
+    clocks = sampler.stop() if sampler else None
+    barrier(world)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    return ms, clocks
+
+
+def time_e2e(runner: StackRunner, steps: int, warmup: int):
+    """Public-API step with host buffers: H2D of the step's activations from pinned memory,
+    graph replay of the 129 projections, D2H of the logits (the step's result)."""
+    s = runner.stream
+    host_x = torch.empty(runner.x_all.numel(), dtype=torch.bfloat16, pin_memory=True)
+    host_x.copy_(runner.x_all.cpu())
+    logits = runner.outs[-1]
+    host_y = torch.empty(logits.shape, dtype=logits.dtype, pin_memory=True)
+
+    def one():
+        runner.x_all.copy_(host_x, non_blocking=True)
+        runner.replay()
+        host_y.copy_(logits, non_blocking=True)
+
+    with torch.cuda.stream(s):
+        for _ in range(warmup):
+            one()
+    s.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(steps):
+            one()
+        e1.record(s)
+    e1.synchronize()
+    return e0.elapsed_time(e1), host_x.numel() * 2, host_y.numel() * 2
+
+
+def config1_sweep(dev, copies=40):
+    """Config 1 (9728 x 2560) for M in {1,2,4,6,8,12,16}: GB/s over `copies` rotated copies."""
+    shapes = [(f"c1.{i}", 9728, 2560) for i in range(copies)]
+    weights = build_weights(shapes, dev, seed=7)
+    out = {}
+    for m in (1, 2, 4, 6, 8, 12, 16):
+        r = StackRunner(shapes, weights, m, dev, seed=m)
+        ms, _ = time_replays(r, 20, 3, 1)
+        out[str(m)] = round(r.algorithmic_bytes() * 20 / (ms * 1e-3) / 1e9, 1)
+        del r
+    del weights
+    torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------------------------------------------------
+# arms
+# ------------------------------------------------------------------------------------------------
+def run_reference(args, world, rank):
+    """--impl reference: the reference's CPU path (MLX quantized_matmul semantics, ported in the
+    oracle because MLX cannot be installed here) timed on this host's cores."""
+    if rank != 0:
+        return
+    from oracle import cpu_baseline
+    from skinny_mlx_b200.configs import hybrid_stack_shapes
+
+    shapes = [(n, k) for _, n, k in hybrid_stack_shapes()]
+    torch.set_num_threads(os.cpu_count() or 1)
+    per_step = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline.time_stack(shapes[(i * 5) % len(shapes):] + shapes, M_STACK, budget_s=4.0, seed=i)
+        if i >= args.warmup:
+            per_step.append(r)
+    bps = sum(r["bytes_per_s"] for r in per_step) / len(per_step)
+    value = bps / 1e9
+    line = {
+        "impl": "reference", "metric": "qmm HBM GB/s, 129 fused projections of the 32-layer hybrid stack at M=8",
+        "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(2024755200 / bps * 1e3, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config 2: 129-projection hybrid stack, M=8", "tokens": M_STACK},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": per_step[0]["cores"],
+                         "kind": "port",
+                         "sample": "oracle f32 dequant+GEMM over consecutive stack projections, ~4 s of "
+                                   "CPU work per step, scaled to bytes/s"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_skinny(args, world, rank, local):
+    from skinny_mlx_b200.configs import hybrid_stack_shapes
+    from skinny_mlx_b200.qmm import device_errors
+
+    dev = torch.device("cuda", local)
+    shapes = hybrid_stack_shapes()
+    weights = build_weights(shapes, dev, seed=0)
+    runner = StackRunner(shapes, weights, M_STACK, dev, seed=1)
+    per_step_bytes = runner.algorithmic_bytes()
+    sampler = ClockSampler(local) if rank == 0 else None
+    ms, clocks = time_replays(runner, args.steps, args.warmup, world, sampler)
+    ms_max = max_over_ranks(ms, world)
+    ms_step = ms_max / args.steps
+    value = per_step_bytes * world / (ms_step * 1e-3) / 1e9
+
+    # M=1 stack (cost of 8 tokens vs 1 token per weight read)
+    r1 = StackRunner(shapes, weights, 1, dev, seed=2)
+    ms1, _ = time_replays(r1, args.steps, args.warmup, world)
+    ms1_step = max_over_ranks(ms1, world) / args.steps
+    del r1
+
+    e2e_ms, h2d, d2h = time_e2e(runner, args.steps, args.warmup)
+    e2e_ms = max_over_ranks(e2e_ms, world) / args.steps
+    e2e_value = per_step_bytes * world / (e2e_ms * 1e-3) / 1e9
+
+    sweep = config1_sweep(dev) if (rank == 0 and not args.no_sweep) else None
+    errs = device_errors(dev)
+    peak, peak_kind = measured_hbm_peak()
+    qmm_bytes = per_step_bytes
+    achieved = qmm_bytes / (ms_step * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        from oracle import cpu_baseline
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        cshapes = [(n, k) for _, n, k in shapes]
+        r = cpu_baseline.time_stack(cshapes, M_STACK, budget_s=12.0)
+        cpu = {"value": round(r["bytes_per_s"] / 1e9, 3), "unit": "GB/s", "cores": r["cores"], "kind": "port",
+               "sample": f"{r['calls']} consecutive stack projections at M=8 through the oracle's f32 "
+                         f"dequant+GEMM ({r['seconds']:.1f} s of CPU work), scaled to bytes/s"}
+
+    traffic = None
+    tp = ROOT / "profiles" / "qmm_traffic.json"
+    if tp.exists():
+        try:
+            traffic = json.loads(tp.read_text()).get("stack_m8_bytes_per_step")
+        except Exception:
+            traffic = None
+
+    if rank == 0:
+        line = {
+            "metric": "qmm HBM GB/s, 129 fused projections of the 32-layer hybrid stack at M=8",
+            "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16xu4->f32", "data": "synthetic",
+            "config": {"workload": "config 2: 129-projection hybrid stack (hidden 2560, 32 layers, 4-bit g64) at M=8",
+                       "tokens": M_STACK, "weight_bytes_per_step": 2024755200,
+                       "algorithmic_bytes_per_step": per_step_bytes, "l2": "inputs larger than L2 (2.0 GB of weights)",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
+                    "path": "pinned H2D of activations, CUDA-graph replay of skinny_qmm calls, D2H of logits"},
+            "gpu_launches": 2 * len(shapes) * args.steps,
+            "clocks": clocks,
+            "stack_m1_ms": round(ms1_step, 4),
+            "cost_m8_vs_m1": round(ms_step / ms1_step, 3),
+            "config1_sweep_gbs": sweep,
+            "device_error_bits": errs,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="skinny", choices=["skinny", "reference"])
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = init_dist()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_skinny(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

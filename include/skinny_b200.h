@@ -1,0 +1,84 @@
+/*
+ * skinny_b200 — C ABI of the B200 (sm_100a) flat multi-token verify path.
+ *
+ * Plain pointers and sizes only; every device pointer is caller-owned CUDA memory, `stream` is a
+ * cudaStream_t passed as void*, and every call is stream-ordered on it.  No entry point allocates
+ * device memory, synchronises the stream, or retains a pointer after it returns.
+ *
+ * Return value: SKINNY_OK (0) or a negative status (see skinny_strerror).  Argument errors are
+ * detected on the host before anything is launched.  Kernel-side errors (a bounded wait that ran
+ * out, an activation outside the f16 range) are OR-ed into 32-bit word 0 of the workspace; read
+ * it after the stream work completes.  A workspace that recorded an error must be zero-filled
+ * again before reuse.
+ *
+ * Reference interfaces replaced (paths inside rachittshah/skinny-mlx):
+ *   skinny_repack_w4g64  <- skinny_mlx/qmm.py:96  repack_for_skinny(w)
+ *   skinny_qmm_w4g64     <- skinny_mlx/qmm.py:132 skinny_qmm(x, w, scales, biases) and the Metal
+ *                           kernel it launches, skinny_mlx/qmm.py:21-86; routed to by
+ *                           skinny_mlx/patch.py:30-35 _qmm
+ */
+#ifndef SKINNY_B200_H
+#define SKINNY_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SKINNY_OK 0
+#define SKINNY_ERR_INVALID_ARG -1
+#define SKINNY_ERR_SHAPE -2
+#define SKINNY_ERR_TOKENS -3
+#define SKINNY_ERR_ALIGNMENT -4
+#define SKINNY_ERR_WORKSPACE -5
+#define SKINNY_ERR_CUDA -6
+#define SKINNY_ERR_DEVICE -7
+#define SKINNY_ERR_UNSUPPORTED -8
+
+/* Library version, e.g. 100 for 0.1.0. */
+int skinny_version(void);
+
+/* Human-readable text for a status code. */
+const char* skinny_strerror(int status);
+
+/* The cudaError_t of the most recent failing CUDA call made by this library on this thread. */
+int skinny_last_cuda_error(void);
+
+/* ---------------------------------------------------------------------------------------------
+ * 4-bit affine group-64 weights (MLX packing: uint32 [N, K/8], element 8j+i at bits 4i of word
+ * j; bf16 scales and biases [N, K/64]).
+ * ------------------------------------------------------------------------------------------- */
+
+/* Bytes of the relaid weight buffer for an N x K matrix (N rounded up to 128 rows). */
+size_t skinny_repack_bytes(int N, int K);
+
+/* One-time relayout of MLX packs + scales + biases into the kernel's unit order.
+ * Replaces skinny_mlx/qmm.py:96 repack_for_skinny.  w_tc must hold skinny_repack_bytes(N, K)
+ * bytes and be 16-byte aligned.  K % 64 == 0, N >= 1. */
+int skinny_repack_w4g64(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                        void* w_tc, int N, int K, void* stream);
+
+/* Workspace bytes a qmm of this shape needs on the current device. */
+size_t skinny_qmm_workspace_bytes(int N, int K);
+
+/* out[M, N] (bf16, leading dimension ldo) = x[M, K] (bf16, leading dimension ldx) . W^T for
+ * 1 <= M <= 16 tokens, computing sum_g s*sum(x*q) + b*sum(x) in f32 (skinny_mlx/qmm.py:8-9).
+ * Activations are rounded to f16 for the tensor-core product, as skinny_mlx/qmm.py:136 does;
+ * |x| > 65504 sets an error bit.  x and ldx*2 must be 16-byte aligned.  The workspace must be
+ * zero-filled before its first use, hold skinny_qmm_workspace_bytes(N, K) bytes, and not be
+ * shared by calls that may run concurrently.  Replaces skinny_mlx/qmm.py:132 skinny_qmm. */
+int skinny_qmm_w4g64(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M, int N,
+                     int K, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Same contract with plain CUDA cores (no tcgen05), one thread per output.  A slow cross-check
+ * used by the tests to localise a mismatch; it has no counterpart in the reference. */
+int skinny_qmm_w4g64_simt(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
+                          int N, int K, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SKINNY_B200_H */

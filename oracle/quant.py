@@ -1,0 +1,203 @@
+"""CPU restatement of MLX affine 4-bit group-64 quantization and quantized matmul.
+
+TEST INFRASTRUCTURE ONLY (see oracle/__init__.py).
+
+Follows:
+  * the packing decode of skinny_mlx/qmm.py:104 (element k = 8j + i at bits 4i of word j);
+  * the quantizer stated for BASELINE config 1: per 64-column group scale = (max - min) / 15,
+    bias = min, bf16 scale/bias, q = clamp(round((w - bias) / scale), 0, 15);
+  * mx.quantized_matmul(x, w, s, b, transpose=True, group_size=64, bits=4) as called at
+    skinny_mlx/qmm.py:183 and skinny_mlx/patch.py:35: y = x @ (q * s + b)^T;
+  * the reference kernel's affine identity sum_k x (q s + b) = s sum_k x q + b sum_k x with x
+    rounded to f16 (skinny_mlx/qmm.py:8-9, 64-71, 136, 143).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+GROUP = 64
+
+
+# ------------------------------------------------------------------------------------------------
+# bf16 / f16 helpers (round-to-nearest-even, as the hardware conversions do)
+# ------------------------------------------------------------------------------------------------
+def f32_to_bf16_bits(a) -> np.ndarray:
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    rounding = ((u >> 16) & 1) + 0x7FFF
+    out = ((u + rounding) >> 16).astype(np.uint16)
+    nan = np.isnan(np.asarray(a, dtype=np.float32))
+    if nan.any():
+        out = np.where(nan, np.uint16(0x7FC0), out)
+    return out
+
+
+def bf16_bits_to_f32(b) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def round_bf16(a) -> np.ndarray:
+    return bf16_bits_to_f32(f32_to_bf16_bits(a))
+
+
+def round_f16(a) -> np.ndarray:
+    return np.asarray(a, dtype=np.float32).astype(np.float16).astype(np.float32)
+
+
+# ------------------------------------------------------------------------------------------------
+# quantize / pack / dequantize
+# ------------------------------------------------------------------------------------------------
+def quantize(w: np.ndarray):
+    """w [N, K] float32 -> (packed uint32 [N, K/8], scales bf16 bits [N, K/64], biases bf16 bits)."""
+    n, k = w.shape
+    assert k % GROUP == 0, k
+    wg = np.asarray(w, dtype=np.float32).reshape(n, k // GROUP, GROUP)
+    wmax = wg.max(-1)
+    wmin = wg.min(-1)
+    s_bits = f32_to_bf16_bits((wmax - wmin) / np.float32(15.0))
+    b_bits = f32_to_bf16_bits(wmin)
+    s = bf16_bits_to_f32(s_bits)[..., None]
+    b = bf16_bits_to_f32(b_bits)[..., None]
+    safe = np.where(s == 0, np.float32(1.0), s)
+    q = np.clip(np.rint((wg - b) / safe), 0, 15)
+    q = np.where(s == 0, 0, q).astype(np.uint32).reshape(n, k // 8, 8)
+    packed = np.zeros((n, k // 8), dtype=np.uint32)
+    for i in range(8):
+        packed |= q[..., i] << np.uint32(4 * i)
+    return packed, s_bits, b_bits
+
+
+def unpack(packed: np.ndarray) -> np.ndarray:
+    """uint32 [N, K/8] -> uint8 nibbles [N, K] (element 8j + i = bits 4i of word j)."""
+    n, kw = packed.shape
+    q = np.stack([(packed >> np.uint32(4 * i)) & np.uint32(0xF) for i in range(8)], axis=-1)
+    return q.reshape(n, kw * 8).astype(np.uint8)
+
+
+def dequantize(packed, s_bits, b_bits) -> np.ndarray:
+    q = unpack(packed).astype(np.float64)
+    s = np.repeat(bf16_bits_to_f32(s_bits).astype(np.float64), GROUP, axis=1)
+    b = np.repeat(bf16_bits_to_f32(b_bits).astype(np.float64), GROUP, axis=1)
+    return q * s + b
+
+
+# ------------------------------------------------------------------------------------------------
+# quantized matmul
+# ------------------------------------------------------------------------------------------------
+def qmm_ref(x: np.ndarray, packed, s_bits, b_bits) -> np.ndarray:
+    """MLX quantized_matmul semantics in float64: x [M, K] @ (q s + b)^T -> [M, N]."""
+    return np.asarray(x, dtype=np.float64) @ dequantize(packed, s_bits, b_bits).T
+
+
+def qmm_identity(x: np.ndarray, packed, s_bits, b_bits) -> np.ndarray:
+    """The reference kernel's arithmetic in float64: x rounded to f16, then per 64-group
+    s * sum(x q) + b * sum(x) (skinny_mlx/qmm.py:64-71, 143)."""
+    xf = round_f16(x).astype(np.float64)
+    m, k = xf.shape
+    q = unpack(packed).astype(np.float64)
+    n = q.shape[0]
+    g = k // GROUP
+    s = bf16_bits_to_f32(s_bits).astype(np.float64)
+    b = bf16_bits_to_f32(b_bits).astype(np.float64)
+    xg = xf.reshape(m, g, GROUP)
+    qg = q.reshape(n, g, GROUP)
+    dots = np.einsum("mgk,ngk->mng", xg, qg)
+    xsum = xg.sum(-1)  # [m, g]
+    return (dots * s[None] + xsum[:, None, :] * b[None]).sum(-1)
+
+
+def rel_err(ref, got) -> float:
+    """max |ref - got| / max |ref| (the metric of skinny_mlx/qmm.py:185)."""
+    ref = np.asarray(ref, dtype=np.float64)
+    got = np.asarray(got, dtype=np.float64)
+    den = np.abs(ref).max()
+    return float(np.abs(ref - got).max() / (den if den > 0 else 1.0))
+
+
+# ------------------------------------------------------------------------------------------------
+# the reference's Metal lane-order relayout, restated (pinned against the reference's own code)
+# ------------------------------------------------------------------------------------------------
+def _lane_maps():
+    lane = np.arange(32)
+    qid = lane // 4
+    fm = (qid & 4) + ((lane // 2) % 4)  # skinny_mlx/qmm.py:35, :107
+    fn = (qid & 2) * 2 + (lane % 2) * 2  # skinny_mlx/qmm.py:36, :108
+    return fm, fn
+
+
+def repack_metal_order(packed: np.ndarray) -> np.ndarray:
+    """skinny_mlx/qmm.py:96-115: [N, K/8] -> [N/8, K/64, 32 lanes, 2 words] (same bytes)."""
+    n, kw = packed.shape
+    kg = kw // 8
+    q = unpack(packed).reshape(n // 8, 8, kg, 8, 8)  # [R, row-in-fragment, g, step, col]
+    fm, fn = _lane_maps()
+    out = np.zeros((n // 8, kg, 32, 2), dtype=np.uint32)
+    for lane in range(32):
+        e0 = q[:, fm[lane], :, :, fn[lane]].astype(np.uint32)      # [R, g, step]
+        e1 = q[:, fm[lane], :, :, fn[lane] + 1].astype(np.uint32)
+        for h in range(2):
+            for i in range(4):
+                out[:, :, lane, h] |= (e0[..., 4 * h + i] << np.uint32(4 * i)) | (
+                    e1[..., 4 * h + i] << np.uint32(16 + 4 * i))
+    return out.reshape(n, kw)
+
+
+def qmm_metal_order(x: np.ndarray, relaid: np.ndarray, s_bits, b_bits) -> np.ndarray:
+    """The reference kernel's inner loop restated over its own relaid layout
+    (skinny_mlx/qmm.py:42-71): lane (fm, fn) of fragment R, group g, step s holds
+    W[8R + fm, 64g + 8s + fn + {0, 1}] at bits (4(s%4), 16 + 4(s%4)) of word s // 4."""
+    xf = round_f16(x).astype(np.float64)
+    m, k = xf.shape
+    n = relaid.shape[0]
+    kg = k // GROUP
+    words = relaid.reshape(n // 8, kg, 32, 2)
+    fm, fn = _lane_maps()
+    q = np.zeros((n, k), dtype=np.float64)
+    for lane in range(32):
+        for s in range(8):
+            wv = words[:, :, lane, s // 4]
+            bits = (wv >> np.uint32(4 * (s % 4))) & np.uint32(0x000F000F)
+            lo = (bits & 0xF).astype(np.float64)
+            hi = ((bits >> 16) & 0xF).astype(np.float64)
+            rows = np.arange(n // 8) * 8 + fm[lane]
+            for g in range(kg):
+                col = 64 * g + 8 * s + fn[lane]
+                q[rows, col] = lo[:, g]
+                q[rows, col + 1] = hi[:, g]
+    s = bf16_bits_to_f32(s_bits).astype(np.float64)
+    b = bf16_bits_to_f32(b_bits).astype(np.float64)
+    xg = xf.reshape(m, kg, GROUP)
+    qg = q.reshape(n, kg, GROUP)
+    dots = np.einsum("mgk,ngk->mng", xg, qg)
+    return (dots * s[None] + xg.sum(-1)[:, None, :] * b[None]).sum(-1)
+
+
+# ------------------------------------------------------------------------------------------------
+# the B200 unit layout (byte-exact statement of what skinny_repack_w4g64 must produce)
+# ------------------------------------------------------------------------------------------------
+TILE = 128
+UNIT_BYTES = 4608
+
+
+def repack_tc(packed: np.ndarray, s_bits, b_bits) -> np.ndarray:
+    """MLX packs -> the kernel's unit order as uint8 bytes (see csrc/qmm_layout.cuh)."""
+    n, kw = packed.shape
+    k = kw * 8
+    g = k // GROUP
+    t = (n + TILE - 1) // TILE
+    npad = t * TILE
+    q = np.zeros((npad, k), dtype=np.uint32)
+    q[:n] = unpack(packed)
+    sb = np.zeros((npad, g), dtype=np.uint32)
+    sb[:n] = s_bits.astype(np.uint32) | (b_bits.astype(np.uint32) << np.uint32(16))
+    # word for 8 columns c0..c7: bits 0-3 c0, 4-7 c2, 8-11 c4, 12-15 c6, 16-19 c1, ... 28-31 c7
+    q8 = q.reshape(npad, k // 8, 8)
+    slot = [0, 4, 1, 5, 2, 6, 3, 7]  # column i -> nibble slot
+    words = np.zeros((npad, k // 8), dtype=np.uint32)
+    for i in range(8):
+        words |= q8[..., i] << np.uint32(4 * slot[i])
+    # [tile, row, group, chunk, 4 words] -> [tile, group, chunk, row, 4 words]
+    w5 = words.reshape(t, TILE, g, 2, 4).transpose(0, 2, 3, 1, 4)
+    nib = np.ascontiguousarray(w5).reshape(t, g, 2 * TILE * 4).view(np.uint8).reshape(t, g, 4096)
+    sbu = np.ascontiguousarray(sb.reshape(t, TILE, g).transpose(0, 2, 1)).view(np.uint8).reshape(t, g, 512)
+    return np.concatenate([nib, sbu], axis=-1).reshape(-1)

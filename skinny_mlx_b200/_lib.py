@@ -1,0 +1,79 @@
+"""ctypes binding of the C-ABI library (include/skinny_b200.h).
+
+There is no fallback: if `_skinny_b200.so` is missing or does not load, every operation raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_int, c_size_t, c_uint32, c_void_p
+from pathlib import Path
+
+_LIB_PATH = Path(__file__).resolve().parent / "_skinny_b200.so"
+_lib = None
+
+STATUS_NAMES = {
+    0: "SKINNY_OK",
+    -1: "SKINNY_ERR_INVALID_ARG",
+    -2: "SKINNY_ERR_SHAPE",
+    -3: "SKINNY_ERR_TOKENS",
+    -4: "SKINNY_ERR_ALIGNMENT",
+    -5: "SKINNY_ERR_WORKSPACE",
+    -6: "SKINNY_ERR_CUDA",
+    -7: "SKINNY_ERR_DEVICE",
+    -8: "SKINNY_ERR_UNSUPPORTED",
+}
+
+# name -> (restype, argtypes); mirrors include/skinny_b200.h
+SIGNATURES = {
+    "skinny_version": (c_int, []),
+    "skinny_strerror": (ctypes.c_char_p, [c_int]),
+    "skinny_last_cuda_error": (c_int, []),
+    "skinny_repack_bytes": (c_size_t, [c_int, c_int]),
+    "skinny_repack_w4g64": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "skinny_qmm_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "skinny_qmm_w4g64": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                 c_void_p, c_size_t, c_void_p]),
+    "skinny_qmm_w4g64_simt": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int,
+                                      c_int, c_void_p]),
+}
+
+
+class SkinnyError(RuntimeError):
+    def __init__(self, fn: str, status: int, detail: str = ""):
+        lib = _lib
+        text = lib.skinny_strerror(status).decode() if lib is not None else STATUS_NAMES.get(status, "?")
+        extra = ""
+        if status == -6 and lib is not None:
+            extra = f" (cudaError {lib.skinny_last_cuda_error()})"
+        super().__init__(f"{fn}: {STATUS_NAMES.get(status, status)}: {text}{extra}{detail}")
+        self.status = status
+
+
+def lib() -> ctypes.CDLL:
+    """Load the library (once).  Raises if the CUDA extension was not built."""
+    global _lib
+    if _lib is None:
+        if not _LIB_PATH.exists():
+            raise RuntimeError(
+                f"skinny_b200 CUDA library not built: {_LIB_PATH} is missing "
+                "(run `python -m skinny_mlx_b200.build`)")
+        handle = ctypes.CDLL(str(_LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def check(fn: str, status: int) -> None:
+    if status != 0:
+        raise SkinnyError(fn, status)
+
+
+def call(name: str, *args) -> None:
+    check(name, getattr(lib(), name)(*args))
+
+
+__all__ = ["lib", "call", "check", "SkinnyError", "SIGNATURES", "c_uint32"]

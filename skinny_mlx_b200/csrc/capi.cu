@@ -1,0 +1,117 @@
+// C-ABI entry points: host-side validation, then stream-ordered kernel launches.
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/skinny_b200.h"
+#include "qmm_layout.cuh"
+
+namespace skinny {
+int device_sm_count(int dev);
+cudaError_t qmm_tc_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M, int N,
+                          int K, void* ws, int C, cudaStream_t stream, bool pdl);
+cudaError_t qmm_repack_launch(const uint32_t* w, const uint16_t* s, const uint16_t* b, void* w_tc,
+                              int N, int K, cudaStream_t stream);
+cudaError_t qmm_simt_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
+                            int N, int K, cudaStream_t stream);
+}  // namespace skinny
+
+namespace {
+thread_local int g_last_cuda = 0;
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return SKINNY_OK;
+  g_last_cuda = static_cast<int>(e);
+  return SKINNY_ERR_CUDA;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  return dev;
+}
+
+int ctas_for(int N, int K) {
+  const skinny::QmmShape sh = skinny::qmm_shape(N, K);
+  long long C = skinny::device_sm_count(current_device());
+  if (C > sh.U) C = sh.U;
+  return static_cast<int>(C);
+}
+
+int check_qmm_shape(int N, int K) {
+  if (N < 1 || K < skinny::kGroup) return SKINNY_ERR_SHAPE;
+  if (K % skinny::kGroup != 0) return SKINNY_ERR_SHAPE;
+  return SKINNY_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int skinny_version(void) { return 100; }
+
+const char* skinny_strerror(int status) {
+  switch (status) {
+    case SKINNY_OK: return "ok";
+    case SKINNY_ERR_INVALID_ARG: return "invalid argument (null pointer or negative size)";
+    case SKINNY_ERR_SHAPE: return "unsupported shape (K must be a positive multiple of 64, N >= 1)";
+    case SKINNY_ERR_TOKENS: return "token count outside [1, 16]";
+    case SKINNY_ERR_ALIGNMENT: return "pointer or leading dimension not 16-byte aligned";
+    case SKINNY_ERR_WORKSPACE: return "workspace missing or smaller than required";
+    case SKINNY_ERR_CUDA: return "CUDA runtime call failed";
+    case SKINNY_ERR_DEVICE: return "kernel recorded an error in the workspace";
+    case SKINNY_ERR_UNSUPPORTED: return "unsupported device or option";
+    default: return "unknown status";
+  }
+}
+
+int skinny_last_cuda_error(void) { return g_last_cuda; }
+
+size_t skinny_repack_bytes(int N, int K) {
+  if (check_qmm_shape(N, K) != SKINNY_OK) return 0;
+  const skinny::QmmShape sh = skinny::qmm_shape(N, K);
+  return static_cast<size_t>(sh.U) * skinny::kUnitWBytes;
+}
+
+int skinny_repack_w4g64(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                        void* w_tc, int N, int K, void* stream) {
+  if (!w || !scales || !biases || !w_tc) return SKINNY_ERR_INVALID_ARG;
+  const int st = check_qmm_shape(N, K);
+  if (st != SKINNY_OK) return st;
+  if (!aligned16(w_tc)) return SKINNY_ERR_ALIGNMENT;
+  return cuda_status(skinny::qmm_repack_launch(w, scales, biases, w_tc, N, K,
+                                               static_cast<cudaStream_t>(stream)));
+}
+
+size_t skinny_qmm_workspace_bytes(int N, int K) {
+  if (check_qmm_shape(N, K) != SKINNY_OK) return 0;
+  return skinny::ws_layout(N, K, ctas_for(N, K)).total;
+}
+
+int skinny_qmm_w4g64(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M, int N,
+                     int K, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!x || !w_tc || !out) return SKINNY_ERR_INVALID_ARG;
+  int st = check_qmm_shape(N, K);
+  if (st != SKINNY_OK) return st;
+  if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
+  if (ldx < K || ldo < N) return SKINNY_ERR_INVALID_ARG;
+  if (!aligned16(x) || (ldx % 8) != 0 || !aligned16(w_tc)) return SKINNY_ERR_ALIGNMENT;
+  const int C = ctas_for(N, K);
+  const skinny::WsLayout wl = skinny::ws_layout(N, K, C);
+  if (!workspace || workspace_bytes < wl.total || !aligned16(workspace)) return SKINNY_ERR_WORKSPACE;
+  return cuda_status(skinny::qmm_tc_launch(x, ldx, w_tc, out, ldo, M, N, K, workspace, C,
+                                           static_cast<cudaStream_t>(stream), true));
+}
+
+int skinny_qmm_w4g64_simt(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
+                          int N, int K, void* stream) {
+  if (!x || !w_tc || !out) return SKINNY_ERR_INVALID_ARG;
+  int st = check_qmm_shape(N, K);
+  if (st != SKINNY_OK) return st;
+  if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
+  if (ldx < K || ldo < N) return SKINNY_ERR_INVALID_ARG;
+  return cuda_status(skinny::qmm_simt_launch(x, ldx, w_tc, out, ldo, M, N, K,
+                                             static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

@@ -1,0 +1,266 @@
+"""4-bit affine group-64 quantized matmul for 1..16 tokens per weight read, on B200.
+
+Mirrors skinny_mlx/qmm.py (rachittshah/skinny-mlx):
+
+* ``repack_for_skinny`` (qmm.py:96) relays MLX 4-bit packs once at load, here into the
+  tcgen05 unit order (128 rows x 64 columns per 4608-byte unit, scales and biases folded in).
+* ``skinny_qmm`` (qmm.py:132) runs the sm_100a kernel: x [M, K] @ dequant(W)[N, K]^T -> [M, N],
+  computing sum_g s * sum(x q) + b * sum(x) per 64-group in f32 (the affine identity of
+  qmm.py:8-9), with x rounded to f16 for the tensor-core product as qmm.py:136 does.
+* ``qmm`` is the drop-in ``mx.quantized_matmul(x, w, scales, biases, transpose=True,
+  group_size=64, bits=4)`` entry: MLX packing in, relayout cached per weight.
+* ``quantize`` produces MLX's packing with the affine rule scale = (max - min) / 15,
+  bias = min per 64-column group.
+
+There is no CPU or library fallback: everything runs through the C-ABI in _skinny_b200.so.
+"""
+
+from __future__ import annotations
+
+import threading
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+GROUP = 64
+BITS = 4
+MAX_TOKENS = 16
+
+
+# ---------------------------------------------------------------------------------------------
+# quantization (MLX affine packing)
+# ---------------------------------------------------------------------------------------------
+def quantize(w: torch.Tensor, group_size: int = GROUP, bits: int = BITS):
+    """w [N, K] float -> (w_packed uint32-as-int32 [N, K/8], scales bf16 [N, K/64], biases bf16).
+
+    Per 64-column group: scale = (max - min) / 15, bias = min, both rounded to bf16, then
+    q = clamp(round((w - bias) / scale), 0, 15) with round-half-even; a constant group
+    (scale 0) gets q = 0.  Element k = 8j + i sits at bits 4i of word j, the order
+    skinny_mlx/qmm.py:104 decodes.
+    """
+    if group_size != GROUP or bits != BITS:
+        raise ValueError("only group_size=64, bits=4 is supported")
+    n, k = w.shape
+    if k % GROUP:
+        raise ValueError(f"K={k} is not a multiple of {GROUP}")
+    wg = w.float().reshape(n, k // GROUP, GROUP)
+    wmax = wg.amax(-1)
+    wmin = wg.amin(-1)
+    scales = ((wmax - wmin) / 15.0).to(torch.bfloat16)
+    biases = wmin.to(torch.bfloat16)
+    s32 = scales.float().unsqueeze(-1)
+    b32 = biases.float().unsqueeze(-1)
+    safe = torch.where(s32 == 0, torch.ones_like(s32), s32)
+    q = torch.round((wg - b32) / safe).clamp_(0, 15)
+    q = torch.where(s32 == 0, torch.zeros_like(q), q).to(torch.int64).reshape(n, k // 8, 8)
+    shifts = torch.arange(8, device=w.device, dtype=torch.int64) * 4
+    words = (q << shifts).sum(-1)
+    packed = words.to(torch.int64).bitwise_and(0xFFFFFFFF)
+    packed = torch.where(packed >= 2**31, packed - 2**32, packed).to(torch.int32)
+    return packed, scales, biases
+
+
+def dequantize(w_packed: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor) -> torch.Tensor:
+    """MLX packs -> float32 [N, K] (q * scale + bias)."""
+    n, kw = w_packed.shape
+    words = w_packed.to(torch.int64) & 0xFFFFFFFF
+    shifts = torch.arange(8, device=w_packed.device, dtype=torch.int64) * 4
+    q = ((words.unsqueeze(-1) >> shifts) & 0xF).reshape(n, kw * 8).float()
+    s = scales.float().repeat_interleave(GROUP, dim=1)
+    b = biases.float().repeat_interleave(GROUP, dim=1)
+    return q * s + b
+
+
+# ---------------------------------------------------------------------------------------------
+# relaid weights
+# ---------------------------------------------------------------------------------------------
+@dataclass
+class SkinnyWeight:
+    """Relaid 4-bit weight: `w_tc` holds ceil(N/128) * (K/64) units of 4608 bytes."""
+
+    w_tc: torch.Tensor
+    N: int
+    K: int
+
+    @property
+    def nbytes_mlx(self) -> int:
+        """Bytes of the original MLX packing (nibbles + bf16 scales + bf16 biases)."""
+        return self.N * self.K // 2 + self.N * (self.K // GROUP) * 4
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (no CPU fallback)")
+
+
+def repack_for_skinny(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor) -> SkinnyWeight:
+    """One-time relayout of MLX packs [N, K/8] + bf16 scales/biases [N, K/64] (C-ABI
+    skinny_repack_w4g64; replaces skinny_mlx/qmm.py:96)."""
+    for t, nm in ((w, "w"), (scales, "scales"), (biases, "biases")):
+        _require_cuda(t, nm)
+    n, kw = w.shape
+    k = kw * 8
+    if scales.shape != (n, k // GROUP) or biases.shape != (n, k // GROUP):
+        raise ValueError(f"scales/biases must be [{n}, {k // GROUP}]")
+    if scales.dtype != torch.bfloat16 or biases.dtype != torch.bfloat16:
+        raise ValueError("scales and biases must be bfloat16")
+    w = w.contiguous()
+    scales = scales.contiguous()
+    biases = biases.contiguous()
+    L = _lib.lib()
+    nbytes = L.skinny_repack_bytes(n, k)
+    if nbytes == 0:
+        raise ValueError(f"unsupported shape N={n} K={k}")
+    with torch.cuda.device(w.device):
+        out = torch.empty(nbytes, dtype=torch.uint8, device=w.device)
+        _lib.call("skinny_repack_w4g64", w.data_ptr(), scales.data_ptr(), biases.data_ptr(),
+                  out.data_ptr(), n, k, _stream_handle(w.device))
+    return SkinnyWeight(out, n, k)
+
+
+# ---------------------------------------------------------------------------------------------
+# workspace (one per device and stream; zero-filled; grows on demand)
+# ---------------------------------------------------------------------------------------------
+_ws_lock = threading.Lock()
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def workspace_bytes(n: int, k: int) -> int:
+    return int(_lib.lib().skinny_qmm_workspace_bytes(n, k))
+
+
+def get_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    key = (device.index if device.index is not None else torch.cuda.current_device(),
+           _stream_handle(device))
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            size = max(nbytes, 1 << 22)
+            if ws is not None:
+                size = max(size, 2 * ws.numel())
+            ws = torch.zeros(size, dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+        return ws
+
+
+def device_errors(device: torch.device | None = None) -> int:
+    """OR of the error words of every workspace on `device` (synchronises)."""
+    bits = 0
+    with _ws_lock:
+        for (dev, _), ws in _workspaces.items():
+            if device is None or dev == (device.index or 0):
+                bits |= int(ws[:4].view(torch.int32).item())
+    return bits
+
+
+def reset_workspaces() -> None:
+    with _ws_lock:
+        for ws in _workspaces.values():
+            ws.zero_()
+
+
+def config_for(m: int, n: int, k: int) -> dict:
+    """Launch configuration the library picks (mirrors skinny_mlx/qmm.py:118 config_for).
+
+    ``token_slots``: token columns each CTA reads back from TMEM (2, 4, 8 or 16);
+    ``units``: 128-row x 64-column units; ``ctas``: stream-K CTAs (one per SM, at most units).
+    """
+    t = (n + 127) // 128
+    units = t * (k // GROUP)
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    slots = 2 if m <= 2 else 4 if m <= 4 else 8 if m <= 8 else 16
+    return {"token_slots": slots, "units": units, "ctas": min(sms, units)}
+
+
+def skinny_qmm(x: torch.Tensor, w: SkinnyWeight, out: torch.Tensor | None = None) -> torch.Tensor:
+    """x [..., K] (bf16) @ dequant(W)^T -> [..., N] bf16 through the tcgen05 kernel.
+
+    Token counts above 16 are processed in 16-token chunks by the same kernel (each token's
+    result does not depend on the chunking).  Replaces skinny_mlx/qmm.py:132.
+    """
+    _require_cuda(x, "x")
+    if x.shape[-1] != w.K:
+        raise ValueError(f"x has K={x.shape[-1]}, weight has K={w.K}")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, w.K)
+    if x2.dtype != torch.bfloat16:
+        x2 = x2.to(torch.bfloat16)
+    if not x2.is_contiguous() or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    if m == 0:
+        return x.new_empty(*lead, w.N, dtype=torch.bfloat16)
+    dev = x2.device
+    if out is None:
+        out = torch.empty(m, w.N, dtype=torch.bfloat16, device=dev)
+    elif out.shape != (m, w.N) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 [M, N] tensor")
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        need = L.skinny_qmm_workspace_bytes(w.N, w.K)
+        ws = get_workspace(dev, need)
+        stream = _stream_handle(dev)
+        for c0 in range(0, m, MAX_TOKENS):
+            mc = min(MAX_TOKENS, m - c0)
+            xs = x2[c0:c0 + mc]
+            _lib.check("skinny_qmm_w4g64", L.skinny_qmm_w4g64(
+                xs.data_ptr(), w.K, w.w_tc.data_ptr(), out[c0].data_ptr(), w.N, mc, w.N, w.K,
+                ws.data_ptr(), ws.numel(), stream))
+    return out.reshape(*lead, w.N)
+
+
+def skinny_qmm_simt(x: torch.Tensor, w: SkinnyWeight) -> torch.Tensor:
+    """CUDA-core cross-check of the relaid format (tests only)."""
+    _require_cuda(x, "x")
+    x2 = x.reshape(-1, w.K).to(torch.bfloat16).contiguous()
+    m = x2.shape[0]
+    out = torch.empty(m, w.N, dtype=torch.bfloat16, device=x2.device)
+    with torch.cuda.device(x2.device):
+        for c0 in range(0, m, MAX_TOKENS):
+            mc = min(MAX_TOKENS, m - c0)
+            _lib.call("skinny_qmm_w4g64_simt", x2[c0].data_ptr(), w.K, w.w_tc.data_ptr(),
+                      out[c0].data_ptr(), w.N, mc, w.N, w.K, _stream_handle(x2.device))
+    return out.reshape(*x.shape[:-1], w.N)
+
+
+# ---------------------------------------------------------------------------------------------
+# MLX-style drop-in entry
+# ---------------------------------------------------------------------------------------------
+# value: (relaid weight, the source tensors) -- the strong references keep a freed tensor's
+# address from being reused under a stale key, as skinny_mlx/patch.py:66 does for its inputs.
+_repack_cache: dict[tuple, tuple] = {}
+
+
+def _cache_key(w, s, b):
+    return tuple((t.data_ptr(), tuple(t.shape), t._version) for t in (w, s, b))
+
+
+def qmm(x: torch.Tensor, w_packed: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+        group_size: int = GROUP, bits: int = BITS, transpose: bool = True) -> torch.Tensor:
+    """Drop-in for ``mx.quantized_matmul(x, w, scales, biases, transpose=True, group_size=64,
+    bits=4)`` (the call skinny_mlx/patch.py:35 and qmm.py:183 make) on MLX-packed weights.
+
+    The relayout is done on first use and cached per (w, scales, biases) storage and version.
+    Returns bf16 (x of another dtype is cast to bf16 first).
+    """
+    if group_size != GROUP or bits != BITS:
+        raise ValueError("skinny qmm supports group_size=64, bits=4 only")
+    if not transpose:
+        raise ValueError("skinny qmm computes x @ W^T (transpose=True) only")
+    key = _cache_key(w_packed, scales, biases)
+    hit = _repack_cache.get(key)
+    if hit is None:
+        hit = (repack_for_skinny(w_packed, scales, biases), (w_packed, scales, biases))
+        _repack_cache[key] = hit
+    return skinny_qmm(x, hit[0])
+
+
+__all__ = ["GROUP", "BITS", "MAX_TOKENS", "quantize", "dequantize", "SkinnyWeight",
+           "repack_for_skinny", "skinny_qmm", "skinny_qmm_simt", "qmm", "config_for",
+           "device_errors", "reset_workspaces", "workspace_bytes"]
