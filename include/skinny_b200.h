@@ -65,10 +65,13 @@ size_t skinny_qmm_workspace_bytes(int N, int K);
 
 /* out[M, N] (bf16, leading dimension ldo) = x[M, K] (bf16, leading dimension ldx) . W^T for
  * 1 <= M <= 16 tokens, computing sum_g s*sum(x*q) + b*sum(x) in f32 (skinny_mlx/qmm.py:8-9).
- * Activations are rounded to f16 for the tensor-core product, as skinny_mlx/qmm.py:136 does;
- * |x| > 65504 sets an error bit.  x and ldx*2 must be 16-byte aligned.  The workspace must be
- * zero-filled before its first use, hold skinny_qmm_workspace_bytes(N, K) bytes, and not be
- * shared by calls that may run concurrently.  Replaces skinny_mlx/qmm.py:132 skinny_qmm. */
+ * The tensor-core products use x exactly as given (bf16) and q exactly, accumulating in f32.
+ * Each token's output depends only on that token's row of x: it is bit-identical for any M.
+ * x and ldx*2 must be 16-byte aligned.  The workspace must be zero-filled before its first use,
+ * hold skinny_qmm_workspace_bytes(N, K) bytes, and not be shared by calls that may run
+ * concurrently; calls of different shapes may share it.  Launches use programmatic dependent
+ * launch, so the weight stream of a call overlaps the tail of the kernel before it.
+ * Replaces skinny_mlx/qmm.py:132 skinny_qmm. */
 int skinny_qmm_w4g64(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M, int N,
                      int K, void* workspace, size_t workspace_bytes, void* stream);
 

@@ -41,6 +41,7 @@ int ctas_for(int N, int K) {
 
 int check_qmm_shape(int N, int K) {
   if (N < 1 || K < skinny::kGroup) return SKINNY_ERR_SHAPE;
+  if (N > skinny::kMaxTiles * skinny::kTileRows) return SKINNY_ERR_SHAPE;
   if (K % skinny::kGroup != 0) return SKINNY_ERR_SHAPE;
   return SKINNY_OK;
 }
@@ -85,7 +86,7 @@ int skinny_repack_w4g64(const uint32_t* w, const uint16_t* scales, const uint16_
 
 size_t skinny_qmm_workspace_bytes(int N, int K) {
   if (check_qmm_shape(N, K) != SKINNY_OK) return 0;
-  return skinny::ws_layout(N, K, ctas_for(N, K)).total;
+  return skinny::ws_layout(N, K, skinny::device_sm_count(current_device())).total;
 }
 
 int skinny_qmm_w4g64(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M, int N,
@@ -97,7 +98,7 @@ int skinny_qmm_w4g64(const void* x, int ldx, const void* w_tc, void* out, int ld
   if (ldx < K || ldo < N) return SKINNY_ERR_INVALID_ARG;
   if (!aligned16(x) || (ldx % 8) != 0 || !aligned16(w_tc)) return SKINNY_ERR_ALIGNMENT;
   const int C = ctas_for(N, K);
-  const skinny::WsLayout wl = skinny::ws_layout(N, K, C);
+  const skinny::WsLayout wl = skinny::ws_layout(N, K, skinny::device_sm_count(current_device()));
   if (!workspace || workspace_bytes < wl.total || !aligned16(workspace)) return SKINNY_ERR_WORKSPACE;
   return cuda_status(skinny::qmm_tc_launch(x, ldx, w_tc, out, ldo, M, N, K, workspace, C,
                                            static_cast<cudaStream_t>(stream), true));

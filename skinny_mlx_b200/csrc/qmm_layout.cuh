@@ -14,11 +14,8 @@
 // and one shift produce f16 pairs in natural column order (the 0x6400 "1024 + q" trick):
 //   bits 0-3 k0 | 4-7 k2 | 8-11 k4 | 12-15 k6 | 16-19 k1 | 20-23 k3 | 24-27 k5 | 28-31 k7
 //
-// Activations.  For each 64-column group the x-prep kernel writes one 2112-byte block:
-//   2048 B: x^T as f16 for 16 token slots in the tcgen05 K-major no-swizzle canonical layout,
-//           four 16-column MMA slices of 512 B, each [token-block tb][k-half kh][8 tok][8 col],
-//           so LBO (k-half stride) = 128 B and SBO (token-block stride) = 256 B;
-//     64 B: xsum[16] f32 = sum of the group's 64 f16-rounded activations per token slot.
+// Activations are read as given (bf16 [M, K], row stride ldx) through a TMA tensor map: one box
+// of 64 columns x 8 or 16 token rows per unit, 128-byte swizzled, rows past M zero-filled.
 #pragma once
 #include <cstddef>
 #include <cstdint>
@@ -30,9 +27,6 @@ constexpr int kGroup = 64;
 constexpr int kMaxTokens = 16;
 constexpr int kUnitWBytes = 4608;   // 4096 nibble bytes + 512 scale/bias bytes
 constexpr int kUnitNibBytes = 4096;
-constexpr int kUnitXBytes = 2112;   // 2048 f16 bytes + 64 xsum bytes
-constexpr int kUnitXMatBytes = 2048;
-constexpr int kXsumOffset = 2048;
 
 // Stream-K CTA partition: CTA c owns units [u_begin(c), u_begin(c+1)).
 __host__ __device__ inline long long u_begin(long long c, long long U, long long C) {
@@ -60,21 +54,22 @@ __host__ __device__ inline QmmShape qmm_shape(int N, int K) {
 
 inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Workspace layout for one qmm call (caller-owned, zero-filled before its first use):
-//   [0, 256)            header; word 0 = device error bits
-//   [256, +T*4)         per-tile arrival counters (every launch leaves them at zero)
-//   partials            C x 2 slots x 16 tokens x 128 rows f32
-//   x blocks            G x 2112 bytes
+// Workspace layout (caller-owned, zero-filled before its first use).  The counter region has a
+// fixed offset and capacity so that calls of different shapes can share one workspace: only the
+// counters must persist between launches (each launch leaves them at zero); partials are
+// rewritten by every launch before they are read.
+//   [0, 256)                      header; word 0 = device error bits
+//   [256, 256 + 4*kMaxTiles)      per-tile arrival counters
+//   partials                      C_dev x 2 slots x 16 tokens x 128 rows f32
+constexpr int kMaxTiles = 16384;  // N <= 2,097,152 rows
 struct WsLayout {
-  size_t cnt_off, part_off, x_off, total;
+  size_t cnt_off, part_off, total;
 };
-inline WsLayout ws_layout(int N, int K, int C) {
-  QmmShape s = qmm_shape(N, K);
+inline WsLayout ws_layout(int /*N*/, int /*K*/, int C_dev) {
   WsLayout w;
   w.cnt_off = 256;
-  w.part_off = round_up(w.cnt_off + static_cast<size_t>(s.T) * 4, 256);
-  w.x_off = round_up(w.part_off + static_cast<size_t>(C) * 2 * kMaxTokens * kTileRows * 4, 256);
-  w.total = round_up(w.x_off + static_cast<size_t>(s.G) * kUnitXBytes, 256);
+  w.part_off = w.cnt_off + static_cast<size_t>(kMaxTiles) * 4;
+  w.total = round_up(w.part_off + static_cast<size_t>(C_dev) * 2 * kMaxTokens * kTileRows * 4, 256);
   return w;
 }
 

@@ -2,33 +2,54 @@
 //
 //   out[t, n] = sum_g ( s[n,g] * sum_{k in g} x[t,k] * q[n,k]  +  b[n,g] * xsum[t,g] )
 //
-// This is the affine identity of skinny_mlx/qmm.py:8-9 and :64-71 (scale and bias applied once
-// per 64-group), computed "swap-AB": weight rows are the 128-row MMA operand A and the tokens are
-// the N=16 operand B, so a 1..16-token step reads every weight byte exactly once.
+// This is the affine identity of skinny_mlx/qmm.py:8-9 and :64-71: scale and bias are applied
+// once per 64-column group, in f32.  It is computed "swap-AB": weight rows are the 128-row MMA
+// operand A and the tokens are the N=16 operand B, so a 1..16-token step reads every weight byte
+// exactly once.
+//
+// Operands are bf16.  A nibble q OR-ed into the bf16 0x4300 (= 128) gives 128 + q exactly (the
+// bf16 form of the reference's f16 0x6400 "1024 + q" trick, skinny_mlx/qmm.py:57-58), so the MMA
+// sees A = 128 + q and x exactly as given, with f32 products exact.  A helper warp sums each x
+// tile per token (xsum, f32, fixed reduction tree), and the epilogue folds the offset away:
+//   s * sum x (128 + q) + (b - 128 s) * xsum  =  s * sum x q + b * xsum.
 //
 // Work split (stream-K): the matrix is cut into units of 128 rows x 64 columns (4608 relaid
 // bytes, see qmm_layout.cuh) and each of the C CTAs (one per SM) takes a contiguous range of
-// units in tile-major order.  A CTA therefore streams one contiguous byte range of the relaid
-// weights.  Tiles that straddle CTAs are finished by whichever contributing CTA arrives last; it
-// adds the partial sums in contributor order, so results are deterministic and do not depend on
-// the token count (row t of a 16-token call equals the same row of a 1-token call, bit for bit).
+// units in tile-major order, i.e. one contiguous byte range of the relaid weights.  Tiles that
+// straddle CTAs are finished by the contributing CTA that arrives last; it adds the partial sums
+// in contributor order, so results are deterministic and independent of the token count (row t
+// of a 16-token call equals the same row of a 1-token call bit for bit).
 //
-// Warp roles in a CTA of 320 threads:
-//   warp 0 lane 0  TMA producer: bulk-copies weight units and x blocks into a 12-stage ring.
-//                  Weight units are prefetched before griddepcontrol.wait (they do not depend on
-//                  the previous kernel), so with programmatic dependent launch the weight stream
-//                  of this launch overlaps the tail of the previous one.
-//   warp 1         allocates TMEM; lane 0 issues 4 tcgen05.mma (128x16x16) per unit, A read from
-//                  TMEM, B = x^T from shared memory, D (f32) into a TMEM slot per unit.
-//   warps 2..9     two warpgroups; thread <-> weight row (TMEM lane).  Warpgroup h dequantizes
-//                  columns 32h..32h+31 of every unit: 0x6400 | nibble gives the f16 1024+q, the
-//                  high nibble of each byte gives 1024+16q, and one HSUB2/HFMA2 yields q exactly;
-//                  tcgen05.st writes the pairs into the unit's A slot.  One unit later the same
-//                  threads read the unit's 16 partial dot products from TMEM and apply scale and
-//                  bias in f32 (warpgroup h owns token slots h*NTH .. h*NTH+NTH-1).
+// Load stages.  A TMA bulk copy costs a roughly fixed amount of engine time, so small copies cap
+// the stream well below HBM bandwidth (measured on B200: 4.6 KB copies ~2.6 TB/s per CTA-per-SM,
+// 18 KB copies ~6.6 TB/s).  A stage therefore carries up to 4 consecutive units of one tile:
+// one bulk copy of their weights and one tensor-map box per unit for its x tile
+// (64 columns x 8 or 16 token rows, SWIZZLE_128B, rows past M zero-filled).  Stages
+// alternate between two (dequant warpgroup, MMA issuer) pairs, so each stage is consumed and
+// released by exactly one pair plus the xsum warp.
+//
+// Warp roles in a CTA of 512 threads (16 warps):
+//   warp 0 lane 0   TMA producer over a 3-stage ring.  The first stages are issued before
+//                   griddepcontrol.wait only for their weights (weights do not depend on the
+//                   previous kernel), so under programmatic dependent launch this launch's weight
+//                   stream overlaps the tail of the previous one.  Tensor memory is allocated
+//                   after that, since the previous kernel's CTA on this SM may still hold it.
+//   warps 1, 15     MMA issuers for even / odd stages (warp 1 also allocates TMEM): per unit 4
+//                   independent tcgen05.mma 128x16x16 (one per 16-column K slice, A = the unit's
+//                   dequantized slot in TMEM, B = its x tile) as two independent 2-deep chains
+//                   into two 16-column D sub-slots (long accumulation chains serialise in the
+//                   tensor pipe).
+//   warps 2..5      epilogue warpgroup, units in order: thread = weight row = TMEM lane; sums
+//                   the 4 partial dot products, applies scale/bias with the tile's xsums and
+//                   accumulates in f32 registers; writes finished tiles or publishes partials.
+//   warps 6..9      dequant warpgroup for even stages, warps 10..13 for odd stages: thread =
+//                   weight row; 64 nibbles (two 16-byte shared loads) -> 32 bf16x2 words ->
+//                   tcgen05.st into the unit's A slot.
+//   warp 14         xsum: per unit sums each token row of its x tile from shared memory.
 #include <cstdint>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
-#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "ptx.cuh"
@@ -37,63 +58,80 @@
 
 namespace skinny {
 
-constexpr int kStages = 12;
-constexpr int kStageBytes = 6784;  // 4608 + 2112 rounded up to 128
-constexpr int kNumA = 4;           // TMEM A slots (32 columns each)
-constexpr int kNumD = 4;           // TMEM D slots (16 columns each)
-constexpr int kTmemCols = 256;
-constexpr int kDCol0 = kNumA * 32;
-constexpr int kThreads = 320;
-constexpr int kEpiThreads = 256;
+constexpr int kStages = 3;
+constexpr int kUPS = 4;                            // units per stage (same tile)
+constexpr int kXTileBytes = 2048;                  // 16 token rows x 128 B (SWIZZLE_128B)
+constexpr int kXStageBytes = kUPS * kXTileBytes;   // 8 KB
+constexpr int kWStageBytes = kUPS * kUnitWBytes;   // 18 KB
+constexpr int kXRingBytes = kStages * kXStageBytes;
+constexpr int kWRingBytes = kStages * kWStageBytes;
+constexpr int kNumA = 2 * kUPS;                    // TMEM A slots: 4 per dequant warpgroup
+// TMEM D slots (2 x 16 columns each).  The two MMA issuers own alternate 4-unit stages, so one
+// issuer's consecutive units can be up to 5 apart; the D ring must be at least that deep or a
+// parity wait on d_empty can alias a phase two ahead.
+constexpr int kNumD = 8;
+constexpr int kTmemCols = 512;
+constexpr int kDCol0 = kNumA * 32;                 // 256
+constexpr int kThreads = 512;
+constexpr int kEpiThreads = 128;
+constexpr int kDeqThreads = 128;                   // per warpgroup
+constexpr int kXsumWarp = 14;
+constexpr int kRS = 16;                            // per-unit scale/bias + xsum ring for the epilogue
 
 struct QmmParams {
   const uint8_t* w_tc;  // relaid weight units
-  const uint8_t* xw;    // x blocks [G][2112] (workspace)
   __nv_bfloat16* out;   // [M, ldo]
-  float* part;          // [C][2][16][128] partial sums (workspace)
-  uint32_t* cnt;        // [T] arrival counters (workspace)
+  float* part;          // [C_dev][2][16][128] partial sums (workspace)
+  uint32_t* cnt;        // [kMaxTiles] arrival counters (workspace)
   uint32_t* err;        // device error word (workspace)
-  int M, N, G, T, C, ldo;
+  int M, N, G, T, C, ldo, x_rows;
   long long U;
 };
 
-struct __align__(8) QmmSmemBarriers {
+// The epilogue, which trails the MMA, reads each unit's scale/bias words and xsums from a
+// kRS-deep ring, so a load stage is released as soon as its dequant warpgroup, the xsum warp and
+// its MMA issuer are done with it and the epilogue's lag never throttles the TMA stream.
+struct __align__(16) QmmSmemBarriers {
+  uint32_t sbr[kRS][kTileRows];        // per-unit (bf16 scale, bf16 bias) of each row
+  float xsr[kRS][kMaxTokens];          // per-unit xsum of each token
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t a_full[kNumA];
   uint64_t a_empty[kNumA];
   uint64_t d_full[kNumD];
   uint64_t d_empty[kNumD];
-  uint64_t mma_done;
+  uint64_t sb_full[kRS];
+  uint64_t xs_full[kRS];
+  uint64_t ep_empty[kRS];
+  uint64_t mma_done[2];
   uint32_t tmem_base;
   int abort_flag;
   int last_flag;
 };
 
-constexpr size_t kQmmSmemBytes = static_cast<size_t>(kStages) * kStageBytes + 1024;
+constexpr int kBarBytes = 12288;
+constexpr size_t kQmmSmemBytes = static_cast<size_t>(kXRingBytes) + kWRingBytes + kBarBytes + 1024;
+static_assert(sizeof(QmmSmemBarriers) <= kBarBytes, "barrier block");
 
-// 16 nibbles of one row (4 relaid words) -> 8 f16x2 pairs holding q exactly, natural column order.
-__device__ __forceinline__ void decode4(const uint4& w, uint32_t (&o)[16]) {
-  const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-  const __half2 k1024 = __half2half2(__ushort_as_half(0x6400));  // 1024
-  const __half2 k1_16 = __half2half2(__float2half(0.0625f));
-  const __half2 km64 = __half2half2(__float2half(-64.0f));
+// Units of the next stage starting at unit u: at most kUPS, never past the range end or a tile.
+__device__ __forceinline__ int stage_units(long long u, long long u1, int G) {
+  long long n = u1 - u;
+  const int to_tile_end = G - static_cast<int>(u % G);
+  if (n > to_tile_end) n = to_tile_end;
+  return n < kUPS ? static_cast<int>(n) : kUPS;
+}
+
+// 64 nibbles of one row (8 relaid words) -> 32 bf16x2 words holding (128 + q) exactly, in
+// natural column order: pair j of word w covers columns 8w + 2j, 8w + 2j + 1.
+__device__ __forceinline__ void decode8(const uint4& lo, const uint4& hi, uint32_t (&o)[32]) {
+  const uint32_t words[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < 8; ++j) {
     const uint32_t v = words[j];
-    const uint32_t v8 = v >> 8;
-    uint32_t p0 = (v & 0x000F000Fu) | 0x64006400u;   // 1024 + (k0, k1)
-    uint32_t p1 = (v & 0x00F000F0u) | 0x64006400u;   // 1024 + 16 (k2, k3)
-    uint32_t p2 = (v8 & 0x000F000Fu) | 0x64006400u;  // 1024 + (k4, k5)
-    uint32_t p3 = (v8 & 0x00F000F0u) | 0x64006400u;  // 1024 + 16 (k6, k7)
-    __half2 h0 = __hsub2(*reinterpret_cast<__half2*>(&p0), k1024);
-    __half2 h1 = __hfma2(*reinterpret_cast<__half2*>(&p1), k1_16, km64);
-    __half2 h2 = __hsub2(*reinterpret_cast<__half2*>(&p2), k1024);
-    __half2 h3 = __hfma2(*reinterpret_cast<__half2*>(&p3), k1_16, km64);
-    o[4 * j + 0] = *reinterpret_cast<uint32_t*>(&h0);
-    o[4 * j + 1] = *reinterpret_cast<uint32_t*>(&h1);
-    o[4 * j + 2] = *reinterpret_cast<uint32_t*>(&h2);
-    o[4 * j + 3] = *reinterpret_cast<uint32_t*>(&h3);
+    o[4 * j + 0] = (v & 0x000F000Fu) | 0x43004300u;
+    o[4 * j + 1] = ((v >> 4) & 0x000F000Fu) | 0x43004300u;
+    o[4 * j + 2] = ((v >> 8) & 0x000F000Fu) | 0x43004300u;
+    o[4 * j + 3] = ((v >> 12) & 0x000F000Fu) | 0x43004300u;
   }
 }
 
@@ -101,251 +139,362 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-template <int NTH>
-__global__ void __launch_bounds__(kThreads, 1) qmm_w4g64_tc_kernel(const QmmParams p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  QmmSmemBarriers* sb = reinterpret_cast<QmmSmemBarriers*>(smem + kStages * kStageBytes);
+// NT: token columns read back per unit (2, 4, 8 or 16).
+template <int NT>
+__global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
+    qmm_w4g64_tc_kernel(const QmmParams p, const __grid_constant__ CUtensorMap tmap_x) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the SWIZZLE_128B x tiles
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* xring = smem;
+  uint8_t* wring = smem + kXRingBytes;
+  QmmSmemBarriers* sb = reinterpret_cast<QmmSmemBarriers*>(wring + kWRingBytes);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int c = blockIdx.x;
   const long long u0 = u_begin(c, p.U, p.C);
   const long long u1 = u_begin(c + 1, p.U, p.C);
   const int L = static_cast<int>(u1 - u0);
+  const int xtile = p.x_rows * 128;  // bytes of one x tile in shared memory
   volatile int* abort_flag = &sb->abort_flag;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(smem_u32(&sb->full[i]), 1);
-      mbar_init(smem_u32(&sb->empty[i]), 1);
+      mbar_init(smem_u32(&sb->empty[i]), 1 + kDeqThreads + 32);  // MMA commit + dequant wg + xsum warp
     }
     for (int i = 0; i < kNumA; ++i) {
-      mbar_init(smem_u32(&sb->a_full[i]), kEpiThreads);
+      mbar_init(smem_u32(&sb->a_full[i]), kDeqThreads);
       mbar_init(smem_u32(&sb->a_empty[i]), 1);
     }
     for (int i = 0; i < kNumD; ++i) {
       mbar_init(smem_u32(&sb->d_full[i]), 1);
       mbar_init(smem_u32(&sb->d_empty[i]), kEpiThreads);
     }
-    mbar_init(smem_u32(&sb->mma_done), 1);
+    for (int i = 0; i < kRS; ++i) {
+      mbar_init(smem_u32(&sb->sb_full[i]), kDeqThreads);
+      mbar_init(smem_u32(&sb->xs_full[i]), 32);
+      mbar_init(smem_u32(&sb->ep_empty[i]), kEpiThreads);
+    }
+    mbar_init(smem_u32(&sb->mma_done[0]), 1);
+    mbar_init(smem_u32(&sb->mma_done[1]), 1);
     sb->abort_flag = 0;
     sb->last_flag = 0;
     fence_mbar_init();
+    prefetch_tmap(&tmap_x);
   }
-  if (warp == 1) {
-    tmem_alloc(smem_u32(&sb->tmem_base), kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
   __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = sb->tmem_base;
   pdl_launch_dependents();
+  // The producer starts streaming before tensor memory is allocated: under programmatic
+  // dependent launch the CTA of the previous kernel on this SM may still hold its columns.
+  uint32_t tmem = 0;
+  if (warp != 0) {
+    if (warp == 1) {
+      tmem_alloc(smem_u32(&sb->tmem_base), kTmemCols);
+      tmem_relinquish();
+    }
+    tc_fence_before();
+    named_bar_sync(2, kThreads - 32);
+    tc_fence_after();
+    tmem = sb->tmem_base;
+  }
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------ TMA producer ------------------------------
       const uint64_t pol_w = policy_evict_first();
-      const uint64_t pol_x = policy_evict_last();
-      const int pre = L < kStages ? L : kStages;
-      for (int i = 0; i < pre; ++i) {
-        const uint32_t stage = smem_u32(smem + i * kStageBytes);
-        mbar_arrive_expect_tx(smem_u32(&sb->full[i]), kUnitWBytes + kUnitXBytes);
-        bulk_g2s_hint(stage, p.w_tc + (u0 + i) * kUnitWBytes, kUnitWBytes, smem_u32(&sb->full[i]),
-                      pol_w);
+      const uint32_t xbytes = static_cast<uint32_t>(xtile);
+      long long u = u0;
+      int k = 0;
+      // first stages: weights before griddepcontrol.wait, x tiles after
+      long long first_u[kStages];
+      int nfirst = 0;
+      while (u < u1 && k < kStages) {
+        const int n = stage_units(u, u1, p.G);
+        mbar_arrive_expect_tx(smem_u32(&sb->full[k]), static_cast<uint32_t>(n) * (kUnitWBytes + xbytes));
+        bulk_g2s_hint(smem_u32(wring + k * kWStageBytes), p.w_tc + u * kUnitWBytes,
+                      static_cast<uint32_t>(n) * kUnitWBytes, smem_u32(&sb->full[k]), pol_w);
+        first_u[k] = u;
+        u += n;
+        ++k;
+        ++nfirst;
       }
-      pdl_wait_prior_grid();  // x blocks are written by the x-prep kernel
-      for (int i = 0; i < pre; ++i) {
-        const uint32_t stage = smem_u32(smem + i * kStageBytes);
-        const int g = static_cast<int>((u0 + i) % p.G);
-        bulk_g2s_hint(stage + kUnitWBytes, p.xw + static_cast<size_t>(g) * kUnitXBytes, kUnitXBytes,
-                      smem_u32(&sb->full[i]), pol_x);
+      pdl_wait_prior_grid();  // x is produced by the previous kernel
+      for (int f = 0; f < nfirst; ++f) {
+        const int g = static_cast<int>(first_u[f] % p.G);
+        const int n = stage_units(first_u[f], u1, p.G);
+        for (int j = 0; j < n; ++j)
+          tma_load_2d(smem_u32(xring + f * kXStageBytes + j * xtile), &tmap_x, (g + j) * kGroup, 0,
+                      smem_u32(&sb->full[f]));
       }
-      for (int i = kStages; i < L; ++i) {
-        const int s = i % kStages;
-        if (!mbar_wait(smem_u32(&sb->empty[s]), ((i / kStages) - 1) & 1, p.err, kErrBitWaitEmpty,
+      while (u < u1) {
+        const int s = k % kStages;
+        if (!mbar_wait(smem_u32(&sb->empty[s]), ((k / kStages) - 1) & 1, p.err, kErrBitWaitEmpty,
                        abort_flag))
           break;
-        const uint32_t stage = smem_u32(smem + s * kStageBytes);
-        const int g = static_cast<int>((u0 + i) % p.G);
-        mbar_arrive_expect_tx(smem_u32(&sb->full[s]), kUnitWBytes + kUnitXBytes);
-        bulk_g2s_hint(stage, p.w_tc + (u0 + i) * kUnitWBytes, kUnitWBytes, smem_u32(&sb->full[s]),
-                      pol_w);
-        bulk_g2s_hint(stage + kUnitWBytes, p.xw + static_cast<size_t>(g) * kUnitXBytes, kUnitXBytes,
-                      smem_u32(&sb->full[s]), pol_x);
+        const int n = stage_units(u, u1, p.G);
+        const int g = static_cast<int>(u % p.G);
+        mbar_arrive_expect_tx(smem_u32(&sb->full[s]), static_cast<uint32_t>(n) * (kUnitWBytes + xbytes));
+        bulk_g2s_hint(smem_u32(wring + s * kWStageBytes), p.w_tc + u * kUnitWBytes,
+                      static_cast<uint32_t>(n) * kUnitWBytes, smem_u32(&sb->full[s]), pol_w);
+        for (int j = 0; j < n; ++j)
+          tma_load_2d(smem_u32(xring + s * kXStageBytes + j * xtile), &tmap_x, (g + j) * kGroup, 0,
+                      smem_u32(&sb->full[s]));
+        u += n;
+        ++k;
       }
       // Never leave the CTA with copies in flight: wait (bounded, ignoring abort) for the last
       // stages issued.  On the normal path they completed long ago.
       int zero = 0;
-      for (int i = (L > kStages ? L - kStages : 0); i < L; ++i) {
-        const int s = i % kStages;
-        mbar_wait(smem_u32(&sb->full[s]), (i / kStages) & 1, p.err, kErrBitWaitDrain, &zero);
-      }
+      for (int kk = (k > kStages ? k - kStages : 0); kk < k; ++kk)
+        mbar_wait(smem_u32(&sb->full[kk % kStages]), (kk / kStages) & 1, p.err, kErrBitWaitDrain, &zero);
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 15) {
     if (lane == 0) {
-      // ------------------------------ MMA issuer ------------------------------
-      constexpr uint32_t idesc = idesc_f16_f32(128, 16);
-      for (int i = 0; i < L; ++i) {
-        const int s = i % kStages, a = i % kNumA, d = i % kNumD;
-        if (!mbar_wait(smem_u32(&sb->full[s]), (i / kStages) & 1, p.err, kErrBitWaitFull, abort_flag))
-          break;
-        if (!mbar_wait(smem_u32(&sb->a_full[a]), (i / kNumA) & 1, p.err, kErrBitWaitAFull, abort_flag))
-          break;
-        if (i >= kNumD &&
-            !mbar_wait(smem_u32(&sb->d_empty[d]), ((i / kNumD) - 1) & 1, p.err, kErrBitWaitDEmpty,
-                       abort_flag))
-          break;
-        tc_fence_after();
-        const uint32_t xs = smem_u32(smem + s * kStageBytes + kUnitWBytes);
-        const uint32_t d_tmem = tmem + kDCol0 + d * 16;
-        const uint32_t a_tmem = tmem + a * 32;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint64_t bdesc = smem_desc_noswizzle(xs + j * 512, 128, 256);
-          umma_f16_ts(d_tmem, a_tmem + j * 8, bdesc, idesc, j > 0 ? 1u : 0u);
+      // ------------------------------ MMA issuers (stages alternate) ---------------------------
+      const int w = warp == 1 ? 0 : 1;
+      constexpr uint32_t idesc = idesc_bf16_f32(128, 16);
+      const uint64_t desc0 = smem_desc_sw128(smem_u32(xring));
+      uint32_t a_uses[kUPS] = {0, 0, 0, 0};
+      long long u = u0;
+      int i = 0;  // unit index within this CTA
+      bool live = true;
+      for (int k = 0; u < u1 && live; ++k) {
+        const int n = stage_units(u, u1, p.G);
+        if ((k & 1) == w) {
+          const int s = k % kStages;
+          if (!mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag))
+            break;
+          for (int j = 0; j < n; ++j) {
+            const int a = w * kUPS + j;
+            const int d = (i + j) % kNumD;
+            if (!mbar_wait(smem_u32(&sb->a_full[a]), a_uses[j] & 1, p.err, kErrBitWaitAFull, abort_flag) ||
+                (i + j >= kNumD &&
+                 !mbar_wait(smem_u32(&sb->d_empty[d]), (((i + j) / kNumD) - 1) & 1, p.err,
+                            kErrBitWaitDEmpty, abort_flag))) {
+              live = false;
+              break;
+            }
+            ++a_uses[j];
+            tc_fence_after();
+            // start-address field: stage base + j x-tile + 32 bytes per 16-column K slice
+            const uint64_t bdesc = desc0 + static_cast<uint64_t>((s * kXStageBytes + j * xtile) >> 4);
+            const uint32_t d_dot = tmem + kDCol0 + d * 32;
+            const uint32_t a_tmem = tmem + a * 32;
+            umma_f16_ts(d_dot, a_tmem, bdesc, idesc, 0u);                 // columns 0-15
+            umma_f16_ts(d_dot + 16, a_tmem + 16, bdesc + 4, idesc, 0u);   // columns 32-47
+            umma_f16_ts(d_dot, a_tmem + 8, bdesc + 2, idesc, 1u);         // columns 16-31
+            umma_f16_ts(d_dot + 16, a_tmem + 24, bdesc + 6, idesc, 1u);   // columns 48-63
+            umma_commit(smem_u32(&sb->a_empty[a]));
+            umma_commit(smem_u32(&sb->d_full[d]));
+          }
+          if (!live) break;
+          umma_commit(smem_u32(&sb->empty[s]));
         }
-        umma_commit(smem_u32(&sb->empty[s]));
-        umma_commit(smem_u32(&sb->a_empty[a]));
-        umma_commit(smem_u32(&sb->d_full[d]));
+        u += n;
+        i += n;
       }
-      // All MMAs issued by this thread must be complete before TMEM is released.
-      umma_commit(smem_u32(&sb->mma_done));
+      // Every MMA issued by this thread completes before TMEM is released.
+      umma_commit(smem_u32(&sb->mma_done[w]));
       int zero = 0;
-      mbar_wait(smem_u32(&sb->mma_done), 0, p.err, kErrBitWaitDrain, &zero);
+      mbar_wait(smem_u32(&sb->mma_done[w]), 0, p.err, kErrBitWaitDrain, &zero);
     }
-  } else {
-    // ------------------------------ dequant + epilogue ------------------------------
-    const int e = threadIdx.x - 64;
-    const int wg = e >> 7;
-    const int quad = warp & 3;
-    const int r = quad * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    float acc[NTH];
+  } else if (warp == kXsumWarp) {
+    // ------------------------------ xsum of each x tile ------------------------------
+    // lane = (token t = lane / 2, half h = lane % 2); chunk sums are combined in the same tree
+    // for every token count, so a token's xsum is bit-identical for any M.
+    const int t = lane >> 1, h = lane & 1;
+    long long u = u0;
+    int i = 0;
+    bool live = true;
+    for (int k = 0; u < u1 && live; ++k) {
+      const int n = stage_units(u, u1, p.G);
+      const int s = k % kStages;
+      if (!mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag))
+        break;
+      float part[kUPS];
+      for (int j = 0; j < n; ++j) {
+        // rows >= x_rows of a tile belong to the next tile (or are stale): their sums are unused
+        const uint8_t* row = xring + s * kXStageBytes + j * xtile + t * 128;
+        float cs[4];
 #pragma unroll
-    for (int t = 0; t < NTH; ++t) acc[t] = 0.f;
-    // pending epilogue (unit i-1)
-    float pend_s = 0.f, pend_b = 0.f, pend_xs[NTH];
+        for (int q = 0; q < 4; ++q) {
+          const int cch = 4 * h + q;  // 16-byte chunk = 8 columns; SWIZZLE_128B permutes chunks by row
+          const uint4 v = *reinterpret_cast<const uint4*>(row + ((cch ^ (t & 7)) << 4));
+          const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+          float acc = 0.f;
 #pragma unroll
-    for (int t = 0; t < NTH; ++t) pend_xs[t] = 0.f;
-    bool dep_waited = false;
-
-    auto flush = [&](long long tile, bool full_tile, bool first_seg) {
-      const int row_g = static_cast<int>(tile) * kTileRows + r;
-      const bool ok = !*abort_flag;
-      if (!dep_waited) {
-        pdl_wait_prior_grid();
-        dep_waited = true;
-      }
-      if (full_tile) {
-        if (ok && row_g < p.N) {
-#pragma unroll
-          for (int t = 0; t < NTH; ++t) {
-            const int tok = wg * NTH + t;
-            if (tok < p.M) p.out[static_cast<size_t>(tok) * p.ldo + row_g] = __float2bfloat16_rn(acc[t]);
+          for (int kk = 0; kk < 4; ++kk) {
+            acc += __uint_as_float(wv[kk] << 16);
+            acc += __uint_as_float(wv[kk] & 0xFFFF0000u);
           }
+          cs[q] = acc;
         }
-        return;
+        float pt = (cs[0] + cs[1]) + (cs[2] + cs[3]);
+        pt += __shfl_xor_sync(0xFFFFFFFFu, pt, 1);
+        part[j] = pt;
       }
-      const int slot = first_seg ? 0 : 1;
-      float* mine = p.part + (static_cast<size_t>(c) * 2 + slot) * kMaxTokens * kTileRows;
-#pragma unroll
-      for (int t = 0; t < NTH; ++t) mine[(wg * NTH + t) * kTileRows + r] = acc[t];
-      __threadfence();
-      named_bar_sync(1, kEpiThreads);
-      if (e == 0) {
-        const long long cf = cta_of_unit(tile * p.G, p.U, p.C);
-        const long long cl = cta_of_unit(tile * p.G + p.G - 1, p.U, p.C);
-        const unsigned n_contrib = static_cast<unsigned>(cl - cf + 1);
-        const unsigned old = ok ? atomicAdd(&p.cnt[tile], 1u) : 0u;
-        sb->last_flag = ok && (old == n_contrib - 1);
-      }
-      named_bar_sync(1, kEpiThreads);
-      if (sb->last_flag) {
-        __threadfence();
-        const long long cf = cta_of_unit(tile * p.G, p.U, p.C);
-        const long long cl = cta_of_unit(tile * p.G + p.G - 1, p.U, p.C);
-        float v[NTH];
-#pragma unroll
-        for (int t = 0; t < NTH; ++t) v[t] = 0.f;
-        for (long long cc = cf; cc <= cl; ++cc) {
-          const long long cu0 = u_begin(cc, p.U, p.C);
-          const int cs = (cu0 / p.G == tile) ? 0 : 1;
-          const float* src = p.part + (static_cast<size_t>(cc) * 2 + cs) * kMaxTokens * kTileRows;
-#pragma unroll
-          for (int t = 0; t < NTH; ++t) v[t] += __ldcg(src + (wg * NTH + t) * kTileRows + r);
+      mbar_arrive(smem_u32(&sb->empty[s]));  // this warp is done with the stage's x tiles
+      for (int j = 0; j < n; ++j) {
+        const int jr = (i + j) % kRS;
+        if (i + j >= kRS && !mbar_wait(smem_u32(&sb->ep_empty[jr]), (((i + j) / kRS) - 1) & 1, p.err,
+                                       kErrBitWaitEmpty, abort_flag)) {
+          live = false;
+          break;
         }
-        if (row_g < p.N) {
-#pragma unroll
-          for (int t = 0; t < NTH; ++t) {
-            const int tok = wg * NTH + t;
-            if (tok < p.M) p.out[static_cast<size_t>(tok) * p.ldo + row_g] = __float2bfloat16_rn(v[t]);
+        if (h == 0) sb->xsr[jr][t] = part[j];
+        __syncwarp();
+        mbar_arrive(smem_u32(&sb->xs_full[jr]));
+      }
+      u += n;
+      i += n;
+    }
+  } else if (warp >= 6 && warp < 14) {
+    // ------------------------------ dequant (two warpgroups, stages alternate) ----------------
+    const int w = (warp - 6) >> 2;
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    uint32_t a_uses[kUPS] = {0, 0, 0, 0};
+    long long u = u0;
+    int i = 0;
+    bool live = true;
+    for (int k = 0; u < u1 && live; ++k) {
+      const int n = stage_units(u, u1, p.G);
+      if ((k & 1) == w) {
+        const int s = k % kStages;
+        if (!mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag))
+          break;
+        for (int j = 0; j < n; ++j) {
+          const uint8_t* wu = wring + s * kWStageBytes + j * kUnitWBytes;
+          const uint4 lo = *reinterpret_cast<const uint4*>(wu + r * 16);
+          const uint4 hi = *reinterpret_cast<const uint4*>(wu + 2048 + r * 16);
+          const uint32_t sbw = *reinterpret_cast<const uint32_t*>(wu + kUnitNibBytes + r * 4);
+          if (j == n - 1) mbar_arrive(smem_u32(&sb->empty[s]));  // done reading the weight stage
+          const int jr = (i + j) % kRS;
+          if (i + j >= kRS && !mbar_wait(smem_u32(&sb->ep_empty[jr]), (((i + j) / kRS) - 1) & 1,
+                                         p.err, kErrBitWaitEmpty, abort_flag)) {
+            live = false;
+            break;
           }
-        }
-        if (e == 0) p.cnt[tile] = 0u;
-      }
-      named_bar_sync(1, kEpiThreads);
-    };
-
-    auto epilogue = [&](int j) {
-      const int d = j % kNumD;
-      float gsum[NTH];
-      const bool ok = mbar_wait(smem_u32(&sb->d_full[d]), (j / kNumD) & 1, p.err, kErrBitWaitDFull,
-                                abort_flag);
-      if (ok) {
-        tc_fence_after();
-        tmem_ld<NTH>(tmem + lane_off + kDCol0 + d * 16 + wg * NTH, gsum);
-        tc_wait_ld();
-        tc_fence_before();
-        mbar_arrive(smem_u32(&sb->d_empty[d]));
-#pragma unroll
-        for (int t = 0; t < NTH; ++t) acc[t] = fmaf(pend_s, gsum[t], fmaf(pend_b, pend_xs[t], acc[t]));
-      }
-      const long long u = u0 + j;
-      const int g = static_cast<int>(u % p.G);
-      if (g == p.G - 1 || j == L - 1) {
-        const long long tile = u / p.G;
-        const long long seg_start = (tile * p.G > u0) ? tile * p.G : u0;
-        const bool full_tile = (seg_start == tile * p.G) && (g == p.G - 1);
-        const bool first_seg = (seg_start == u0);
-        flush(tile, full_tile, first_seg);
-#pragma unroll
-        for (int t = 0; t < NTH; ++t) acc[t] = 0.f;
-      }
-    };
-
-    for (int i = 0; i < L; ++i) {
-      const int s = i % kStages, a = i % kNumA;
-      const uint8_t* stage = smem + s * kStageBytes;
-      float sc = 0.f, bi = 0.f, xs[NTH];
-#pragma unroll
-      for (int t = 0; t < NTH; ++t) xs[t] = 0.f;
-      if (mbar_wait(smem_u32(&sb->full[s]), (i / kStages) & 1, p.err, kErrBitWaitFull, abort_flag)) {
-        const uint4 w4 = *reinterpret_cast<const uint4*>(stage + wg * 2048 + r * 16);
-        const uint32_t sbw = *reinterpret_cast<const uint32_t*>(stage + kUnitNibBytes + r * 4);
-        sc = __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(sbw & 0xFFFFu)));
-        bi = __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(sbw >> 16)));
-        const float* xsum = reinterpret_cast<const float*>(stage + kUnitWBytes + kXsumOffset);
-#pragma unroll
-        for (int t = 0; t < NTH; ++t) xs[t] = xsum[wg * NTH + t];
-        uint32_t q[16];
-        decode4(w4, q);
-        if (i < kNumA ||
-            mbar_wait(smem_u32(&sb->a_empty[a]), ((i / kNumA) - 1) & 1, p.err, kErrBitWaitAEmpty,
-                      abort_flag)) {
+          sb->sbr[jr][r] = sbw;
+          mbar_arrive(smem_u32(&sb->sb_full[jr]));
+          uint32_t q[32];
+          decode8(lo, hi, q);
+          const int a = w * kUPS + j;
+          if (a_uses[j] > 0 &&
+              !mbar_wait(smem_u32(&sb->a_empty[a]), (a_uses[j] - 1) & 1, p.err, kErrBitWaitAEmpty,
+                         abort_flag)) {
+            live = false;
+            break;
+          }
+          ++a_uses[j];
           tc_fence_after();
-          tmem_st_x16(tmem + lane_off + a * 32 + wg * 16, q);
+          tmem_st_x32(tmem + lane_off + a * 32, q);
           tc_wait_st();
           tc_fence_before();
           mbar_arrive(smem_u32(&sb->a_full[a]));
         }
       }
-      if (i > 0) epilogue(i - 1);
-      pend_s = sc;
-      pend_b = bi;
-#pragma unroll
-      for (int t = 0; t < NTH; ++t) pend_xs[t] = xs[t];
+      u += n;
+      i += n;
     }
-    if (L > 0) epilogue(L - 1);
+  } else {
+    // ------------------------------ epilogue (warps 2..5), units in order ----------------------
+    const int e = threadIdx.x - 64;
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    float acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+    bool dep_waited = false;
+
+    for (int i = 0; i < L; ++i) {
+      const int d = i % kNumD;
+      const int jr = i % kRS;
+      const uint32_t ph = (i / kRS) & 1;
+      const bool ok = mbar_wait(smem_u32(&sb->xs_full[jr]), ph, p.err, kErrBitWaitFull, abort_flag) &&
+                      mbar_wait(smem_u32(&sb->sb_full[jr]), ph, p.err, kErrBitWaitFull, abort_flag) &&
+                      mbar_wait(smem_u32(&sb->d_full[d]), (i / kNumD) & 1, p.err, kErrBitWaitDFull,
+                                abort_flag);
+      if (ok) {
+        const uint32_t sbw = sb->sbr[jr][r];
+        const float sc = __uint_as_float(sbw << 16);
+        const float bi = __uint_as_float(sbw & 0xFFFF0000u);
+        const float bo = fmaf(-128.0f, sc, bi);  // bias with the +128 operand offset folded in
+        // acc += (b - 128 s) * xsum, then acc += s * dot  (same order for every NT)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] = fmaf(bo, sb->xsr[jr][t], acc[t]);
+        mbar_arrive(smem_u32(&sb->ep_empty[jr]));
+        // dot = (columns 0-31 partial) + (columns 32-63 partial)
+        const uint32_t dbase = tmem + lane_off + kDCol0 + d * 32;
+        float s01[NT], v[NT];
+        tc_fence_after();
+        tmem_ld<NT>(dbase, s01);
+        tmem_ld<NT>(dbase + 16, v);
+        tc_wait_ld();
+        tc_fence_before();
+        mbar_arrive(smem_u32(&sb->d_empty[d]));
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] = fmaf(sc, s01[t] + v[t], acc[t]);
+      }
+      const long long u = u0 + i;
+      const int g = static_cast<int>(u % p.G);
+      if (g != p.G - 1 && i != L - 1) continue;
+      // ---- end of a tile segment: write the tile, or publish a partial and maybe finish it
+      const long long tile = u / p.G;
+      const long long seg_start = (tile * p.G > u0) ? tile * p.G : u0;
+      const bool full_tile = (seg_start == tile * p.G) && (g == p.G - 1);
+      const bool first_seg = (seg_start == u0);
+      const int row_g = static_cast<int>(tile) * kTileRows + r;
+      const bool live = !*abort_flag;
+      if (!dep_waited) {
+        pdl_wait_prior_grid();  // outputs may alias buffers the previous kernel still reads
+        dep_waited = true;
+      }
+      if (full_tile) {
+        if (live && row_g < p.N) {
+#pragma unroll
+          for (int t = 0; t < NT; ++t)
+            if (t < p.M) p.out[static_cast<size_t>(t) * p.ldo + row_g] = __float2bfloat16_rn(acc[t]);
+        }
+      } else {
+        float* mine = p.part + (static_cast<size_t>(c) * 2 + (first_seg ? 0 : 1)) * kMaxTokens * kTileRows;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) mine[t * kTileRows + r] = acc[t];
+        __threadfence();
+        named_bar_sync(1, kEpiThreads);
+        const long long cf = cta_of_unit(tile * p.G, p.U, p.C);
+        const long long cl = cta_of_unit(tile * p.G + p.G - 1, p.U, p.C);
+        if (e == 0) {
+          const unsigned n_contrib = static_cast<unsigned>(cl - cf + 1);
+          const unsigned old = live ? atomicAdd(&p.cnt[tile], 1u) : 0u;
+          sb->last_flag = live && (old == n_contrib - 1);
+        }
+        named_bar_sync(1, kEpiThreads);
+        if (sb->last_flag) {
+          __threadfence();
+          float v[NT];
+#pragma unroll
+          for (int t = 0; t < NT; ++t) v[t] = 0.f;
+          for (long long cc = cf; cc <= cl; ++cc) {
+            const long long cu0 = u_begin(cc, p.U, p.C);
+            const int cs = (cu0 / p.G == tile) ? 0 : 1;
+            const float* src = p.part + (static_cast<size_t>(cc) * 2 + cs) * kMaxTokens * kTileRows;
+#pragma unroll
+            for (int t = 0; t < NT; ++t) v[t] += __ldcg(src + t * kTileRows + r);
+          }
+          if (row_g < p.N) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+              if (t < p.M) p.out[static_cast<size_t>(t) * p.ldo + row_g] = __float2bfloat16_rn(v[t]);
+          }
+          if (e == 0) p.cnt[tile] = 0u;
+        }
+        named_bar_sync(1, kEpiThreads);
+      }
+#pragma unroll
+      for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+    }
   }
 
   tc_fence_before();
@@ -353,52 +502,6 @@ __global__ void __launch_bounds__(kThreads, 1) qmm_w4g64_tc_kernel(const QmmPara
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
-  }
-}
-
-// x [M, ldx] bf16  ->  per-group blocks of f16 x^T in the canonical B layout + f32 group sums.
-// One CTA per 64-column group, 128 threads, each converting 8 consecutive columns of one token.
-__global__ void __launch_bounds__(128) qmm_xprep_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
-                                                        int M, uint8_t* __restrict__ xw,
-                                                        uint32_t* err) {
-  __shared__ float red[kMaxTokens][8];
-  pdl_launch_dependents();
-  pdl_wait_prior_grid();
-  const int g = blockIdx.x;
-  const int e = threadIdx.x;
-  const int tr = e & 7, tb = (e >> 3) & 1, kh = (e >> 4) & 1, j = e >> 5;
-  const int t = tb * 8 + tr;
-  const int k0 = g * kGroup + j * 16 + kh * 8;
-  uint4 packed = make_uint4(0, 0, 0, 0);
-  float psum = 0.f;
-  if (t < M) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * ldx + k0);
-    const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
-    uint32_t hw[4];
-    bool overflow = false;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float lo = __uint_as_float(rw[i] << 16);
-      const float hi = __uint_as_float(rw[i] & 0xFFFF0000u);
-      const __half2 h = __floats2half2_rn(lo, hi);
-      const float2 back = __half22float2(h);
-      overflow |= (isinf(back.x) && !isinf(lo)) || (isinf(back.y) && !isinf(hi));
-      psum += back.x;
-      psum += back.y;
-      hw[i] = *reinterpret_cast<const uint32_t*>(&h);
-    }
-    if (overflow) atomicOr(err, kErrBitXOverflow);
-    packed = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-  }
-  uint8_t* blk = xw + static_cast<size_t>(g) * kUnitXBytes;
-  *reinterpret_cast<uint4*>(blk + j * 512 + tb * 256 + kh * 128 + tr * 16) = packed;
-  red[t][j * 2 + kh] = psum;
-  __syncthreads();
-  if (e < kMaxTokens) {
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s += red[e][i];
-    reinterpret_cast<float*>(blk + kXsumOffset)[e] = s;
   }
 }
 
@@ -443,8 +546,8 @@ __global__ void qmm_repack_kernel(const uint32_t* __restrict__ w, const uint16_t
   *reinterpret_cast<uint32_t*>(base + kUnitNibBytes + r * 4) = sbw;
 }
 
-// Plain CUDA-core cross-check of the relaid format: same decode, same identity, same x rounding.
-// One thread per (row, token).  Used by the tests to localise a mismatch; not a product path.
+// Plain CUDA-core cross-check of the relaid format: decodes the same units and computes
+// sum_g s * sum(x q) + b * sum(x) in f32.  One thread per (row, token); tests only.
 __global__ void qmm_simt_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                                 const uint8_t* __restrict__ w_tc, __nv_bfloat16* __restrict__ out,
                                 int ldo, int M, int N, int K) {
@@ -458,24 +561,23 @@ __global__ void qmm_simt_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
   for (int g = 0; g < G; ++g) {
     const uint8_t* base = w_tc + (static_cast<long long>(tile) * G + g) * kUnitWBytes;
     const uint32_t sbw = *reinterpret_cast<const uint32_t*>(base + kUnitNibBytes + r * 4);
-    const float sc = __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(sbw & 0xFFFFu)));
-    const float bi = __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(sbw >> 16)));
+    const float sc = __uint_as_float(sbw << 16);
+    const float bi = __uint_as_float(sbw & 0xFFFF0000u);
+    const uint4 lo = *reinterpret_cast<const uint4*>(base + r * 16);
+    const uint4 hi = *reinterpret_cast<const uint4*>(base + 2048 + r * 16);
+    uint32_t q[32];
+    decode8(lo, hi, q);
     float gs = 0.f, xsum = 0.f;
-    for (int ch = 0; ch < 2; ++ch) {
-      const uint4 w4 = *reinterpret_cast<const uint4*>(base + ch * 2048 + r * 16);
-      uint32_t q[16];
-      decode4(w4, q);
-      for (int pidx = 0; pidx < 16; ++pidx) {
-        const __half2 h = *reinterpret_cast<const __half2*>(&q[pidx]);
-        const float2 qf = __half22float2(h);
-        const int k = g * kGroup + ch * 32 + pidx * 2;
-        const float x0 = __half2float(__float2half_rn(__bfloat162float(x[static_cast<size_t>(tok) * ldx + k])));
-        const float x1 = __half2float(__float2half_rn(__bfloat162float(x[static_cast<size_t>(tok) * ldx + k + 1])));
-        gs = fmaf(qf.x, x0, gs);
-        gs = fmaf(qf.y, x1, gs);
-        xsum += x0;
-        xsum += x1;
-      }
+    for (int pidx = 0; pidx < 32; ++pidx) {
+      const int k = g * kGroup + pidx * 2;
+      const float x0 = __bfloat162float(x[static_cast<size_t>(tok) * ldx + k]);
+      const float x1 = __bfloat162float(x[static_cast<size_t>(tok) * ldx + k + 1]);
+      const float q0 = static_cast<float>(q[pidx] & 0xFu);
+      const float q1 = static_cast<float>((q[pidx] >> 16) & 0xFu);
+      gs = fmaf(q0, x0, gs);
+      gs = fmaf(q1, x1, gs);
+      xsum += x0;
+      xsum += x1;
     }
     acc = fmaf(sc, gs, fmaf(bi, xsum, acc));
   }
@@ -487,6 +589,7 @@ __global__ void qmm_simt_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
 // ---------------------------------------------------------------------------------------------
 static int g_num_sms[64] = {0};
 static bool g_attr_set[64][4] = {};
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int device_sm_count(int dev) {
   if (dev < 0 || dev >= 64) return 148;
@@ -499,11 +602,39 @@ int device_sm_count(int dev) {
   return g_num_sms[dev];
 }
 
-template <int NTH>
-static cudaError_t launch_tc(const QmmParams& prm, int dev, cudaStream_t stream, bool pdl) {
-  constexpr int slot = NTH == 1 ? 0 : NTH == 2 ? 1 : NTH == 4 ? 2 : 3;
+static cudaError_t get_encoder() {
+  if (g_encode) return cudaSuccess;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess) return e;
+  if (q != cudaDriverEntryPointSuccess || fn == nullptr) return cudaErrorNotSupported;
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return cudaSuccess;
+}
+
+// x [M rows, K columns] bf16, row stride ldx elements; box 64 columns x `rows` rows, 128B swizzle.
+// (A 3-D view {64, rows, groups} would need a group stride below the row stride, which tensor maps
+// do not support: each stride must include the previous dimension's.)
+static cudaError_t encode_x_map(CUtensorMap* map, const void* x, int M, int K, int ldx, int rows) {
+  cudaError_t e = get_encoder();
+  if (e != cudaSuccess) return e;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldx) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kGroup), static_cast<cuuint32_t>(rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides,
+                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int NT>
+static cudaError_t launch_tc(const QmmParams& prm, const CUtensorMap& map, int dev,
+                             cudaStream_t stream, bool pdl) {
+  constexpr int slot = NT == 2 ? 0 : NT == 4 ? 1 : NT == 8 ? 2 : 3;
   if (dev >= 0 && dev < 64 && !g_attr_set[dev][slot]) {
-    cudaError_t e = cudaFuncSetAttribute(qmm_w4g64_tc_kernel<NTH>,
+    cudaError_t e = cudaFuncSetAttribute(qmm_w4g64_tc_kernel<NT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kQmmSmemBytes));
     if (e != cudaSuccess) return e;
@@ -519,22 +650,7 @@ static cudaError_t launch_tc(const QmmParams& prm, int dev, cudaStream_t stream,
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, qmm_w4g64_tc_kernel<NTH>, prm);
-}
-
-static cudaError_t launch_xprep(const __nv_bfloat16* x, int ldx, int M, int G, uint8_t* xw,
-                                uint32_t* err, cudaStream_t stream, bool pdl) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(G);
-  cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, qmm_xprep_kernel, x, ldx, M, xw, err);
+  return cudaLaunchKernelEx(&cfg, qmm_w4g64_tc_kernel<NT>, prm, map);
 }
 
 cudaError_t qmm_tc_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M, int N,
@@ -542,11 +658,10 @@ cudaError_t qmm_tc_launch(const void* x, int ldx, const void* w_tc, void* out, i
   int dev = 0;
   cudaGetDevice(&dev);
   const QmmShape sh = qmm_shape(N, K);
-  const WsLayout wl = ws_layout(N, K, C);
+  const WsLayout wl = ws_layout(N, K, device_sm_count(dev));
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   QmmParams prm;
   prm.w_tc = static_cast<const uint8_t*>(w_tc);
-  prm.xw = wsb + wl.x_off;
   prm.out = static_cast<__nv_bfloat16*>(out);
   prm.part = reinterpret_cast<float*>(wsb + wl.part_off);
   prm.cnt = reinterpret_cast<uint32_t*>(wsb + wl.cnt_off);
@@ -558,13 +673,14 @@ cudaError_t qmm_tc_launch(const void* x, int ldx, const void* w_tc, void* out, i
   prm.C = C;
   prm.ldo = ldo;
   prm.U = sh.U;
-  cudaError_t e = launch_xprep(static_cast<const __nv_bfloat16*>(x), ldx, M, sh.G, wsb + wl.x_off,
-                               prm.err, stream, pdl);
+  prm.x_rows = M <= 8 ? 8 : 16;
+  CUtensorMap map;
+  cudaError_t e = encode_x_map(&map, x, M, K, ldx, prm.x_rows);
   if (e != cudaSuccess) return e;
-  if (M <= 2) return launch_tc<1>(prm, dev, stream, true);
-  if (M <= 4) return launch_tc<2>(prm, dev, stream, true);
-  if (M <= 8) return launch_tc<4>(prm, dev, stream, true);
-  return launch_tc<8>(prm, dev, stream, true);
+  if (M <= 2) return launch_tc<2>(prm, map, dev, stream, pdl);
+  if (M <= 4) return launch_tc<4>(prm, map, dev, stream, pdl);
+  if (M <= 8) return launch_tc<8>(prm, map, dev, stream, pdl);
+  return launch_tc<16>(prm, map, dev, stream, pdl);
 }
 
 cudaError_t qmm_repack_launch(const uint32_t* w, const uint16_t* s, const uint16_t* b, void* w_tc,

@@ -6,7 +6,7 @@ Mirrors skinny_mlx/qmm.py (rachittshah/skinny-mlx):
   tcgen05 unit order (128 rows x 64 columns per 4608-byte unit, scales and biases folded in).
 * ``skinny_qmm`` (qmm.py:132) runs the sm_100a kernel: x [M, K] @ dequant(W)[N, K]^T -> [M, N],
   computing sum_g s * sum(x q) + b * sum(x) per 64-group in f32 (the affine identity of
-  qmm.py:8-9), with x rounded to f16 for the tensor-core product as qmm.py:136 does.
+  qmm.py:8-9); the tensor-core products use bf16 x as given and exact nibbles, in f32.
 * ``qmm`` is the drop-in ``mx.quantized_matmul(x, w, scales, biases, transpose=True,
   group_size=64, bits=4)`` entry: MLX packing in, relayout cached per weight.
 * ``quantize`` produces MLX's packing with the affine rule scale = (max - min) / 15,

@@ -95,7 +95,7 @@ def test_qmm_tc_matches_simt_crosscheck(cuda_lib, dev):
     xf, x = make_x(16, 1024, 10, dev)
     a = skinny_qmm(x, sw).float()
     c = skinny_qmm_simt(x, sw).float()
-    ref = quant.qmm_identity(xf, packed, s, b)
+    ref = quant.qmm_ref(xf, packed, s, b)
     assert quant.rel_err(ref, c.cpu().numpy()) <= TIGHT
     assert quant.rel_err(c.cpu().numpy(), a.cpu().numpy()) <= TIGHT
 
