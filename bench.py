@@ -1,10 +1,12 @@
 """Benchmark of the flat multi-token verify path on B200 (one JSON line on rank 0).
 
 Workload: every fused 4-bit projection of one synthetic 32-layer hybrid
-decoder step at M=8 tokens: 129 qmm launches, 2,024,755,200 packed weight bytes per step.
-A step is one pass over all 129 projections, replayed from a CUDA graph with programmatic
-dependent launch between kernels.  Weights total 2.0 GB, far above the 126 MB L2, so no L2
-flush is needed between steps.
+decoder step at M=8 tokens: 129 matrices, 2,024,755,200 packed weight bytes per step.  A step is
+one grouped qmm launch over all 129 projections (skinny_qmm_w4g64_grouped: the B200 form of
+evaluating the list of quantized matmuls at once, as the reference's bench/model_matmuls.py does),
+replayed from a CUDA graph.  The same step issued as 129 separate launches (PDL-chained, one
+CUDA graph) is reported beside it.  Weights total 2.0 GB, far above the 126 MB L2, so no L2 flush
+is needed between steps.
 
 metric: qmm HBM GB/s over the step (algorithmic bytes = packed weights + bf16 activations in
 and out, per step, divided by the device time of the step).  Extra keys report the config-1
@@ -158,12 +160,14 @@ def build_weights(shapes, dev, seed=0):
 
 
 class StackRunner:
-    """All projections of the stack at a fixed token count, captured in one CUDA graph."""
+    """All projections of the stack at a fixed token count, captured in one CUDA graph: one grouped
+    launch (mode "grouped") or one launch per projection (mode "launches")."""
 
-    def __init__(self, shapes, weights, m, dev, seed=1):
-        from skinny_mlx_b200.qmm import skinny_qmm
+    def __init__(self, shapes, weights, m, dev, seed=1, mode="grouped"):
+        from skinny_mlx_b200.qmm import skinny_qmm, skinny_qmm_grouped
 
-        self.shapes, self.weights, self.m = shapes, weights, m
+        self.shapes, self.weights, self.m, self.mode = shapes, weights, m, mode
+        self._grouped = skinny_qmm_grouped
         ks = sorted({k for _, _, k in shapes})
         self.koff, off = {}, 0
         for k in ks:
@@ -185,6 +189,11 @@ class StackRunner:
         self.stream.synchronize()
 
     def run_eager(self):
+        if self.mode == "grouped":
+            for a in range(0, len(self.weights), 192):
+                sl = slice(a, a + 192)
+                self._grouped([self.xs[k] for _, _, k in self.shapes[sl]], self.weights[sl], self.outs[sl])
+            return
         for (_, _, k), w, o in zip(self.shapes, self.weights, self.outs):
             self._qmm(self.xs[k], w, out=o)
 
@@ -250,15 +259,17 @@ def time_e2e(runner: StackRunner, steps: int, warmup: int):
 
 
 def config1_sweep(dev, copies=40):
-    """Config 1 (9728 x 2560) for M in {1,2,4,6,8,12,16}: GB/s over `copies` rotated copies."""
+    """Config 1 (9728 x 2560) for M in {1,2,4,6,8,12,16}: GB/s over `copies` rotated copies, as
+    one grouped launch and as `copies` separate launches."""
     shapes = [(f"c1.{i}", 9728, 2560) for i in range(copies)]
     weights = build_weights(shapes, dev, seed=7)
-    out = {}
-    for m in (1, 2, 4, 6, 8, 12, 16):
-        r = StackRunner(shapes, weights, m, dev, seed=m)
-        ms, _ = time_replays(r, 20, 3, 1)
-        out[str(m)] = round(r.algorithmic_bytes() * 20 / (ms * 1e-3) / 1e9, 1)
-        del r
+    out = {"grouped": {}, "launches": {}}
+    for mode in ("grouped", "launches"):
+        for m in (1, 2, 4, 6, 8, 12, 16):
+            r = StackRunner(shapes, weights, m, dev, seed=m, mode=mode)
+            ms, _ = time_replays(r, 20, 3, 1)
+            out[mode][str(m)] = round(r.algorithmic_bytes() * 20 / (ms * 1e-3) / 1e9, 1)
+            del r
     del weights
     torch.cuda.empty_cache()
     return out
@@ -319,6 +330,11 @@ def run_skinny(args, world, rank, local):
     ms1, _ = time_replays(r1, args.steps, args.warmup, world)
     ms1_step = max_over_ranks(ms1, world) / args.steps
     del r1
+    # the same step as 129 separate launches (one per projection, PDL-chained in a CUDA graph)
+    rl = StackRunner(shapes, weights, M_STACK, dev, seed=1, mode="launches")
+    msl, _ = time_replays(rl, args.steps, args.warmup, world)
+    msl_step = max_over_ranks(msl, world) / args.steps
+    del rl
 
     e2e_ms, h2d, d2h = time_e2e(runner, args.steps, args.warmup)
     e2e_ms = max_over_ranks(e2e_ms, world) / args.steps
@@ -364,8 +380,11 @@ def run_skinny(args, world, rank, local):
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
-                    "path": "pinned H2D of activations, CUDA-graph replay of skinny_qmm calls, D2H of logits"},
-            "gpu_launches": 2 * len(shapes) * args.steps,
+                    "path": "pinned H2D of activations, CUDA-graph replay of the skinny_qmm_grouped call, D2H of logits"},
+            "gpu_launches": args.steps,
+            "per_projection_launches": {"ms_per_step": round(msl_step, 4),
+                                        "GBps": round(per_step_bytes / (msl_step * 1e-3) / 1e9, 1),
+                                        "launches_per_step": len(shapes)},
             "clocks": clocks,
             "stack_m1_ms": round(ms1_step, 4),
             "cost_m8_vs_m1": round(ms_step / ms1_step, 3),

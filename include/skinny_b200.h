@@ -75,6 +75,20 @@ size_t skinny_qmm_workspace_bytes(int N, int K);
 int skinny_qmm_w4g64(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M, int N,
                      int K, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Limits of one grouped call. */
+#define SKINNY_QMM_MAX_GROUP 192       /* matrices per grouped call */
+#define SKINNY_QMM_MAX_GROUP_INPUTS 8  /* distinct activation buffers per grouped call */
+
+/* n independent products out[i][M, N[i]] = x[i][M, K[i]] . W_i^T in ONE persistent launch that
+ * streams the concatenated weights of all n matrices (same token count M for all).  The launch
+ * overhead, pipeline fill and split-K fix-up are paid once for the group instead of per matrix.
+ * Same per-matrix contract and bit-identical results as skinny_qmm_w4g64.  This is the B200 form
+ * of evaluating a list of quantized matmuls at once, as skinny_mlx/qmm.py:195-196 and
+ * bench/model_matmuls.py:188-191 do with mx.eval on a list. */
+int skinny_qmm_w4g64_grouped(int n, const void* const* x, const int* ldx, const void* const* w_tc,
+                             void* const* out, const int* ldo, const int* N, const int* K, int M,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* Same contract with plain CUDA cores (no tcgen05), one thread per output.  A slow cross-check
  * used by the tests to localise a mismatch; it has no counterpart in the reference. */
 int skinny_qmm_w4g64_simt(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,

@@ -201,3 +201,49 @@ def repack_tc(packed: np.ndarray, s_bits, b_bits) -> np.ndarray:
     nib = np.ascontiguousarray(w5).reshape(t, g, 2 * TILE * 4).view(np.uint8).reshape(t, g, 4096)
     sbu = np.ascontiguousarray(sb.reshape(t, TILE, g).transpose(0, 2, 1)).view(np.uint8).reshape(t, g, 512)
     return np.concatenate([nib, sbu], axis=-1).reshape(-1)
+
+
+# ------------------------------------------------------------------------------------------------
+# 16-bit fixed-point activations as two int8 digits (the B200 kernel's B operand)
+# ------------------------------------------------------------------------------------------------
+XQ_MAXINT = 32639  # 127 * 256 + 127: the largest value two signed int8 digits (hi*256 + lo) hold
+
+
+def xq_digits(x: np.ndarray):
+    """x [M, K] float32 (bf16 values) -> per (token, 64-group) power-of-two scale, int16 value,
+    hi/lo int8 digits and exact group sum, as the x-prep kernel computes them:
+      e = smallest integer with max|x_g| <= 32639 * 2^e (e = -133 for an all-zero group),
+      v = rint(x * 2^-e) (|v| <= 32639), hi = (v + 128) >> 8, lo = v - 256 hi, xsum = sum(v) * 2^e.
+    """
+    m, k = x.shape
+    g = k // GROUP
+    xg = np.asarray(x, dtype=np.float64).reshape(m, g, GROUP)
+    amax = np.abs(xg).max(-1)
+    e = np.full((m, g), -133, dtype=np.int64)
+    nz = amax > 0
+    # smallest e with amax <= 32639 * 2^e
+    e_nz = np.ceil(np.log2(amax[nz] / XQ_MAXINT)).astype(np.int64)
+    # fix float rounding of log2 at exact powers
+    e_nz = np.where(amax[nz] <= XQ_MAXINT * np.exp2(e_nz - 1), e_nz - 1, e_nz)
+    e_nz = np.where(amax[nz] > XQ_MAXINT * np.exp2(e_nz), e_nz + 1, e_nz)
+    e[nz] = e_nz
+    v = np.rint(xg * np.exp2(-e)[..., None]).astype(np.int64)
+    assert np.abs(v).max() <= XQ_MAXINT
+    hi = (v + 128) >> 8
+    lo = v - 256 * hi
+    xsum = v.sum(-1).astype(np.float64) * np.exp2(e)
+    return e, v, hi.astype(np.int8), lo.astype(np.int8), xsum
+
+
+def qmm_xq(x: np.ndarray, packed, s_bits, b_bits) -> np.ndarray:
+    """The B200 kernel's arithmetic: integer dot products of nibbles with the 16-bit fixed-point x,
+    then per group s * 2^e * dot + b * xsum (float64 here)."""
+    e, v, hi, lo, xsum = xq_digits(x)
+    q = unpack(packed).astype(np.int64)
+    n = q.shape[0]
+    m, g = e.shape
+    qg = q.reshape(n, g, GROUP)
+    dot = np.einsum("mgk,ngk->mng", hi.astype(np.int64), qg) * 256 + np.einsum("mgk,ngk->mng", lo.astype(np.int64), qg)
+    s = bf16_bits_to_f32(s_bits).astype(np.float64)
+    b = bf16_bits_to_f32(b_bits).astype(np.float64)
+    return (dot * np.exp2(e)[:, None, :] * s[None] + xsum[:, None, :] * b[None]).sum(-1)

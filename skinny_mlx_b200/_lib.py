@@ -36,6 +36,8 @@ SIGNATURES = {
                                  c_void_p, c_size_t, c_void_p]),
     "skinny_qmm_w4g64_simt": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int,
                                       c_int, c_void_p]),
+    "skinny_qmm_w4g64_grouped": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                         c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
 }
 
 

@@ -9,6 +9,9 @@ namespace skinny {
 int device_sm_count(int dev);
 cudaError_t qmm_tc_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M, int N,
                           int K, void* ws, int C, cudaStream_t stream, bool pdl);
+cudaError_t qmm_tc_launch_grouped(int n, const void* const* x, const int* ldx, const void* const* w_tc,
+                                  void* const* out, const int* ldo, const int* N, const int* K, int M,
+                                  void* ws, cudaStream_t stream, bool pdl);
 cudaError_t qmm_repack_launch(const uint32_t* w, const uint16_t* s, const uint16_t* b, void* w_tc,
                               int N, int K, cudaStream_t stream);
 cudaError_t qmm_simt_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
@@ -102,6 +105,33 @@ int skinny_qmm_w4g64(const void* x, int ldx, const void* w_tc, void* out, int ld
   if (!workspace || workspace_bytes < wl.total || !aligned16(workspace)) return SKINNY_ERR_WORKSPACE;
   return cuda_status(skinny::qmm_tc_launch(x, ldx, w_tc, out, ldo, M, N, K, workspace, C,
                                            static_cast<cudaStream_t>(stream), true));
+}
+
+int skinny_qmm_w4g64_grouped(int n, const void* const* x, const int* ldx, const void* const* w_tc,
+                             void* const* out, const int* ldo, const int* N, const int* K, int M,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  if (n < 1 || n > SKINNY_QMM_MAX_GROUP || !x || !ldx || !w_tc || !out || !ldo || !N || !K)
+    return SKINNY_ERR_INVALID_ARG;
+  if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
+  long long tiles = 0;
+  int distinct = 0;
+  for (int i = 0; i < n; ++i) {
+    if (!x[i] || !w_tc[i] || !out[i]) return SKINNY_ERR_INVALID_ARG;
+    const int st = check_qmm_shape(N[i], K[i]);
+    if (st != SKINNY_OK) return st;
+    if (ldx[i] < K[i] || ldo[i] < N[i]) return SKINNY_ERR_INVALID_ARG;
+    if (!aligned16(x[i]) || (ldx[i] % 8) != 0 || !aligned16(w_tc[i])) return SKINNY_ERR_ALIGNMENT;
+    tiles += skinny::qmm_shape(N[i], K[i]).T;
+    bool seen = false;
+    for (int q = 0; q < i; ++q)
+      if (x[q] == x[i] && K[q] == K[i] && ldx[q] == ldx[i]) seen = true;
+    if (!seen) ++distinct;
+  }
+  if (tiles > skinny::kMaxTiles || distinct > SKINNY_QMM_MAX_GROUP_INPUTS) return SKINNY_ERR_SHAPE;
+  const skinny::WsLayout wl = skinny::ws_layout(0, 0, skinny::device_sm_count(current_device()));
+  if (!workspace || workspace_bytes < wl.total || !aligned16(workspace)) return SKINNY_ERR_WORKSPACE;
+  return cuda_status(skinny::qmm_tc_launch_grouped(n, x, ldx, w_tc, out, ldo, N, K, M, workspace,
+                                                   static_cast<cudaStream_t>(stream), true));
 }
 
 int skinny_qmm_w4g64_simt(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,

@@ -78,15 +78,44 @@ constexpr int kDeqThreads = 128;                   // per warpgroup
 constexpr int kXsumWarp = 14;
 constexpr int kRS = 16;                            // per-unit scale/bias + xsum ring for the epilogue
 
+// Grouped launch: one persistent grid streams the concatenated units of up to kMaxMats
+// independent matrices (same token count), so launch overhead, pipeline fill and the stream-K
+// fix-up tail are paid once for the whole group.  A single qmm is a group of one.
+constexpr int kMaxMats = 192;
+constexpr int kMaxX = 8;
+
+struct QmmMat {
+  const uint8_t* w_tc;  // relaid weight units of this matrix
+  __nv_bfloat16* out;   // [M, N] (leading dimension N)
+  long long unit_off;   // first global unit of this matrix
+  int N, G;             // rows, 64-column groups
+  int tile_off;         // first global tile (counter index) of this matrix
+  int xi;               // index of this matrix's activation tensor map
+  int ldo;              // leading dimension of out (>= N)
+};
+
 struct QmmParams {
-  const uint8_t* w_tc;  // relaid weight units
-  __nv_bfloat16* out;   // [M, ldo]
   float* part;          // [C_dev][2][16][128] partial sums (workspace)
   uint32_t* cnt;        // [kMaxTiles] arrival counters (workspace)
   uint32_t* err;        // device error word (workspace)
-  int M, N, G, T, C, ldo, x_rows;
-  long long U;
+  int M, C, x_rows, n_mats;
+  long long U;          // total units
+  QmmMat mats[kMaxMats];
 };
+
+struct XMaps {
+  CUtensorMap m[kMaxX];
+};
+
+// Matrix holding global unit u (largest m with unit_off <= u).
+__device__ __forceinline__ int mat_of(const QmmParams& p, long long u) {
+  int lo = 0, hi = p.n_mats - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.mats[mid].unit_off <= u) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
 
 // The epilogue, which trails the MMA, reads each unit's scale/bias words and xsums from a
 // kRS-deep ring, so a load stage is released as soon as its dequant warpgroup, the xsum warp and
@@ -113,10 +142,12 @@ constexpr int kBarBytes = 12288;
 constexpr size_t kQmmSmemBytes = static_cast<size_t>(kXRingBytes) + kWRingBytes + kBarBytes + 1024;
 static_assert(sizeof(QmmSmemBarriers) <= kBarBytes, "barrier block");
 
-// Units of the next stage starting at unit u: at most kUPS, never past the range end or a tile.
-__device__ __forceinline__ int stage_units(long long u, long long u1, int G) {
+// Units of the next stage starting at global unit u: at most kUPS, never past the CTA's range
+// end or the end of u's tile (hence never across matrices).
+__device__ __forceinline__ int stage_units(const QmmParams& p, long long u, long long u1) {
+  const QmmMat& mt = p.mats[mat_of(p, u)];
   long long n = u1 - u;
-  const int to_tile_end = G - static_cast<int>(u % G);
+  const int to_tile_end = mt.G - static_cast<int>((u - mt.unit_off) % mt.G);
   if (n > to_tile_end) n = to_tile_end;
   return n < kUPS ? static_cast<int>(n) : kUPS;
 }
@@ -142,7 +173,7 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 // NT: token columns read back per unit (2, 4, 8 or 16).
 template <int NT>
 __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
-    qmm_w4g64_tc_kernel(const QmmParams p, const __grid_constant__ CUtensorMap tmap_x) {
+    qmm_w4g64_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ XMaps xmaps) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the SWIZZLE_128B x tiles
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -181,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
     sb->abort_flag = 0;
     sb->last_flag = 0;
     fence_mbar_init();
-    prefetch_tmap(&tmap_x);
+    for (int q = 0; q < kMaxX; ++q) prefetch_tmap(&xmaps.m[q]);
   }
   __syncthreads();
   pdl_launch_dependents();
@@ -210,9 +241,10 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
       long long first_u[kStages];
       int nfirst = 0;
       while (u < u1 && k < kStages) {
-        const int n = stage_units(u, u1, p.G);
+        const int n = stage_units(p, u, u1);
+        const QmmMat& mt = p.mats[mat_of(p, u)];
         mbar_arrive_expect_tx(smem_u32(&sb->full[k]), static_cast<uint32_t>(n) * (kUnitWBytes + xbytes));
-        bulk_g2s_hint(smem_u32(wring + k * kWStageBytes), p.w_tc + u * kUnitWBytes,
+        bulk_g2s_hint(smem_u32(wring + k * kWStageBytes), mt.w_tc + (u - mt.unit_off) * kUnitWBytes,
                       static_cast<uint32_t>(n) * kUnitWBytes, smem_u32(&sb->full[k]), pol_w);
         first_u[k] = u;
         u += n;
@@ -221,10 +253,11 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
       }
       pdl_wait_prior_grid();  // x is produced by the previous kernel
       for (int f = 0; f < nfirst; ++f) {
-        const int g = static_cast<int>(first_u[f] % p.G);
-        const int n = stage_units(first_u[f], u1, p.G);
+        const QmmMat& mt = p.mats[mat_of(p, first_u[f])];
+        const int g = static_cast<int>((first_u[f] - mt.unit_off) % mt.G);
+        const int n = stage_units(p, first_u[f], u1);
         for (int j = 0; j < n; ++j)
-          tma_load_2d(smem_u32(xring + f * kXStageBytes + j * xtile), &tmap_x, (g + j) * kGroup, 0,
+          tma_load_2d(smem_u32(xring + f * kXStageBytes + j * xtile), &xmaps.m[mt.xi], (g + j) * kGroup, 0,
                       smem_u32(&sb->full[f]));
       }
       while (u < u1) {
@@ -232,13 +265,14 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
         if (!mbar_wait(smem_u32(&sb->empty[s]), ((k / kStages) - 1) & 1, p.err, kErrBitWaitEmpty,
                        abort_flag))
           break;
-        const int n = stage_units(u, u1, p.G);
-        const int g = static_cast<int>(u % p.G);
+        const int n = stage_units(p, u, u1);
+        const QmmMat& mt = p.mats[mat_of(p, u)];
+        const int g = static_cast<int>((u - mt.unit_off) % mt.G);
         mbar_arrive_expect_tx(smem_u32(&sb->full[s]), static_cast<uint32_t>(n) * (kUnitWBytes + xbytes));
-        bulk_g2s_hint(smem_u32(wring + s * kWStageBytes), p.w_tc + u * kUnitWBytes,
+        bulk_g2s_hint(smem_u32(wring + s * kWStageBytes), mt.w_tc + (u - mt.unit_off) * kUnitWBytes,
                       static_cast<uint32_t>(n) * kUnitWBytes, smem_u32(&sb->full[s]), pol_w);
         for (int j = 0; j < n; ++j)
-          tma_load_2d(smem_u32(xring + s * kXStageBytes + j * xtile), &tmap_x, (g + j) * kGroup, 0,
+          tma_load_2d(smem_u32(xring + s * kXStageBytes + j * xtile), &xmaps.m[mt.xi], (g + j) * kGroup, 0,
                       smem_u32(&sb->full[s]));
         u += n;
         ++k;
@@ -260,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
       int i = 0;  // unit index within this CTA
       bool live = true;
       for (int k = 0; u < u1 && live; ++k) {
-        const int n = stage_units(u, u1, p.G);
+        const int n = stage_units(p, u, u1);
         if ((k & 1) == w) {
           const int s = k % kStages;
           if (!mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag))
@@ -308,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
     int i = 0;
     bool live = true;
     for (int k = 0; u < u1 && live; ++k) {
-      const int n = stage_units(u, u1, p.G);
+      const int n = stage_units(p, u, u1);
       const int s = k % kStages;
       if (!mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag))
         break;
@@ -359,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
     int i = 0;
     bool live = true;
     for (int k = 0; u < u1 && live; ++k) {
-      const int n = stage_units(u, u1, p.G);
+      const int n = stage_units(p, u, u1);
       if ((k & 1) == w) {
         const int s = k % kStages;
         if (!mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag))
@@ -438,24 +472,28 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
         for (int t = 0; t < NT; ++t) acc[t] = fmaf(sc, s01[t] + v[t], acc[t]);
       }
       const long long u = u0 + i;
-      const int g = static_cast<int>(u % p.G);
-      if (g != p.G - 1 && i != L - 1) continue;
+      const QmmMat& mt = p.mats[mat_of(p, u)];
+      const long long lu = u - mt.unit_off;
+      const int g = static_cast<int>(lu % mt.G);
+      if (g != mt.G - 1 && i != L - 1) continue;
       // ---- end of a tile segment: write the tile, or publish a partial and maybe finish it
-      const long long tile = u / p.G;
-      const long long seg_start = (tile * p.G > u0) ? tile * p.G : u0;
-      const bool full_tile = (seg_start == tile * p.G) && (g == p.G - 1);
+      const long long ltile = lu / mt.G;                     // tile within the matrix
+      const long long tile_u0 = mt.unit_off + ltile * mt.G;  // its first global unit
+      const long long tile = mt.tile_off + ltile;            // global tile (counter index)
+      const long long seg_start = (tile_u0 > u0) ? tile_u0 : u0;
+      const bool full_tile = (seg_start == tile_u0) && (g == mt.G - 1);
       const bool first_seg = (seg_start == u0);
-      const int row_g = static_cast<int>(tile) * kTileRows + r;
+      const int row_g = static_cast<int>(ltile) * kTileRows + r;
       const bool live = !*abort_flag;
       if (!dep_waited) {
         pdl_wait_prior_grid();  // outputs may alias buffers the previous kernel still reads
         dep_waited = true;
       }
       if (full_tile) {
-        if (live && row_g < p.N) {
+        if (live && row_g < mt.N) {
 #pragma unroll
           for (int t = 0; t < NT; ++t)
-            if (t < p.M) p.out[static_cast<size_t>(t) * p.ldo + row_g] = __float2bfloat16_rn(acc[t]);
+            if (t < p.M) mt.out[static_cast<size_t>(t) * mt.ldo + row_g] = __float2bfloat16_rn(acc[t]);
         }
       } else {
         float* mine = p.part + (static_cast<size_t>(c) * 2 + (first_seg ? 0 : 1)) * kMaxTokens * kTileRows;
@@ -463,8 +501,8 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
         for (int t = 0; t < NT; ++t) mine[t * kTileRows + r] = acc[t];
         __threadfence();
         named_bar_sync(1, kEpiThreads);
-        const long long cf = cta_of_unit(tile * p.G, p.U, p.C);
-        const long long cl = cta_of_unit(tile * p.G + p.G - 1, p.U, p.C);
+        const long long cf = cta_of_unit(tile_u0, p.U, p.C);
+        const long long cl = cta_of_unit(tile_u0 + mt.G - 1, p.U, p.C);
         if (e == 0) {
           const unsigned n_contrib = static_cast<unsigned>(cl - cf + 1);
           const unsigned old = live ? atomicAdd(&p.cnt[tile], 1u) : 0u;
@@ -478,15 +516,15 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
           for (int t = 0; t < NT; ++t) v[t] = 0.f;
           for (long long cc = cf; cc <= cl; ++cc) {
             const long long cu0 = u_begin(cc, p.U, p.C);
-            const int cs = (cu0 / p.G == tile) ? 0 : 1;
+            const int cs = (cu0 >= tile_u0) ? 0 : 1;  // the tile is this contributor's first segment
             const float* src = p.part + (static_cast<size_t>(cc) * 2 + cs) * kMaxTokens * kTileRows;
 #pragma unroll
             for (int t = 0; t < NT; ++t) v[t] += __ldcg(src + t * kTileRows + r);
           }
-          if (row_g < p.N) {
+          if (row_g < mt.N) {
 #pragma unroll
             for (int t = 0; t < NT; ++t)
-              if (t < p.M) p.out[static_cast<size_t>(t) * p.ldo + row_g] = __float2bfloat16_rn(v[t]);
+              if (t < p.M) mt.out[static_cast<size_t>(t) * mt.ldo + row_g] = __float2bfloat16_rn(v[t]);
           }
           if (e == 0) p.cnt[tile] = 0u;
         }
@@ -630,8 +668,8 @@ static cudaError_t encode_x_map(CUtensorMap* map, const void* x, int M, int K, i
 }
 
 template <int NT>
-static cudaError_t launch_tc(const QmmParams& prm, const CUtensorMap& map, int dev,
-                             cudaStream_t stream, bool pdl) {
+static cudaError_t launch_tc(const QmmParams& prm, const XMaps& maps, int dev, cudaStream_t stream,
+                             bool pdl) {
   constexpr int slot = NT == 2 ? 0 : NT == 4 ? 1 : NT == 8 ? 2 : 3;
   if (dev >= 0 && dev < 64 && !g_attr_set[dev][slot]) {
     cudaError_t e = cudaFuncSetAttribute(qmm_w4g64_tc_kernel<NT>,
@@ -650,37 +688,73 @@ static cudaError_t launch_tc(const QmmParams& prm, const CUtensorMap& map, int d
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, qmm_w4g64_tc_kernel<NT>, prm, map);
+  return cudaLaunchKernelEx(&cfg, qmm_w4g64_tc_kernel<NT>, prm, maps);
 }
 
-cudaError_t qmm_tc_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M, int N,
-                          int K, void* ws, int C, cudaStream_t stream, bool pdl) {
+// Grouped launch over n matrices sharing the token count M.  Shapes and pointers were validated
+// by the caller; distinct (x, K, ldx) inputs share tensor maps (at most kMaxX of them).
+cudaError_t qmm_tc_launch_grouped(int n, const void* const* x, const int* ldx, const void* const* w_tc,
+                                  void* const* out, const int* ldo, const int* N, const int* K, int M,
+                                  void* ws, cudaStream_t stream, bool pdl) {
+  if (n < 1 || n > kMaxMats) return cudaErrorInvalidValue;
   int dev = 0;
   cudaGetDevice(&dev);
-  const QmmShape sh = qmm_shape(N, K);
-  const WsLayout wl = ws_layout(N, K, device_sm_count(dev));
+  const int C_dev = device_sm_count(dev);
+  const WsLayout wl = ws_layout(0, 0, C_dev);
   uint8_t* wsb = static_cast<uint8_t*>(ws);
-  QmmParams prm;
-  prm.w_tc = static_cast<const uint8_t*>(w_tc);
-  prm.out = static_cast<__nv_bfloat16*>(out);
+  static thread_local QmmParams prm;  // ~10 KB: keep it off the stack
+  static thread_local XMaps maps;
   prm.part = reinterpret_cast<float*>(wsb + wl.part_off);
   prm.cnt = reinterpret_cast<uint32_t*>(wsb + wl.cnt_off);
   prm.err = reinterpret_cast<uint32_t*>(wsb);
   prm.M = M;
-  prm.N = N;
-  prm.G = sh.G;
-  prm.T = sh.T;
-  prm.C = C;
-  prm.ldo = ldo;
-  prm.U = sh.U;
   prm.x_rows = M <= 8 ? 8 : 16;
-  CUtensorMap map;
-  cudaError_t e = encode_x_map(&map, x, M, K, ldx, prm.x_rows);
-  if (e != cudaSuccess) return e;
-  if (M <= 2) return launch_tc<2>(prm, map, dev, stream, pdl);
-  if (M <= 4) return launch_tc<4>(prm, map, dev, stream, pdl);
-  if (M <= 8) return launch_tc<8>(prm, map, dev, stream, pdl);
-  return launch_tc<16>(prm, map, dev, stream, pdl);
+  prm.n_mats = n;
+  const void* xkey[kMaxX];
+  int kkey[kMaxX], lkey[kMaxX];
+  int nx = 0;
+  long long U = 0;
+  long long T = 0;
+  for (int i = 0; i < n; ++i) {
+    const QmmShape sh = qmm_shape(N[i], K[i]);
+    int xi = -1;
+    for (int q = 0; q < nx; ++q)
+      if (xkey[q] == x[i] && kkey[q] == K[i] && lkey[q] == ldx[i]) xi = q;
+    if (xi < 0) {
+      if (nx == kMaxX) return cudaErrorInvalidValue;
+      xi = nx++;
+      xkey[xi] = x[i];
+      kkey[xi] = K[i];
+      lkey[xi] = ldx[i];
+      cudaError_t e = encode_x_map(&maps.m[xi], x[i], M, K[i], ldx[i], prm.x_rows);
+      if (e != cudaSuccess) return e;
+    }
+    QmmMat& mt = prm.mats[i];
+    mt.w_tc = static_cast<const uint8_t*>(w_tc[i]);
+    mt.out = static_cast<__nv_bfloat16*>(out[i]);
+    mt.unit_off = U;
+    mt.N = N[i];
+    mt.G = sh.G;
+    mt.tile_off = static_cast<int>(T);
+    mt.xi = xi;
+    mt.ldo = ldo[i];
+    U += sh.U;
+    T += sh.T;
+  }
+  if (T > kMaxTiles) return cudaErrorInvalidValue;
+  for (int q = nx; q < kMaxX; ++q) maps.m[q] = maps.m[0];
+  prm.U = U;
+  prm.C = static_cast<int>(U < C_dev ? U : C_dev);
+  if (M <= 2) return launch_tc<2>(prm, maps, dev, stream, pdl);
+  if (M <= 4) return launch_tc<4>(prm, maps, dev, stream, pdl);
+  if (M <= 8) return launch_tc<8>(prm, maps, dev, stream, pdl);
+  return launch_tc<16>(prm, maps, dev, stream, pdl);
+}
+
+cudaError_t qmm_tc_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M, int N,
+                          int K, void* ws, int /*C*/, cudaStream_t stream, bool pdl) {
+  void* o = out;
+  return qmm_tc_launch_grouped(1, &x, &ldx, &w_tc, &o, &ldo, &N, &K, M, ws, stream, pdl);
 }
 
 cudaError_t qmm_repack_launch(const uint32_t* w, const uint16_t* s, const uint16_t* b, void* w_tc,

@@ -215,6 +215,51 @@ def skinny_qmm(x: torch.Tensor, w: SkinnyWeight, out: torch.Tensor | None = None
     return out.reshape(*lead, w.N)
 
 
+MAX_GROUP = 192
+MAX_GROUP_INPUTS = 8
+
+
+def skinny_qmm_grouped(xs, weights, outs=None):
+    """Many independent products at once: outs[i] = xs[i] @ dequant(weights[i])^T, one persistent
+    launch over all matrices (C-ABI skinny_qmm_w4g64_grouped).  All xs share the token count
+    (<= 16); at most 8 distinct x tensors.  Per-matrix results are bit-identical to skinny_qmm."""
+    import ctypes
+
+    n = len(weights)
+    if n == 0:
+        return []
+    if n > MAX_GROUP:
+        raise ValueError(f"at most {MAX_GROUP} matrices per grouped call")
+    if len(xs) != n:
+        raise ValueError("one x per weight")
+    xs2 = []
+    for x, w in zip(xs, weights):
+        _require_cuda(x, "x")
+        if x.shape[-1] != w.K:
+            raise ValueError(f"x has K={x.shape[-1]}, weight has K={w.K}")
+        x2 = x.reshape(-1, w.K)
+        if x2.dtype != torch.bfloat16 or not x2.is_contiguous():
+            x2 = x2.to(torch.bfloat16).contiguous()
+        xs2.append(x2)
+    m = xs2[0].shape[0]
+    if any(x.shape[0] != m for x in xs2) or not 1 <= m <= MAX_TOKENS:
+        raise ValueError(f"all inputs need the same token count in [1, {MAX_TOKENS}]")
+    dev = xs2[0].device
+    if outs is None:
+        outs = [torch.empty(m, w.N, dtype=torch.bfloat16, device=dev) for w in weights]
+    arr_p = ctypes.c_void_p * n
+    arr_i = ctypes.c_int * n
+    L = _lib.lib()
+    with torch.cuda.device(dev):
+        ws = get_workspace(dev, L.skinny_qmm_workspace_bytes(weights[0].N, weights[0].K))
+        _lib.check("skinny_qmm_w4g64_grouped", L.skinny_qmm_w4g64_grouped(
+            n, arr_p(*[x.data_ptr() for x in xs2]), arr_i(*[w.K for w in weights]),
+            arr_p(*[w.w_tc.data_ptr() for w in weights]), arr_p(*[o.data_ptr() for o in outs]),
+            arr_i(*[w.N for w in weights]), arr_i(*[w.N for w in weights]), arr_i(*[w.K for w in weights]),
+            m, ws.data_ptr(), ws.numel(), _stream_handle(dev)))
+    return outs
+
+
 def skinny_qmm_simt(x: torch.Tensor, w: SkinnyWeight) -> torch.Tensor:
     """CUDA-core cross-check of the relaid format (tests only)."""
     _require_cuda(x, "x")
@@ -262,5 +307,5 @@ def qmm(x: torch.Tensor, w_packed: torch.Tensor, scales: torch.Tensor, biases: t
 
 
 __all__ = ["GROUP", "BITS", "MAX_TOKENS", "quantize", "dequantize", "SkinnyWeight",
-           "repack_for_skinny", "skinny_qmm", "skinny_qmm_simt", "qmm", "config_for",
+           "repack_for_skinny", "skinny_qmm", "skinny_qmm_grouped", "skinny_qmm_simt", "qmm", "config_for",
            "device_errors", "reset_workspaces", "workspace_bytes"]

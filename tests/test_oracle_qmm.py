@@ -130,3 +130,19 @@ def test_stream_k_partition(U, C):
     for u in range(U):
         c = cta_of(u)
         assert u_begin(c) <= u < u_begin(c + 1)
+
+
+def test_xq_digits_exact_and_accurate():
+    """The kernel's B operand: per (token, group) power-of-two scale, two int8 digits holding a
+    16-bit fixed-point value; integer dot products, then s * 2^e * dot + b * xsum."""
+    rng = np.random.default_rng(4)
+    w = (rng.standard_normal((192, 640)) * 0.02).astype(np.float32)
+    packed, s, b = quant.quantize(w)
+    for scale in (1.0, 1e-4, 500.0):
+        x = quant.round_bf16((rng.standard_normal((5, 640)) * scale).astype(np.float32))
+        x[0, :64] = 0.0
+        x[2, 70] = 1000.0 * scale
+        e, v, hi, lo, xsum = quant.xq_digits(x)
+        assert np.array_equal(hi.astype(np.int64) * 256 + lo, v)
+        assert np.abs(v).max() <= quant.XQ_MAXINT and hi.min() >= -128 and lo.max() <= 127
+        assert quant.rel_err(quant.qmm_ref(x, packed, s, b), quant.qmm_xq(x, packed, s, b)) < 1e-3

@@ -161,3 +161,34 @@ def test_qmm_argument_errors(cuda_lib, dev):
     assert L.skinny_qmm_w4g64(*args(4, 128, wsb=16)) == -5
     assert L.skinny_qmm_w4g64(*args(4, 128)) == 0
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("m", [1, 8, 16])
+def test_qmm_grouped_matches_single_calls(cuda_lib, dev, m):
+    """One grouped launch over matrices of different shapes and inputs matches the single-call
+    results within bf16 rounding (the stream-K split points differ, so the f32 summation order of a
+    straddling tile differs) and is itself deterministic and token-count invariant."""
+    from skinny_mlx_b200.qmm import repack_for_skinny, skinny_qmm, skinny_qmm_grouped, device_errors
+
+    shapes = [(5120, 2560), (2560, 4096), (8224, 2560), (2560, 2048), (19456 // 4, 2560), (2560, 9728),
+              (200, 192), (1, 64)]
+    ws, xs, refs = [], [], []
+    xcache = {}
+    for i, (n, k) in enumerate(shapes):
+        (packed, s, b), (tw, ts, tb) = make_weight(n, k, 50 + i, dev)
+        ws.append(repack_for_skinny(tw, ts, tb))
+        if k not in xcache:
+            xcache[k] = make_x(m, k, 60 + k, dev)
+        xf, x = xcache[k]
+        xs.append(x)
+        refs.append(quant.qmm_ref(xf, packed, s, b))
+    outs = skinny_qmm_grouped(xs, ws)
+    again = skinny_qmm_grouped(xs, ws)
+    one_token = skinny_qmm_grouped([x[:1].clone() for x in xs], ws)
+    for o, o2, o1, x, w, ref in zip(outs, again, one_token, xs, ws, refs):
+        assert torch.equal(o, o2)
+        assert torch.equal(o1[0], o[0])
+        single = skinny_qmm(x, w).float().cpu().numpy()
+        assert quant.rel_err(single, o.float().cpu().numpy()) <= TIGHT
+        assert quant.rel_err(ref, o.float().cpu().numpy()) <= TIGHT
+    assert device_errors(dev) == 0
