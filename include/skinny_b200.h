@@ -36,6 +36,7 @@ extern "C" {
 #define SKINNY_ERR_CUDA -6
 #define SKINNY_ERR_DEVICE -7
 #define SKINNY_ERR_UNSUPPORTED -8
+#define SKINNY_ERR_SCRATCH_LIMIT -9
 
 /* Library version, e.g. 100 for 0.1.0. */
 int skinny_version(void);
@@ -93,6 +94,20 @@ int skinny_qmm_w4g64_grouped(int n, const void* const* x, const int* ldx, const 
  * used by the tests to localise a mismatch; it has no counterpart in the reference. */
 int skinny_qmm_w4g64_simt(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
                           int N, int K, void* stream);
+
+/* skinny_qmm_w4g64 without a workspace argument and without allocating anything: no cudaMalloc,
+ * no cudaFree, no allocating library routine.  It has NO counterpart in the reference; it exists
+ * for callers that cannot provide or allocate device memory per call (a plain C FFI host with no
+ * device-buffer type, a serving loop with a fixed memory budget, a step where an allocation's
+ * implicit device synchronisation is not acceptable).  Its scratch is one static 2,629,888-byte
+ * array in the library's device memory per device.  Limit: N <= 262,144 rows (2048 tiles of 128);
+ * larger N returns SKINNY_ERR_SCRATCH_LIMIT before anything is launched.  The first call on a
+ * device does the set-up (scratch address lookup, kernel attributes) and should come before any
+ * stream capture.  Calls that may overlap on one device (other streams or threads without
+ * ordering) race on the shared scratch; order them.  Each call clears the scratch's counters on
+ * `stream` and then launches, without programmatic dependent launch. */
+int skinny_qmm_w4g64_noalloc(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
+                             int N, int K, void* stream);
 
 #ifdef __cplusplus
 }

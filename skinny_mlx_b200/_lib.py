@@ -22,6 +22,7 @@ STATUS_NAMES = {
     -6: "SKINNY_ERR_CUDA",
     -7: "SKINNY_ERR_DEVICE",
     -8: "SKINNY_ERR_UNSUPPORTED",
+    -9: "SKINNY_ERR_SCRATCH_LIMIT",
 }
 
 # name -> (restype, argtypes); mirrors include/skinny_b200.h
@@ -38,6 +39,8 @@ SIGNATURES = {
                                       c_int, c_void_p]),
     "skinny_qmm_w4g64_grouped": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                          c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "skinny_qmm_w4g64_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int,
+                                         c_int, c_void_p]),
 }
 
 

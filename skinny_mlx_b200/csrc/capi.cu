@@ -16,6 +16,9 @@ cudaError_t qmm_repack_launch(const uint32_t* w, const uint16_t* s, const uint16
                               int N, int K, cudaStream_t stream);
 cudaError_t qmm_simt_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
                             int N, int K, cudaStream_t stream);
+bool qmm_noalloc_fits(int N, int K);
+cudaError_t qmm_tc_launch_noalloc(const void* x, int ldx, const void* w_tc, void* out, int ldo,
+                                  int M, int N, int K, cudaStream_t stream);
 }  // namespace skinny
 
 namespace {
@@ -65,6 +68,8 @@ const char* skinny_strerror(int status) {
     case SKINNY_ERR_CUDA: return "CUDA runtime call failed";
     case SKINNY_ERR_DEVICE: return "kernel recorded an error in the workspace";
     case SKINNY_ERR_UNSUPPORTED: return "unsupported device or option";
+    case SKINNY_ERR_SCRATCH_LIMIT:
+      return "shape exceeds the static scratch of skinny_qmm_w4g64_noalloc (N <= 262144 rows)";
     default: return "unknown status";
   }
 }
@@ -143,6 +148,19 @@ int skinny_qmm_w4g64_simt(const void* x, int ldx, const void* w_tc, void* out, i
   if (ldx < K || ldo < N) return SKINNY_ERR_INVALID_ARG;
   return cuda_status(skinny::qmm_simt_launch(x, ldx, w_tc, out, ldo, M, N, K,
                                              static_cast<cudaStream_t>(stream)));
+}
+
+int skinny_qmm_w4g64_noalloc(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
+                             int N, int K, void* stream) {
+  if (!x || !w_tc || !out) return SKINNY_ERR_INVALID_ARG;
+  int st = check_qmm_shape(N, K);
+  if (st != SKINNY_OK) return st;
+  if (!skinny::qmm_noalloc_fits(N, K)) return SKINNY_ERR_SCRATCH_LIMIT;
+  if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
+  if (ldx < K || ldo < N) return SKINNY_ERR_INVALID_ARG;
+  if (!aligned16(x) || (ldx % 8) != 0 || !aligned16(w_tc)) return SKINNY_ERR_ALIGNMENT;
+  return cuda_status(skinny::qmm_tc_launch_noalloc(x, ldx, w_tc, out, ldo, M, N, K,
+                                                   static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

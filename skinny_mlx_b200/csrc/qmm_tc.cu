@@ -52,6 +52,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "ptx.cuh"
 #include "qmm_layout.cuh"
 #include "skinny_status.h"
@@ -692,21 +694,21 @@ static cudaError_t launch_tc(const QmmParams& prm, const XMaps& maps, int dev, c
 }
 
 // Grouped launch over n matrices sharing the token count M.  Shapes and pointers were validated
-// by the caller; distinct (x, K, ldx) inputs share tensor maps (at most kMaxX of them).
-cudaError_t qmm_tc_launch_grouped(int n, const void* const* x, const int* ldx, const void* const* w_tc,
-                                  void* const* out, const int* ldo, const int* N, const int* K, int M,
-                                  void* ws, cudaStream_t stream, bool pdl) {
+// by the caller; distinct (x, K, ldx) inputs share tensor maps (at most kMaxX of them).  The
+// scratch is given as its three parts: error word, per-tile counters (zero on entry, left zero)
+// and partial sums for up to `C_cap` CTAs.
+static cudaError_t launch_grouped_on(int n, const void* const* x, const int* ldx,
+                                     const void* const* w_tc, void* const* out, const int* ldo,
+                                     const int* N, const int* K, int M, uint32_t* err,
+                                     uint32_t* cnt, float* part, int C_cap, int dev,
+                                     cudaStream_t stream, bool pdl) {
   if (n < 1 || n > kMaxMats) return cudaErrorInvalidValue;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int C_dev = device_sm_count(dev);
-  const WsLayout wl = ws_layout(0, 0, C_dev);
-  uint8_t* wsb = static_cast<uint8_t*>(ws);
+  const int C_dev = C_cap;
   static thread_local QmmParams prm;  // ~10 KB: keep it off the stack
   static thread_local XMaps maps;
-  prm.part = reinterpret_cast<float*>(wsb + wl.part_off);
-  prm.cnt = reinterpret_cast<uint32_t*>(wsb + wl.cnt_off);
-  prm.err = reinterpret_cast<uint32_t*>(wsb);
+  prm.part = part;
+  prm.cnt = cnt;
+  prm.err = err;
   prm.M = M;
   prm.x_rows = M <= 8 ? 8 : 16;
   prm.n_mats = n;
@@ -749,6 +751,96 @@ cudaError_t qmm_tc_launch_grouped(int n, const void* const* x, const int* ldx, c
   if (M <= 4) return launch_tc<4>(prm, maps, dev, stream, pdl);
   if (M <= 8) return launch_tc<8>(prm, maps, dev, stream, pdl);
   return launch_tc<16>(prm, maps, dev, stream, pdl);
+}
+
+cudaError_t qmm_tc_launch_grouped(int n, const void* const* x, const int* ldx, const void* const* w_tc,
+                                  void* const* out, const int* ldo, const int* N, const int* K, int M,
+                                  void* ws, cudaStream_t stream, bool pdl) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int C_dev = device_sm_count(dev);
+  const WsLayout wl = ws_layout(0, 0, C_dev);
+  uint8_t* wsb = static_cast<uint8_t*>(ws);
+  return launch_grouped_on(n, x, ldx, w_tc, out, ldo, N, K, M, reinterpret_cast<uint32_t*>(wsb),
+                           reinterpret_cast<uint32_t*>(wsb + wl.cnt_off),
+                           reinterpret_cast<float*>(wsb + wl.part_off), C_dev, dev, stream, pdl);
+}
+
+// ---------------------------------------------------------------------------------------------
+// No-allocation variant: the scratch is a fixed array in this module's device memory.
+//
+// Some callers have no way to hand us device memory for the workspace: a host runtime reached
+// through a plain C FFI that owns no CUDA allocator and carries no device-buffer type, a serving
+// loop whose memory budget is fixed when it starts and which must not grow it per request, or a
+// step that must never call cudaMalloc/cudaFree because those calls can synchronise the whole
+// device and stall the other streams sharing it.  For them the scratch lives in a file-scope
+// __device__ array, sized once for the largest call it accepts, and its address is looked up
+// with cudaGetSymbolAddress; nothing is allocated by this path, by the CUDA runtime on its behalf,
+// or by any library.
+//
+// Limits: N <= kNoAllocMaxTiles * 128 rows (tail tiles count whole) and at most kNoAllocMaxCtas
+// CTAs (a device with more SMs uses kNoAllocMaxCtas of them).  There is ONE scratch per device,
+// so two calls that may run at the same time on one device (different streams, threads without
+// ordering) race on it and corrupt each other's results; calls must be ordered, e.g. on a single
+// stream.  The first call on a device does the set-up (symbol lookup, kernel attributes, tensor-
+// map encoder lookup) and should come before any stream capture.
+// ---------------------------------------------------------------------------------------------
+constexpr int kNoAllocMaxTiles = 2048;  // N <= 262,144 rows
+constexpr int kNoAllocMaxCtas = 160;
+constexpr size_t kNoAllocCntOff = 256;
+constexpr size_t kNoAllocPartOff = kNoAllocCntOff + static_cast<size_t>(kNoAllocMaxTiles) * 4;
+constexpr size_t kNoAllocScratchBytes =
+    kNoAllocPartOff + static_cast<size_t>(kNoAllocMaxCtas) * 2 * kMaxTokens * kTileRows * 4;
+static_assert(kNoAllocScratchBytes == 2629888, "2.5 MiB of static scratch per device");
+static_assert(kNoAllocPartOff % 256 == 0, "partials start on a 256-byte boundary");
+
+// [0, 256) error word + padding | [256, 8448) tile counters | [8448, ...) partial sums
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_noalloc_mutex;
+static uint8_t* g_noalloc_ptr[64] = {};
+
+// Looks the scratch up on the current device (once per device).
+static cudaError_t noalloc_scratch(int dev, uint8_t** out) {
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    if (p == nullptr || (reinterpret_cast<uintptr_t>(p) & 255u) != 0) return cudaErrorInvalidValue;
+    g_noalloc_ptr[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+
+bool qmm_noalloc_fits(int N, int K) {
+  return qmm_shape(N, K).T <= kNoAllocMaxTiles;
+}
+
+// The error word and the counters must be zero when the kernel starts.  A launch that completes
+// leaves the counters at zero, but one that stopped on a timed-out wait may not, so both are
+// cleared on the stream before every launch (a memset node: no allocation).  The launch does not
+// use programmatic dependent launch, so it cannot start before that clear has finished.
+cudaError_t qmm_tc_launch_noalloc(const void* x, int ldx, const void* w_tc, void* out, int ldo,
+                                  int M, int N, int K, cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  uint8_t* scratch = nullptr;
+  e = noalloc_scratch(dev, &scratch);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(scratch, 0, kNoAllocPartOff, stream);
+  if (e != cudaSuccess) return e;
+  const int sms = device_sm_count(dev);
+  const int C_cap = sms < kNoAllocMaxCtas ? sms : kNoAllocMaxCtas;
+  void* o = out;
+  return launch_grouped_on(1, &x, &ldx, &w_tc, &o, &ldo, &N, &K, M,
+                           reinterpret_cast<uint32_t*>(scratch),
+                           reinterpret_cast<uint32_t*>(scratch + kNoAllocCntOff),
+                           reinterpret_cast<float*>(scratch + kNoAllocPartOff), C_cap, dev, stream,
+                           false);
 }
 
 cudaError_t qmm_tc_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M, int N,

@@ -10,6 +10,7 @@
 #define SKINNY_ERR_CUDA -6            /* a CUDA runtime call failed (see skinny_last_cuda_error) */
 #define SKINNY_ERR_DEVICE -7          /* a kernel recorded an error bit in the workspace */
 #define SKINNY_ERR_UNSUPPORTED -8     /* device is not sm_100 or option not supported */
+#define SKINNY_ERR_SCRATCH_LIMIT -9   /* shape larger than the no-alloc entry's static scratch */
 
 namespace skinny {
 // Bits OR-ed into workspace word 0 by the kernels.  The wait bits mean a bounded wait on an
