@@ -180,7 +180,11 @@ UNIT_BYTES = 4608
 
 
 def repack_tc(packed: np.ndarray, s_bits, b_bits) -> np.ndarray:
-    """MLX packs -> the kernel's unit order as uint8 bytes (see csrc/qmm_layout.cuh)."""
+    """MLX packs -> the kernel's unit order as uint8 bytes (see csrc/qmm_layout.cuh).
+
+    Each nibble is stored as q ^ 8 (q - 8 in 4-bit two's complement).  Within the 32-bit word of
+    columns c0..c7: c0..c3 sit in the high nibbles of bytes 0..3 and c4..c7 in the low nibbles,
+    so `w & 0xF0F0F0F0` and `(w << 4) & 0xF0F0F0F0` are four int8 values 16 * (q - 8) each."""
     n, kw = packed.shape
     k = kw * 8
     g = k // GROUP
@@ -190,17 +194,28 @@ def repack_tc(packed: np.ndarray, s_bits, b_bits) -> np.ndarray:
     q[:n] = unpack(packed)
     sb = np.zeros((npad, g), dtype=np.uint32)
     sb[:n] = s_bits.astype(np.uint32) | (b_bits.astype(np.uint32) << np.uint32(16))
-    # word for 8 columns c0..c7: bits 0-3 c0, 4-7 c2, 8-11 c4, 12-15 c6, 16-19 c1, ... 28-31 c7
-    q8 = q.reshape(npad, k // 8, 8)
-    slot = [0, 4, 1, 5, 2, 6, 3, 7]  # column i -> nibble slot
+    q8 = q.reshape(npad, k // 8, 8) ^ np.uint32(8)
+    shift = [4, 12, 20, 28, 0, 8, 16, 24]  # column i -> bit position
     words = np.zeros((npad, k // 8), dtype=np.uint32)
     for i in range(8):
-        words |= q8[..., i] << np.uint32(4 * slot[i])
+        words |= q8[..., i] << np.uint32(shift[i])
+    if n < npad:
+        words[n:] = 0  # padding rows hold zero bytes, not the q ^ 8 of q = 0
     # [tile, row, group, chunk, 4 words] -> [tile, group, chunk, row, 4 words]
     w5 = words.reshape(t, TILE, g, 2, 4).transpose(0, 2, 3, 1, 4)
     nib = np.ascontiguousarray(w5).reshape(t, g, 2 * TILE * 4).view(np.uint8).reshape(t, g, 4096)
     sbu = np.ascontiguousarray(sb.reshape(t, TILE, g).transpose(0, 2, 1)).view(np.uint8).reshape(t, g, 512)
     return np.concatenate([nib, sbu], axis=-1).reshape(-1)
+
+
+def unit_int8(unit_bytes: np.ndarray) -> np.ndarray:
+    """Decode one relaid unit's nibble bytes as the kernel does -> int8 [128 rows, 64 columns]
+    holding 16 * (q - 8)."""
+    words = unit_bytes[:4096].view(np.uint32).reshape(2, TILE, 4).transpose(1, 0, 2).reshape(TILE, 8)
+    lo = words & np.uint32(0xF0F0F0F0)
+    hi = (words << np.uint32(4)) & np.uint32(0xF0F0F0F0)
+    out = np.stack([lo, hi], axis=-1).reshape(TILE, 16)  # word order: k 0-3, 4-7, 8-11, ...
+    return out.view(np.int8).reshape(TILE, 64)
 
 
 # ------------------------------------------------------------------------------------------------
@@ -247,3 +262,55 @@ def qmm_xq(x: np.ndarray, packed, s_bits, b_bits) -> np.ndarray:
     s = bf16_bits_to_f32(s_bits).astype(np.float64)
     b = bf16_bits_to_f32(b_bits).astype(np.float64)
     return (dot * np.exp2(e)[:, None, :] * s[None] + xsum[:, None, :] * b[None]).sum(-1)
+
+
+def xq_block_bytes(mpad: int) -> int:
+    """Bytes of one x-prep block: int8 digits [2 MMAs][mpad/4 row groups][2][8 rows][16 B], then
+    f32 xs[mpad] and f32 xsum[mpad]."""
+    return 2 * mpad * 64 + 8 * mpad
+
+
+def xq_blocks(x: np.ndarray, mpad: int) -> np.ndarray:
+    """The x-prep kernel's output for x [M, K] (bf16 values as float32), as bytes [G, block].
+
+    Digit rows 0..mpad-1 are the hi digits of tokens 0..mpad-1, rows mpad..2*mpad-1 the lo digits;
+    byte (row r, column k) of a group sits at
+      (k >> 5) * (mpad * 64) + (r >> 3) * 256 + ((k >> 4) & 1) * 128 + (r & 7) * 16 + (k & 15),
+    i.e. per 32-column MMA step a K-major no-swizzle layout of 8-row x 16-byte core matrices with
+    128 bytes between the two K halves (leading offset) and 256 between 8-row groups (stride
+    offset).  xs = 2^(e-4) (0 for an all-zero group), xsum = 2^e * sum(v); tokens >= M are zero."""
+    m, k = x.shape
+    g = k // GROUP
+    e, v, hi, lo, xsum = xq_digits(x)
+    nz = np.abs(np.asarray(x, np.float64).reshape(m, g, GROUP)).max(-1) > 0
+    dig = np.zeros((g, 2 * mpad, GROUP), np.int8)
+    dig[:, :m] = hi.transpose(1, 0, 2)
+    dig[:, mpad:mpad + m] = lo.transpose(1, 0, 2)
+    rr, kk = np.meshgrid(np.arange(2 * mpad), np.arange(GROUP), indexing="ij")
+    off = (kk >> 5) * (mpad * 64) + (rr >> 3) * 256 + ((kk >> 4) & 1) * 128 + (rr & 7) * 16 + (kk & 15)
+    blk = np.zeros((g, xq_block_bytes(mpad)), np.uint8)
+    blk[:, off.reshape(-1)] = dig.reshape(g, -1).view(np.uint8)
+    xs = np.zeros((g, mpad), np.float32)
+    xs[:, :m] = np.where(nz, np.exp2(e - 4.0), 0.0).T.astype(np.float32)
+    xsm = np.zeros((g, mpad), np.float32)
+    xsm[:, :m] = np.where(nz, xsum, 0.0).T.astype(np.float32)
+    blk[:, 2 * mpad * 64: 2 * mpad * 64 + 4 * mpad] = xs.view(np.uint8)
+    blk[:, 2 * mpad * 64 + 4 * mpad:] = xsm.view(np.uint8)
+    return blk
+
+
+def qmm_kernel_arith(x: np.ndarray, packed, s_bits, b_bits) -> np.ndarray:
+    """The B200 kernel's arithmetic restated in float64 over its own operands: int8 weights
+    16 * (q - 8), int8 x digits, integer dot products G = 256 * dot(hi) + dot(lo), then per group
+    out += s * xs * G + (b + 8 s) * xsum.  Equals qmm_xq up to float rounding."""
+    e, v, hi, lo, xsum = xq_digits(x)
+    q = unpack(packed).astype(np.int64)
+    n = q.shape[0]
+    m, g = e.shape
+    a = 16 * (q.reshape(n, g, GROUP) - 8)
+    G = (np.einsum("mgk,ngk->mng", hi.astype(np.int64), a) * 256
+         + np.einsum("mgk,ngk->mng", lo.astype(np.int64), a))
+    s = bf16_bits_to_f32(s_bits).astype(np.float64)
+    b = bf16_bits_to_f32(b_bits).astype(np.float64)
+    xs = np.exp2(e - 4.0)
+    return (G * xs[:, None, :] * s[None] + xsum[:, None, :] * (b + 8 * s)[None]).sum(-1)

@@ -61,7 +61,9 @@ const char* skinny_strerror(int status) {
   switch (status) {
     case SKINNY_OK: return "ok";
     case SKINNY_ERR_INVALID_ARG: return "invalid argument (null pointer or negative size)";
-    case SKINNY_ERR_SHAPE: return "unsupported shape (K must be a positive multiple of 64, N >= 1)";
+    case SKINNY_ERR_SHAPE:
+      return "unsupported shape (K must be a positive multiple of 64 up to 131072, N >= 1; grouped: "
+             "at most 16384 row tiles and 2048 input groups in total)";
     case SKINNY_ERR_TOKENS: return "token count outside [1, 16]";
     case SKINNY_ERR_ALIGNMENT: return "pointer or leading dimension not 16-byte aligned";
     case SKINNY_ERR_WORKSPACE: return "workspace missing or smaller than required";
@@ -69,7 +71,8 @@ const char* skinny_strerror(int status) {
     case SKINNY_ERR_DEVICE: return "kernel recorded an error in the workspace";
     case SKINNY_ERR_UNSUPPORTED: return "unsupported device or option";
     case SKINNY_ERR_SCRATCH_LIMIT:
-      return "shape exceeds the static scratch of skinny_qmm_w4g64_noalloc (N <= 262144 rows)";
+      return "shape exceeds the static scratch of skinny_qmm_w4g64_noalloc (N <= 262144 rows, "
+             "K <= 32768 columns)";
     default: return "unknown status";
   }
 }
@@ -94,7 +97,7 @@ int skinny_repack_w4g64(const uint32_t* w, const uint16_t* scales, const uint16_
 
 size_t skinny_qmm_workspace_bytes(int N, int K) {
   if (check_qmm_shape(N, K) != SKINNY_OK) return 0;
-  return skinny::ws_layout(N, K, skinny::device_sm_count(current_device())).total;
+  return skinny::ws_layout(skinny::device_sm_count(current_device())).total;
 }
 
 int skinny_qmm_w4g64(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M, int N,
@@ -105,8 +108,9 @@ int skinny_qmm_w4g64(const void* x, int ldx, const void* w_tc, void* out, int ld
   if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
   if (ldx < K || ldo < N) return SKINNY_ERR_INVALID_ARG;
   if (!aligned16(x) || (ldx % 8) != 0 || !aligned16(w_tc)) return SKINNY_ERR_ALIGNMENT;
+  if (K / skinny::kGroup > skinny::kMaxXGroups) return SKINNY_ERR_SHAPE;
   const int C = ctas_for(N, K);
-  const skinny::WsLayout wl = skinny::ws_layout(N, K, skinny::device_sm_count(current_device()));
+  const skinny::WsLayout wl = skinny::ws_layout(skinny::device_sm_count(current_device()));
   if (!workspace || workspace_bytes < wl.total || !aligned16(workspace)) return SKINNY_ERR_WORKSPACE;
   return cuda_status(skinny::qmm_tc_launch(x, ldx, w_tc, out, ldo, M, N, K, workspace, C,
                                            static_cast<cudaStream_t>(stream), true));
@@ -120,6 +124,7 @@ int skinny_qmm_w4g64_grouped(int n, const void* const* x, const int* ldx, const 
   if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
   long long tiles = 0;
   int distinct = 0;
+  long long xgroups = 0;
   for (int i = 0; i < n; ++i) {
     if (!x[i] || !w_tc[i] || !out[i]) return SKINNY_ERR_INVALID_ARG;
     const int st = check_qmm_shape(N[i], K[i]);
@@ -130,10 +135,15 @@ int skinny_qmm_w4g64_grouped(int n, const void* const* x, const int* ldx, const 
     bool seen = false;
     for (int q = 0; q < i; ++q)
       if (x[q] == x[i] && K[q] == K[i] && ldx[q] == ldx[i]) seen = true;
-    if (!seen) ++distinct;
+    if (!seen) {
+      ++distinct;
+      xgroups += K[i] / skinny::kGroup;
+    }
   }
-  if (tiles > skinny::kMaxTiles || distinct > SKINNY_QMM_MAX_GROUP_INPUTS) return SKINNY_ERR_SHAPE;
-  const skinny::WsLayout wl = skinny::ws_layout(0, 0, skinny::device_sm_count(current_device()));
+  if (tiles > skinny::kMaxTiles || distinct > SKINNY_QMM_MAX_GROUP_INPUTS ||
+      xgroups > skinny::kMaxXGroups)
+    return SKINNY_ERR_SHAPE;
+  const skinny::WsLayout wl = skinny::ws_layout(skinny::device_sm_count(current_device()));
   if (!workspace || workspace_bytes < wl.total || !aligned16(workspace)) return SKINNY_ERR_WORKSPACE;
   return cuda_status(skinny::qmm_tc_launch_grouped(n, x, ldx, w_tc, out, ldo, N, K, M, workspace,
                                                    static_cast<cudaStream_t>(stream), true));

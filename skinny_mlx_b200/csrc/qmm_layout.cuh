@@ -8,14 +8,23 @@
 //   [chunk c in {0,1}][row r in 0..127][16 bytes]   4096 B: row r's columns 32c .. 32c+31
 //   [row r in 0..127][bf16 scale, bf16 bias]          512 B
 //
-// Units are ordered tile-major (tile = 128-row block, rows padded with zeros up to a multiple
-// of 128), group-minor, so any contiguous range of units is one contiguous byte range.
-// Inside each 32-bit word the eight nibbles of columns k0..k7 are placed so that two masks
-// and one shift produce f16 pairs in natural column order (the 0x6400 "1024 + q" trick):
-//   bits 0-3 k0 | 4-7 k2 | 8-11 k4 | 12-15 k6 | 16-19 k1 | 20-23 k3 | 24-27 k5 | 28-31 k7
+// Units are ordered tile-major (tile = 128-row block, rows padded with zero bytes up to a
+// multiple of 128), group-minor, so any contiguous range of units is one contiguous byte range.
+// Each nibble is stored as q ^ 8, i.e. q - 8 in 4-bit two's complement, and inside the 32-bit
+// word of columns k0..k7 the nibbles sit at
+//   bits 0-3 k4 | 4-7 k0 | 8-11 k5 | 12-15 k1 | 16-19 k6 | 20-23 k2 | 24-27 k7 | 28-31 k3
+// so that  w & 0xF0F0F0F0  is the int8 quadruple 16*(q-8) of k0..k3 and
+//  (w << 4) & 0xF0F0F0F0  that of k4..k7: the tensor-core A operand in one or two ALU ops.
 //
-// Activations are read as given (bf16 [M, K], row stride ldx) through a TMA tensor map: one box
-// of 64 columns x 8 or 16 token rows per unit, 128-byte swizzled, rows past M zero-filled.
+// Activations.  An x-prep kernel turns x (bf16 [M, K], row stride ldx) into one block per
+// 64-column group (xq_block_bytes(mpad) bytes, mpad = 8 for M <= 8 else 16):
+//   int8 digits  [2 MMA steps of 32 columns][mpad/4 row groups][2 halves of 16 columns][8 rows][16 B]
+//   f32 xs[mpad]    2^(e-4) for the token's power-of-two exponent e in this group (0 if all zero)
+//   f32 xsum[mpad]  2^e * sum(v), the exact sum of the fixed-point values
+// Digit row t < mpad holds hi(t), row mpad + t holds lo(t), where v = rint(x * 2^-e) has
+// |v| <= 32639 = 127 * 256 + 127 and v = 256 hi + lo with hi, lo signed 8-bit.  Tokens >= M are
+// zero.  Per MMA step the digits form a K-major, no-swizzle operand of 8-row x 16-byte core
+// matrices: 128 bytes between the two 16-column halves, 256 bytes between 8-row groups.
 #pragma once
 #include <cstddef>
 #include <cstdint>
@@ -54,22 +63,28 @@ __host__ __device__ inline QmmShape qmm_shape(int N, int K) {
 
 inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Workspace layout (caller-owned, zero-filled before its first use).  The counter region has a
-// fixed offset and capacity so that calls of different shapes can share one workspace: only the
-// counters must persist between launches (each launch leaves them at zero); partials are
-// rewritten by every launch before they are read.
+// Bytes of one x-prep block for `mpad` (8 or 16) token rows.
+__host__ __device__ constexpr int xq_block_bytes(int mpad) { return 2 * mpad * 64 + 8 * mpad; }
+
+// Workspace layout (caller-owned, zero-filled before its first use).  Every region has a fixed
+// offset and capacity so that calls of different shapes can share one workspace: only the
+// counters must persist between launches (each launch leaves them at zero); partials and x-prep
+// blocks are rewritten by every launch before they are read.
 //   [0, 256)                      header; word 0 = device error bits
 //   [256, 256 + 4*kMaxTiles)      per-tile arrival counters
 //   partials                      C_dev x 2 slots x 16 tokens x 128 rows f32
-constexpr int kMaxTiles = 16384;  // N <= 2,097,152 rows
+//   x-prep blocks                 kMaxXGroups x xq_block_bytes(16)
+constexpr int kMaxTiles = 16384;   // N <= 2,097,152 rows per call (all matrices of a group)
+constexpr int kMaxXGroups = 2048;  // sum over distinct inputs of K/64 (K <= 131,072)
 struct WsLayout {
-  size_t cnt_off, part_off, total;
+  size_t cnt_off, part_off, xq_off, total;
 };
-inline WsLayout ws_layout(int /*N*/, int /*K*/, int C_dev) {
+inline WsLayout ws_layout(int C_dev) {
   WsLayout w;
   w.cnt_off = 256;
   w.part_off = w.cnt_off + static_cast<size_t>(kMaxTiles) * 4;
-  w.total = round_up(w.part_off + static_cast<size_t>(C_dev) * 2 * kMaxTokens * kTileRows * 4, 256);
+  w.xq_off = round_up(w.part_off + static_cast<size_t>(C_dev) * 2 * kMaxTokens * kTileRows * 4, 256);
+  w.total = round_up(w.xq_off + static_cast<size_t>(kMaxXGroups) * xq_block_bytes(16), 256);
   return w;
 }
 

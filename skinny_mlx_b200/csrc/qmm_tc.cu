@@ -4,14 +4,20 @@
 //
 // This is the affine identity of skinny_mlx/qmm.py:8-9 and :64-71: scale and bias are applied
 // once per 64-column group, in f32.  It is computed "swap-AB": weight rows are the 128-row MMA
-// operand A and the tokens are the N=16 operand B, so a 1..16-token step reads every weight byte
-// exactly once.
+// operand A and the tokens are the narrow operand B, so a 1..16-token step reads every weight
+// byte exactly once.
 //
-// Operands are bf16.  A nibble q OR-ed into the bf16 0x4300 (= 128) gives 128 + q exactly (the
-// bf16 form of the reference's f16 0x6400 "1024 + q" trick, skinny_mlx/qmm.py:57-58), so the MMA
-// sees A = 128 + q and x exactly as given, with f32 products exact.  A helper warp sums each x
-// tile per token (xsum, f32, fixed reduction tree), and the epilogue folds the offset away:
-//   s * sum x (128 + q) + (b - 128 s) * xsum  =  s * sum x q + b * xsum.
+// Integer tensor cores (tcgen05.mma kind::i8).  The relaid nibble q ^ 8 shifted into the high
+// half of a byte is the signed 8-bit value 16 (q - 8): two ALU ops per eight weights produce the
+// A operand.  x is given to the tensor core as 16-bit fixed point per (token, group): with the
+// power-of-two exponent e chosen so that |v| <= 32639, v = rint(x 2^-e) = 256 hi + lo with
+// signed 8-bit digits hi, lo, which an x-prep kernel writes once per call.  B holds the hi
+// digits of every token in its first rows and the lo digits in the next, so one MMA gives both
+// integer dot products exactly (s32 accumulators).  The epilogue computes, per group,
+//   G = 256 dot(hi) + dot(lo) = sum v * 16 (q - 8)
+//   out += (s 2^(e-4)) * G + (b + 8 s) * (2^e sum v)  =  s * sum x q + b * sum x   (x := v 2^e)
+// The only rounding before the f32 accumulation is that of x to 16 significant bits relative
+// to its group maximum (at most 2^-16 of it), far below the bf16 output rounding.
 //
 // Work split (stream-K): the matrix is cut into units of 128 rows x 64 columns (4608 relaid
 // bytes, see qmm_layout.cuh) and each of the C CTAs (one per SM) takes a contiguous range of
@@ -22,33 +28,31 @@
 //
 // Load stages.  A TMA bulk copy costs a roughly fixed amount of engine time, so small copies cap
 // the stream well below HBM bandwidth (measured on B200: 4.6 KB copies ~2.6 TB/s per CTA-per-SM,
-// 18 KB copies ~6.6 TB/s).  A stage therefore carries up to 4 consecutive units of one tile:
-// one bulk copy of their weights and one tensor-map box per unit for its x tile
-// (64 columns x 8 or 16 token rows, SWIZZLE_128B, rows past M zero-filled).  Stages
-// alternate between two (dequant warpgroup, MMA issuer) pairs, so each stage is consumed and
-// released by exactly one pair plus the xsum warp.
+// 18 KB copies ~6.6 TB/s).  A stage therefore carries up to 4 consecutive units of one tile: one
+// bulk copy of their weights and one of their x-prep blocks (consecutive groups are adjacent).
+// Stages alternate between two "lanes", each with its own MMA issuer, tensor-memory slots and
+// epilogue warpgroup, so the MMAs and the epilogue of one stage overlap those of the other.
 //
 // Warp roles in a CTA of 512 threads (16 warps):
-//   warp 0 lane 0   TMA producer over a 3-stage ring.  The first stages are issued before
+//   warp 0 lane 0   TMA producer over a 4-stage ring.  The first stages are issued before
 //                   griddepcontrol.wait only for their weights (weights do not depend on the
 //                   previous kernel), so under programmatic dependent launch this launch's weight
 //                   stream overlaps the tail of the previous one.  Tensor memory is allocated
 //                   after that, since the previous kernel's CTA on this SM may still hold it.
-//   warps 1, 15     MMA issuers for even / odd stages (warp 1 also allocates TMEM): per unit 4
-//                   independent tcgen05.mma 128x16x16 (one per 16-column K slice, A = the unit's
-//                   dequantized slot in TMEM, B = its x tile) as two independent 2-deep chains
-//                   into two 16-column D sub-slots (long accumulation chains serialise in the
-//                   tensor pipe).
-//   warps 2..5      epilogue warpgroup, units in order: thread = weight row = TMEM lane; sums
-//                   the 4 partial dot products, applies scale/bias with the tile's xsums and
-//                   accumulates in f32 registers; writes finished tiles or publishes partials.
-//   warps 6..9      dequant warpgroup for even stages, warps 10..13 for odd stages: thread =
-//                   weight row; 64 nibbles (two 16-byte shared loads) -> 32 bf16x2 words ->
-//                   tcgen05.st into the unit's A slot.
-//   warp 14         xsum: per unit sums each token row of its x tile from shared memory.
+//   warps 1, 2      MMA issuers of lane 0 / lane 1 (warp 1 also allocates TMEM): per unit two
+//                   chained tcgen05.mma 128 x (2 mpad) x 32 into the unit's D slot.
+//   warps 4..7      dequant warpgroup, every stage: thread = weight row; 64 nibbles (two 16-byte
+//                   shared loads) -> 16 int8x4 words -> tcgen05.st into the unit's A slot; also
+//                   copies the unit's scale/bias and x scales to a small ring read by the
+//                   epilogue, so a load stage is released early.
+//   warps 8..11     epilogue warpgroup of lane 0, warps 12..15 of lane 1: thread = weight row =
+//                   TMEM lane; combines the digit dot products, applies scale/bias once per group
+//                   and accumulates in f32 registers; at each tile end the two lanes' sums are
+//                   added in a fixed order and the tile is written or its partial published.
+//   warp 3          allocation helper only.
+#include <cfloat>
 #include <cstdint>
 #include <cuda.h>
-#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -60,25 +64,15 @@
 
 namespace skinny {
 
-constexpr int kStages = 3;
+constexpr int kStages = 4;                         // even: stage slot s is always used by lane s % 2
 constexpr int kUPS = 4;                            // units per stage (same tile)
-constexpr int kXTileBytes = 2048;                  // 16 token rows x 128 B (SWIZZLE_128B)
-constexpr int kXStageBytes = kUPS * kXTileBytes;   // 8 KB
 constexpr int kWStageBytes = kUPS * kUnitWBytes;   // 18 KB
-constexpr int kXRingBytes = kStages * kXStageBytes;
 constexpr int kWRingBytes = kStages * kWStageBytes;
-constexpr int kNumA = 2 * kUPS;                    // TMEM A slots: 4 per dequant warpgroup
-// TMEM D slots (2 x 16 columns each).  The two MMA issuers own alternate 4-unit stages, so one
-// issuer's consecutive units can be up to 5 apart; the D ring must be at least that deep or a
-// parity wait on d_empty can alias a phase two ahead.
-constexpr int kNumD = 8;
-constexpr int kTmemCols = 512;
-constexpr int kDCol0 = kNumA * 32;                 // 256
 constexpr int kThreads = 512;
+constexpr int kEpiWarp0 = 8;                       // warps 8..11 lane 0, 12..15 lane 1
 constexpr int kEpiThreads = 128;
-constexpr int kDeqThreads = 128;                   // per warpgroup
-constexpr int kXsumWarp = 14;
-constexpr int kRS = 16;                            // per-unit scale/bias + xsum ring for the epilogue
+constexpr int kACols = 16;                         // TMEM columns of one unit's int8 A operand
+constexpr int kDCol0 = 2 * kUPS * kACols;          // 128: D slots follow the 8 A slots
 
 // Grouped launch: one persistent grid streams the concatenated units of up to kMaxMats
 // independent matrices (same token count), so launch overhead, pipeline fill and the stream-K
@@ -86,85 +80,116 @@ constexpr int kRS = 16;                            // per-unit scale/bias + xsum
 constexpr int kMaxMats = 192;
 constexpr int kMaxX = 8;
 
+// Unit indices fit in 32 bits: at most kMaxTiles tiles of at most kMaxXGroups groups (2^25).
 struct QmmMat {
   const uint8_t* w_tc;  // relaid weight units of this matrix
-  __nv_bfloat16* out;   // [M, N] (leading dimension N)
-  long long unit_off;   // first global unit of this matrix
+  __nv_bfloat16* out;   // [M, N] (leading dimension ldo)
+  int unit_off;         // first global unit of this matrix
   int N, G;             // rows, 64-column groups
   int tile_off;         // first global tile (counter index) of this matrix
-  int xi;               // index of this matrix's activation tensor map
+  int xg_off;           // first x-prep block of this matrix's input
   int ldo;              // leading dimension of out (>= N)
 };
 
 struct QmmParams {
-  float* part;          // [C_dev][2][16][128] partial sums (workspace)
+  float* part;          // [C][2][16][128] partial sums (workspace)
   uint32_t* cnt;        // [kMaxTiles] arrival counters (workspace)
   uint32_t* err;        // device error word (workspace)
-  int M, C, x_rows, n_mats;
-  long long U;          // total units
+  const uint8_t* xq;    // x-prep blocks (workspace)
+  int M, C, n_mats;
+  int U;                // total units
   QmmMat mats[kMaxMats];
 };
 
-struct XMaps {
-  CUtensorMap m[kMaxX];
+struct XPrepIn {
+  const __nv_bfloat16* x;
+  int ldx, G, xg_off, pad_;
 };
 
-// Matrix holding global unit u (largest m with unit_off <= u).
-__device__ __forceinline__ int mat_of(const QmmParams& p, long long u) {
-  int lo = 0, hi = p.n_mats - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (p.mats[mid].unit_off <= u) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
+struct XPrepParams {
+  XPrepIn in[kMaxX];
+  uint8_t* xq;
+  int n_in, M, mpad, total_groups;
+};
 
-// The epilogue, which trails the MMA, reads each unit's scale/bias words and xsums from a
-// kRS-deep ring, so a load stage is released as soon as its dequant warpgroup, the xsum warp and
-// its MMA issuer are done with it and the epilogue's lag never throttles the TMA stream.
-struct __align__(16) QmmSmemBarriers {
-  uint32_t sbr[kRS][kTileRows];        // per-unit (bf16 scale, bf16 bias) of each row
-  float xsr[kRS][kMaxTokens];          // per-unit xsum of each token
+// Per-unit data the epilogue needs after the load stage is gone: each row's (scale, bias) and
+// the tokens' xs / xsum.  One slot per (lane, unit of the stage), like the D slots.
+struct __align__(16) QmmMeta {
+  uint32_t sb[kTileRows];
+  float x[2 * kMaxTokens];  // xs[0..15] then xsum[0..15]
+};
+
+struct __align__(16) QmmSmem {
+  QmmMeta meta[2][kUPS];
   uint64_t full[kStages];
   uint64_t empty[kStages];
-  uint64_t a_full[kNumA];
-  uint64_t a_empty[kNumA];
-  uint64_t d_full[kNumD];
-  uint64_t d_empty[kNumD];
-  uint64_t sb_full[kRS];
-  uint64_t xs_full[kRS];
-  uint64_t ep_empty[kRS];
+  // Per lane, one phase per stage of that lane ("lane-stage"):
+  uint64_t a_full[2];   // dequant -> MMA/epilogue: A slots stored, meta slots written
+  uint64_t a_empty[2];  // MMA -> dequant: the stage's MMAs completed (A slots free)
+  uint64_t d_full[2];   // MMA -> epilogue: accumulators ready
+  uint64_t d_empty[2];  // epilogue -> MMA/dequant: D and meta slots read
   uint64_t mma_done[2];
   uint32_t tmem_base;
   int abort_flag;
-  int last_flag;
+  int last_flag[2];
+};
+// followed by the epilogue's partial-sum exchange, float [2][NT][128]
+
+__host__ __device__ constexpr int mpad_of(int NT) { return NT <= 8 ? 8 : 16; }
+__host__ __device__ constexpr int xstage_bytes(int NT) { return kUPS * xq_block_bytes(mpad_of(NT)); }
+__host__ __device__ constexpr size_t qmm_smem_bytes(int NT) {
+  return static_cast<size_t>(kStages) * xstage_bytes(NT) + kWRingBytes + sizeof(QmmSmem) +
+         static_cast<size_t>(2) * NT * kTileRows * 4 + 128;
+}
+static_assert(qmm_smem_bytes(8) * 2 <= 227 * 1024, "two CTAs per SM for M <= 8");
+static_assert(qmm_smem_bytes(16) <= 227 * 1024, "one CTA per SM for M <= 16");
+
+// Walks a CTA's unit range in stages, tracking the matrix, the tile within it and the group
+// within the tile incrementally (no division per unit).  A stage never crosses a tile end.
+struct UnitWalk {
+  int u;   // global unit at the start of the current stage
+  int mi;  // matrix of unit u
+  int lt;  // tile of unit u within its matrix
+  int g;   // group of unit u within its tile
+  __device__ __forceinline__ void init(const QmmParams& p, int u0) {
+    int lo = 0, hi = p.n_mats - 1;  // largest m with unit_off <= u0
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (p.mats[mid].unit_off <= u0) lo = mid; else hi = mid - 1;
+    }
+    mi = lo;
+    const int lu = u0 - p.mats[mi].unit_off;
+    lt = lu / p.mats[mi].G;
+    g = lu - lt * p.mats[mi].G;
+    u = u0;
+  }
+  // Units of the stage starting at u: at most kUPS, never past u1 or the end of u's tile.
+  __device__ __forceinline__ int stage_n(const QmmMat& mt, int u1) const {
+    int n = u1 - u;
+    if (n > mt.G - g) n = mt.G - g;
+    return n < kUPS ? n : kUPS;
+  }
+  __device__ __forceinline__ void advance(const QmmParams& p, int n) {
+    u += n;
+    g += n;
+    if (g == p.mats[mi].G) {
+      g = 0;
+      ++lt;
+      if (mi + 1 < p.n_mats && u == p.mats[mi + 1].unit_off) {
+        ++mi;
+        lt = 0;
+      }
+    }
+  }
 };
 
-constexpr int kBarBytes = 12288;
-constexpr size_t kQmmSmemBytes = static_cast<size_t>(kXRingBytes) + kWRingBytes + kBarBytes + 1024;
-static_assert(sizeof(QmmSmemBarriers) <= kBarBytes, "barrier block");
-
-// Units of the next stage starting at global unit u: at most kUPS, never past the CTA's range
-// end or the end of u's tile (hence never across matrices).
-__device__ __forceinline__ int stage_units(const QmmParams& p, long long u, long long u1) {
-  const QmmMat& mt = p.mats[mat_of(p, u)];
-  long long n = u1 - u;
-  const int to_tile_end = mt.G - static_cast<int>((u - mt.unit_off) % mt.G);
-  if (n > to_tile_end) n = to_tile_end;
-  return n < kUPS ? static_cast<int>(n) : kUPS;
-}
-
-// 64 nibbles of one row (8 relaid words) -> 32 bf16x2 words holding (128 + q) exactly, in
-// natural column order: pair j of word w covers columns 8w + 2j, 8w + 2j + 1.
-__device__ __forceinline__ void decode8(const uint4& lo, const uint4& hi, uint32_t (&o)[32]) {
-  const uint32_t words[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+// 64 relaid nibbles of one row -> 16 words of four int8 values 16 (q - 8), in column order.
+__device__ __forceinline__ void decode_i8(const uint4& c0, const uint4& c1, uint32_t (&o)[16]) {
+  const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const uint32_t v = words[j];
-    o[4 * j + 0] = (v & 0x000F000Fu) | 0x43004300u;
-    o[4 * j + 1] = ((v >> 4) & 0x000F000Fu) | 0x43004300u;
-    o[4 * j + 2] = ((v >> 8) & 0x000F000Fu) | 0x43004300u;
-    o[4 * j + 3] = ((v >> 12) & 0x000F000Fu) | 0x43004300u;
+    o[2 * j] = w[j] & 0xF0F0F0F0u;
+    o[2 * j + 1] = (w[j] << 4) & 0xF0F0F0F0u;
   }
 }
 
@@ -172,49 +197,111 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// NT: token columns read back per unit (2, 4, 8 or 16).
+// ---------------------------------------------------------------------------------------------
+// x-prep: one warp per (token, group).  Lane l holds columns 2l, 2l+1 of the group.
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) qmm_xprep_kernel(const __grid_constant__ XPrepParams p) {
+  pdl_launch_dependents();  // the qmm kernel may start streaming weights now
+  pdl_wait_prior_grid();    // x is written by the previous kernel
+  const int wid = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int mpad = p.mpad;
+  if (wid >= p.total_groups * mpad) return;
+  const int gg = wid / mpad;  // global x-prep block
+  const int t = wid - gg * mpad;
+  int i = 0;
+  while (i + 1 < p.n_in && gg >= p.in[i + 1].xg_off) ++i;
+  const XPrepIn& in = p.in[i];
+  const int g = gg - in.xg_off;
+
+  float x0 = 0.f, x1 = 0.f;
+  if (t < p.M) {
+    const uint32_t w2 = *reinterpret_cast<const uint32_t*>(in.x + static_cast<size_t>(t) * in.ldx +
+                                                           g * kGroup + 2 * lane);
+    x0 = __uint_as_float(w2 << 16);
+    x1 = __uint_as_float(w2 & 0xFFFF0000u);
+  }
+  float amax = fmaxf(fabsf(x0), fabsf(x1));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  // fmaxf drops a NaN operand: detect non-finite values separately
+  const bool bad = __any_sync(0xFFFFFFFFu, !(fabsf(x0) <= FLT_MAX) || !(fabsf(x1) <= FLT_MAX));
+
+  int v0 = 0, v1 = 0;
+  float xs = 0.f, xsum = 0.f;
+  if (bad) {
+    xs = __int_as_float(0x7FC00000);  // the group's products become NaN, as in f32 arithmetic
+    xsum = xs;
+  } else if (amax > 0.f) {
+    int e2;
+    frexpf(amax, &e2);                 // amax = m 2^e2, m in [0.5, 1)
+    int e = e2 - 15;                   // smallest e with amax <= 32639 2^e is e2-15 or e2-14
+    if (ldexpf(amax, -e) > 32639.f) e += 1;
+    v0 = __float2int_rn(ldexpf(x0, -e));  // exact scaling, round half to even
+    v1 = __float2int_rn(ldexpf(x1, -e));
+    int vs = v0 + v1;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) vs += __shfl_xor_sync(0xFFFFFFFFu, vs, o);
+    xs = ldexpf(1.f, e - 4);
+    xsum = ldexpf(static_cast<float>(vs), e);  // |vs| < 2^21: exact
+  }
+  const int hi0 = (v0 + 128) >> 8, hi1 = (v1 + 128) >> 8;
+  const int lo0 = v0 - 256 * hi0, lo1 = v1 - 256 * hi1;
+  uint8_t* blk = p.xq + static_cast<size_t>(gg) * xq_block_bytes(mpad);
+  const int k = 2 * lane;
+  const int kofs = (k >> 5) * (mpad * 64) + ((k >> 4) & 1) * 128 + (k & 15);
+  const int rh = t, rl = mpad + t;
+  *reinterpret_cast<uint16_t*>(blk + kofs + (rh >> 3) * 256 + (rh & 7) * 16) =
+      static_cast<uint16_t>((hi0 & 0xFF) | ((hi1 & 0xFF) << 8));
+  *reinterpret_cast<uint16_t*>(blk + kofs + (rl >> 3) * 256 + (rl & 7) * 16) =
+      static_cast<uint16_t>((lo0 & 0xFF) | ((lo1 & 0xFF) << 8));
+  if (lane == 0) {
+    float* xf = reinterpret_cast<float*>(blk + 2 * mpad * 64);
+    xf[t] = xs;
+    xf[mpad + t] = xsum;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// The qmm kernel.  NT: token columns read back per unit (2, 4, 8 or 16).
+// ---------------------------------------------------------------------------------------------
 template <int NT>
 __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
-    qmm_w4g64_tc_kernel(const __grid_constant__ QmmParams p, const __grid_constant__ XMaps xmaps) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // 1024-byte alignment for the SWIZZLE_128B x tiles
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* xring = smem;
-  uint8_t* wring = smem + kXRingBytes;
-  QmmSmemBarriers* sb = reinterpret_cast<QmmSmemBarriers*>(wring + kWRingBytes);
+    qmm_w4g64_tc_kernel(const __grid_constant__ QmmParams p) {
+  constexpr int MP = mpad_of(NT);
+  constexpr int XB = xq_block_bytes(MP);
+  constexpr int XSTAGE = xstage_bytes(NT);
+  constexpr int DW = 2 * MP;                          // D columns per unit (hi rows, lo rows)
+  constexpr int kTmemCols = NT == 16 ? 512 : 256;
+  static_assert(kDCol0 + 2 * kUPS * DW <= kTmemCols, "tensor memory budget");
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint8_t* xring = smem;                              // kStages x XSTAGE
+  uint8_t* wring = smem + kStages * XSTAGE;           // kStages x kWStageBytes
+  QmmSmem* sb = reinterpret_cast<QmmSmem*>(wring + kWRingBytes);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int c = blockIdx.x;
-  const long long u0 = u_begin(c, p.U, p.C);
-  const long long u1 = u_begin(c + 1, p.U, p.C);
-  const int L = static_cast<int>(u1 - u0);
-  const int xtile = p.x_rows * 128;  // bytes of one x tile in shared memory
+  const int u0 = static_cast<int>(u_begin(c, p.U, p.C));
+  const int u1 = static_cast<int>(u_begin(c + 1, p.U, p.C));
   volatile int* abort_flag = &sb->abort_flag;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(smem_u32(&sb->full[i]), 1);
-      mbar_init(smem_u32(&sb->empty[i]), 1 + kDeqThreads + 32);  // MMA commit + dequant wg + xsum warp
+      mbar_init(smem_u32(&sb->empty[i]), 1 + 4);  // MMA commit + the 4 dequant warps of the lane
     }
-    for (int i = 0; i < kNumA; ++i) {
-      mbar_init(smem_u32(&sb->a_full[i]), kDeqThreads);
-      mbar_init(smem_u32(&sb->a_empty[i]), 1);
-    }
-    for (int i = 0; i < kNumD; ++i) {
-      mbar_init(smem_u32(&sb->d_full[i]), 1);
-      mbar_init(smem_u32(&sb->d_empty[i]), kEpiThreads);
-    }
-    for (int i = 0; i < kRS; ++i) {
-      mbar_init(smem_u32(&sb->sb_full[i]), kDeqThreads);
-      mbar_init(smem_u32(&sb->xs_full[i]), 32);
-      mbar_init(smem_u32(&sb->ep_empty[i]), kEpiThreads);
+    for (int l = 0; l < 2; ++l) {
+      mbar_init(smem_u32(&sb->a_full[l]), 4);   // the 4 dequant warps
+      mbar_init(smem_u32(&sb->a_empty[l]), 1);  // MMA commit
+      mbar_init(smem_u32(&sb->d_full[l]), 1);   // MMA commit
+      mbar_init(smem_u32(&sb->d_empty[l]), 4);  // the 4 warps of epilogue warpgroup l
     }
     mbar_init(smem_u32(&sb->mma_done[0]), 1);
     mbar_init(smem_u32(&sb->mma_done[1]), 1);
     sb->abort_flag = 0;
-    sb->last_flag = 0;
+    sb->last_flag[0] = sb->last_flag[1] = 0;
     fence_mbar_init();
-    for (int q = 0; q < kMaxX; ++q) prefetch_tmap(&xmaps.m[q]);
   }
   __syncthreads();
   pdl_launch_dependents();
@@ -236,47 +323,46 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
     if (lane == 0) {
       // ------------------------------ TMA producer ------------------------------
       const uint64_t pol_w = policy_evict_first();
-      const uint32_t xbytes = static_cast<uint32_t>(xtile);
-      long long u = u0;
+      UnitWalk wk;
+      wk.init(p, u0);
       int k = 0;
-      // first stages: weights before griddepcontrol.wait, x tiles after
-      long long first_u[kStages];
-      int nfirst = 0;
-      while (u < u1 && k < kStages) {
-        const int n = stage_units(p, u, u1);
-        const QmmMat& mt = p.mats[mat_of(p, u)];
-        mbar_arrive_expect_tx(smem_u32(&sb->full[k]), static_cast<uint32_t>(n) * (kUnitWBytes + xbytes));
-        bulk_g2s_hint(smem_u32(wring + k * kWStageBytes), mt.w_tc + (u - mt.unit_off) * kUnitWBytes,
+      // first stages: weights before griddepcontrol.wait, x blocks after
+      while (wk.u < u1 && k < kStages) {
+        const QmmMat& mt = p.mats[wk.mi];
+        const int n = wk.stage_n(mt, u1);
+        mbar_arrive_expect_tx(smem_u32(&sb->full[k]), static_cast<uint32_t>(n) * (kUnitWBytes + XB));
+        bulk_g2s_hint(smem_u32(wring + k * kWStageBytes),
+                      mt.w_tc + static_cast<size_t>(wk.u - mt.unit_off) * kUnitWBytes,
                       static_cast<uint32_t>(n) * kUnitWBytes, smem_u32(&sb->full[k]), pol_w);
-        first_u[k] = u;
-        u += n;
+        wk.advance(p, n);
         ++k;
-        ++nfirst;
       }
-      pdl_wait_prior_grid();  // x is produced by the previous kernel
-      for (int f = 0; f < nfirst; ++f) {
-        const QmmMat& mt = p.mats[mat_of(p, first_u[f])];
-        const int g = static_cast<int>((first_u[f] - mt.unit_off) % mt.G);
-        const int n = stage_units(p, first_u[f], u1);
-        for (int j = 0; j < n; ++j)
-          tma_load_2d(smem_u32(xring + f * kXStageBytes + j * xtile), &xmaps.m[mt.xi], (g + j) * kGroup, 0,
-                      smem_u32(&sb->full[f]));
+      pdl_wait_prior_grid();  // the x-prep blocks are written by the previous kernel
+      {
+        UnitWalk w2;
+        w2.init(p, u0);
+        for (int f = 0; f < k; ++f) {
+          const QmmMat& mt = p.mats[w2.mi];
+          const int n = w2.stage_n(mt, u1);
+          bulk_g2s(smem_u32(xring + f * XSTAGE), p.xq + static_cast<size_t>(mt.xg_off + w2.g) * XB,
+                   static_cast<uint32_t>(n) * XB, smem_u32(&sb->full[f]));
+          w2.advance(p, n);
+        }
       }
-      while (u < u1) {
+      while (wk.u < u1) {
         const int s = k % kStages;
         if (!mbar_wait(smem_u32(&sb->empty[s]), ((k / kStages) - 1) & 1, p.err, kErrBitWaitEmpty,
                        abort_flag))
           break;
-        const int n = stage_units(p, u, u1);
-        const QmmMat& mt = p.mats[mat_of(p, u)];
-        const int g = static_cast<int>((u - mt.unit_off) % mt.G);
-        mbar_arrive_expect_tx(smem_u32(&sb->full[s]), static_cast<uint32_t>(n) * (kUnitWBytes + xbytes));
-        bulk_g2s_hint(smem_u32(wring + s * kWStageBytes), mt.w_tc + (u - mt.unit_off) * kUnitWBytes,
+        const QmmMat& mt = p.mats[wk.mi];
+        const int n = wk.stage_n(mt, u1);
+        mbar_arrive_expect_tx(smem_u32(&sb->full[s]), static_cast<uint32_t>(n) * (kUnitWBytes + XB));
+        bulk_g2s_hint(smem_u32(wring + s * kWStageBytes),
+                      mt.w_tc + static_cast<size_t>(wk.u - mt.unit_off) * kUnitWBytes,
                       static_cast<uint32_t>(n) * kUnitWBytes, smem_u32(&sb->full[s]), pol_w);
-        for (int j = 0; j < n; ++j)
-          tma_load_2d(smem_u32(xring + s * kXStageBytes + j * xtile), &xmaps.m[mt.xi], (g + j) * kGroup, 0,
-                      smem_u32(&sb->full[s]));
-        u += n;
+        bulk_g2s(smem_u32(xring + s * XSTAGE), p.xq + static_cast<size_t>(mt.xg_off + wk.g) * XB,
+                 static_cast<uint32_t>(n) * XB, smem_u32(&sb->full[s]));
+        wk.advance(p, n);
         ++k;
       }
       // Never leave the CTA with copies in flight: wait (bounded, ignoring abort) for the last
@@ -285,255 +371,231 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
       for (int kk = (k > kStages ? k - kStages : 0); kk < k; ++kk)
         mbar_wait(smem_u32(&sb->full[kk % kStages]), (kk / kStages) & 1, p.err, kErrBitWaitDrain, &zero);
     }
-  } else if (warp == 1 || warp == 15) {
+  } else if (warp == 1 || warp == 2) {
     if (lane == 0) {
-      // ------------------------------ MMA issuers (stages alternate) ---------------------------
-      const int w = warp == 1 ? 0 : 1;
-      constexpr uint32_t idesc = idesc_bf16_f32(128, 16);
-      const uint64_t desc0 = smem_desc_sw128(smem_u32(xring));
-      uint32_t a_uses[kUPS] = {0, 0, 0, 0};
-      long long u = u0;
-      int i = 0;  // unit index within this CTA
-      bool live = true;
-      for (int k = 0; u < u1 && live; ++k) {
-        const int n = stage_units(p, u, u1);
-        if ((k & 1) == w) {
+      // ------------------------------ MMA issuers (lane = stage parity) ------------------------
+      const int L = warp - 1;
+      constexpr uint32_t idesc = idesc_s8_s32(128, DW);
+      UnitWalk wk;
+      wk.init(p, u0);
+      int ls = 0;  // stages of this lane so far
+      for (int k = 0; wk.u < u1; ++k) {
+        const int n = wk.stage_n(p.mats[wk.mi], u1);
+        if ((k & 1) == L) {
           const int s = k % kStages;
-          if (!mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag))
+          if (!mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag) ||
+              !mbar_wait(smem_u32(&sb->a_full[L]), ls & 1, p.err, kErrBitWaitAFull, abort_flag) ||
+              (ls > 0 && !mbar_wait(smem_u32(&sb->d_empty[L]), (ls - 1) & 1, p.err, kErrBitWaitDEmpty,
+                                    abort_flag)))
             break;
+          tc_fence_after();
           for (int j = 0; j < n; ++j) {
-            const int a = w * kUPS + j;
-            const int d = (i + j) % kNumD;
-            if (!mbar_wait(smem_u32(&sb->a_full[a]), a_uses[j] & 1, p.err, kErrBitWaitAFull, abort_flag) ||
-                (i + j >= kNumD &&
-                 !mbar_wait(smem_u32(&sb->d_empty[d]), (((i + j) / kNumD) - 1) & 1, p.err,
-                            kErrBitWaitDEmpty, abort_flag))) {
-              live = false;
-              break;
-            }
-            ++a_uses[j];
-            tc_fence_after();
-            // start-address field: stage base + j x-tile + 32 bytes per 16-column K slice
-            const uint64_t bdesc = desc0 + static_cast<uint64_t>((s * kXStageBytes + j * xtile) >> 4);
-            const uint32_t d_dot = tmem + kDCol0 + d * 32;
-            const uint32_t a_tmem = tmem + a * 32;
-            umma_f16_ts(d_dot, a_tmem, bdesc, idesc, 0u);                 // columns 0-15
-            umma_f16_ts(d_dot + 16, a_tmem + 16, bdesc + 4, idesc, 0u);   // columns 32-47
-            umma_f16_ts(d_dot, a_tmem + 8, bdesc + 2, idesc, 1u);         // columns 16-31
-            umma_f16_ts(d_dot + 16, a_tmem + 24, bdesc + 6, idesc, 1u);   // columns 48-63
-            umma_commit(smem_u32(&sb->a_empty[a]));
-            umma_commit(smem_u32(&sb->d_full[d]));
+            const uint32_t xb = smem_u32(xring + s * XSTAGE + j * XB);
+            const uint32_t a_tmem = tmem + (L * kUPS + j) * kACols;
+            const uint32_t d_tmem = tmem + kDCol0 + (L * kUPS + j) * DW;
+            umma_i8_ts(d_tmem, a_tmem, smem_desc_noswizzle(xb, 128, 256), idesc, 0u);               // k 0-31
+            umma_i8_ts(d_tmem, a_tmem + 8, smem_desc_noswizzle(xb + MP * 64, 128, 256), idesc, 1u);  // k 32-63
           }
-          if (!live) break;
+          umma_commit(smem_u32(&sb->d_full[L]));
+          umma_commit(smem_u32(&sb->a_empty[L]));
           umma_commit(smem_u32(&sb->empty[s]));
+          ++ls;
         }
-        u += n;
-        i += n;
+        wk.advance(p, n);
       }
       // Every MMA issued by this thread completes before TMEM is released.
-      umma_commit(smem_u32(&sb->mma_done[w]));
+      umma_commit(smem_u32(&sb->mma_done[L]));
       int zero = 0;
-      mbar_wait(smem_u32(&sb->mma_done[w]), 0, p.err, kErrBitWaitDrain, &zero);
+      mbar_wait(smem_u32(&sb->mma_done[L]), 0, p.err, kErrBitWaitDrain, &zero);
     }
-  } else if (warp == kXsumWarp) {
-    // ------------------------------ xsum of each x tile ------------------------------
-    // lane = (token t = lane / 2, half h = lane % 2); chunk sums are combined in the same tree
-    // for every token count, so a token's xsum is bit-identical for any M.
-    const int t = lane >> 1, h = lane & 1;
-    long long u = u0;
-    int i = 0;
-    bool live = true;
-    for (int k = 0; u < u1 && live; ++k) {
-      const int n = stage_units(p, u, u1);
+  } else if (warp >= 4 && warp < kEpiWarp0) {
+    // ------------------------------ dequant (one warpgroup, every stage) ----------------------
+    // Per stage: one wait for the lane's slots, then decode + tensor-memory store of every unit
+    // (the stores are asynchronous; the shared loads of unit j+1 are issued before unit j is
+    // decoded), then one wait for all stores and one arrival for the whole stage.
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    int lsn0 = 0, lsn1 = 0;  // stages of each lane so far
+    UnitWalk wk;
+    wk.init(p, u0);
+    for (int k = 0; wk.u < u1; ++k) {
+      const int n = wk.stage_n(p.mats[wk.mi], u1);
+      const int L = k & 1;
       const int s = k % kStages;
-      if (!mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag))
-        break;
-      float part[kUPS];
+      const int ls = L ? lsn1++ : lsn0++;
+      // Every wait result is made warp-uniform: a lane that left the loop alone would strand
+      // the others at __syncwarp or at a .sync.aligned tensor-memory store.
+      const bool ok =
+          mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag) &&
+          (ls == 0 ||
+           (mbar_wait(smem_u32(&sb->a_empty[L]), (ls - 1) & 1, p.err, kErrBitWaitAEmpty, abort_flag) &&
+            mbar_wait(smem_u32(&sb->d_empty[L]), (ls - 1) & 1, p.err, kErrBitWaitDEmpty, abort_flag)));
+      if (!__all_sync(0xFFFFFFFFu, ok)) break;
+      tc_fence_after();
+      const uint8_t* wst = wring + s * kWStageBytes;
+      const uint8_t* xst = xring + s * XSTAGE + 2 * MP * 64;
+      uint4 c0 = *reinterpret_cast<const uint4*>(wst + r * 16);
+      uint4 c1 = *reinterpret_cast<const uint4*>(wst + 2048 + r * 16);
+      uint32_t sbw = *reinterpret_cast<const uint32_t*>(wst + kUnitNibBytes + r * 4);
+      float xm = r < 2 * MP ? *reinterpret_cast<const float*>(xst + r * 4) : 0.f;
       for (int j = 0; j < n; ++j) {
-        // rows >= x_rows of a tile belong to the next tile (or are stale): their sums are unused
-        const uint8_t* row = xring + s * kXStageBytes + j * xtile + t * 128;
-        float cs[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int cch = 4 * h + q;  // 16-byte chunk = 8 columns; SWIZZLE_128B permutes chunks by row
-          const uint4 v = *reinterpret_cast<const uint4*>(row + ((cch ^ (t & 7)) << 4));
-          const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-          float acc = 0.f;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            acc += __uint_as_float(wv[kk] << 16);
-            acc += __uint_as_float(wv[kk] & 0xFFFF0000u);
-          }
-          cs[q] = acc;
+        const uint4 d0 = c0, d1 = c1;
+        QmmMeta& mm = sb->meta[L][j];
+        mm.sb[r] = sbw;
+        if (r < 2 * MP) mm.x[r < MP ? r : kMaxTokens + r - MP] = xm;
+        if (j + 1 < n) {
+          const uint8_t* wu = wst + (j + 1) * kUnitWBytes;
+          c0 = *reinterpret_cast<const uint4*>(wu + r * 16);
+          c1 = *reinterpret_cast<const uint4*>(wu + 2048 + r * 16);
+          sbw = *reinterpret_cast<const uint32_t*>(wu + kUnitNibBytes + r * 4);
+          if (r < 2 * MP) xm = *reinterpret_cast<const float*>(xst + (j + 1) * XB + r * 4);
         }
-        float pt = (cs[0] + cs[1]) + (cs[2] + cs[3]);
-        pt += __shfl_xor_sync(0xFFFFFFFFu, pt, 1);
-        part[j] = pt;
+        uint32_t a[16];
+        decode_i8(d0, d1, a);
+        tmem_st_x16(tmem + lane_off + (L * kUPS + j) * kACols, a);
       }
-      mbar_arrive(smem_u32(&sb->empty[s]));  // this warp is done with the stage's x tiles
-      for (int j = 0; j < n; ++j) {
-        const int jr = (i + j) % kRS;
-        if (i + j >= kRS && !mbar_wait(smem_u32(&sb->ep_empty[jr]), (((i + j) / kRS) - 1) & 1, p.err,
-                                       kErrBitWaitEmpty, abort_flag)) {
-          live = false;
-          break;
-        }
-        if (h == 0) sb->xsr[jr][t] = part[j];
-        __syncwarp();
-        mbar_arrive(smem_u32(&sb->xs_full[jr]));
-      }
-      u += n;
-      i += n;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sb->empty[s]));  // this warp's shared loads are done
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sb->a_full[L]));
+      wk.advance(p, n);
     }
-  } else if (warp >= 6 && warp < 14) {
-    // ------------------------------ dequant (two warpgroups, stages alternate) ----------------
-    const int w = (warp - 6) >> 2;
+  } else if (warp >= kEpiWarp0) {
+    // ------------------------------ epilogue: one warpgroup per lane --------------------------
+    // Warpgroup L accumulates the units of the stages of lane L.  At the end of each tile
+    // segment the two partial sums are added in a fixed order (lane 0's + lane 1's) by the
+    // warpgroup that holds the segment's last stage, which then writes or publishes the tile.
+    const int L = (warp - kEpiWarp0) >> 2;
+    const int e = threadIdx.x - kEpiWarp0 * 32 - L * kEpiThreads;
     const int r = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    uint32_t a_uses[kUPS] = {0, 0, 0, 0};
-    long long u = u0;
-    int i = 0;
-    bool live = true;
-    for (int k = 0; u < u1 && live; ++k) {
-      const int n = stage_units(p, u, u1);
-      if ((k & 1) == w) {
-        const int s = k % kStages;
-        if (!mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag))
-          break;
-        for (int j = 0; j < n; ++j) {
-          const uint8_t* wu = wring + s * kWStageBytes + j * kUnitWBytes;
-          const uint4 lo = *reinterpret_cast<const uint4*>(wu + r * 16);
-          const uint4 hi = *reinterpret_cast<const uint4*>(wu + 2048 + r * 16);
-          const uint32_t sbw = *reinterpret_cast<const uint32_t*>(wu + kUnitNibBytes + r * 4);
-          if (j == n - 1) mbar_arrive(smem_u32(&sb->empty[s]));  // done reading the weight stage
-          const int jr = (i + j) % kRS;
-          if (i + j >= kRS && !mbar_wait(smem_u32(&sb->ep_empty[jr]), (((i + j) / kRS) - 1) & 1,
-                                         p.err, kErrBitWaitEmpty, abort_flag)) {
-            live = false;
-            break;
-          }
-          sb->sbr[jr][r] = sbw;
-          mbar_arrive(smem_u32(&sb->sb_full[jr]));
-          uint32_t q[32];
-          decode8(lo, hi, q);
-          const int a = w * kUPS + j;
-          if (a_uses[j] > 0 &&
-              !mbar_wait(smem_u32(&sb->a_empty[a]), (a_uses[j] - 1) & 1, p.err, kErrBitWaitAEmpty,
-                         abort_flag)) {
-            live = false;
-            break;
-          }
-          ++a_uses[j];
-          tc_fence_after();
-          tmem_st_x32(tmem + lane_off + a * 32, q);
-          tc_wait_st();
-          tc_fence_before();
-          mbar_arrive(smem_u32(&sb->a_full[a]));
-        }
-      }
-      u += n;
-      i += n;
-    }
-  } else {
-    // ------------------------------ epilogue (warps 2..5), units in order ----------------------
-    const int e = threadIdx.x - 64;
-    const int r = (warp & 3) * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    float* xchg = reinterpret_cast<float*>(sb + 1);  // [2][NT][128] partial-sum exchange
     float acc[NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t] = 0.f;
     bool dep_waited = false;
-
-    for (int i = 0; i < L; ++i) {
-      const int d = i % kNumD;
-      const int jr = i % kRS;
-      const uint32_t ph = (i / kRS) & 1;
-      const bool ok = mbar_wait(smem_u32(&sb->xs_full[jr]), ph, p.err, kErrBitWaitFull, abort_flag) &&
-                      mbar_wait(smem_u32(&sb->sb_full[jr]), ph, p.err, kErrBitWaitFull, abort_flag) &&
-                      mbar_wait(smem_u32(&sb->d_full[d]), (i / kNumD) & 1, p.err, kErrBitWaitDFull,
-                                abort_flag);
-      if (ok) {
-        const uint32_t sbw = sb->sbr[jr][r];
-        const float sc = __uint_as_float(sbw << 16);
-        const float bi = __uint_as_float(sbw & 0xFFFF0000u);
-        const float bo = fmaf(-128.0f, sc, bi);  // bias with the +128 operand offset folded in
-        // acc += (b - 128 s) * xsum, then acc += s * dot  (same order for every NT)
+    int ls = 0;   // stages of this lane so far
+    int seg = 0;  // tile segments finished by this CTA
+    UnitWalk wk;
+    wk.init(p, u0);
+    for (int k = 0; wk.u < u1; ++k) {
+      const QmmMat& mt = p.mats[wk.mi];
+      const int n = wk.stage_n(mt, u1);
+      if ((k & 1) == L) {
+        // a_full: the meta slots this stage reads were written (and d_full: the MMAs are done)
+        const bool ok = __all_sync(
+            0xFFFFFFFFu,
+            mbar_wait(smem_u32(&sb->a_full[L]), ls & 1, p.err, kErrBitWaitAFull, abort_flag) &&
+                mbar_wait(smem_u32(&sb->d_full[L]), ls & 1, p.err, kErrBitWaitDFull, abort_flag));
+        ++ls;
+        if (ok) tc_fence_after();
+        for (int j = 0; j < n && ok; ++j) {
+          {
+            const QmmMeta& mm = sb->meta[L][j];
+            const uint32_t sbw = mm.sb[r];
+            float xs[NT], xsum[NT];
 #pragma unroll
-        for (int t = 0; t < NT; ++t) acc[t] = fmaf(bo, sb->xsr[jr][t], acc[t]);
-        mbar_arrive(smem_u32(&sb->ep_empty[jr]));
-        // dot = (columns 0-31 partial) + (columns 32-63 partial)
-        const uint32_t dbase = tmem + lane_off + kDCol0 + d * 32;
-        float s01[NT], v[NT];
-        tc_fence_after();
-        tmem_ld<NT>(dbase, s01);
-        tmem_ld<NT>(dbase + 16, v);
-        tc_wait_ld();
-        tc_fence_before();
-        mbar_arrive(smem_u32(&sb->d_empty[d]));
+            for (int t = 0; t < NT; ++t) {
+              xs[t] = mm.x[t];
+              xsum[t] = mm.x[kMaxTokens + t];
+            }
+            float dh[NT], dl[NT];
+            const uint32_t dbase = tmem + lane_off + kDCol0 + (L * kUPS + j) * DW;
+            tmem_ld<NT>(dbase, dh);
+            tmem_ld<NT>(dbase + MP, dl);
+            tc_wait_ld();
+            const float sc = __uint_as_float(sbw << 16);
+            const float bo = fmaf(8.0f, sc, __uint_as_float(sbw & 0xFFFF0000u));  // b + 8 s
 #pragma unroll
-        for (int t = 0; t < NT; ++t) acc[t] = fmaf(sc, s01[t] + v[t], acc[t]);
-      }
-      const long long u = u0 + i;
-      const QmmMat& mt = p.mats[mat_of(p, u)];
-      const long long lu = u - mt.unit_off;
-      const int g = static_cast<int>(lu % mt.G);
-      if (g != mt.G - 1 && i != L - 1) continue;
-      // ---- end of a tile segment: write the tile, or publish a partial and maybe finish it
-      const long long ltile = lu / mt.G;                     // tile within the matrix
-      const long long tile_u0 = mt.unit_off + ltile * mt.G;  // its first global unit
-      const long long tile = mt.tile_off + ltile;            // global tile (counter index)
-      const long long seg_start = (tile_u0 > u0) ? tile_u0 : u0;
-      const bool full_tile = (seg_start == tile_u0) && (g == mt.G - 1);
-      const bool first_seg = (seg_start == u0);
-      const int row_g = static_cast<int>(ltile) * kTileRows + r;
-      const bool live = !*abort_flag;
-      if (!dep_waited) {
-        pdl_wait_prior_grid();  // outputs may alias buffers the previous kernel still reads
-        dep_waited = true;
-      }
-      if (full_tile) {
-        if (live && row_g < mt.N) {
-#pragma unroll
-          for (int t = 0; t < NT; ++t)
-            if (t < p.M) mt.out[static_cast<size_t>(t) * mt.ldo + row_g] = __float2bfloat16_rn(acc[t]);
-        }
-      } else {
-        float* mine = p.part + (static_cast<size_t>(c) * 2 + (first_seg ? 0 : 1)) * kMaxTokens * kTileRows;
-#pragma unroll
-        for (int t = 0; t < NT; ++t) mine[t * kTileRows + r] = acc[t];
-        __threadfence();
-        named_bar_sync(1, kEpiThreads);
-        const long long cf = cta_of_unit(tile_u0, p.U, p.C);
-        const long long cl = cta_of_unit(tile_u0 + mt.G - 1, p.U, p.C);
-        if (e == 0) {
-          const unsigned n_contrib = static_cast<unsigned>(cl - cf + 1);
-          const unsigned old = live ? atomicAdd(&p.cnt[tile], 1u) : 0u;
-          sb->last_flag = live && (old == n_contrib - 1);
-        }
-        named_bar_sync(1, kEpiThreads);
-        if (sb->last_flag) {
-          __threadfence();
-          float v[NT];
-#pragma unroll
-          for (int t = 0; t < NT; ++t) v[t] = 0.f;
-          for (long long cc = cf; cc <= cl; ++cc) {
-            const long long cu0 = u_begin(cc, p.U, p.C);
-            const int cs = (cu0 >= tile_u0) ? 0 : 1;  // the tile is this contributor's first segment
-            const float* src = p.part + (static_cast<size_t>(cc) * 2 + cs) * kMaxTokens * kTileRows;
-#pragma unroll
-            for (int t = 0; t < NT; ++t) v[t] += __ldcg(src + t * kTileRows + r);
+            for (int t = 0; t < NT; ++t) {
+              const int G = __float_as_int(dh[t]) * 256 + __float_as_int(dl[t]);
+              acc[t] = fmaf(sc * xs[t], static_cast<float>(G), fmaf(bo, xsum[t], acc[t]));
+            }
           }
-          if (row_g < mt.N) {
-#pragma unroll
-            for (int t = 0; t < NT; ++t)
-              if (t < p.M) mt.out[static_cast<size_t>(t) * mt.ldo + row_g] = __float2bfloat16_rn(v[t]);
-          }
-          if (e == 0) p.cnt[tile] = 0u;
         }
-        named_bar_sync(1, kEpiThreads);
+        if (ok) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&sb->d_empty[L]));  // D and meta slots read
+        }
       }
+      const int g = wk.g + n - 1;  // group of the stage's last unit
+      if (g == mt.G - 1 || wk.u + n == u1) {
+        // ---- end of a tile segment: combine the lanes, then write the tile or publish a partial
+        const int own = k & 1;  // the warpgroup that holds the segment's last stage finishes it
+        float* xb = xchg + (seg & 1) * NT * kTileRows;
+        if (L != own) {
 #pragma unroll
-      for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+          for (int t = 0; t < NT; ++t) xb[t * kTileRows + r] = acc[t];
+        }
+        named_bar_sync(3, 2 * kEpiThreads);
+        if (L == own) {
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            const float o = xb[t * kTileRows + r];
+            acc[t] = L == 0 ? acc[t] + o : o + acc[t];
+          }
+          const int tile_u0 = mt.unit_off + wk.lt * mt.G;        // the tile's first global unit
+          const int tile = mt.tile_off + wk.lt;                  // global tile (counter index)
+          const int seg_start = (tile_u0 > u0) ? tile_u0 : u0;
+          const bool full_tile = (seg_start == tile_u0) && (g == mt.G - 1);
+          const bool first_seg = (seg_start == u0);
+          const int row_g = wk.lt * kTileRows + r;
+          const bool live = !*abort_flag;
+          if (!dep_waited) {
+            pdl_wait_prior_grid();  // outputs may alias buffers an earlier kernel still reads
+            dep_waited = true;
+          }
+          if (full_tile) {
+            if (live && row_g < mt.N) {
+#pragma unroll
+              for (int t = 0; t < NT; ++t)
+                if (t < p.M) mt.out[static_cast<size_t>(t) * mt.ldo + row_g] = __float2bfloat16_rn(acc[t]);
+            }
+          } else {
+            const int bar = 4 + L;
+            float* mine = p.part + (static_cast<size_t>(c) * 2 + (first_seg ? 0 : 1)) * kMaxTokens * kTileRows;
+#pragma unroll
+            for (int t = 0; t < NT; ++t) mine[t * kTileRows + r] = acc[t];
+            __threadfence();
+            named_bar_sync(bar, kEpiThreads);
+            const long long cf = cta_of_unit(tile_u0, p.U, p.C);
+            const long long cl = cta_of_unit(tile_u0 + mt.G - 1, p.U, p.C);
+            if (e == 0) {
+              const unsigned n_contrib = static_cast<unsigned>(cl - cf + 1);
+              const unsigned old = live ? atomicAdd(&p.cnt[tile], 1u) : 0u;
+              sb->last_flag[L] = live && (old == n_contrib - 1);
+            }
+            named_bar_sync(bar, kEpiThreads);
+            if (sb->last_flag[L]) {
+              __threadfence();
+              float v[NT];
+#pragma unroll
+              for (int t = 0; t < NT; ++t) v[t] = 0.f;
+              for (long long cc = cf; cc <= cl; ++cc) {
+                const long long cu0 = u_begin(cc, p.U, p.C);
+                const int cs = (cu0 >= tile_u0) ? 0 : 1;  // the tile is this contributor's first segment
+                const float* src = p.part + (static_cast<size_t>(cc) * 2 + cs) * kMaxTokens * kTileRows;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) v[t] += __ldcg(src + t * kTileRows + r);
+              }
+              if (row_g < mt.N) {
+#pragma unroll
+                for (int t = 0; t < NT; ++t)
+                  if (t < p.M) mt.out[static_cast<size_t>(t) * mt.ldo + row_g] = __float2bfloat16_rn(v[t]);
+              }
+              if (e == 0) p.cnt[tile] = 0u;
+            }
+            named_bar_sync(bar, kEpiThreads);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+        ++seg;
+      }
+      wk.advance(p, n);
     }
   }
 
@@ -569,10 +631,10 @@ __global__ void qmm_repack_kernel(const uint32_t* __restrict__ w, const uint16_t
       uint32_t o = 0;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const uint32_t nib = (v >> (4 * i)) & 0xFu;
-        // even columns go to the low half-word, odd ones to the high half-word
-        const int slot = (i & 1) ? (4 + (i >> 1)) : (i >> 1);
-        o |= nib << (4 * slot);
+        const uint32_t nib = ((v >> (4 * i)) & 0xFu) ^ 0x8u;
+        // columns 0-3 -> high nibbles of bytes 0-3, columns 4-7 -> low nibbles
+        const int shift = i < 4 ? 8 * i + 4 : 8 * (i - 4);
+        o |= nib << shift;
       }
       outw[jj] = o;
     }
@@ -587,7 +649,7 @@ __global__ void qmm_repack_kernel(const uint32_t* __restrict__ w, const uint16_t
 }
 
 // Plain CUDA-core cross-check of the relaid format: decodes the same units and computes
-// sum_g s * sum(x q) + b * sum(x) in f32.  One thread per (row, token); tests only.
+// sum_g s * sum(x q) + b * sum(x) in f32 from x as given.  One thread per (row, token); tests only.
 __global__ void qmm_simt_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                                 const uint8_t* __restrict__ w_tc, __nv_bfloat16* __restrict__ out,
                                 int ldo, int M, int N, int K) {
@@ -603,21 +665,16 @@ __global__ void qmm_simt_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
     const uint32_t sbw = *reinterpret_cast<const uint32_t*>(base + kUnitNibBytes + r * 4);
     const float sc = __uint_as_float(sbw << 16);
     const float bi = __uint_as_float(sbw & 0xFFFF0000u);
-    const uint4 lo = *reinterpret_cast<const uint4*>(base + r * 16);
-    const uint4 hi = *reinterpret_cast<const uint4*>(base + 2048 + r * 16);
-    uint32_t q[32];
-    decode8(lo, hi, q);
+    const uint4 c0 = *reinterpret_cast<const uint4*>(base + r * 16);
+    const uint4 c1 = *reinterpret_cast<const uint4*>(base + 2048 + r * 16);
+    uint32_t a[16];
+    decode_i8(c0, c1, a);
     float gs = 0.f, xsum = 0.f;
-    for (int pidx = 0; pidx < 32; ++pidx) {
-      const int k = g * kGroup + pidx * 2;
-      const float x0 = __bfloat162float(x[static_cast<size_t>(tok) * ldx + k]);
-      const float x1 = __bfloat162float(x[static_cast<size_t>(tok) * ldx + k + 1]);
-      const float q0 = static_cast<float>(q[pidx] & 0xFu);
-      const float q1 = static_cast<float>((q[pidx] >> 16) & 0xFu);
-      gs = fmaf(q0, x0, gs);
-      gs = fmaf(q1, x1, gs);
-      xsum += x0;
-      xsum += x1;
+    for (int col = 0; col < kGroup; ++col) {
+      const int q = (static_cast<int>(static_cast<int8_t>(a[col >> 2] >> (8 * (col & 3)))) >> 4) + 8;
+      const float xv = __bfloat162float(x[static_cast<size_t>(tok) * ldx + g * kGroup + col]);
+      gs = fmaf(static_cast<float>(q), xv, gs);
+      xsum += xv;
     }
     acc = fmaf(sc, gs, fmaf(bi, xsum, acc));
   }
@@ -629,7 +686,6 @@ __global__ void qmm_simt_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
 // ---------------------------------------------------------------------------------------------
 static int g_num_sms[64] = {0};
 static bool g_attr_set[64][4] = {};
-static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int device_sm_count(int dev) {
   if (dev < 0 || dev >= 64) return 148;
@@ -642,115 +698,109 @@ int device_sm_count(int dev) {
   return g_num_sms[dev];
 }
 
-static cudaError_t get_encoder() {
-  if (g_encode) return cudaSuccess;
-  void* fn = nullptr;
-  cudaDriverEntryPointQueryResult q;
-  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-  if (e != cudaSuccess) return e;
-  if (q != cudaDriverEntryPointSuccess || fn == nullptr) return cudaErrorNotSupported;
-  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  return cudaSuccess;
-}
-
-// x [M rows, K columns] bf16, row stride ldx elements; box 64 columns x `rows` rows, 128B swizzle.
-// (A 3-D view {64, rows, groups} would need a group stride below the row stride, which tensor maps
-// do not support: each stride must include the previous dimension's.)
-static cudaError_t encode_x_map(CUtensorMap* map, const void* x, int M, int K, int ldx, int rows) {
-  cudaError_t e = get_encoder();
-  if (e != cudaSuccess) return e;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldx) * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kGroup), static_cast<cuuint32_t>(rows)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides,
-                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+static void pdl_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, bool pdl) {
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
 }
 
 template <int NT>
-static cudaError_t launch_tc(const QmmParams& prm, const XMaps& maps, int dev, cudaStream_t stream,
-                             bool pdl) {
+static cudaError_t launch_tc(const QmmParams& prm, int dev, cudaStream_t stream, bool pdl) {
   constexpr int slot = NT == 2 ? 0 : NT == 4 ? 1 : NT == 8 ? 2 : 3;
+  constexpr size_t smem = qmm_smem_bytes(NT);
   if (dev >= 0 && dev < 64 && !g_attr_set[dev][slot]) {
     cudaError_t e = cudaFuncSetAttribute(qmm_w4g64_tc_kernel<NT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kQmmSmemBytes));
+                                         static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     g_attr_set[dev][slot] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(prm.C);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kQmmSmemBytes;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, qmm_w4g64_tc_kernel<NT>, prm, maps);
+  pdl_config(cfg, attr, pdl);
+  return cudaLaunchKernelEx(&cfg, qmm_w4g64_tc_kernel<NT>, prm);
 }
 
-// Grouped launch over n matrices sharing the token count M.  Shapes and pointers were validated
-// by the caller; distinct (x, K, ldx) inputs share tensor maps (at most kMaxX of them).  The
-// scratch is given as its three parts: error word, per-tile counters (zero on entry, left zero)
-// and partial sums for up to `C_cap` CTAs.
+static cudaError_t launch_xprep(const XPrepParams& xp, cudaStream_t stream, bool pdl) {
+  const long long warps = static_cast<long long>(xp.total_groups) * xp.mpad;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((warps + 7) / 8));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  pdl_config(cfg, attr, pdl);
+  return cudaLaunchKernelEx(&cfg, qmm_xprep_kernel, xp);
+}
+
+// Grouped launch over n matrices sharing the token count M: an x-prep launch over the distinct
+// (x, K, ldx) inputs (at most kMaxX, sum of K/64 at most xq_groups), then the qmm launch.
+// Shapes and pointers were validated by the caller.  The scratch is given as its parts: error
+// word, per-tile counters (zero on entry, left zero), partial sums for up to `C_cap` CTAs and
+// the x-prep blocks.  `pdl` applies to the x-prep launch (towards the caller's previous work);
+// the qmm launch always overlaps the x-prep launch.
 static cudaError_t launch_grouped_on(int n, const void* const* x, const int* ldx,
                                      const void* const* w_tc, void* const* out, const int* ldo,
                                      const int* N, const int* K, int M, uint32_t* err,
-                                     uint32_t* cnt, float* part, int C_cap, int dev,
-                                     cudaStream_t stream, bool pdl) {
+                                     uint32_t* cnt, float* part, uint8_t* xq, int xq_groups,
+                                     int C_cap, int dev, cudaStream_t stream, bool pdl) {
   if (n < 1 || n > kMaxMats) return cudaErrorInvalidValue;
-  const int C_dev = C_cap;
-  static thread_local QmmParams prm;  // ~10 KB: keep it off the stack
-  static thread_local XMaps maps;
+  static thread_local QmmParams prm;  // ~9 KB: keep it off the stack
+  static thread_local XPrepParams xp;
+  const int mpad = M <= 8 ? 8 : 16;
   prm.part = part;
   prm.cnt = cnt;
   prm.err = err;
+  prm.xq = xq;
   prm.M = M;
-  prm.x_rows = M <= 8 ? 8 : 16;
   prm.n_mats = n;
-  const void* xkey[kMaxX];
-  int kkey[kMaxX], lkey[kMaxX];
-  int nx = 0;
+  xp.xq = xq;
+  xp.M = M;
+  xp.mpad = mpad;
+  int nx = 0, groups = 0;
   long long U = 0;
   long long T = 0;
   for (int i = 0; i < n; ++i) {
     const QmmShape sh = qmm_shape(N[i], K[i]);
     int xi = -1;
     for (int q = 0; q < nx; ++q)
-      if (xkey[q] == x[i] && kkey[q] == K[i] && lkey[q] == ldx[i]) xi = q;
+      if (xp.in[q].x == x[i] && xp.in[q].G == sh.G && xp.in[q].ldx == ldx[i]) xi = q;
     if (xi < 0) {
-      if (nx == kMaxX) return cudaErrorInvalidValue;
+      if (nx == kMaxX || groups + sh.G > xq_groups) return cudaErrorInvalidValue;
       xi = nx++;
-      xkey[xi] = x[i];
-      kkey[xi] = K[i];
-      lkey[xi] = ldx[i];
-      cudaError_t e = encode_x_map(&maps.m[xi], x[i], M, K[i], ldx[i], prm.x_rows);
-      if (e != cudaSuccess) return e;
+      xp.in[xi].x = static_cast<const __nv_bfloat16*>(x[i]);
+      xp.in[xi].ldx = ldx[i];
+      xp.in[xi].G = sh.G;
+      xp.in[xi].xg_off = groups;
+      groups += sh.G;
     }
     QmmMat& mt = prm.mats[i];
     mt.w_tc = static_cast<const uint8_t*>(w_tc[i]);
     mt.out = static_cast<__nv_bfloat16*>(out[i]);
-    mt.unit_off = U;
+    mt.unit_off = static_cast<int>(U);
     mt.N = N[i];
     mt.G = sh.G;
     mt.tile_off = static_cast<int>(T);
-    mt.xi = xi;
+    mt.xg_off = xp.in[xi].xg_off;
     mt.ldo = ldo[i];
     U += sh.U;
     T += sh.T;
   }
   if (T > kMaxTiles) return cudaErrorInvalidValue;
-  for (int q = nx; q < kMaxX; ++q) maps.m[q] = maps.m[0];
-  prm.U = U;
-  prm.C = static_cast<int>(U < C_dev ? U : C_dev);
-  if (M <= 2) return launch_tc<2>(prm, maps, dev, stream, pdl);
-  if (M <= 4) return launch_tc<4>(prm, maps, dev, stream, pdl);
-  if (M <= 8) return launch_tc<8>(prm, maps, dev, stream, pdl);
-  return launch_tc<16>(prm, maps, dev, stream, pdl);
+  xp.n_in = nx;
+  xp.total_groups = groups;
+  prm.U = static_cast<int>(U);
+  prm.C = static_cast<int>(U < C_cap ? U : C_cap);
+  cudaError_t e = launch_xprep(xp, stream, pdl);
+  if (e != cudaSuccess) return e;
+  if (M <= 2) return launch_tc<2>(prm, dev, stream, true);
+  if (M <= 4) return launch_tc<4>(prm, dev, stream, true);
+  if (M <= 8) return launch_tc<8>(prm, dev, stream, true);
+  return launch_tc<16>(prm, dev, stream, true);
 }
 
 cudaError_t qmm_tc_launch_grouped(int n, const void* const* x, const int* ldx, const void* const* w_tc,
@@ -759,11 +809,12 @@ cudaError_t qmm_tc_launch_grouped(int n, const void* const* x, const int* ldx, c
   int dev = 0;
   cudaGetDevice(&dev);
   const int C_dev = device_sm_count(dev);
-  const WsLayout wl = ws_layout(0, 0, C_dev);
+  const WsLayout wl = ws_layout(C_dev);
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   return launch_grouped_on(n, x, ldx, w_tc, out, ldo, N, K, M, reinterpret_cast<uint32_t*>(wsb),
                            reinterpret_cast<uint32_t*>(wsb + wl.cnt_off),
-                           reinterpret_cast<float*>(wsb + wl.part_off), C_dev, dev, stream, pdl);
+                           reinterpret_cast<float*>(wsb + wl.part_off), wsb + wl.xq_off, kMaxXGroups,
+                           C_dev, dev, stream, pdl);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -778,23 +829,26 @@ cudaError_t qmm_tc_launch_grouped(int n, const void* const* x, const int* ldx, c
 // with cudaGetSymbolAddress; nothing is allocated by this path, by the CUDA runtime on its behalf,
 // or by any library.
 //
-// Limits: N <= kNoAllocMaxTiles * 128 rows (tail tiles count whole) and at most kNoAllocMaxCtas
-// CTAs (a device with more SMs uses kNoAllocMaxCtas of them).  There is ONE scratch per device,
-// so two calls that may run at the same time on one device (different streams, threads without
-// ordering) race on it and corrupt each other's results; calls must be ordered, e.g. on a single
-// stream.  The first call on a device does the set-up (symbol lookup, kernel attributes, tensor-
-// map encoder lookup) and should come before any stream capture.
+// Limits: N <= kNoAllocMaxTiles * 128 rows (tail tiles count whole), K <= kNoAllocMaxGroups * 64
+// columns, and at most kNoAllocMaxCtas CTAs (a device with more SMs uses kNoAllocMaxCtas of
+// them).  There is ONE scratch per device, so two calls that may run at the same time on one
+// device (different streams, threads without ordering) race on it and corrupt each other's
+// results; calls must be ordered, e.g. on a single stream.  The first call on a device does the
+// set-up (symbol lookup, kernel attributes) and should come before any stream capture.
 // ---------------------------------------------------------------------------------------------
-constexpr int kNoAllocMaxTiles = 2048;  // N <= 262,144 rows
+constexpr int kNoAllocMaxTiles = 2048;   // N <= 262,144 rows
+constexpr int kNoAllocMaxGroups = 512;   // K <= 32,768 columns
 constexpr int kNoAllocMaxCtas = 160;
 constexpr size_t kNoAllocCntOff = 256;
 constexpr size_t kNoAllocPartOff = kNoAllocCntOff + static_cast<size_t>(kNoAllocMaxTiles) * 4;
-constexpr size_t kNoAllocScratchBytes =
+constexpr size_t kNoAllocXqOff =
     kNoAllocPartOff + static_cast<size_t>(kNoAllocMaxCtas) * 2 * kMaxTokens * kTileRows * 4;
-static_assert(kNoAllocScratchBytes == 2629888, "2.5 MiB of static scratch per device");
-static_assert(kNoAllocPartOff % 256 == 0, "partials start on a 256-byte boundary");
+constexpr size_t kNoAllocScratchBytes =
+    kNoAllocXqOff + static_cast<size_t>(kNoAllocMaxGroups) * xq_block_bytes(16);
+static_assert(kNoAllocScratchBytes == 3744000, "3.6 MiB of static scratch per device");
+static_assert(kNoAllocPartOff % 256 == 0 && kNoAllocXqOff % 256 == 0, "256-byte aligned regions");
 
-// [0, 256) error word + padding | [256, 8448) tile counters | [8448, ...) partial sums
+// [0, 256) error word + padding | [256, 8448) tile counters | partial sums | x-prep blocks
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 static std::mutex g_noalloc_mutex;
@@ -816,13 +870,14 @@ static cudaError_t noalloc_scratch(int dev, uint8_t** out) {
 }
 
 bool qmm_noalloc_fits(int N, int K) {
-  return qmm_shape(N, K).T <= kNoAllocMaxTiles;
+  const QmmShape sh = qmm_shape(N, K);
+  return sh.T <= kNoAllocMaxTiles && sh.G <= kNoAllocMaxGroups;
 }
 
 // The error word and the counters must be zero when the kernel starts.  A launch that completes
 // leaves the counters at zero, but one that stopped on a timed-out wait may not, so both are
-// cleared on the stream before every launch (a memset node: no allocation).  The launch does not
-// use programmatic dependent launch, so it cannot start before that clear has finished.
+// cleared on the stream before every call (a memset node: no allocation).  The x-prep launch
+// does not use programmatic dependent launch, so neither kernel can start before that clear.
 cudaError_t qmm_tc_launch_noalloc(const void* x, int ldx, const void* w_tc, void* out, int ldo,
                                   int M, int N, int K, cudaStream_t stream) {
   int dev = 0;
@@ -839,8 +894,8 @@ cudaError_t qmm_tc_launch_noalloc(const void* x, int ldx, const void* w_tc, void
   return launch_grouped_on(1, &x, &ldx, &w_tc, &o, &ldo, &N, &K, M,
                            reinterpret_cast<uint32_t*>(scratch),
                            reinterpret_cast<uint32_t*>(scratch + kNoAllocCntOff),
-                           reinterpret_cast<float*>(scratch + kNoAllocPartOff), C_cap, dev, stream,
-                           false);
+                           reinterpret_cast<float*>(scratch + kNoAllocPartOff),
+                           scratch + kNoAllocXqOff, kNoAllocMaxGroups, C_cap, dev, stream, false);
 }
 
 cudaError_t qmm_tc_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M, int N,

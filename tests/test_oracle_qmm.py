@@ -90,7 +90,8 @@ def test_config_for_fixture_is_reference_table():
 
 
 def test_unit_relayout_is_a_permutation():
-    """The B200 unit order holds the same nibbles, scales and biases (padding rows zero)."""
+    """The B200 unit order holds the same nibbles (as int8 16 * (q - 8)), scales and biases;
+    padding rows are zero."""
     rng = np.random.default_rng(5)
     n, k = 200, 192
     w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
@@ -99,21 +100,49 @@ def test_unit_relayout_is_a_permutation():
     t, g = 2, 3
     assert tc.size == t * g * quant.UNIT_BYTES
     units = tc.reshape(t, g, quant.UNIT_BYTES)
-    # decode one row back: tile 1, row 7 -> global row 135, group 2
+    q = quant.unpack(packed).astype(np.int32)
+    for tile in range(t):
+        for grp in range(g):
+            a = quant.unit_int8(units[tile, grp]).astype(np.int32)
+            rows = min(128, n - 128 * tile)
+            assert np.array_equal(a[:rows], 16 * (q[128 * tile: 128 * tile + rows, 64 * grp: 64 * grp + 64] - 8))
+            assert not a[rows:].any()
     row, tile, grp = 7, 1, 2
-    words = np.concatenate([units[tile, grp, c * 2048 + row * 16: c * 2048 + row * 16 + 16].view(np.uint32)
-                            for c in range(2)])
-    slot = [0, 4, 1, 5, 2, 6, 3, 7]
-    cols = [(wd >> np.uint32(4 * slot[i])) & 0xF for wd in words for i in range(8)]
-    assert np.array_equal(np.array(cols, np.uint8), quant.unpack(packed)[128 + row, 64 * grp: 64 * grp + 64])
     sbw = units[tile, grp, 4096 + 4 * row: 4096 + 4 * row + 4].view(np.uint32)[0]
     assert sbw & 0xFFFF == s[128 + row, grp] and sbw >> 16 == b[128 + row, grp]
-    # padding rows (200..255) are zero
-    assert not units[1, :, :].reshape(g, -1)[:, 0:0].any()
-    pad_rows = [r for r in range(72, 128)]
-    for c in range(2):
-        blk = units[1, 0, c * 2048:(c + 1) * 2048].reshape(128, 16)
-        assert not blk[pad_rows].any()
+
+
+def test_kernel_arithmetic_matches_mlx_semantics():
+    rng = np.random.default_rng(8)
+    w = (rng.standard_normal((96, 256)) * 0.02).astype(np.float32)
+    packed, s, b = quant.quantize(w)
+    x = quant.round_bf16(rng.standard_normal((6, 256)).astype(np.float32))
+    ref = quant.qmm_ref(x, packed, s, b)
+    got = quant.qmm_kernel_arith(x, packed, s, b)
+    assert np.allclose(got, quant.qmm_xq(x, packed, s, b), rtol=1e-9, atol=1e-12)
+    assert quant.rel_err(ref, got) < 1e-3
+
+
+@pytest.mark.parametrize("mpad", [8, 16])
+def test_xq_blocks_layout(mpad):
+    """Reading the digits back through the documented offsets gives v = 256 hi + lo."""
+    rng = np.random.default_rng(9)
+    m = 5 if mpad == 8 else 13
+    x = quant.round_bf16(rng.standard_normal((m, 192)).astype(np.float32))
+    x[1, 64:128] = 0
+    blk = quant.xq_blocks(x, mpad)
+    assert blk.shape == (3, quant.xq_block_bytes(mpad))
+    e, v, hi, lo, xsum = quant.xq_digits(x)
+    for grp in range(3):
+        for r in (0, m - 1, mpad, mpad + m - 1):
+            for kk in (0, 17, 31, 32, 63):
+                off = (kk >> 5) * (mpad * 64) + (r >> 3) * 256 + ((kk >> 4) & 1) * 128 + (r & 7) * 16 + (kk & 15)
+                d = blk[grp, off].astype(np.int8)
+                want = hi[r, grp, kk] if r < mpad else lo[r - mpad, grp, kk]
+                assert d == want
+    xs = blk[:, 2 * mpad * 64: 2 * mpad * 64 + 4 * mpad].view(np.float32)
+    assert xs[1, 1] == 0 and xs[0, m:].max() == 0
+    assert xs[0, 0] == np.float32(2.0 ** (e[0, 0] - 4))
 
 
 @pytest.mark.parametrize("U,C", [(10, 3), (7, 3), (3040, 148), (47480, 148), (5, 5), (641, 148), (8, 1)])
