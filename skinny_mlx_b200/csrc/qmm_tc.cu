@@ -30,22 +30,24 @@
 // the stream well below HBM bandwidth (measured on B200: 4.6 KB copies ~2.6 TB/s per CTA-per-SM,
 // 18 KB copies ~6.6 TB/s).  A stage therefore carries up to 4 consecutive units of one tile: one
 // bulk copy of their weights and one of their x-prep blocks (consecutive groups are adjacent).
-// Stages alternate between two "lanes", each with its own MMA issuer, tensor-memory slots and
-// epilogue warpgroup, so the MMAs and the epilogue of one stage overlap those of the other.
+// Stages alternate between two "lanes", each with its own dequant warpgroup, MMA issuer,
+// tensor-memory slots and epilogue warpgroup, so every step of one stage overlaps the same step
+// of the other.  The hand-offs between the roles are per stage, not per unit: one mbarrier phase
+// per lane and stage.
 //
-// Warp roles in a CTA of 512 threads (16 warps):
-//   warp 0 lane 0   TMA producer over a 4-stage ring.  The first stages are issued before
+// Warp roles in a CTA of 640 threads (20 warps), one CTA per SM:
+//   warp 0 lane 0   TMA producer over an 8-stage ring (6 for M > 8).  The first stages are issued before
 //                   griddepcontrol.wait only for their weights (weights do not depend on the
 //                   previous kernel), so under programmatic dependent launch this launch's weight
 //                   stream overlaps the tail of the previous one.  Tensor memory is allocated
 //                   after that, since the previous kernel's CTA on this SM may still hold it.
-//   warps 1, 2      MMA issuers of lane 0 / lane 1 (warp 1 also allocates TMEM): per unit two
-//                   chained tcgen05.mma 128 x (2 mpad) x 32 into the unit's D slot.
-//   warps 4..7      dequant warpgroup, every stage: thread = weight row; 64 nibbles (two 16-byte
-//                   shared loads) -> 16 int8x4 words -> tcgen05.st into the unit's A slot; also
-//                   copies the unit's scale/bias and x scales to a small ring read by the
-//                   epilogue, so a load stage is released early.
-//   warps 8..11     epilogue warpgroup of lane 0, warps 12..15 of lane 1: thread = weight row =
+//   warps 1, 2      MMA issuers of lane 0 / lane 1 (warp 1 also allocates TMEM): per stage two
+//                   chained tcgen05.mma 128 x (2 mpad) x 32 per unit into the unit's D slot.
+//   warps 4..7      dequant warpgroup of lane 0, warps 8..11 of lane 1: thread = weight row;
+//                   per unit 64 nibbles (two 16-byte shared loads) -> 16 int8x4 words ->
+//                   tcgen05.st into the unit's A slot; also copies the units' scale/bias and x
+//                   scales to a small ring read by the epilogue, so a load stage is released early.
+//   warps 12..15    epilogue warpgroup of lane 0, warps 16..19 of lane 1: thread = weight row =
 //                   TMEM lane; combines the digit dot products, applies scale/bias once per group
 //                   and accumulates in f32 registers; at each tile end the two lanes' sums are
 //                   added in a fixed order and the tile is written or its partial published.
@@ -64,15 +66,26 @@
 
 namespace skinny {
 
-constexpr int kStages = 4;                         // even: stage slot s is always used by lane s % 2
+// Load stages in flight: as many as shared memory holds (one CTA per SM), since the stream is
+// bounded by (load latency + processing) / stages.  Even, so stage slot s is always used by lane
+// s % 2 (a role then only ever waits on slots its own lane used before).
+__host__ __device__ constexpr int stages_for(int NT) { return NT <= 8 ? 8 : 6; }
+constexpr int kMaxStages = 8;
 constexpr int kUPS = 4;                            // units per stage (same tile)
 constexpr int kWStageBytes = kUPS * kUnitWBytes;   // 18 KB
-constexpr int kWRingBytes = kStages * kWStageBytes;
-constexpr int kThreads = 512;
-constexpr int kEpiWarp0 = 8;                       // warps 8..11 lane 0, 12..15 lane 1
+constexpr int kThreads = 640;
+constexpr int kDeqWarp0 = 4;                       // warps 4..7 lane 0, 8..11 lane 1
+constexpr int kEpiWarp0 = 12;                      // warps 12..15 lane 0, 16..19 lane 1
 constexpr int kEpiThreads = 128;
 constexpr int kACols = 16;                         // TMEM columns of one unit's int8 A operand
-constexpr int kDCol0 = 2 * kUPS * kACols;          // 128: D slots follow the 8 A slots
+// Slot sets: stage k uses set q = k % sets (A slots in TMEM, D slots in TMEM, meta slots in
+// shared memory for its units) and lane k % 2 (dequant warpgroup, MMA issuer, epilogue
+// warpgroup).  sets is even, so a set always belongs to the same lane, and with 4 sets a lane
+// starts decoding its next stage while the epilogue still reads its previous one.  Tensor memory
+// bounds it: 4 sets x 4 units x (16 A + 16 D columns) = 512 for M <= 8; M > 8 needs 32 D columns
+// per unit and keeps 2 sets.
+__host__ __device__ constexpr int sets_for(int NT) { return NT <= 8 ? 4 : 2; }
+constexpr int kMaxSets = 4;
 
 // Grouped launch: one persistent grid streams the concatenated units of up to kMaxMats
 // independent matrices (same token count), so launch overhead, pipeline fill and the stream-K
@@ -120,14 +133,14 @@ struct __align__(16) QmmMeta {
 };
 
 struct __align__(16) QmmSmem {
-  QmmMeta meta[2][kUPS];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  QmmMeta meta[kMaxSets][kUPS];
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
   // Per lane, one phase per stage of that lane ("lane-stage"):
-  uint64_t a_full[2];   // dequant -> MMA/epilogue: A slots stored, meta slots written
-  uint64_t a_empty[2];  // MMA -> dequant: the stage's MMAs completed (A slots free)
-  uint64_t d_full[2];   // MMA -> epilogue: accumulators ready
-  uint64_t d_empty[2];  // epilogue -> MMA/dequant: D and meta slots read
+  // Per slot set, one phase per use (one stage):
+  uint64_t a_full[kMaxSets];  // dequant -> MMA/epilogue: A slots stored, meta slots written
+  uint64_t d_full[kMaxSets];  // MMA -> epilogue: accumulators ready
+  uint64_t free[kMaxSets];    // MMA commit + epilogue -> dequant/MMA: the set's slots free
   uint64_t mma_done[2];
   uint32_t tmem_base;
   int abort_flag;
@@ -138,11 +151,15 @@ struct __align__(16) QmmSmem {
 __host__ __device__ constexpr int mpad_of(int NT) { return NT <= 8 ? 8 : 16; }
 __host__ __device__ constexpr int xstage_bytes(int NT) { return kUPS * xq_block_bytes(mpad_of(NT)); }
 __host__ __device__ constexpr size_t qmm_smem_bytes(int NT) {
-  return static_cast<size_t>(kStages) * xstage_bytes(NT) + kWRingBytes + sizeof(QmmSmem) +
+  return static_cast<size_t>(stages_for(NT)) * (xstage_bytes(NT) + kWStageBytes) + sizeof(QmmSmem) +
          static_cast<size_t>(2) * NT * kTileRows * 4 + 128;
 }
-static_assert(qmm_smem_bytes(8) * 2 <= 227 * 1024, "two CTAs per SM for M <= 8");
-static_assert(qmm_smem_bytes(16) <= 227 * 1024, "one CTA per SM for M <= 16");
+// One CTA per SM: the register budget (up to 128 per thread) keeps each warp's working set of
+// a whole stage in registers, which matters more than co-residency with the next launch.
+static_assert(qmm_smem_bytes(8) <= 227 * 1024 && qmm_smem_bytes(16) <= 227 * 1024,
+              "shared memory of one CTA");
+static_assert(stages_for(8) % 2 == 0 && stages_for(16) % 2 == 0 && stages_for(16) <= kMaxStages,
+              "stage ring");
 
 // Walks a CTA's unit range in stages, tracking the matrix, the tile within it and the group
 // within the tile incrementally (no division per unit).  A stage never crosses a tile end.
@@ -266,19 +283,23 @@ __global__ void __launch_bounds__(256) qmm_xprep_kernel(const __grid_constant__ 
 // The qmm kernel.  NT: token columns read back per unit (2, 4, 8 or 16).
 // ---------------------------------------------------------------------------------------------
 template <int NT>
-__global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
+__global__ void __launch_bounds__(kThreads, 1)
     qmm_w4g64_tc_kernel(const __grid_constant__ QmmParams p) {
   constexpr int MP = mpad_of(NT);
   constexpr int XB = xq_block_bytes(MP);
   constexpr int XSTAGE = xstage_bytes(NT);
   constexpr int DW = 2 * MP;                          // D columns per unit (hi rows, lo rows)
-  constexpr int kTmemCols = NT == 16 ? 512 : 256;
-  static_assert(kDCol0 + 2 * kUPS * DW <= kTmemCols, "tensor memory budget");
+  constexpr int kTmemCols = 512;
+  constexpr int kStages = stages_for(NT);
+  constexpr int kSets = sets_for(NT);
+  constexpr int kDCol0 = kSets * kUPS * kACols;        // D slots follow the A slots
+  static_assert(kDCol0 + kSets * kUPS * DW <= kTmemCols, "tensor memory budget");
+  static_assert(kSets % 2 == 0, "a set belongs to one lane");
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   uint8_t* xring = smem;                              // kStages x XSTAGE
   uint8_t* wring = smem + kStages * XSTAGE;           // kStages x kWStageBytes
-  QmmSmem* sb = reinterpret_cast<QmmSmem*>(wring + kWRingBytes);
+  QmmSmem* sb = reinterpret_cast<QmmSmem*>(wring + kStages * kWStageBytes);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int c = blockIdx.x;
@@ -291,11 +312,10 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
       mbar_init(smem_u32(&sb->full[i]), 1);
       mbar_init(smem_u32(&sb->empty[i]), 1 + 4);  // MMA commit + the 4 dequant warps of the lane
     }
-    for (int l = 0; l < 2; ++l) {
-      mbar_init(smem_u32(&sb->a_full[l]), 4);   // the 4 dequant warps
-      mbar_init(smem_u32(&sb->a_empty[l]), 1);  // MMA commit
-      mbar_init(smem_u32(&sb->d_full[l]), 1);   // MMA commit
-      mbar_init(smem_u32(&sb->d_empty[l]), 4);  // the 4 warps of epilogue warpgroup l
+    for (int q = 0; q < kSets; ++q) {
+      mbar_init(smem_u32(&sb->a_full[q]), 4);  // the 4 dequant warps of the set's lane
+      mbar_init(smem_u32(&sb->d_full[q]), 1);  // MMA commit
+      mbar_init(smem_u32(&sb->free[q]), 5);    // MMA commit + the 4 epilogue warps of the lane
     }
     mbar_init(smem_u32(&sb->mma_done[0]), 1);
     mbar_init(smem_u32(&sb->mma_done[1]), 1);
@@ -378,28 +398,27 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
       constexpr uint32_t idesc = idesc_s8_s32(128, DW);
       UnitWalk wk;
       wk.init(p, u0);
-      int ls = 0;  // stages of this lane so far
       for (int k = 0; wk.u < u1; ++k) {
         const int n = wk.stage_n(p.mats[wk.mi], u1);
         if ((k & 1) == L) {
           const int s = k % kStages;
+          const int q = k % kSets, use = k / kSets;
           if (!mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag) ||
-              !mbar_wait(smem_u32(&sb->a_full[L]), ls & 1, p.err, kErrBitWaitAFull, abort_flag) ||
-              (ls > 0 && !mbar_wait(smem_u32(&sb->d_empty[L]), (ls - 1) & 1, p.err, kErrBitWaitDEmpty,
-                                    abort_flag)))
+              !mbar_wait(smem_u32(&sb->a_full[q]), use & 1, p.err, kErrBitWaitAFull, abort_flag) ||
+              (use > 0 && !mbar_wait(smem_u32(&sb->free[q]), (use - 1) & 1, p.err, kErrBitWaitDEmpty,
+                                     abort_flag)))
             break;
           tc_fence_after();
           for (int j = 0; j < n; ++j) {
             const uint32_t xb = smem_u32(xring + s * XSTAGE + j * XB);
-            const uint32_t a_tmem = tmem + (L * kUPS + j) * kACols;
-            const uint32_t d_tmem = tmem + kDCol0 + (L * kUPS + j) * DW;
+            const uint32_t a_tmem = tmem + (q * kUPS + j) * kACols;
+            const uint32_t d_tmem = tmem + kDCol0 + (q * kUPS + j) * DW;
             umma_i8_ts(d_tmem, a_tmem, smem_desc_noswizzle(xb, 128, 256), idesc, 0u);               // k 0-31
             umma_i8_ts(d_tmem, a_tmem + 8, smem_desc_noswizzle(xb + MP * 64, 128, 256), idesc, 1u);  // k 32-63
           }
-          umma_commit(smem_u32(&sb->d_full[L]));
-          umma_commit(smem_u32(&sb->a_empty[L]));
+          umma_commit(smem_u32(&sb->d_full[q]));
+          umma_commit(smem_u32(&sb->free[q]));
           umma_commit(smem_u32(&sb->empty[s]));
-          ++ls;
         }
         wk.advance(p, n);
       }
@@ -408,58 +427,67 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
       int zero = 0;
       mbar_wait(smem_u32(&sb->mma_done[L]), 0, p.err, kErrBitWaitDrain, &zero);
     }
-  } else if (warp >= 4 && warp < kEpiWarp0) {
-    // ------------------------------ dequant (one warpgroup, every stage) ----------------------
-    // Per stage: one wait for the lane's slots, then decode + tensor-memory store of every unit
-    // (the stores are asynchronous; the shared loads of unit j+1 are issued before unit j is
-    // decoded), then one wait for all stores and one arrival for the whole stage.
+  } else if (warp >= kDeqWarp0 && warp < kEpiWarp0) {
+    // ------------------------------ dequant: one warpgroup per lane ---------------------------
+    // Per stage of its lane: one wait for the stage and one for the lane's slots; all shared
+    // loads of the stage issued together; decode + tensor-memory store of every unit
+    // (asynchronous); one wait for the stores and one arrival for the whole stage.
+    const int L = (warp - kDeqWarp0) >> 2;
     const int r = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    int lsn0 = 0, lsn1 = 0;  // stages of each lane so far
     UnitWalk wk;
     wk.init(p, u0);
     for (int k = 0; wk.u < u1; ++k) {
       const int n = wk.stage_n(p.mats[wk.mi], u1);
-      const int L = k & 1;
-      const int s = k % kStages;
-      const int ls = L ? lsn1++ : lsn0++;
-      // Every wait result is made warp-uniform: a lane that left the loop alone would strand
-      // the others at __syncwarp or at a .sync.aligned tensor-memory store.
-      const bool ok =
-          mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag) &&
-          (ls == 0 ||
-           (mbar_wait(smem_u32(&sb->a_empty[L]), (ls - 1) & 1, p.err, kErrBitWaitAEmpty, abort_flag) &&
-            mbar_wait(smem_u32(&sb->d_empty[L]), (ls - 1) & 1, p.err, kErrBitWaitDEmpty, abort_flag)));
-      if (!__all_sync(0xFFFFFFFFu, ok)) break;
-      tc_fence_after();
-      const uint8_t* wst = wring + s * kWStageBytes;
-      const uint8_t* xst = xring + s * XSTAGE + 2 * MP * 64;
-      uint4 c0 = *reinterpret_cast<const uint4*>(wst + r * 16);
-      uint4 c1 = *reinterpret_cast<const uint4*>(wst + 2048 + r * 16);
-      uint32_t sbw = *reinterpret_cast<const uint32_t*>(wst + kUnitNibBytes + r * 4);
-      float xm = r < 2 * MP ? *reinterpret_cast<const float*>(xst + r * 4) : 0.f;
-      for (int j = 0; j < n; ++j) {
-        const uint4 d0 = c0, d1 = c1;
-        QmmMeta& mm = sb->meta[L][j];
-        mm.sb[r] = sbw;
-        if (r < 2 * MP) mm.x[r < MP ? r : kMaxTokens + r - MP] = xm;
-        if (j + 1 < n) {
-          const uint8_t* wu = wst + (j + 1) * kUnitWBytes;
-          c0 = *reinterpret_cast<const uint4*>(wu + r * 16);
-          c1 = *reinterpret_cast<const uint4*>(wu + 2048 + r * 16);
-          sbw = *reinterpret_cast<const uint32_t*>(wu + kUnitNibBytes + r * 4);
-          if (r < 2 * MP) xm = *reinterpret_cast<const float*>(xst + (j + 1) * XB + r * 4);
+      if ((k & 1) == L) {
+        const int s = k % kStages;
+        const int q = k % kSets, use = k / kSets;
+        // Every wait result is made warp-uniform: a lane that left the loop alone would strand
+        // the others at __syncwarp or at a .sync.aligned tensor-memory store.
+        const bool ok =
+            mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag) &&
+            (use == 0 ||
+             mbar_wait(smem_u32(&sb->free[q]), (use - 1) & 1, p.err, kErrBitWaitAEmpty, abort_flag));
+        if (!__all_sync(0xFFFFFFFFu, ok)) break;
+        const uint8_t* wst = wring + s * kWStageBytes;
+        const uint8_t* xst = xring + s * XSTAGE + 2 * MP * 64;
+        uint4 c0[kUPS], c1[kUPS];
+        uint32_t sbw[kUPS];
+        float xm[kUPS];
+#pragma unroll
+        for (int j = 0; j < kUPS; ++j) {
+          if (j < n) {
+            const uint8_t* wu = wst + j * kUnitWBytes;
+            c0[j] = *reinterpret_cast<const uint4*>(wu + r * 16);
+            c1[j] = *reinterpret_cast<const uint4*>(wu + 2048 + r * 16);
+            sbw[j] = *reinterpret_cast<const uint32_t*>(wu + kUnitNibBytes + r * 4);
+            xm[j] = r < 2 * MP ? *reinterpret_cast<const float*>(xst + j * XB + r * 4) : 0.f;
+          }
         }
-        uint32_t a[16];
-        decode_i8(d0, d1, a);
-        tmem_st_x16(tmem + lane_off + (L * kUPS + j) * kACols, a);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sb->empty[s]));  // this warp's shared loads are done
+#pragma unroll
+        for (int j = 0; j < kUPS; ++j) {
+          if (j < n) {
+            QmmMeta& mm = sb->meta[q][j];
+            mm.sb[r] = sbw[j];
+            if (r < 2 * MP) mm.x[r < MP ? r : kMaxTokens + r - MP] = xm[j];
+          }
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < kUPS; ++j) {
+          if (j < n) {
+            uint32_t a[16];
+            decode_i8(c0[j], c1[j], a);
+            tmem_st_x16(tmem + lane_off + (q * kUPS + j) * kACols, a);
+          }
+        }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sb->a_full[q]));
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sb->empty[s]));  // this warp's shared loads are done
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sb->a_full[L]));
       wk.advance(p, n);
     }
   } else if (warp >= kEpiWarp0) {
@@ -476,7 +504,6 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t] = 0.f;
     bool dep_waited = false;
-    int ls = 0;   // stages of this lane so far
     int seg = 0;  // tile segments finished by this CTA
     UnitWalk wk;
     wk.init(p, u0);
@@ -485,15 +512,15 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
       const int n = wk.stage_n(mt, u1);
       if ((k & 1) == L) {
         // a_full: the meta slots this stage reads were written (and d_full: the MMAs are done)
+        const int q = k % kSets, use = k / kSets;
         const bool ok = __all_sync(
             0xFFFFFFFFu,
-            mbar_wait(smem_u32(&sb->a_full[L]), ls & 1, p.err, kErrBitWaitAFull, abort_flag) &&
-                mbar_wait(smem_u32(&sb->d_full[L]), ls & 1, p.err, kErrBitWaitDFull, abort_flag));
-        ++ls;
+            mbar_wait(smem_u32(&sb->a_full[q]), use & 1, p.err, kErrBitWaitAFull, abort_flag) &&
+                mbar_wait(smem_u32(&sb->d_full[q]), use & 1, p.err, kErrBitWaitDFull, abort_flag));
         if (ok) tc_fence_after();
         for (int j = 0; j < n && ok; ++j) {
           {
-            const QmmMeta& mm = sb->meta[L][j];
+            const QmmMeta& mm = sb->meta[q][j];
             const uint32_t sbw = mm.sb[r];
             float xs[NT], xsum[NT];
 #pragma unroll
@@ -502,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
               xsum[t] = mm.x[kMaxTokens + t];
             }
             float dh[NT], dl[NT];
-            const uint32_t dbase = tmem + lane_off + kDCol0 + (L * kUPS + j) * DW;
+            const uint32_t dbase = tmem + lane_off + kDCol0 + (q * kUPS + j) * DW;
             tmem_ld<NT>(dbase, dh);
             tmem_ld<NT>(dbase + MP, dl);
             tc_wait_ld();
@@ -518,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, NT == 16 ? 1 : 2)
         if (ok) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&sb->d_empty[L]));  // D and meta slots read
+          if (lane == 0) mbar_arrive(smem_u32(&sb->free[q]));  // D and meta slots read
         }
       }
       const int g = wk.g + n - 1;  // group of the stage's last unit
