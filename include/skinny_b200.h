@@ -99,9 +99,10 @@ int skinny_qmm_w4g64_simt(const void* x, int ldx, const void* w_tc, void* out, i
  * no cudaFree, no allocating library routine.  It has NO counterpart in the reference; it exists
  * for callers that cannot provide or allocate device memory per call (a plain C FFI host with no
  * device-buffer type, a serving loop with a fixed memory budget, a step where an allocation's
- * implicit device synchronisation is not acceptable).  Its scratch is one static 2,629,888-byte
- * array in the library's device memory per device.  Limit: N <= 262,144 rows (2048 tiles of 128);
- * larger N returns SKINNY_ERR_SCRATCH_LIMIT before anything is launched.  The first call on a
+ * implicit device synchronisation is not acceptable).  Its scratch is one static 3,744,000-byte
+ * array in the library's device memory per device.  Limits: N <= 262,144 rows (2048 tiles of 128)
+ * and K <= 32,768 columns; larger shapes return SKINNY_ERR_SCRATCH_LIMIT before anything is
+ * launched.  The first call on a
  * device does the set-up (scratch address lookup, kernel attributes) and should come before any
  * stream capture.  Calls that may overlap on one device (other streams or threads without
  * ordering) race on the shared scratch; order them.  Each call clears the scratch's counters on

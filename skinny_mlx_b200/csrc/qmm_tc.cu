@@ -78,13 +78,16 @@ constexpr int kDeqWarp0 = 4;                       // warps 4..7 lane 0, 8..11 l
 constexpr int kEpiWarp0 = 12;                      // warps 12..15 lane 0, 16..19 lane 1
 constexpr int kEpiThreads = 128;
 constexpr int kACols = 16;                         // TMEM columns of one unit's int8 A operand
-// Slot sets: stage k uses set q = k % sets (A slots in TMEM, D slots in TMEM, meta slots in
-// shared memory for its units) and lane k % 2 (dequant warpgroup, MMA issuer, epilogue
-// warpgroup).  sets is even, so a set always belongs to the same lane, and with 4 sets a lane
-// starts decoding its next stage while the epilogue still reads its previous one.  Tensor memory
-// bounds it: 4 sets x 4 units x (16 A + 16 D columns) = 512 for M <= 8; M > 8 needs 32 D columns
-// per unit and keeps 2 sets.
-__host__ __device__ constexpr int sets_for(int NT) { return NT <= 8 ? 4 : 2; }
+// Slot sets: stage k runs on lane k % 2 (dequant warpgroup, MMA issuer, epilogue warpgroup) and
+// uses A-set k % kSetsA (its units' A operands in TMEM and meta slots in shared memory, free once
+// its MMAs completed and the epilogue read the meta) and D-set k % setsD (accumulators in TMEM,
+// free once the epilogue read them).  Both counts are even, so a set always belongs to one lane,
+// and with several sets per lane the decode, MMAs and epilogue of consecutive stages of a lane
+// overlap instead of forming one chain.  Tensor memory bounds them: 4 A-sets x 4 units x 16
+// columns plus 4 D-sets x 4 units x 16 columns for M <= 8 (32 D columns per unit, 2 D-sets, for
+// M > 8) = 512 columns.
+constexpr int kSetsA = 4;
+__host__ __device__ constexpr int sets_d_for(int NT) { return NT <= 8 ? 4 : 2; }
 constexpr int kMaxSets = 4;
 
 // Grouped launch: one persistent grid streams the concatenated units of up to kMaxMats
@@ -133,14 +136,15 @@ struct __align__(16) QmmMeta {
 };
 
 struct __align__(16) QmmSmem {
-  QmmMeta meta[kMaxSets][kUPS];
+  QmmMeta meta[kSetsA][kUPS];
   uint64_t full[kMaxStages];
   uint64_t empty[kMaxStages];
   // Per lane, one phase per stage of that lane ("lane-stage"):
   // Per slot set, one phase per use (one stage):
-  uint64_t a_full[kMaxSets];  // dequant -> MMA/epilogue: A slots stored, meta slots written
+  uint64_t a_full[kSetsA];    // dequant -> MMA/epilogue: A slots stored, meta slots written
+  uint64_t a_free[kSetsA];    // MMA commit + epilogue (meta read) -> dequant
   uint64_t d_full[kMaxSets];  // MMA -> epilogue: accumulators ready
-  uint64_t free[kMaxSets];    // MMA commit + epilogue -> dequant/MMA: the set's slots free
+  uint64_t d_free[kMaxSets];  // epilogue -> MMA: accumulators read
   uint64_t mma_done[2];
   uint32_t tmem_base;
   int abort_flag;
@@ -291,10 +295,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int DW = 2 * MP;                          // D columns per unit (hi rows, lo rows)
   constexpr int kTmemCols = 512;
   constexpr int kStages = stages_for(NT);
-  constexpr int kSets = sets_for(NT);
-  constexpr int kDCol0 = kSets * kUPS * kACols;        // D slots follow the A slots
-  static_assert(kDCol0 + kSets * kUPS * DW <= kTmemCols, "tensor memory budget");
-  static_assert(kSets % 2 == 0, "a set belongs to one lane");
+  constexpr int kSetsD = sets_d_for(NT);
+  constexpr int kDCol0 = kSetsA * kUPS * kACols;       // D slots follow the A slots
+  static_assert(kDCol0 + kSetsD * kUPS * DW <= kTmemCols, "tensor memory budget");
+  static_assert(kSetsA % 2 == 0 && kSetsD % 2 == 0, "a set belongs to one lane");
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   uint8_t* xring = smem;                              // kStages x XSTAGE
@@ -312,10 +316,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&sb->full[i]), 1);
       mbar_init(smem_u32(&sb->empty[i]), 1 + 4);  // MMA commit + the 4 dequant warps of the lane
     }
-    for (int q = 0; q < kSets; ++q) {
+    for (int q = 0; q < kSetsA; ++q) {
       mbar_init(smem_u32(&sb->a_full[q]), 4);  // the 4 dequant warps of the set's lane
+      mbar_init(smem_u32(&sb->a_free[q]), 5);  // MMA commit + the 4 epilogue warps of the lane
+    }
+    for (int q = 0; q < kSetsD; ++q) {
       mbar_init(smem_u32(&sb->d_full[q]), 1);  // MMA commit
-      mbar_init(smem_u32(&sb->free[q]), 5);    // MMA commit + the 4 epilogue warps of the lane
+      mbar_init(smem_u32(&sb->d_free[q]), 4);  // the 4 epilogue warps of the lane
     }
     mbar_init(smem_u32(&sb->mma_done[0]), 1);
     mbar_init(smem_u32(&sb->mma_done[1]), 1);
@@ -402,22 +409,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n = wk.stage_n(p.mats[wk.mi], u1);
         if ((k & 1) == L) {
           const int s = k % kStages;
-          const int q = k % kSets, use = k / kSets;
+          const int qa = k % kSetsA, qd = k % kSetsD, used = k / kSetsD;
           if (!mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag) ||
-              !mbar_wait(smem_u32(&sb->a_full[q]), use & 1, p.err, kErrBitWaitAFull, abort_flag) ||
-              (use > 0 && !mbar_wait(smem_u32(&sb->free[q]), (use - 1) & 1, p.err, kErrBitWaitDEmpty,
-                                     abort_flag)))
+              !mbar_wait(smem_u32(&sb->a_full[qa]), (k / kSetsA) & 1, p.err, kErrBitWaitAFull, abort_flag) ||
+              (used > 0 && !mbar_wait(smem_u32(&sb->d_free[qd]), (used - 1) & 1, p.err, kErrBitWaitDEmpty,
+                                      abort_flag)))
             break;
           tc_fence_after();
           for (int j = 0; j < n; ++j) {
             const uint32_t xb = smem_u32(xring + s * XSTAGE + j * XB);
-            const uint32_t a_tmem = tmem + (q * kUPS + j) * kACols;
-            const uint32_t d_tmem = tmem + kDCol0 + (q * kUPS + j) * DW;
+            const uint32_t a_tmem = tmem + (qa * kUPS + j) * kACols;
+            const uint32_t d_tmem = tmem + kDCol0 + (qd * kUPS + j) * DW;
             umma_i8_ts(d_tmem, a_tmem, smem_desc_noswizzle(xb, 128, 256), idesc, 0u);               // k 0-31
             umma_i8_ts(d_tmem, a_tmem + 8, smem_desc_noswizzle(xb + MP * 64, 128, 256), idesc, 1u);  // k 32-63
           }
-          umma_commit(smem_u32(&sb->d_full[q]));
-          umma_commit(smem_u32(&sb->free[q]));
+          umma_commit(smem_u32(&sb->d_full[qd]));
+          umma_commit(smem_u32(&sb->a_free[qa]));
           umma_commit(smem_u32(&sb->empty[s]));
         }
         wk.advance(p, n);
@@ -441,13 +448,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = wk.stage_n(p.mats[wk.mi], u1);
       if ((k & 1) == L) {
         const int s = k % kStages;
-        const int q = k % kSets, use = k / kSets;
+        const int q = k % kSetsA, use = k / kSetsA;
         // Every wait result is made warp-uniform: a lane that left the loop alone would strand
         // the others at __syncwarp or at a .sync.aligned tensor-memory store.
         const bool ok =
             mbar_wait(smem_u32(&sb->full[s]), (k / kStages) & 1, p.err, kErrBitWaitFull, abort_flag) &&
             (use == 0 ||
-             mbar_wait(smem_u32(&sb->free[q]), (use - 1) & 1, p.err, kErrBitWaitAEmpty, abort_flag));
+             mbar_wait(smem_u32(&sb->a_free[q]), (use - 1) & 1, p.err, kErrBitWaitAEmpty, abort_flag));
         if (!__all_sync(0xFFFFFFFFu, ok)) break;
         const uint8_t* wst = wring + s * kWStageBytes;
         const uint8_t* xst = xring + s * XSTAGE + 2 * MP * 64;
@@ -512,15 +519,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = wk.stage_n(mt, u1);
       if ((k & 1) == L) {
         // a_full: the meta slots this stage reads were written (and d_full: the MMAs are done)
-        const int q = k % kSets, use = k / kSets;
+        const int qa = k % kSetsA, qd = k % kSetsD;
         const bool ok = __all_sync(
             0xFFFFFFFFu,
-            mbar_wait(smem_u32(&sb->a_full[q]), use & 1, p.err, kErrBitWaitAFull, abort_flag) &&
-                mbar_wait(smem_u32(&sb->d_full[q]), use & 1, p.err, kErrBitWaitDFull, abort_flag));
+            mbar_wait(smem_u32(&sb->a_full[qa]), (k / kSetsA) & 1, p.err, kErrBitWaitAFull, abort_flag) &&
+                mbar_wait(smem_u32(&sb->d_full[qd]), (k / kSetsD) & 1, p.err, kErrBitWaitDFull, abort_flag));
         if (ok) tc_fence_after();
         for (int j = 0; j < n && ok; ++j) {
           {
-            const QmmMeta& mm = sb->meta[q][j];
+            const QmmMeta& mm = sb->meta[qa][j];
             const uint32_t sbw = mm.sb[r];
             float xs[NT], xsum[NT];
 #pragma unroll
@@ -529,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               xsum[t] = mm.x[kMaxTokens + t];
             }
             float dh[NT], dl[NT];
-            const uint32_t dbase = tmem + lane_off + kDCol0 + (q * kUPS + j) * DW;
+            const uint32_t dbase = tmem + lane_off + kDCol0 + (qd * kUPS + j) * DW;
             tmem_ld<NT>(dbase, dh);
             tmem_ld<NT>(dbase + MP, dl);
             tc_wait_ld();
@@ -545,7 +552,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&sb->free[q]));  // D and meta slots read
+          if (lane == 0) {  // D and meta slots read
+            mbar_arrive(smem_u32(&sb->d_free[qd]));
+            mbar_arrive(smem_u32(&sb->a_free[qa]));
+          }
         }
       }
       const int g = wk.g + n - 1;  // group of the stage's last unit

@@ -71,3 +71,11 @@ def test_noalloc_rejects_shapes_over_the_scratch(cuda_lib, dev):
         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert st == SCRATCH_LIMIT
     assert b"262144" in cuda_lib.skinny_strerror(st)
+    # K over the x-prep capacity of the scratch (512 groups of 64 columns); checked on the host,
+    # nothing is read through these pointers
+    kbig = 513 * 64
+    st = cuda_lib.skinny_qmm_w4g64_noalloc(
+        ctypes.c_void_p(x.data_ptr()), kbig, ctypes.c_void_p(w.data_ptr()),
+        ctypes.c_void_p(out.data_ptr()), 64, 1, 64, kbig,
+        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == SCRATCH_LIMIT
