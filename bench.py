@@ -37,6 +37,7 @@ import torch  # noqa: E402
 
 FALLBACK_HBM_GBS = 6650.0
 M_STACK = 8
+KERNELS_PER_CALL = 2  # every qmm call (single or grouped) launches the x-prep and the qmm kernel
 
 
 # ------------------------------------------------------------------------------------------------
@@ -370,7 +371,9 @@ def run_skinny(args, world, rank, local):
             "metric": "qmm HBM GB/s, 129 fused projections of the 32-layer hybrid stack at M=8",
             "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16xu4->f32", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "data": "synthetic",
+            "dtype": "s8 x s8 -> s32 tensor-core products (4-bit weights as int8, activations as two int8 "
+                     "digits of 16-bit fixed point), f32 scale/bias and accumulation",
             "config": {"workload": "config 2: 129-projection hybrid stack (hidden 2560, 32 layers, 4-bit g64) at M=8",
                        "tokens": M_STACK, "weight_bytes_per_step": 2024755200,
                        "algorithmic_bytes_per_step": per_step_bytes, "l2": "inputs larger than L2 (2.0 GB of weights)",
@@ -381,10 +384,10 @@ def run_skinny(args, world, rank, local):
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
                     "path": "pinned H2D of activations, CUDA-graph replay of the skinny_qmm_grouped call, D2H of logits"},
-            "gpu_launches": args.steps,
+            "gpu_launches": KERNELS_PER_CALL * args.steps,
             "per_projection_launches": {"ms_per_step": round(msl_step, 4),
                                         "GBps": round(per_step_bytes / (msl_step * 1e-3) / 1e9, 1),
-                                        "launches_per_step": len(shapes)},
+                                        "launches_per_step": KERNELS_PER_CALL * len(shapes)},
             "clocks": clocks,
             "stack_m1_ms": round(ms1_step, 4),
             "cost_m8_vs_m1": round(ms_step / ms1_step, 3),
@@ -392,6 +395,22 @@ def run_skinny(args, world, rank, local):
             "device_error_bits": errs,
         }
         print(json.dumps(line), flush=True)
+
+
+def run_head_case(args):
+    """--case head: the single largest matrix of the step (tied LM head, 151936 x 2560, 218.8 MB
+    packed) at --m tokens, one qmm call per step.  A small, self-contained case for profilers
+    (one launch of each kernel per step, a few hundred MB on the device)."""
+    from skinny_mlx_b200.configs import packed_bytes
+
+    dev = torch.device("cuda", 0)
+    shapes = [("head", 151936, 2560)]
+    runner = StackRunner(shapes, build_weights(shapes, dev, seed=3), args.m, dev, seed=4, mode="launches")
+    ms, _ = time_replays(runner, args.steps, args.warmup, 1)
+    ms_step = ms / args.steps
+    print(json.dumps({"case": "head", "tokens": args.m, "ms_per_step": round(ms_step, 4),
+                      "GBps": round(runner.algorithmic_bytes() / (ms_step * 1e-3) / 1e9, 1),
+                      "packed_bytes": packed_bytes(151936, 2560)}), flush=True)
 
 
 def main():
@@ -402,8 +421,14 @@ def main():
     ap.add_argument("--impl", default="skinny", choices=["skinny", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--case", default="stack", choices=["stack", "head"],
+                    help="head: single-matrix profiling case instead of the bench line")
+    ap.add_argument("--m", type=int, default=M_STACK, help="tokens for --case head")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.case == "head":
+        run_head_case(args)
+        return
     world, rank, local = init_dist()
     try:
         if args.impl == "reference":
