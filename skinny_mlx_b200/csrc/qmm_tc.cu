@@ -166,12 +166,23 @@ static_assert(stages_for(8) % 2 == 0 && stages_for(16) % 2 == 0 && stages_for(16
               "stage ring");
 
 // Walks a CTA's unit range in stages, tracking the matrix, the tile within it and the group
-// within the tile incrementally (no division per unit).  A stage never crosses a tile end.
+// within the tile incrementally (no division per unit).  A stage never crosses a tile end.  The
+// current matrix's fields are held in registers and reloaded only when the walk enters the next
+// matrix: indexed reads of the kernel-parameter table cost hundreds of cycles each, which every
+// role would otherwise pay on every stage.
 struct UnitWalk {
-  int u;   // global unit at the start of the current stage
-  int mi;  // matrix of unit u
-  int lt;  // tile of unit u within its matrix
-  int g;   // group of unit u within its tile
+  int u;         // global unit at the start of the current stage
+  int mi;        // matrix of unit u
+  int lt;        // tile of unit u within its matrix
+  int g;         // group of unit u within its tile
+  int G;         // groups per tile of matrix mi
+  int uoff;      // first global unit of matrix mi
+  int next_off;  // first global unit of matrix mi + 1 (INT_MAX for the last)
+  __device__ __forceinline__ void load(const QmmParams& p) {
+    G = p.mats[mi].G;
+    uoff = p.mats[mi].unit_off;
+    next_off = mi + 1 < p.n_mats ? p.mats[mi + 1].unit_off : 0x7FFFFFFF;
+  }
   __device__ __forceinline__ void init(const QmmParams& p, int u0) {
     int lo = 0, hi = p.n_mats - 1;  // largest m with unit_off <= u0
     while (lo < hi) {
@@ -179,26 +190,28 @@ struct UnitWalk {
       if (p.mats[mid].unit_off <= u0) lo = mid; else hi = mid - 1;
     }
     mi = lo;
-    const int lu = u0 - p.mats[mi].unit_off;
-    lt = lu / p.mats[mi].G;
-    g = lu - lt * p.mats[mi].G;
+    load(p);
+    const int lu = u0 - uoff;
+    lt = lu / G;
+    g = lu - lt * G;
     u = u0;
   }
   // Units of the stage starting at u: at most kUPS, never past u1 or the end of u's tile.
-  __device__ __forceinline__ int stage_n(const QmmMat& mt, int u1) const {
+  __device__ __forceinline__ int stage_n(int u1) const {
     int n = u1 - u;
-    if (n > mt.G - g) n = mt.G - g;
+    if (n > G - g) n = G - g;
     return n < kUPS ? n : kUPS;
   }
   __device__ __forceinline__ void advance(const QmmParams& p, int n) {
     u += n;
     g += n;
-    if (g == p.mats[mi].G) {
+    if (g == G) {
       g = 0;
       ++lt;
-      if (mi + 1 < p.n_mats && u == p.mats[mi + 1].unit_off) {
+      if (u == next_off) {
         ++mi;
         lt = 0;
+        load(p);
       }
     }
   }
@@ -352,14 +365,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_w = policy_evict_first();
       UnitWalk wk;
       wk.init(p, u0);
+      int cmi = wk.mi;  // matrix whose weight pointer and x-prep offset are cached
+      const uint8_t* w_tc = p.mats[cmi].w_tc;
+      int xg_off = p.mats[cmi].xg_off;
       int k = 0;
       // first stages: weights before griddepcontrol.wait, x blocks after
       while (wk.u < u1 && k < kStages) {
-        const QmmMat& mt = p.mats[wk.mi];
-        const int n = wk.stage_n(mt, u1);
+        if (wk.mi != cmi) {
+          cmi = wk.mi;
+          w_tc = p.mats[cmi].w_tc;
+        }
+        const int n = wk.stage_n(u1);
         mbar_arrive_expect_tx(smem_u32(&sb->full[k]), static_cast<uint32_t>(n) * (kUnitWBytes + XB));
         bulk_g2s_hint(smem_u32(wring + k * kWStageBytes),
-                      mt.w_tc + static_cast<size_t>(wk.u - mt.unit_off) * kUnitWBytes,
+                      w_tc + static_cast<size_t>(wk.u - wk.uoff) * kUnitWBytes,
                       static_cast<uint32_t>(n) * kUnitWBytes, smem_u32(&sb->full[k]), pol_w);
         wk.advance(p, n);
         ++k;
@@ -369,25 +388,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         UnitWalk w2;
         w2.init(p, u0);
         for (int f = 0; f < k; ++f) {
-          const QmmMat& mt = p.mats[w2.mi];
-          const int n = w2.stage_n(mt, u1);
-          bulk_g2s(smem_u32(xring + f * XSTAGE), p.xq + static_cast<size_t>(mt.xg_off + w2.g) * XB,
+          const int n = w2.stage_n(u1);
+          bulk_g2s(smem_u32(xring + f * XSTAGE), p.xq + static_cast<size_t>(p.mats[w2.mi].xg_off + w2.g) * XB,
                    static_cast<uint32_t>(n) * XB, smem_u32(&sb->full[f]));
           w2.advance(p, n);
         }
+        cmi = wk.mi;
+        w_tc = p.mats[cmi].w_tc;
+        xg_off = p.mats[cmi].xg_off;
       }
       while (wk.u < u1) {
         const int s = k % kStages;
         if (!mbar_wait(smem_u32(&sb->empty[s]), ((k / kStages) - 1) & 1, p.err, kErrBitWaitEmpty,
                        abort_flag))
           break;
-        const QmmMat& mt = p.mats[wk.mi];
-        const int n = wk.stage_n(mt, u1);
+        if (wk.mi != cmi) {
+          cmi = wk.mi;
+          w_tc = p.mats[cmi].w_tc;
+          xg_off = p.mats[cmi].xg_off;
+        }
+        const int n = wk.stage_n(u1);
         mbar_arrive_expect_tx(smem_u32(&sb->full[s]), static_cast<uint32_t>(n) * (kUnitWBytes + XB));
         bulk_g2s_hint(smem_u32(wring + s * kWStageBytes),
-                      mt.w_tc + static_cast<size_t>(wk.u - mt.unit_off) * kUnitWBytes,
+                      w_tc + static_cast<size_t>(wk.u - wk.uoff) * kUnitWBytes,
                       static_cast<uint32_t>(n) * kUnitWBytes, smem_u32(&sb->full[s]), pol_w);
-        bulk_g2s(smem_u32(xring + s * XSTAGE), p.xq + static_cast<size_t>(mt.xg_off + wk.g) * XB,
+        bulk_g2s(smem_u32(xring + s * XSTAGE), p.xq + static_cast<size_t>(xg_off + wk.g) * XB,
                  static_cast<uint32_t>(n) * XB, smem_u32(&sb->full[s]));
         wk.advance(p, n);
         ++k;
@@ -406,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       UnitWalk wk;
       wk.init(p, u0);
       for (int k = 0; wk.u < u1; ++k) {
-        const int n = wk.stage_n(p.mats[wk.mi], u1);
+        const int n = wk.stage_n(u1);
         if ((k & 1) == L) {
           const int s = k % kStages;
           const int qa = k % kSetsA, qd = k % kSetsD, used = k / kSetsD;
@@ -445,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     UnitWalk wk;
     wk.init(p, u0);
     for (int k = 0; wk.u < u1; ++k) {
-      const int n = wk.stage_n(p.mats[wk.mi], u1);
+      const int n = wk.stage_n(u1);
       if ((k & 1) == L) {
         const int s = k % kStages;
         const int q = k % kSetsA, use = k / kSetsA;
@@ -515,8 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     UnitWalk wk;
     wk.init(p, u0);
     for (int k = 0; wk.u < u1; ++k) {
-      const QmmMat& mt = p.mats[wk.mi];
-      const int n = wk.stage_n(mt, u1);
+      const int n = wk.stage_n(u1);
       if ((k & 1) == L) {
         // a_full: the meta slots this stage reads were written (and d_full: the MMAs are done)
         const int qa = k % kSetsA, qd = k % kSetsD;
@@ -559,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const int g = wk.g + n - 1;  // group of the stage's last unit
-      if (g == mt.G - 1 || wk.u + n == u1) {
+      if (g == wk.G - 1 || wk.u + n == u1) {
         // ---- end of a tile segment: combine the lanes, then write the tile or publish a partial
         const int own = k & 1;  // the warpgroup that holds the segment's last stage finishes it
         float* xb = xchg + (seg & 1) * NT * kTileRows;
@@ -574,6 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float o = xb[t * kTileRows + r];
             acc[t] = L == 0 ? acc[t] + o : o + acc[t];
           }
+          const QmmMat& mt = p.mats[wk.mi];                     // read once per tile segment
           const int tile_u0 = mt.unit_off + wk.lt * mt.G;        // the tile's first global unit
           const int tile = mt.tile_off + wk.lt;                  // global tile (counter index)
           const int seg_start = (tile_u0 > u0) ? tile_u0 : u0;
