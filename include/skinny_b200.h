@@ -66,8 +66,10 @@ size_t skinny_qmm_workspace_bytes(int N, int K);
 
 /* out[M, N] (bf16, leading dimension ldo) = x[M, K] (bf16, leading dimension ldx) . W^T for
  * 1 <= M <= 16 tokens, computing sum_g s*sum(x*q) + b*sum(x) in f32 (skinny_mlx/qmm.py:8-9).
- * The tensor-core products use x exactly as given (bf16) and q exactly, accumulating in f32.
- * Each token's output depends only on that token's row of x: it is bit-identical for any M.
+ * Products are exact integer dot products (int8 tensor cores) of q with x rounded to 16-bit
+ * fixed point per token and 64-column group (relative to the group's largest |x|, at most 2^-16 of
+ * it), then scaled and accumulated in f32.  Each token's output depends only on that token's row
+ * of x: it is bit-identical for any M.  An x-prep kernel runs first in the same call.
  * x and ldx*2 must be 16-byte aligned.  The workspace must be zero-filled before its first use,
  * hold skinny_qmm_workspace_bytes(N, K) bytes, and not be shared by calls that may run
  * concurrently; calls of different shapes may share it.  Launches use programmatic dependent
@@ -83,7 +85,9 @@ int skinny_qmm_w4g64(const void* x, int ldx, const void* w_tc, void* out, int ld
 /* n independent products out[i][M, N[i]] = x[i][M, K[i]] . W_i^T in ONE persistent launch that
  * streams the concatenated weights of all n matrices (same token count M for all).  The launch
  * overhead, pipeline fill and split-K fix-up are paid once for the group instead of per matrix.
- * Same per-matrix contract and bit-identical results as skinny_qmm_w4g64.  This is the B200 form
+ * Same per-matrix contract as skinny_qmm_w4g64; results equal a single call's up to the f32
+ * summation order of tiles split between CTAs (the split depends on the whole group), and are
+ * deterministic and bit-identical for any M.  This is the B200 form
  * of evaluating a list of quantized matmuls at once, as skinny_mlx/qmm.py:195-196 and
  * bench/model_matmuls.py:188-191 do with mx.eval on a list. */
 int skinny_qmm_w4g64_grouped(int n, const void* const* x, const int* ldx, const void* const* w_tc,
