@@ -99,6 +99,43 @@ int skinny_qmm_w4g64_grouped(int n, const void* const* x, const int* ldx, const 
 int skinny_qmm_w4g64_simt(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
                           int N, int K, void* stream);
 
+/* Bytes of the workspace skinny_spec_accept needs (zero-filled before first use; reusable). */
+size_t skinny_spec_accept_workspace_bytes(void);
+
+/* Greedy acceptance of a verified draft, fused on the device: for the rows = K+1 verified
+ * positions, pred[i] = argmax over the V logits of row i (bf16, leading dimension ld; ties to the
+ * lowest index, NaN never wins); n = the longest prefix with draft[i] == pred[i] (i < K); then
+ * result[0] = n, result[1 .. n+1] = draft[:n] + [pred[n]], result[n+2 .. rows] = -1.  pred (may be
+ * NULL) receives the rows predictions.  rows <= 17, V <= 524,288; logits and ld*2 16-byte aligned.
+ * Replaces the verify tail of skinny_mlx/spec.py:136-147 (argmax, the host sync of pred and
+ * draft, the Python prefix loop): the host reads back rows + 1 int32 values. */
+int skinny_spec_accept(const void* logits, int ld, int rows, int V, const int32_t* draft,
+                       int32_t* result, int32_t* pred, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* Gated DeltaNet verify recurrence with per-token state checkpoints (the B200 form of the
+ * recurrence that skinny_mlx/rollback.py:39-42 records and re-runs).  Per value head h and token t
+ * (state S [Dv, Dk] f32): S <- g S; S <- S + beta (v - S k) k^T; y = S q, with q, k [T, Hk, 128]
+ * bf16 (already normalised and scaled), v [T, Hv, 128] bf16, g (decay) and beta [T, Hv] f32; a k
+ * head serves Hv/Hk value heads.  state [Hv, 128, 128] f32 is read and overwritten with the state
+ * after the last token; y [T, Hv, 128] bf16; ckpt (may be NULL) [T-1, Hv, 128, 128] f32 receives
+ * the state after each of tokens 0 .. T-2 for skinny_gdn_rollback. */
+int skinny_gdn_recurrent(const void* q, const void* k, const void* v, const float* g,
+                         const float* beta, float* state, void* y, float* ckpt, int T, int Hv, int Hk,
+                         int Dk, int Dv, void* stream);
+
+#define SKINNY_GDN_MAX_LAYERS 64
+
+/* Replay-free rollback of all GDN layers after a verify of `fed` tokens that keeps the first
+ * `keep`: state[l] <- ckpt[l][keep-1] when keep < fed (each state_elems f32), and, when conv is
+ * not NULL, conv[l] [W, C] bf16 <- rows keep .. keep+W-1 of conv_full[l] [W + fed, C] bf16 (the
+ * verify step's conv input: old window, then the fed tokens).  One launch for every layer.
+ * Replaces skinny_mlx/rollback.py:58-73 (re-running the recurrence over the accepted prefix and
+ * re-slicing the conv input); attention KV caches are trimmed on the host (a length update). */
+int skinny_gdn_rollback(int n_layers, float* const* state, const float* const* ckpt,
+                        void* const* conv, const void* const* conv_full, long long state_elems,
+                        int keep, int fed, int W, int C, void* stream);
+
 /* skinny_qmm_w4g64 without a workspace argument and without allocating anything: no cudaMalloc,
  * no cudaFree, no allocating library routine.  It has NO counterpart in the reference; it exists
  * for callers that cannot provide or allocate device memory per call (a plain C FFI host with no

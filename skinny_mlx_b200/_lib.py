@@ -39,6 +39,12 @@ SIGNATURES = {
                                       c_int, c_void_p]),
     "skinny_qmm_w4g64_grouped": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                          c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "skinny_spec_accept_workspace_bytes": (c_size_t, []),
+    "skinny_spec_accept": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                   c_void_p, c_size_t, c_void_p]),
+    "skinny_gdn_recurrent": (c_int, [c_void_p] * 8 + [c_int] * 5 + [c_void_p]),
+    "skinny_gdn_rollback": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_longlong,
+                                    c_int, c_int, c_int, c_int, c_void_p]),
     "skinny_qmm_w4g64_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int,
                                          c_int, c_void_p]),
 }

@@ -17,6 +17,17 @@ cudaError_t qmm_repack_launch(const uint32_t* w, const uint16_t* s, const uint16
 cudaError_t qmm_simt_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
                             int N, int K, cudaStream_t stream);
 bool qmm_noalloc_fits(int N, int K);
+size_t spec_accept_ws_bytes();
+cudaError_t gdn_recurrent_launch(const void* q, const void* k, const void* v, const float* g,
+                                 const float* beta, float* state, void* y, float* ckpt, int T, int Hv,
+                                 int Hk, cudaStream_t stream);
+struct GdnRollbackParams;
+cudaError_t gdn_rollback_call(int n_layers, float* const* state, const float* const* ckpt,
+                             void* const* conv, const void* const* conv_full, long long state_elems,
+                             int keep, int fed, int W, int C, cudaStream_t stream);
+bool spec_accept_fits(int rows, int V);
+cudaError_t spec_accept_launch(const void* logits, int ld, int rows, int V, const int32_t* draft,
+                               int32_t* result, int32_t* pred, void* ws, cudaStream_t stream);
 cudaError_t qmm_tc_launch_noalloc(const void* x, int ldx, const void* w_tc, void* out, int ldo,
                                   int M, int N, int K, cudaStream_t stream);
 }  // namespace skinny
@@ -171,6 +182,45 @@ int skinny_qmm_w4g64_noalloc(const void* x, int ldx, const void* w_tc, void* out
   if (!aligned16(x) || (ldx % 8) != 0 || !aligned16(w_tc)) return SKINNY_ERR_ALIGNMENT;
   return cuda_status(skinny::qmm_tc_launch_noalloc(x, ldx, w_tc, out, ldo, M, N, K,
                                                    static_cast<cudaStream_t>(stream)));
+}
+
+size_t skinny_spec_accept_workspace_bytes(void) { return skinny::spec_accept_ws_bytes(); }
+
+int skinny_spec_accept(const void* logits, int ld, int rows, int V, const int32_t* draft,
+                       int32_t* result, int32_t* pred, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  if (!logits || !result || (rows > 1 && !draft)) return SKINNY_ERR_INVALID_ARG;
+  if (!skinny::spec_accept_fits(rows, V) || ld < V) return SKINNY_ERR_SHAPE;
+  if (!aligned16(logits) || (ld % 8) != 0) return SKINNY_ERR_ALIGNMENT;
+  if (!workspace || workspace_bytes < skinny::spec_accept_ws_bytes() || !aligned16(workspace))
+    return SKINNY_ERR_WORKSPACE;
+  return cuda_status(skinny::spec_accept_launch(logits, ld, rows, V, draft, result, pred, workspace,
+                                                static_cast<cudaStream_t>(stream)));
+}
+
+int skinny_gdn_recurrent(const void* q, const void* k, const void* v, const float* g,
+                         const float* beta, float* state, void* y, float* ckpt, int T, int Hv, int Hk,
+                         int Dk, int Dv, void* stream) {
+  if (!q || !k || !v || !g || !beta || !state || !y) return SKINNY_ERR_INVALID_ARG;
+  if (T < 1 || Hv < 1 || Hk < 1 || Hv % Hk != 0 || Dk != 128 || Dv != 128) return SKINNY_ERR_SHAPE;
+  if (!aligned16(state) || (ckpt && !aligned16(ckpt))) return SKINNY_ERR_ALIGNMENT;
+  return cuda_status(skinny::gdn_recurrent_launch(q, k, v, g, beta, state, y, ckpt, T, Hv, Hk,
+                                                  static_cast<cudaStream_t>(stream)));
+}
+
+int skinny_gdn_rollback(int n_layers, float* const* state, const float* const* ckpt,
+                        void* const* conv, const void* const* conv_full, long long state_elems,
+                        int keep, int fed, int W, int C, void* stream) {
+  if (n_layers < 1 || n_layers > SKINNY_GDN_MAX_LAYERS || !state || !ckpt) return SKINNY_ERR_INVALID_ARG;
+  if (keep < 1 || keep > fed || state_elems < 4 || state_elems % 4 != 0) return SKINNY_ERR_SHAPE;
+  if (conv && (!conv_full || W < 0 || C < 1)) return SKINNY_ERR_INVALID_ARG;
+  for (int l = 0; l < n_layers; ++l) {
+    if (!state[l] || (keep < fed && !ckpt[l])) return SKINNY_ERR_INVALID_ARG;
+    if (!aligned16(state[l]) || (ckpt[l] && !aligned16(ckpt[l]))) return SKINNY_ERR_ALIGNMENT;
+    if (conv && (!conv[l] || !conv_full[l])) return SKINNY_ERR_INVALID_ARG;
+  }
+  return cuda_status(skinny::gdn_rollback_call(n_layers, state, ckpt, conv, conv_full, state_elems,
+                                               keep, fed, W, C, static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

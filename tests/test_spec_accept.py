@@ -1,0 +1,69 @@
+"""Fused greedy acceptance (skinny_mlx/spec.py:136-147) against the CPU oracle."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant, spec as ospec
+
+
+def test_oracle_acceptance_rule():
+    lg = np.full((4, 10), -1.0, np.float32)
+    for i, t in enumerate([3, 5, 7, 9]):
+        lg[i, t] = 2.0
+    assert ospec.accept(lg, [3, 5, 1]) == (2, [3, 5, 7], [3, 5, 7, 9])
+    assert ospec.accept(lg, [3, 5, 7]) == (3, [3, 5, 7, 9], [3, 5, 7, 9])
+    assert ospec.accept(lg, [0, 5, 7]) == (0, [3], [3, 5, 7, 9])
+    lg[0, 1] = 2.0  # tie between 1 and 3: first occurrence wins
+    assert ospec.accept(lg, [1, 5, 7])[0] == 3
+    assert ospec.accept(lg[:1], [])[1] == [1]
+
+
+def _case(rng, rows, v, n_match, tie=False):
+    x = rng.standard_normal((rows, v)).astype(np.float32) * 3
+    pred = rng.integers(0, v, rows)
+    x[np.arange(rows), pred] = 20.0
+    if tie:
+        alt = (pred + 1 + rng.integers(0, v - 1, rows)) % v
+        x[np.arange(rows), alt] = 20.0
+    xb = quant.round_bf16(x)
+    truth = ospec.argmax_rows(xb)
+    draft = [int(truth[i]) if i < n_match else int((truth[i] + 1) % v) for i in range(rows - 1)]
+    return xb, draft
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows,v", [(4, 151936), (3, 151936), (9, 151936), (17, 151936), (1, 151936),
+                                    (5, 1000), (2, 8), (16, 32768), (6, 8200)])
+def test_device_acceptance_matches_oracle(cuda_lib, dev, rows, v):
+    from skinny_mlx_b200.spec import accept, accept_device
+
+    rng = np.random.default_rng(rows * 7919 + v)
+    for n_match in sorted({0, (rows - 1) // 2, rows - 1}):
+        for tie in (False, True):
+            xb, draft = _case(rng, rows, v, n_match, tie)
+            lg = torch.from_numpy(quant.f32_to_bf16_bits(xb).view(np.int16)).view(torch.bfloat16).to(dev)
+            dr = torch.tensor(draft, dtype=torch.int32, device=dev)
+            n, toks, pred = ospec.accept(xb, draft)
+            got_n, got = accept(lg, dr)
+            assert (got_n, got) == (n, toks)
+            pr = torch.empty(rows, dtype=torch.int32, device=dev)
+            r = accept_device(lg, dr, pred=pr)
+            assert pr.cpu().tolist() == pred
+            assert r.cpu().tolist()[n + 2:] == [-1] * (rows - 1 - n)
+
+
+@pytest.mark.gpu
+def test_device_acceptance_special_values(cuda_lib, dev):
+    from skinny_mlx_b200.spec import accept
+
+    v = 4096
+    x = np.full((3, v), -np.inf, np.float32)
+    x[0, 17] = 1.0
+    x[1, :] = np.nan
+    x[2, 4095] = -1e30
+    x[2, :5] = np.nan
+    lg = torch.from_numpy(quant.f32_to_bf16_bits(x).view(np.int16)).view(torch.bfloat16).to(dev)
+    draft = [17, 0]
+    n, toks, _ = ospec.accept(quant.bf16_bits_to_f32(quant.f32_to_bf16_bits(x)), draft)
+    assert accept(lg, torch.tensor(draft, dtype=torch.int32, device=dev)) == (n, toks)
