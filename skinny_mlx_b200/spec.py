@@ -54,3 +54,153 @@ def accept(logits: torch.Tensor, draft: torch.Tensor) -> tuple[int, list[int]]:
 
 
 __all__ = ["accept", "accept_device"]
+
+
+# ---------------------------------------------------------------------------------------------
+# decode loops (skinny_mlx/spec.py:54-156 on B200)
+# ---------------------------------------------------------------------------------------------
+def _accept_any(logits: torch.Tensor, draft: torch.Tensor) -> tuple[int, list[int]]:
+    if logits.is_cuda:
+        return accept(logits, draft)
+    pred = torch.argmax(logits.float(), dim=-1).tolist()  # CPU runs of the model (tests)
+    d = draft.tolist()
+    n = 0
+    while n < len(d) and d[n] == pred[n]:
+        n += 1
+    return n, d[:n] + [pred[n]]
+
+
+class HybridRollback:
+    """Replay-free rollback of the hybrid cache (skinny_mlx/rollback.py:19-73): the verify forward
+    writes GDN state checkpoints and records its conv input; rollback selects checkpoint keep-1
+    and re-slices the conv window (one launch for all GDN layers) and trims attention caches."""
+
+    def record(self, cache) -> None:
+        from .model import GDNCache
+
+        for c in cache.layers:
+            if isinstance(c, GDNCache):
+                c.recording = True
+
+    def rollback(self, cache, fed: int, keep: int) -> None:
+        from .model import AttnCache, GDNCache
+
+        gdn = [c for c in cache.layers if isinstance(c, GDNCache)]
+        for c in gdn:
+            c.recording = False
+        if keep == fed:
+            return
+        assert 1 <= keep < fed
+        if gdn and gdn[0].state.is_cuda:
+            from .gdn import rollback
+
+            rollback([c.state for c in gdn], [c.ckpt for c in gdn], keep, fed, [c.conv for c in gdn],
+                     [c.conv_full for c in gdn])
+        else:
+            for c in gdn:
+                c.state.copy_(c.ckpt[keep - 1])
+                c.conv.copy_(c.conv_full[keep: keep + c.conv.shape[0]])
+        for c in cache.layers:
+            if isinstance(c, AttnCache):
+                c.trim(fed - keep)
+
+
+class MTPDrafter:
+    """Chains the MTP head K times (skinny_mlx/spec.py:54-95), scoring drafts over a seeded
+    subset of `vocab` token ids (32768 seeded ids; the reference uses the id
+    prefix [:vocab]).  Verify always uses the full head, so output is unchanged."""
+
+    def __init__(self, model, head, vocab: int | None = 32768, seed: int = 0):
+        from .model import QuantizedLinear
+
+        self.model, self.head = model, head
+        emb = model.embed_tokens
+        V = emb.weight.shape[0]
+        if vocab and vocab < V:
+            gen = torch.Generator(device="cpu").manual_seed(seed)
+            self.ids = torch.randperm(V, generator=gen)[:vocab].sort().values.to(model.device)
+        else:
+            self.ids = torch.arange(V, device=model.device)
+        w, s, b = emb.weight[self.ids], emb.scales[self.ids], emb.biases[self.ids]
+        if hasattr(emb, "skinny_head"):  # patched model: the pruned head runs on the same kernel
+            from .patch import _qmm
+            from .qmm import repack_for_skinny
+
+            rw = repack_for_skinny(w.contiguous(), s.contiguous(), b.contiguous())
+            self._logits = lambda h: _qmm(h, rw)
+        else:
+            ql = QuantizedLinear(w.contiguous(), s.contiguous(), b.contiguous())
+            self._logits = ql
+
+    def _step(self, tokens: torch.Tensor, hidden: torch.Tensor) -> torch.Tensor:
+        return self.head(self.model.embed_tokens(tokens), hidden, self.cache)
+
+    def begin(self, prompt: list[int], h: torch.Tensor, first: int) -> None:
+        self.cache = self.head.make_cache()
+        ids = torch.tensor(list(prompt[1:]) + [first], device=self.model.device)
+        self.h_last = self._step(ids, h)[-1:]
+        self.n_spec = 0
+
+    def draft(self, k: int) -> torch.Tensor:
+        toks, h = [], self.h_last
+        for i in range(k):  # no host sync: the chain feeds verify directly
+            t = self.ids[torch.argmax(self._logits(h[-1:]).float(), dim=-1)]
+            toks.append(t)
+            if i < k - 1:
+                h = self._step(t, h[-1:])
+        self.n_spec = k - 1
+        return torch.cat(toks).to(torch.int32)
+
+    def update(self, h_kept: torch.Tensor, new_tokens: list[int]) -> None:
+        self.cache.trim(self.n_spec)
+        self.h_last = self._step(torch.tensor(new_tokens, device=self.model.device), h_kept)[-1:]
+        self.n_spec = 0
+
+
+def greedy(model, prompt: list[int], max_tokens: int, gaps: list | None = None) -> list[int]:
+    """Plain greedy decoding, one token per forward (skinny_mlx/spec.py:98-107).  `gaps`, when
+    given, receives each step's (top1 - top2 logit gap, top1 logit), for the near-tie check."""
+    cache = model.make_cache()
+    _, logits = model(torch.tensor(prompt, device=model.device), cache)
+    out = []
+    last = logits[-1]
+    for _ in range(max_tokens):
+        if gaps is not None:
+            t2 = torch.topk(last.float(), 2).values
+            gaps.append((float(t2[0] - t2[1]), float(t2[0])))
+        y = int(torch.argmax(last.float()))
+        out.append(y)
+        if len(out) == max_tokens:
+            break
+        _, logits = model(torch.tensor([y], device=model.device), cache)
+        last = logits[-1]
+    return out
+
+
+def speculative(model, prompt: list[int], max_tokens: int, drafter, k: int, stats: dict | None = None) -> list[int]:
+    """Greedy-exact speculative decoding (skinny_mlx/spec.py:110-156): each step verifies
+    [last token] + K drafts in one forward (M = K+1), accepts the longest matching prefix on the
+    device, emits one bonus token and rolls the hybrid cache back to the accepted prefix."""
+    cache = model.make_cache()
+    rb = HybridRollback()
+    h, logits = model(torch.tensor(prompt, device=model.device), cache)
+    out = [int(torch.argmax(logits[-1].float()))]
+    drafter.begin(prompt, h, out[0])
+    steps = accepted = 0
+    while len(out) < max_tokens:
+        draft = drafter.draft(k)
+        x = torch.cat([torch.tensor([out[-1]], dtype=torch.int32, device=model.device), draft])
+        rb.record(cache)
+        h, logits = model(x.long(), cache)
+        n, new = _accept_any(logits, draft)
+        rb.rollback(cache, fed=k + 1, keep=n + 1)
+        drafter.update(h[: n + 1], new)
+        out += new
+        steps += 1
+        accepted += n
+    if stats is not None:
+        stats.update(steps=steps, tokens_per_step=len(out) / max(steps, 1), accepted=accepted)
+    return out[:max_tokens]
+
+
+__all__ += ["HybridRollback", "MTPDrafter", "greedy", "speculative"]
