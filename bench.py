@@ -276,6 +276,103 @@ def config1_sweep(dev, copies=40):
     return out
 
 
+def build_config3(dev):
+    """The config-3 model (config-2 stack, one consistent attention shape), random weights,
+    patched for the B200 kernel."""
+    from skinny_mlx_b200.model import HybridModel, config3
+    from skinny_mlx_b200.patch import patch_model
+
+    model = HybridModel(config3(), seed=11, device=dev)
+    patch_model(model)
+    torch.cuda.empty_cache()
+    return model
+
+
+def config3_step_costs(model, dev, kv_len=2048, ms=(1, 6, 8, 16), steps=20):
+    """one verify step of the full model at M tokens with 2048 cached tokens in
+    every attention layer (filled with random K/V) and live GDN states, GDN checkpoints written as
+    in speculative verify.  Each step is captured in one CUDA graph and replayed."""
+    from skinny_mlx_b200.model import AttnCache, GDNCache
+
+    out = {}
+    gen = torch.Generator(device=dev).manual_seed(5)
+    for m in ms:
+        cache = model.make_cache(max_len=kv_len + 32, max_verify=17)
+        for c in cache.layers:
+            if isinstance(c, AttnCache):
+                c.k.normal_(generator=gen)
+                c.v.normal_(generator=gen)
+                c.length = kv_len
+            else:
+                c.state.normal_(generator=gen).mul_(0.05)
+                c.recording = True
+        ids = torch.randint(0, model.cfg.vocab, (m,), generator=gen, device=dev)
+        s = torch.cuda.Stream(dev)
+
+        def step():
+            for c in cache.layers:
+                if isinstance(c, AttnCache):
+                    c.length = kv_len
+            model(ids, cache)
+
+        with torch.cuda.stream(s):
+            step()
+            step()
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            step()
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                g.replay()
+        s.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            e0.record(s)
+            for _ in range(steps):
+                g.replay()
+            e1.record(s)
+        e1.synchronize()
+        out[str(m)] = round(e0.elapsed_time(e1) / steps, 4)
+        del g, cache
+        torch.cuda.empty_cache()
+    out["cost_m8_vs_m1"] = round(out["8"] / out["1"], 3)
+    return out
+
+
+def config4_spec(model, dev, n_tokens=256, prompt_len=512):
+    """greedy vs speculative (MTP head, drafts over 32768 seeded ids, K = 2, 3)
+    from a 512-token seeded prompt; tok/s and token-exactness against greedy."""
+    from skinny_mlx_b200.mtp import MTPHead
+    from skinny_mlx_b200.patch import patch_model
+    from skinny_mlx_b200.spec import MTPDrafter, greedy, speculative
+
+    g = torch.Generator().manual_seed(512)
+    prompt = torch.randint(0, model.cfg.vocab, (prompt_len,), generator=g).tolist()
+    head = MTPHead(model, seed=13)
+    patch_model(head)
+    greedy(model, prompt, 4)  # warm-up
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    gaps = []
+    ref = greedy(model, prompt, n_tokens, gaps)
+    torch.cuda.synchronize()
+    t_g = time.perf_counter() - t0
+    out = {"greedy_tok_s": round(n_tokens / t_g, 1), "tokens": n_tokens, "prompt": prompt_len}
+    for k in (2, 3):
+        st = {}
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        got = speculative(model, prompt, n_tokens, MTPDrafter(model, head, vocab=32768, seed=3), k, st)
+        torch.cuda.synchronize()
+        t = time.perf_counter() - t0
+        j = next((i for i, (a, b) in enumerate(zip(ref, got)) if a != b), None)
+        out[f"K{k}"] = {"tok_s": round(n_tokens / t, 1), "tokens_per_step": round(st["tokens_per_step"], 3),
+                        "identical_first": n_tokens if j is None else j,
+                        "divergence_gap": None if j is None else round(gaps[j][0], 5)}
+    return out
+
+
 # ------------------------------------------------------------------------------------------------
 # arms
 # ------------------------------------------------------------------------------------------------
@@ -342,6 +439,14 @@ def run_skinny(args, world, rank, local):
     e2e_value = per_step_bytes * world / (e2e_ms * 1e-3) / 1e9
 
     sweep = config1_sweep(dev) if (rank == 0 and not args.no_sweep) else None
+    c3 = c4 = None
+    if rank == 0 and not args.no_model:
+        del runner.graph
+        model = build_config3(dev)
+        c3 = config3_step_costs(model, dev)
+        c4 = config4_spec(model, dev)
+        del model
+        torch.cuda.empty_cache()
     errs = device_errors(dev)
     peak, peak_kind = measured_hbm_peak()
     qmm_bytes = per_step_bytes
@@ -392,6 +497,8 @@ def run_skinny(args, world, rank, local):
             "stack_m1_ms": round(ms1_step, 4),
             "cost_m8_vs_m1": round(ms_step / ms1_step, 3),
             "config1_sweep_gbs": sweep,
+            "config3_verify_step_ms": c3,
+            "config4_spec": c4,
             "device_error_bits": errs,
         }
         print(json.dumps(line), flush=True)
@@ -421,6 +528,7 @@ def main():
     ap.add_argument("--impl", default="skinny", choices=["skinny", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-model", action="store_true", help="skip the config-3/4 model measurements")
     ap.add_argument("--case", default="stack", choices=["stack", "head"],
                     help="head: single-matrix profiling case instead of the bench line")
     ap.add_argument("--m", type=int, default=M_STACK, help="tokens for --case head")
