@@ -373,6 +373,76 @@ def config4_spec(model, dev, n_tokens=256, prompt_len=512):
     return out
 
 
+def config5_steps(world: int, rank: int, dev, kv_len=4096, ms=(8, 16), steps=5, cfg=None):
+    """the 64-layer dense model, column-parallel over the job's ranks (NCCL
+    all-gather of every projection's output), one verify step at M tokens with `kv_len` cached
+    tokens, captured with its collectives in one CUDA graph when possible; max over ranks."""
+    from skinny_mlx_b200.configs import DENSE_64L, packed_bytes
+    from skinny_mlx_b200.dense import DenseModel
+    from skinny_mlx_b200.patch import patch_model
+
+    cfg = cfg or DENSE_64L
+    t0 = time.perf_counter()
+    model = DenseModel(cfg, rank, world, seed=21, device=dev)
+    patch_model(model)
+    torch.cuda.empty_cache()
+    build_s = time.perf_counter() - t0
+    per_layer = (packed_bytes((cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim, cfg.hidden)
+                 + packed_bytes(cfg.hidden, cfg.n_heads * cfg.head_dim)
+                 + packed_bytes(2 * cfg.intermediate, cfg.hidden) + packed_bytes(cfg.hidden, cfg.intermediate))
+    total = cfg.layers * per_layer + packed_bytes(cfg.vocab, cfg.hidden)
+    out = {"weight_bytes": total, "weight_bytes_per_gpu": total // world, "kv_tokens": kv_len,
+           "build_s": round(build_s, 1)}
+    gen = torch.Generator(device=dev).manual_seed(9)
+    peak, _ = measured_hbm_peak()
+    for m in ms:
+        caches = model.make_cache(kv_len + 32)
+        for c in caches:
+            c.k.normal_(generator=gen)
+            c.v.normal_(generator=gen)
+        ids = torch.randint(0, cfg.vocab, (m,), generator=gen, device=dev)
+        s = torch.cuda.Stream(dev)
+
+        def step():
+            for c in caches:
+                c.length = kv_len
+            model(ids, caches)
+
+        with torch.cuda.stream(s):
+            step()
+            step()
+        s.synchronize()
+        graph = None
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                step()
+            graph = g
+        except Exception:  # collectives that cannot be captured: time the eager step
+            graph = None
+        run = graph.replay if graph is not None else step
+        with torch.cuda.stream(s):
+            run()
+        s.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            e0.record(s)
+            for _ in range(steps):
+                run()
+            e1.record(s)
+        e1.synchronize()
+        ms_step = max_over_ranks(e0.elapsed_time(e1), world) / steps
+        out[f"M{m}"] = {"ms_per_step": round(ms_step, 4), "tok_s": round(m / (ms_step * 1e-3), 1),
+                        "cuda_graph": graph is not None,
+                        "hbm_frac_of_weight_floor": round(total / world / (ms_step * 1e-3) / 1e9 / peak, 4)}
+        del graph, caches
+        torch.cuda.empty_cache()
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
 # ------------------------------------------------------------------------------------------------
 # arms
 # ------------------------------------------------------------------------------------------------
@@ -440,6 +510,7 @@ def run_skinny(args, world, rank, local):
 
     sweep = config1_sweep(dev) if (rank == 0 and not args.no_sweep) else None
     c3 = c4 = None
+    c5 = config5_steps(world, rank, dev) if not args.no_dense else None
     if rank == 0 and not args.no_model:
         del runner.graph
         model = build_config3(dev)
@@ -499,6 +570,7 @@ def run_skinny(args, world, rank, local):
             "config1_sweep_gbs": sweep,
             "config3_verify_step_ms": c3,
             "config4_spec": c4,
+            "config5_dense_tp": c5,
             "device_error_bits": errs,
         }
         print(json.dumps(line), flush=True)
@@ -529,6 +601,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the config-3/4 model measurements")
+    ap.add_argument("--no-dense", action="store_true", help="skip the config-5 column-parallel model")
     ap.add_argument("--case", default="stack", choices=["stack", "head"],
                     help="head: single-matrix profiling case instead of the bench line")
     ap.add_argument("--m", type=int, default=M_STACK, help="tokens for --case head")

@@ -244,13 +244,12 @@ class Attention(nn.Module):
         cache.k[L0:L0 + T] = k.to(torch.bfloat16)
         cache.v[L0:L0 + T] = v
         cache.length = L0 + T
-        kk = cache.k[:L0 + T].float().repeat_interleave(nh // nkv, dim=1)
-        vv = cache.v[:L0 + T].float().repeat_interleave(nh // nkv, dim=1)
-        s = torch.einsum("thd,shd->hts", q, kk) / math.sqrt(D)
+        # queries sit at positions L0 .. L0+T-1 after L0 cached keys: bottom-right causal mask
         causal = pos[:, None] >= torch.arange(L0 + T, device=x.device)[None, :]
-        s = s.masked_fill(~causal[None], float("-inf"))
-        o = torch.einsum("hts,shd->thd", torch.softmax(s, dim=-1), vv)
-        o = o * torch.sigmoid(gate.float())
+        o = F.scaled_dot_product_attention(
+            q.to(torch.bfloat16).transpose(0, 1)[None], cache.k[:L0 + T].transpose(0, 1)[None],
+            cache.v[:L0 + T].transpose(0, 1)[None], attn_mask=causal, enable_gqa=True)[0].transpose(0, 1)
+        o = o.float() * torch.sigmoid(gate.float())
         return self.o_proj(o.reshape(T, nh * D).to(torch.bfloat16))
 
 

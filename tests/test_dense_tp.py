@@ -1,0 +1,121 @@
+"""Config 5: the column-parallel dense model.  On CPU, 2 gloo ranks against the unsharded model;
+on one GPU, the patched unsharded model against the unpatched one."""
+
+import os
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from skinny_mlx_b200.dense import DenseModel, small_dense
+
+IDS = [5, 17, 300, 4000, 9, 2222, 123, 77]
+
+
+def _rank(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        m = DenseModel(small_dense(), rank, world, seed=3, device="cpu")
+        caches = m.make_cache(64)
+        m(torch.tensor(IDS[:5]), caches)
+        logits = m(torch.tensor(IDS[5:]), caches)
+        if rank == 0:
+            q.put(logits.float())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_column_parallel_equals_unsharded_on_cpu():
+    ref_m = DenseModel(small_dense(), 0, 1, seed=3, device="cpu")
+    caches = ref_m.make_cache(64)
+    ref_m(torch.tensor(IDS[:5]), caches)
+    ref = ref_m(torch.tensor(IDS[5:]), caches).float()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, 2, 29517, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    # the same rows of the same weights, the same f32 arithmetic per output column
+    assert torch.allclose(got, ref, atol=1e-5, rtol=0), (got - ref).abs().max()
+
+
+@pytest.mark.gpu
+def test_dense_patched_matches_unpatched(cuda_lib, dev):
+    from skinny_mlx_b200.model import QuantizedLinear
+    from skinny_mlx_b200.patch import patch_model
+
+    m = DenseModel(small_dense(), 0, 1, seed=3, device=dev)
+
+    def run():
+        caches = m.make_cache(64)
+        m(torch.tensor(IDS[:5], device=dev), caches)
+        return m(torch.tensor(IDS[5:], device=dev), caches).float()
+
+    rel = lambda a, b: ((a - b).abs().max() / a.abs().max()).item()
+    ref = run()
+    QuantizedLinear.accumulate = torch.float64
+    try:
+        floor = rel(ref, run())
+    finally:
+        QuantizedLinear.accumulate = torch.float32
+    stats = patch_model(m)
+    assert stats["single"] == 2 * 4 + 1 and stats["fused_groups"] == 0
+    got = run()
+    assert rel(ref, got) <= max(1.5e-2, 3 * floor), (rel(ref, got), floor)
+
+
+def _gpu_rank(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    import torch.distributed as dist
+
+    from skinny_mlx_b200.patch import patch_model
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        m = DenseModel(small_dense(), rank, world, seed=3, device=f"cuda:{rank}")
+        patch_model(m)
+        caches = m.make_cache(64)
+        m(torch.tensor(IDS[:5], device=f"cuda:{rank}"), caches)
+        logits = m(torch.tensor(IDS[5:], device=f"cuda:{rank}"), caches).float().cpu()
+        if rank == 0:
+            q.put(logits)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_column_parallel_nccl_two_gpus(cuda_lib, dev):
+    """2 ranks over NCCL (skipped on a 1-GPU box): sharded logits vs the unsharded patched model."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from skinny_mlx_b200.patch import patch_model
+
+    m = DenseModel(small_dense(), 0, 1, seed=3, device=dev)
+    patch_model(m)
+    caches = m.make_cache(64)
+    m(torch.tensor(IDS[:5], device=dev), caches)
+    ref = m(torch.tensor(IDS[5:], device=dev), caches).float().cpu()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gpu_rank, args=(r, 2, 29617, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    # per-row results of the same kernel; stream-K split points differ with the shard sizes
+    assert ((ref - got).abs().max() / ref.abs().max()).item() <= 1e-2
