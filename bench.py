@@ -291,7 +291,8 @@ def build_config3(dev):
 def config3_step_costs(model, dev, kv_len=2048, ms=(1, 6, 8, 16), steps=20):
     """one verify step of the full model at M tokens with 2048 cached tokens in
     every attention layer (filled with random K/V) and live GDN states, GDN checkpoints written as
-    in speculative verify.  Each step is captured in one CUDA graph and replayed."""
+    in speculative verify.  Each step is captured in one CUDA graph and replayed.  `model` is the
+    patched module forward or its FusedStep runtime (same caches, same call)."""
     from skinny_mlx_b200.model import AttnCache, GDNCache
 
     out = {}
@@ -340,9 +341,10 @@ def config3_step_costs(model, dev, kv_len=2048, ms=(1, 6, 8, 16), steps=20):
     return out
 
 
-def config4_spec(model, dev, n_tokens=256, prompt_len=512):
+def config4_spec(model, dev, n_tokens=256, prompt_len=512, fwd=None):
     """greedy vs speculative (MTP head, drafts over 32768 seeded ids, K = 2, 3)
-    from a 512-token seeded prompt; tok/s and token-exactness against greedy."""
+    from a 512-token seeded prompt; tok/s and token-exactness against greedy.  `fwd` (default the
+    model) runs the verify and decode forwards; the MTP head reads the model's embedding."""
     from skinny_mlx_b200.mtp import MTPHead
     from skinny_mlx_b200.patch import patch_model
     from skinny_mlx_b200.spec import MTPDrafter, greedy, speculative
@@ -351,6 +353,7 @@ def config4_spec(model, dev, n_tokens=256, prompt_len=512):
     prompt = torch.randint(0, model.cfg.vocab, (prompt_len,), generator=g).tolist()
     head = MTPHead(model, seed=13)
     patch_model(head)
+    model, base = (fwd or model), model
     greedy(model, prompt, 4)  # warm-up
     torch.cuda.synchronize()
     t0 = time.perf_counter()
@@ -363,7 +366,7 @@ def config4_spec(model, dev, n_tokens=256, prompt_len=512):
         st = {}
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        got = speculative(model, prompt, n_tokens, MTPDrafter(model, head, vocab=32768, seed=3), k, st)
+        got = speculative(model, prompt, n_tokens, MTPDrafter(base, head, vocab=32768, seed=3), k, st)
         torch.cuda.synchronize()
         t = time.perf_counter() - t0
         j = next((i for i, (a, b) in enumerate(zip(ref, got)) if a != b), None)
@@ -509,13 +512,17 @@ def run_skinny(args, world, rank, local):
     e2e_value = per_step_bytes * world / (e2e_ms * 1e-3) / 1e9
 
     sweep = config1_sweep(dev) if (rank == 0 and not args.no_sweep) else None
-    c3 = c4 = None
+    c3 = c3m = c4 = None
     c5 = config5_steps(world, rank, dev) if not args.no_dense else None
     if rank == 0 and not args.no_model:
         del runner.graph
         model = build_config3(dev)
-        c3 = config3_step_costs(model, dev)
-        c4 = config4_spec(model, dev)
+        from skinny_mlx_b200.fused import FusedStep
+
+        fused = FusedStep(model)
+        c3 = config3_step_costs(fused, dev)
+        c3m = config3_step_costs(model, dev, ms=(1, 8))
+        c4 = config4_spec(model, dev, fwd=fused)
         del model
         torch.cuda.empty_cache()
     errs = device_errors(dev)
@@ -569,6 +576,7 @@ def run_skinny(args, world, rank, local):
             "cost_m8_vs_m1": round(ms_step / ms1_step, 3),
             "config1_sweep_gbs": sweep,
             "config3_verify_step_ms": c3,
+            "config3_verify_step_ms_module_path": c3m,
             "config4_spec": c4,
             "config5_dense_tp": c5,
             "device_error_bits": errs,

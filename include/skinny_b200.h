@@ -99,6 +99,68 @@ int skinny_qmm_w4g64_grouped(int n, const void* const* x, const int* ldx, const 
 int skinny_qmm_w4g64_simt(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
                           int N, int K, void* stream);
 
+/* Bytes of one prepared qmm input (the digit blocks the qmm kernel reads) for M tokens, K columns. */
+size_t skinny_xq_bytes(int M, int K);
+
+/* Producers of prepared qmm inputs: compute a bf16 activation row and write it straight in the
+ * qmm's input format, so a step's elementwise work and its next matmul need no x-prep launch or
+ * activation round trip (the B200 form of the glue between the reference model's projections).
+ *   mode 0: h = x (+ d if d != NULL; h written to h_out when given), a = bf16(h / rms(h) * (1 + w))
+ *           with w f32 [K] (zero-centred RMSNorm, eps)
+ *   mode 1: a = bf16(silu(g) * u), x = [g | u] with 2K columns (SwiGLU)
+ *   mode 2: a = x
+ * x, d, h_out bf16 rows with leading dimensions ldx, ldd, ldh (even, 4-byte aligned); xq receives
+ * skinny_xq_bytes(M, K) bytes (16-byte aligned); a_out (mode 0, may be NULL) receives a as bf16
+ * [M, K].  h_out and a_out must not overlap x or d (SKINNY_ERR_INVALID_ARG): column chunks of a
+ * row are written while other chunks of it are still being read.  Launched with programmatic
+ * dependent launch: the next launch on the stream may start before this one ends. */
+int skinny_prep(int mode, const void* x, int ldx, const void* d, int ldd, void* h_out, int ldh,
+                const float* w, float eps, int M, int K, void* xq, void* a_out, void* stream);
+
+/* One Gated DeltaNet mixer from its fused input projection to the prepared input of out_proj,
+ * in one launch: causal depthwise conv (window W <= 4, weights conv_w [C, W+1] f32) + SiLU,
+ * l2-normalised q and k (q / sqrt(128)), g = exp(-exp(A_log) softplus(a + dt_bias)),
+ * beta = sigmoid(b), the gated delta recurrence (state [Hv,128,128] f32 updated; ckpt as in
+ * skinny_gdn_recurrent), gated RMSNorm rmsnorm(y) (1 + norm_w) * silu(z), written as qmm input
+ * digits to xq (K = Hv*128) and, when o_out != NULL, as bf16 [T, Hv*128].  proj [T, ldp] bf16 =
+ * q | k | v (the C = 3*Hv*128 conv channels) | z | b | a (16-byte aligned, ldp % 8 == 0); conv
+ * [W, C] bf16 (16-byte aligned) is updated in place and conv_full [W+T, C] (may be NULL) records
+ * the conv input for skinny_gdn_rollback.  Hk == Hv.  Each head runs on a cluster of 8 CTAs that
+ * exchange y through distributed shared memory; a timed-out wait for a peer ORs a bit into the
+ * 32-bit error word err_word (required; e.g. word 0 of a qmm workspace).  Launched with
+ * programmatic dependent launch.  The layer code this replaces is mlx_lm's (the model the
+ * reference patches); skinny_mlx/rollback.py:14-56 records the same state. */
+int skinny_gdn_fused(const void* proj, int ldp, void* conv, void* conv_full, const float* conv_w,
+                     const float* A_log, const float* dt_bias, const float* norm_w, float eps, float* state,
+                     float* ckpt, void* xq, void* o_out, int T, int Hv, int Hk, int W, void* err_word,
+                     void* stream);
+
+/* Bytes of the workspace skinny_attn_fused needs for a KV cache of max_len positions (0 when the
+ * shape is not supported).  Zero-filled before first use; a completed call leaves it reusable. */
+size_t skinny_attn_workspace_bytes(int T, int n_heads, int n_kv_heads, int max_len);
+
+/* One gated full-attention mixer from its fused projection to the prepared input of o_proj, in
+ * one launch (the attention layers inside the verify forward of skinny_mlx/spec.py:23-28, which
+ * runs the mlx_lm Qwen3.5 model; that layer code is mlx_lm's, not the reference's own):
+ *   q, k = RoPE(bf16(rmsnorm(q|k) (1 + w))) on the first rot dims (inv_freq [rot/2] f32) at
+ *          positions L0 .. L0+T-1; k (bf16) and v are appended to k_cache / v_cache
+ *          [max_len, n_kv_heads, 128] (16-byte aligned) at L0 .. L0+T-1;
+ *   o    = causal (bottom-right) grouped-query softmax(q k^T / sqrt(128)) v over positions
+ *          0 .. L0+t, then bf16(bf16(o) sigmoid(gate)), written as qmm input digits to xq
+ *          (K = n_heads*128) and, when o_out != NULL, as bf16 [T, n_heads*128].
+ * proj [T, ldp] bf16 = per query head [q (128) | gate (128)] | k (n_kv*128) | v (n_kv*128).
+ * head_dim 128, T * n_heads / n_kv_heads <= 128.  The caller advances its cache length by T.
+ * Launched with programmatic dependent launch.  No counterpart in the reference's own code. */
+int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
+                      const float* inv_freq, int rot, float eps, void* k_cache, void* v_cache, int L0, int T,
+                      int n_heads, int n_kv_heads, int max_len, void* workspace, size_t workspace_bytes, void* xq,
+                      void* o_out, void* stream);
+
+/* skinny_qmm_w4g64 on an input prepared by skinny_prep (same result as passing the bf16
+ * activation itself), launched without the x-prep kernel. */
+int skinny_qmm_w4g64_prepared(const void* xq, const void* w_tc, void* out, int ldo, int M, int N, int K,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
 /* Bytes of the workspace skinny_spec_accept needs (zero-filled before first use; reusable). */
 size_t skinny_spec_accept_workspace_bytes(void);
 

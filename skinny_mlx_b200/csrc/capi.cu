@@ -1,5 +1,6 @@
 // C-ABI entry points: host-side validation, then stream-ordered kernel launches.
 #include <cstdint>
+#include <utility>
 #include <cuda_runtime.h>
 
 #include "../../include/skinny_b200.h"
@@ -18,6 +19,28 @@ cudaError_t qmm_simt_launch(const void* x, int ldx, const void* w_tc, void* out,
                             int N, int K, cudaStream_t stream);
 bool qmm_noalloc_fits(int N, int K);
 size_t spec_accept_ws_bytes();
+cudaError_t qmm_tc_launch_prepared(const void* xq, const void* w_tc, void* out, int ldo, int M, int N, int K,
+                                   void* ws, cudaStream_t stream);
+cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd, void* h_out, int ldh,
+                        const float* w, float eps, int K, int M, void* xq, void* a_out, cudaStream_t stream);
+struct GdnFusedParamsHost {
+  const void* proj;
+  int ldp;
+  void* conv;
+  void* conv_full;
+  const float* conv_w;
+  const float* A_log;
+  const float* dt_bias;
+  const float* norm_w;
+  float eps;
+  float* state;
+  float* ckpt;
+  void* xq;
+  void* o_out;
+  uint32_t* err;
+  int T, Hv, Hk, W;
+};
+cudaError_t gdn_fused_call(const GdnFusedParamsHost& prm, cudaStream_t stream);
 cudaError_t gdn_recurrent_launch(const void* q, const void* k, const void* v, const float* g,
                                  const float* beta, float* state, void* y, float* ckpt, int T, int Hv,
                                  int Hk, cudaStream_t stream);
@@ -30,6 +53,11 @@ cudaError_t spec_accept_launch(const void* logits, int ld, int rows, int V, cons
                                int32_t* result, int32_t* pred, void* ws, cudaStream_t stream);
 cudaError_t qmm_tc_launch_noalloc(const void* x, int ldx, const void* w_tc, void* out, int ldo,
                                   int M, int N, int K, cudaStream_t stream);
+size_t attn_ws_bytes(int T, int nh, int nkv, int max_len);
+bool attn_fits(int T, int nh, int nkv);
+cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, const float* kn_w,
+                              const float* inv_freq, int rot, float eps, void* kc, void* vc, int L0, int T,
+                              int nh, int nkv, void* ws, void* xq, void* o_out, cudaStream_t stream);
 }  // namespace skinny
 
 namespace {
@@ -42,6 +70,7 @@ int cuda_status(cudaError_t e) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 
 int current_device() {
   int dev = 0;
@@ -182,6 +211,101 @@ int skinny_qmm_w4g64_noalloc(const void* x, int ldx, const void* w_tc, void* out
   if (!aligned16(x) || (ldx % 8) != 0 || !aligned16(w_tc)) return SKINNY_ERR_ALIGNMENT;
   return cuda_status(skinny::qmm_tc_launch_noalloc(x, ldx, w_tc, out, ldo, M, N, K,
                                                    static_cast<cudaStream_t>(stream)));
+}
+
+size_t skinny_xq_bytes(int M, int K) {
+  if (M < 1 || M > skinny::kMaxTokens || K < skinny::kGroup || K % skinny::kGroup) return 0;
+  return static_cast<size_t>(K / skinny::kGroup) * skinny::xq_block_bytes(M <= 8 ? 8 : 16);
+}
+
+int skinny_prep(int mode, const void* x, int ldx, const void* d, int ldd, void* h_out, int ldh,
+                const float* w, float eps, int M, int K, void* xq, void* a_out, void* stream) {
+  if (!x || !xq || mode < 0 || mode > 2 || (mode == 0 && !w)) return SKINNY_ERR_INVALID_ARG;
+  if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
+  if (K < skinny::kGroup || K % skinny::kGroup) return SKINNY_ERR_SHAPE;
+  const int need = mode == 1 ? 2 * K : K;
+  if (ldx < need || (d && ldd < K) || (h_out && ldh < K)) return SKINNY_ERR_INVALID_ARG;
+  // Outputs are written by one column chunk while other chunks of the row still read the inputs:
+  // h_out and a_out must not overlap x or d.
+  const auto span = [M](const void* p, int ld, int width) {
+    const uintptr_t b = reinterpret_cast<uintptr_t>(p);
+    return std::make_pair(b, b + (static_cast<uintptr_t>(M - 1) * ld + width) * 2);
+  };
+  const auto overlap = [](std::pair<uintptr_t, uintptr_t> a, std::pair<uintptr_t, uintptr_t> b) {
+    return a.first < b.second && b.first < a.second;
+  };
+  if (mode == 0) {
+    const auto xs = span(x, ldx, K);
+    if (h_out && d && (overlap(span(h_out, ldh, K), xs) || overlap(span(h_out, ldh, K), span(d, ldd, K))))
+      return SKINNY_ERR_INVALID_ARG;
+    if (a_out && (overlap(span(a_out, K, K), xs) || (d && overlap(span(a_out, K, K), span(d, ldd, K)))))
+      return SKINNY_ERR_INVALID_ARG;
+  }
+  // bf16 pairs are read and written as 4-byte words
+  if ((ldx % 2) || (d && ldd % 2) || (h_out && ldh % 2) || !aligned16(xq) || !aligned4(x) || !aligned4(d) ||
+      !aligned4(h_out) || !aligned4(a_out))
+    return SKINNY_ERR_ALIGNMENT;
+  return cuda_status(skinny::prep_launch(mode, x, ldx, d, ldd, h_out, ldh, w, eps, K, M, xq, a_out,
+                                         static_cast<cudaStream_t>(stream)));
+}
+
+int skinny_gdn_fused(const void* proj, int ldp, void* conv, void* conv_full, const float* conv_w,
+                     const float* A_log, const float* dt_bias, const float* norm_w, float eps, float* state,
+                     float* ckpt, void* xq, void* o_out, int T, int Hv, int Hk, int W, void* err_word,
+                     void* stream) {
+  if (!proj || !conv || !conv_w || !A_log || !dt_bias || !norm_w || !state || !xq || !err_word)
+    return SKINNY_ERR_INVALID_ARG;
+  if (T < 1 || T > skinny::kMaxTokens || Hv < 1 || Hk != Hv || W < 1 || W > 4) return SKINNY_ERR_SHAPE;
+  const int C = 3 * Hv * 128;
+  if (ldp < C + Hv * 128 + 2 * Hv) return SKINNY_ERR_INVALID_ARG;
+  // conv window and projection rows are read as 16-byte vectors
+  if (!aligned16(state) || (ckpt && !aligned16(ckpt)) || !aligned16(xq) || (ldp % 8) || !aligned16(proj) ||
+      !aligned16(conv) || !aligned4(o_out) || !aligned4(err_word))
+    return SKINNY_ERR_ALIGNMENT;
+  skinny::GdnFusedParamsHost prm{proj, ldp, conv, conv_full, conv_w, A_log, dt_bias, norm_w, eps, state,
+                             T > 1 ? ckpt : nullptr, xq, o_out, static_cast<uint32_t*>(err_word), T, Hv, Hk, W};
+  return cuda_status(skinny::gdn_fused_call(prm, static_cast<cudaStream_t>(stream)));
+}
+
+size_t skinny_attn_workspace_bytes(int T, int n_heads, int n_kv_heads, int max_len) {
+  if (T < 1 || T > skinny::kMaxTokens || max_len < 1 || !skinny::attn_fits(T, n_heads, n_kv_heads)) return 0;
+  return skinny::attn_ws_bytes(T, n_heads, n_kv_heads, max_len);
+}
+
+int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
+                      const float* inv_freq, int rot, float eps, void* k_cache, void* v_cache, int L0, int T,
+                      int n_heads, int n_kv_heads, int max_len, void* workspace, size_t workspace_bytes, void* xq,
+                      void* o_out, void* stream) {
+  if (!proj || !q_norm_w || !k_norm_w || !k_cache || !v_cache || !xq || (rot > 0 && !inv_freq))
+    return SKINNY_ERR_INVALID_ARG;
+  if (T < 1 || T > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
+  if (!skinny::attn_fits(T, n_heads, n_kv_heads) || rot < 0 || rot > 128 || (rot % 2) || L0 < 0 ||
+      L0 + T > max_len)
+    return SKINNY_ERR_SHAPE;
+  if (ldp < (2 * n_heads + 2 * n_kv_heads) * 128) return SKINNY_ERR_INVALID_ARG;
+  if (!aligned16(xq) || !aligned16(k_cache) || !aligned16(v_cache) ||
+      !aligned4(o_out) || (reinterpret_cast<uintptr_t>(proj) & 1u))
+    return SKINNY_ERR_ALIGNMENT;
+  if (!workspace || workspace_bytes < skinny::attn_ws_bytes(T, n_heads, n_kv_heads, max_len) ||
+      !aligned16(workspace))
+    return SKINNY_ERR_WORKSPACE;
+  return cuda_status(skinny::attn_fused_launch(proj, ldp, q_norm_w, k_norm_w, inv_freq, rot, eps, k_cache,
+                                               v_cache, L0, T, n_heads, n_kv_heads, workspace, xq, o_out,
+                                               static_cast<cudaStream_t>(stream)));
+}
+
+int skinny_qmm_w4g64_prepared(const void* xq, const void* w_tc, void* out, int ldo, int M, int N, int K,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  if (!xq || !w_tc || !out) return SKINNY_ERR_INVALID_ARG;
+  const int st = check_qmm_shape(N, K);
+  if (st != SKINNY_OK) return st;
+  if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
+  if (ldo < N) return SKINNY_ERR_INVALID_ARG;
+  if (!aligned16(xq) || !aligned16(w_tc)) return SKINNY_ERR_ALIGNMENT;
+  const skinny::WsLayout wl = skinny::ws_layout(skinny::device_sm_count(current_device()));
+  if (!workspace || workspace_bytes < wl.total || !aligned16(workspace)) return SKINNY_ERR_WORKSPACE;
+  return cuda_status(skinny::qmm_tc_launch_prepared(xq, w_tc, out, ldo, M, N, K, workspace,
+                                                    static_cast<cudaStream_t>(stream)));
 }
 
 size_t skinny_spec_accept_workspace_bytes(void) { return skinny::spec_accept_ws_bytes(); }

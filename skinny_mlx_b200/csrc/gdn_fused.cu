@@ -1,0 +1,361 @@
+// One Gated DeltaNet mixer, from its fused input projection to the prepared input of out_proj,
+// in one launch (the B200 form of everything between in_proj and out_proj of the reference
+// model's GDN layer; skinny_mlx/rollback.py:14-56 records the same intermediate values):
+//
+//   full   = [conv window (W rows); qkv of the T new tokens]          (bf16)
+//   c[t]   = silu( sum_j conv_w[:, j] * full[t + j] )                  (per channel)
+//   q, k   = l2-normalised q and k heads of c (q / sqrt(128)),  v = v heads of c   (-> bf16)
+//   g      = exp(-exp(A_log) * softplus(a + dt_bias)),  beta = sigmoid(b)
+//   y      = gated delta recurrence over the T tokens (state updated, checkpoints written)
+//   o      = bf16( bf16(rmsnorm(y) * (1 + w)) * silu(z) )
+//   digits of o for out_proj (the qmm input format, prep.cu)
+//
+// Work split.  The recurrence is independent per state row (row = value channel): with
+// S_t = g_t S_{t-1} + beta_t (v_t - S_{t-1} k_t g_t) k_t^T a row needs only its own v entry and
+// the head's shared q_t, k_t.  A head is therefore one cluster of kRanks CTAs, each owning 16
+// state rows (16 x 128 f32 in registers: 8 threads per row, 16 columns each), so a layer runs
+// on Hv * 8 SMs instead of Hv.  Every CTA recomputes the head's q and k (conv, norm: a few
+// hundred channels) rather than exchanging them.  The gated RMSNorm and the digits need whole
+// 64-row groups of y, so each CTA pushes its y rows into the shared memory of every CTA
+// of the head (distributed shared memory), and rank r finishes tokens r and r + 8.
+//
+// Rounding points follow the unfused model (skinny_mlx_b200/model.py): q, k, v and y to bf16,
+// the norm output to bf16, o to bf16.  Launched with programmatic dependent launch: the next
+// launch may start at once (it streams weights) and this one waits for the previous grid before
+// its first global read.
+#include <cfloat>
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "digits.cuh"
+#include "ptx.cuh"
+#include "qmm_layout.cuh"
+#include "skinny_status.h"
+
+namespace skinny {
+
+constexpr int kGfThreads = 128;
+constexpr int kGfD = 128;
+constexpr int kGfMaxT = 16;
+constexpr int kGfRanks = 8;                    // CTAs (cluster size) per head
+constexpr int kGfRows = kGfD / kGfRanks;       // state rows per CTA
+constexpr int kGfTpr = kGfThreads / kGfRows;   // threads per row (8)
+constexpr int kGfCols = kGfD / kGfTpr;         // state columns per thread (16)
+static_assert(kGfTpr == 8 && kGfCols == 16, "thread layout");
+
+struct GdnFusedParams {
+  const __nv_bfloat16* proj;  // [T, ldp]: q (Hk*128) | k (Hk*128) | v (Hv*128) | z (Hv*128) | b (Hv) | a (Hv)
+  int ldp;
+  __nv_bfloat16* conv;        // [W, C] window, updated
+  __nv_bfloat16* conv_full;   // [W + T, C] recorded verify input, or null
+  const float* conv_w;        // [C, W + 1]
+  const float* A_log;         // [Hv]
+  const float* dt_bias;       // [Hv]
+  const float* norm_w;        // [128]
+  float eps;
+  float* state;               // [Hv, 128, 128]
+  float* ckpt;                // [T - 1, Hv, 128, 128] or null
+  uint8_t* xq;                // out_proj input digits (K = Hv * 128)
+  __nv_bfloat16* o_out;       // [T, Hv * 128] bf16 copy of o, or null
+  uint32_t* err;              // error word (kErrBitWaitCluster)
+  int T, Hv, Hk;
+};
+
+__device__ __forceinline__ float bf16rf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// 16 bytes into another CTA's shared memory; its mbarrier counts the bytes.
+__device__ __forceinline__ void st_async_v4(uint32_t addr, float4 v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   addr),
+               "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),
+               "r"(__float_as_uint(v.w)), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
+template <int W>
+__global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_constant__ GdnFusedParams p) {
+  constexpr int kCh = 2 * kGfD + kGfRows;  // conv channels a CTA needs: q, k of its head; its 16 v
+  constexpr int kVec = kCh / 8;            // 16-byte vectors per row of them
+  constexpr int kRowsMax = W + kGfMaxT;
+  constexpr int kStg = (kRowsMax * kVec + kGfThreads - 1) / kGfThreads;
+  constexpr int kConvIt = (kCh + kGfThreads - 1) / kGfThreads;
+  const int h = blockIdx.x / kGfRanks;
+  const uint32_t rank = cluster_ctarank();
+  const int r0 = static_cast<int>(rank) * kGfRows;
+  const int rep = p.Hv / p.Hk;
+  const int hk = h / rep;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int T = p.T;
+  const int C = (2 * p.Hk + p.Hv) * kGfD;
+  const int mpad = T <= 8 ? 8 : 16;
+  __shared__ __align__(16) __nv_bfloat16 fw[kRowsMax][kCh];  // [window; new tokens] of the CTA's channels
+  __shared__ float qs[kGfMaxT][kGfD], ks[kGfMaxT][kGfD];
+  __shared__ float vs[kGfMaxT][kGfRows];
+  __shared__ __align__(16) float yl[kGfMaxT][kGfRows];
+  __shared__ __align__(16) float yall[kGfMaxT][kGfD];  // the head's y, pushed by every rank
+  __shared__ float gs[kGfMaxT], bs[kGfMaxT];
+  __shared__ __align__(8) uint64_t ybar;
+  __shared__ int abort_flag;
+
+  // channel of CTA-local conv slot i: q (0..127) and k (128..255) of head hk, v rows r0..r0+15 of h
+  const auto chan = [&](int i) {
+    return i < kGfD ? hk * kGfD + i : i < 2 * kGfD ? (p.Hk + hk) * kGfD + (i - kGfD) : (2 * p.Hk + h) * kGfD + r0 + (i - 2 * kGfD);
+  };
+
+  if (tid == 0) {
+    mbar_init(smem_u32(&ybar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  cluster_arrive_relaxed();  // the mbarrier exists before any peer stores to it (waited below)
+  pdl_launch_dependents();
+  pdl_wait_prior_grid();
+
+  // ---- every global load, issued together
+  const int row = tid / kGfTpr, sub = tid % kGfTpr;  // recurrence: (state row, column phase)
+  const size_t srow = (static_cast<size_t>(h) * kGfD + r0 + row) * kGfD + sub;
+  float S[kGfCols];
+#pragma unroll
+  for (int i = 0; i < kGfCols; ++i) S[i] = p.state[srow + kGfTpr * i];
+  float ga = 0.f, gb = 0.f, gdt = 0.f, galog = 0.f;
+  if (tid < T) {
+    const size_t base = static_cast<size_t>(tid) * p.ldp + C + static_cast<size_t>(p.Hv) * kGfD;
+    gb = __bfloat162float(p.proj[base + h]);
+    ga = __bfloat162float(p.proj[base + p.Hv + h]);
+    gdt = p.dt_bias[h];
+    galog = p.A_log[h];
+  }
+  // digit job: warp w of rank r finishes token r + 8 (w / 2), column half w % 2
+  const int jt = static_cast<int>(rank) + kGfRanks * (warp >> 1), jhalf = warp & 1;
+  const int j0 = jhalf * 64 + 2 * lane;
+  float z0 = 0.f, z1 = 0.f, nw0 = 0.f, nw1 = 0.f;
+  if (jt < T) {
+    const size_t zc = static_cast<size_t>(jt) * p.ldp + C + static_cast<size_t>(h) * kGfD + j0;
+    z0 = __bfloat162float(p.proj[zc]);
+    z1 = __bfloat162float(p.proj[zc + 1]);
+    nw0 = p.norm_w[j0];
+    nw1 = p.norm_w[j0 + 1];
+  }
+  float cw[kConvIt][W + 1];
+#pragma unroll
+  for (int it = 0; it < kConvIt; ++it) {
+    const int i = tid + it * kGfThreads;
+#pragma unroll
+    for (int q = 0; q <= W; ++q) cw[it][q] = i < kCh ? p.conv_w[static_cast<size_t>(chan(i)) * (W + 1) + q] : 0.f;
+  }
+  {
+    const int nvec = (W + T) * kVec;
+    uint4 stg[kStg];
+#pragma unroll
+    for (int u = 0; u < kStg; ++u) {
+      const int e = tid + u * kGfThreads;
+      if (e < nvec) {
+        const int r = e / kVec, c = e - (e / kVec) * kVec;
+        const int col = chan(8 * c);
+        const __nv_bfloat16* src = r < W ? p.conv + static_cast<size_t>(r) * C + col
+                                         : p.proj + static_cast<size_t>(r - W) * p.ldp + col;
+        stg[u] = *reinterpret_cast<const uint4*>(src);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kStg; ++u) {
+      const int e = tid + u * kGfThreads;
+      if (e < nvec) {
+        const int r = e / kVec, c = e - (e / kVec) * kVec;
+        *reinterpret_cast<uint4*>(&fw[r][8 * c]) = stg[u];
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- conv + silu; the window update (one writer per channel: v channels by their row owner,
+  // q/k channels spread over the ranks of the first value head that uses the k head)
+#pragma unroll
+  for (int it = 0; it < kConvIt; ++it) {
+    const int i = tid + it * kGfThreads;
+    if (i < kCh) {
+      const int part = i < kGfD ? 0 : i < 2 * kGfD ? 1 : 2;
+      const int j = part == 0 ? i : part == 1 ? i - kGfD : i - 2 * kGfD;
+      for (int t = 0; t < T; ++t) {
+        float acc = 0.f;
+#pragma unroll
+        for (int q = 0; q <= W; ++q) acc = fmaf(__bfloat162float(fw[t + q][i]), cw[it][q], acc);
+        const float sv = acc / (1.f + __expf(-acc));
+        if (part == 0) qs[t][j] = sv;
+        else if (part == 1) ks[t][j] = sv;
+        else vs[t][j] = bf16rf(sv);
+      }
+      const bool owner = part == 2 || ((h % rep) == 0 && (j / kGfRows) == static_cast<int>(rank));
+      if (owner) {
+        const int ch = chan(i);
+        if (p.conv_full)
+          for (int r = 0; r < W + T; ++r) p.conv_full[static_cast<size_t>(r) * C + ch] = fw[r][i];
+#pragma unroll
+        for (int r = 0; r < W; ++r) p.conv[static_cast<size_t>(r) * C + ch] = fw[T + r][i];  // last W rows
+      }
+    }
+  }
+  __syncthreads();
+  // ---- l2-normalised q (/ sqrt(128)) and k, bf16 (warp per token); gates
+  for (int t = warp; t < T; t += kGfThreads / 32) {
+    float qv[4], kv[4], sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      qv[u] = qs[t][lane + 32 * u];
+      kv[u] = ks[t][lane + 32 * u];
+      sq = fmaf(qv[u], qv[u], sq);
+      sk = fmaf(kv[u], kv[u], sk);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      sq += __shfl_xor_sync(0xFFFFFFFFu, sq, o);
+      sk += __shfl_xor_sync(0xFFFFFFFFu, sk, o);
+    }
+    const float nq = rsqrtf(static_cast<float>(kGfD)) / fmaxf(sqrtf(sq), 1e-12f);
+    const float nk = 1.f / fmaxf(sqrtf(sk), 1e-12f);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      qs[t][lane + 32 * u] = bf16rf(qv[u] * nq);
+      ks[t][lane + 32 * u] = bf16rf(kv[u] * nk);
+    }
+  }
+  if (tid < T) {
+    const float xa = ga + gdt;
+    const float sp = xa > 20.f ? xa : log1pf(expf(xa));
+    gs[tid] = expf(-expf(galog) * sp);
+    bs[tid] = 1.f / (1.f + expf(-gb));
+  }
+  __syncthreads();
+  // ---- recurrence: thread = (row, sub); columns sub + 8 i in registers.  Per token the three
+  // dot products a = S k, b = S q (of the previous state) and c = k q share one reduction round:
+  //   u = beta (v - g a),   S <- g S + u k^T,   y = S q = g b + u c.
+  for (int t = 0; t < T; ++t) {
+    const float gt = gs[t], bt = bs[t], vt = vs[t][row];
+    float kk[kGfCols];
+    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f, c0 = 0.f, c1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < kGfCols; i += 2) {
+      kk[i] = ks[t][sub + kGfTpr * i];
+      kk[i + 1] = ks[t][sub + kGfTpr * (i + 1)];
+      const float q0 = qs[t][sub + kGfTpr * i], q1 = qs[t][sub + kGfTpr * (i + 1)];
+      a0 = fmaf(S[i], kk[i], a0);
+      a1 = fmaf(S[i + 1], kk[i + 1], a1);
+      b0 = fmaf(S[i], q0, b0);
+      b1 = fmaf(S[i + 1], q1, b1);
+      c0 = fmaf(kk[i], q0, c0);
+      c1 = fmaf(kk[i + 1], q1, c1);
+    }
+    float a = a0 + a1, b = b0 + b1, c = c0 + c1;
+#pragma unroll
+    for (int o = 1; o < kGfTpr; o <<= 1) {
+      a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
+      b += __shfl_xor_sync(0xFFFFFFFFu, b, o);
+      c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
+    }
+    const float u = bt * (vt - gt * a);
+#pragma unroll
+    for (int i = 0; i < kGfCols; ++i) S[i] = fmaf(u, kk[i], gt * S[i]);
+    if (sub == 0) yl[t][row] = bf16rf(fmaf(gt, b, u * c));
+    if (p.ckpt && t + 1 < T) {
+      float* cp = p.ckpt + static_cast<size_t>(t) * p.Hv * kGfD * kGfD + srow;
+#pragma unroll
+      for (int i = 0; i < kGfCols; ++i) cp[kGfTpr * i] = S[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kGfCols; ++i) p.state[srow + kGfTpr * i] = S[i];
+  __syncthreads();
+  // ---- every rank receives the head's whole y: 16-byte asynchronous stores into each peer's
+  // shared memory, counted on the peer's mbarrier (no cluster-wide release of global stores)
+  cluster_wait();  // all peers have initialised their mbarriers
+  {
+    const uint32_t ybase = smem_u32(&yall[0][0]), ybl = smem_u32(&ybar);
+    for (int i = tid; i < T * (kGfRows / 4) * kGfRanks; i += kGfThreads) {
+      const int dst = i % kGfRanks, e = i / kGfRanks;
+      const int t = e / (kGfRows / 4), r4 = (e % (kGfRows / 4)) * 4;
+      const float4 v = *reinterpret_cast<const float4*>(&yl[t][r4]);
+      const uint32_t off = static_cast<uint32_t>((t * kGfD + r0 + r4) * 4);
+      st_async_v4(map_shared_rank(ybase + off, dst), v, map_shared_rank(ybl, dst));
+    }
+    if (tid == 0) mbar_arrive_expect_tx(ybl, static_cast<uint32_t>(T * kGfD * 4));
+    if (!mbar_wait(ybl, 0, p.err, kErrBitWaitCluster, &abort_flag)) return;
+  }
+  // ---- gated rmsnorm and digits: warp w of rank r takes token r + 8 (w / 2), column half w % 2
+  if (jt < mpad) {
+    float a0 = 0.f, a1 = 0.f;
+    if (jt < T) {
+      float ss = 0.f;
+#pragma unroll
+      for (int j = lane; j < kGfD; j += 32) ss = fmaf(yall[jt][j], yall[jt][j], ss);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+      const float rstd = rsqrtf(ss / kGfD + p.eps);
+      const float n0 = bf16rf(yall[jt][j0] * rstd * (1.f + nw0));
+      const float n1 = bf16rf(yall[jt][j0 + 1] * rstd * (1.f + nw1));
+      a0 = bf16rf(n0 * (z0 / (1.f + __expf(-z0))));
+      a1 = bf16rf(n1 * (z1 / (1.f + __expf(-z1))));
+      if (p.o_out) {
+        __nv_bfloat16* op = p.o_out + static_cast<size_t>(jt) * p.Hv * kGfD + h * kGfD + j0;
+        op[0] = __float2bfloat16_rn(a0);
+        op[1] = __float2bfloat16_rn(a1);
+      }
+    }
+    write_digits(p.xq, mpad, jt, 2 * h + jhalf, lane, a0, a1);
+  }
+}
+
+// Host-side mirror of the parameter block with untyped pointers (the C-ABI layer's view).
+struct GdnFusedParamsHost {
+  const void* proj;
+  int ldp;
+  void* conv;
+  void* conv_full;
+  const float* conv_w;
+  const float* A_log;
+  const float* dt_bias;
+  const float* norm_w;
+  float eps;
+  float* state;
+  float* ckpt;
+  void* xq;
+  void* o_out;
+  uint32_t* err;
+  int T, Hv, Hk, W;
+};
+
+template <int W>
+static cudaError_t launch_gdn_fused(const GdnFusedParams& prm, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(prm.Hv * kGfRanks);
+  cfg.blockDim = dim3(kGfThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kGfRanks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, gdn_fused_kernel<W>, prm);
+}
+
+cudaError_t gdn_fused_call(const GdnFusedParamsHost& h, cudaStream_t stream) {
+  GdnFusedParams prm{static_cast<const __nv_bfloat16*>(h.proj), h.ldp, static_cast<__nv_bfloat16*>(h.conv),
+                     static_cast<__nv_bfloat16*>(h.conv_full), h.conv_w, h.A_log, h.dt_bias, h.norm_w, h.eps,
+                     h.state, h.ckpt, static_cast<uint8_t*>(h.xq), static_cast<__nv_bfloat16*>(h.o_out),
+                     h.err, h.T, h.Hv, h.Hk};
+  switch (h.W) {
+    case 1: return launch_gdn_fused<1>(prm, stream);
+    case 2: return launch_gdn_fused<2>(prm, stream);
+    case 3: return launch_gdn_fused<3>(prm, stream);
+    case 4: return launch_gdn_fused<4>(prm, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace skinny

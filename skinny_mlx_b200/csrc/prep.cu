@@ -1,0 +1,169 @@
+// Producers of qmm inputs: each computes a bf16 activation row and writes it directly in the
+// x-prep block format the qmm kernel reads (qmm_layout.cuh), so that no separate x-prep launch
+// and no bf16 activation round trip sit between a step's elementwise work and its next matmul.
+//
+//   prep_rmsnorm : h = x (+ d)  [written to h_out as the next residual stream when d is given],
+//                  a = bf16( h / rms(h) * (1 + w) )            -> digits of a
+//   prep_swiglu  : a = bf16( silu(g) * u ) for gu = [g | u]     -> digits of a
+//   prep_plain   : a = x                                         -> digits of a
+//
+// Digits: per (token, 64-column group) v = rint(a 2^-e) with the smallest e such that
+// |v| <= 32639, v = 256 hi + lo (signed 8-bit), xs = 2^(e-4), xsum = 2^e sum v; tokens >= M of the
+// mpad rows are zero.  This is the same rule as the standalone x-prep kernel, so a prepared call
+// and an unprepared call on the same bf16 activations give bit-identical qmm results.
+//
+// Grid: (ceil(G / 8) column chunks, mpad token rows), 256 threads; warp w of chunk c handles
+// group 8c + w, lane l holds its columns 2l, 2l+1.  These launches sit on the latency-bound
+// critical path of a verify step (a few KB of work each), so the grid is wide and every load of a
+// thread is issued before the first one is used.  The RMSNorm needs the whole row: every chunk of
+// a row computes the row's sum of squares itself (the same fixed-order reduction in every chunk,
+// so all chunks use the same rstd), reading the row from L2 rather than waiting for a second
+// launch.  As a consequence h_out must not alias x or d: a chunk writes its columns of h_out
+// while other chunks of the row are still reading x and d.
+//
+// Launched with programmatic dependent launch: a CTA allows the next launch to start at once
+// (the next qmm then streams its weights during this kernel) and waits for the previous grid
+// before its first global read.
+#include <cfloat>
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "digits.cuh"
+#include "ptx.cuh"
+#include "qmm_layout.cuh"
+
+namespace skinny {
+
+constexpr int kPrepThreads = 256;
+constexpr int kPrepWarps = kPrepThreads / 32;
+
+__device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__device__ __forceinline__ float2 ld_bf2(const __nv_bfloat16* p) {
+  const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(p);
+  return make_float2(__low2float(v), __high2float(v));
+}
+
+// mode 0: rmsnorm (optional residual add), 1: swiglu, 2: plain.
+template <int MODE>
+__global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
+                                                            const __nv_bfloat16* __restrict__ d, int ldd,
+                                                            __nv_bfloat16* __restrict__ h_out, int ldh,
+                                                            const float* __restrict__ w, float eps, int K, int M,
+                                                            int mpad, uint8_t* __restrict__ xq,
+                                                            __nv_bfloat16* __restrict__ a_out) {
+  const int t = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = K / 64;
+  const int g = blockIdx.x * kPrepWarps + warp;
+  const bool live = t < M;
+  __shared__ float red[kPrepWarps];
+  pdl_launch_dependents();
+  pdl_wait_prior_grid();  // x, d (and the buffers written below) belong to earlier launches
+  const __nv_bfloat16* xr = x + static_cast<size_t>(t) * ldx;
+  const __nv_bfloat16* dr = d ? d + static_cast<size_t>(t) * ldd : nullptr;
+  float rstd = 1.f;
+  if (MODE == 0 && live) {
+    // row sum of squares of h = bf16(x + d): K/512 pairs per thread, loads batched by 4
+    float ss[4] = {0.f, 0.f, 0.f, 0.f};
+    const int npair = K / 2;
+    for (int base = tid; base < npair; base += 4 * kPrepThreads) {
+      float2 hv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = 2 * (base + u * kPrepThreads);
+        hv[u] = c < K ? ld_bf2(xr + c) : make_float2(0.f, 0.f);
+      }
+      if (dr) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = 2 * (base + u * kPrepThreads);
+          if (c < K) {
+            const float2 dv = ld_bf2(dr + c);
+            hv[u].x = bf16r(hv[u].x + dv.x);
+            hv[u].y = bf16r(hv[u].y + dv.y);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) ss[u] = fmaf(hv[u].x, hv[u].x, fmaf(hv[u].y, hv[u].y, ss[u]));
+    }
+    float s = (ss[0] + ss[1]) + (ss[2] + ss[3]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kPrepWarps; ++i) tot += red[i];  // fixed order, the same in every chunk
+    rstd = rsqrtf(tot / static_cast<float>(K) + eps);
+  }
+  if (g >= G) return;
+  const int c = g * 64 + 2 * lane;
+  float a0 = 0.f, a1 = 0.f;
+  if (live) {
+    if (MODE == 0) {
+      float2 hv = ld_bf2(xr + c);
+      if (dr) {
+        const float2 dv = ld_bf2(dr + c);
+        hv.x = bf16r(hv.x + dv.x);
+        hv.y = bf16r(hv.y + dv.y);
+        if (h_out)
+          *reinterpret_cast<__nv_bfloat162*>(h_out + static_cast<size_t>(t) * ldh + c) =
+              __floats2bfloat162_rn(hv.x, hv.y);
+      }
+      a0 = bf16r(hv.x * rstd * (1.f + w[c]));
+      a1 = bf16r(hv.y * rstd * (1.f + w[c + 1]));
+      if (a_out)
+        *reinterpret_cast<__nv_bfloat162*>(a_out + static_cast<size_t>(t) * K + c) = __floats2bfloat162_rn(a0, a1);
+    } else if (MODE == 1) {
+      const float2 gv = ld_bf2(xr + c), uv = ld_bf2(xr + K + c);
+      a0 = bf16r(gv.x / (1.f + __expf(-gv.x)) * uv.x);
+      a1 = bf16r(gv.y / (1.f + __expf(-gv.y)) * uv.y);
+    } else {
+      const float2 xv = ld_bf2(xr + c);
+      a0 = xv.x;
+      a1 = xv.y;
+    }
+  }
+  write_digits(xq, mpad, t, g, lane, a0, a1);
+}
+
+static cudaError_t launch_pdl(void (*kern)(const __nv_bfloat16*, int, const __nv_bfloat16*, int, __nv_bfloat16*,
+                                           int, const float*, float, int, int, int, uint8_t*, __nv_bfloat16*),
+                              dim3 grid, cudaStream_t stream, const __nv_bfloat16* x, int ldx,
+                              const __nv_bfloat16* d, int ldd, __nv_bfloat16* h, int ldh, const float* w,
+                              float eps, int K, int M, int mpad, uint8_t* xq, __nv_bfloat16* a_out) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kPrepThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, x, ldx, d, ldd, h, ldh, w, eps, K, M, mpad, xq, a_out);
+}
+
+cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd, void* h_out, int ldh,
+                        const float* w, float eps, int K, int M, void* xq, void* a_out, cudaStream_t stream) {
+  const int mpad = M <= 8 ? 8 : 16;
+  const int G = K / 64;
+  const dim3 grid((G + kPrepWarps - 1) / kPrepWarps, mpad);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  auto* q = static_cast<uint8_t*>(xq);
+  if (mode == 0)
+    return launch_pdl(prep_kernel<0>, grid, stream, xb, ldx, static_cast<const __nv_bfloat16*>(d), ldd,
+                      static_cast<__nv_bfloat16*>(h_out), ldh, w, eps, K, M, mpad, q,
+                      static_cast<__nv_bfloat16*>(a_out));
+  if (mode == 1)
+    return launch_pdl(prep_kernel<1>, grid, stream, xb, ldx, nullptr, 0, nullptr, 0, nullptr, 0.f, K, M, mpad, q,
+                      nullptr);
+  return launch_pdl(prep_kernel<2>, grid, stream, xb, ldx, nullptr, 0, nullptr, 0, nullptr, 0.f, K, M, mpad, q,
+                    nullptr);
+}
+
+}  // namespace skinny

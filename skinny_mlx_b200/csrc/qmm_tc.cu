@@ -52,6 +52,7 @@
 //                   and accumulates in f32 registers; at each tile end the two lanes' sums are
 //                   added in a fixed order and the tile is written or its partial published.
 //   warp 3          allocation helper only.
+#include <algorithm>
 #include <cfloat>
 #include <cstdint>
 #include <cuda.h>
@@ -114,6 +115,7 @@ struct QmmParams {
   const uint8_t* xq;    // x-prep blocks (workspace)
   int M, C, n_mats;
   int U;                // total units
+  int split;            // 0: stream-K over all units; S >= 1: one matrix, S CTAs (a cluster) per tile
   QmmMat mats[kMaxMats];
 };
 
@@ -320,8 +322,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int c = blockIdx.x;
-  const int u0 = static_cast<int>(u_begin(c, p.U, p.C));
-  const int u1 = static_cast<int>(u_begin(c + 1, p.U, p.C));
+  int u0, u1;
+  if (p.split > 0) {  // tile c / S, K slice c % S (the CTA's rank in its cluster)
+    const int S = p.split, tile = c / S, rk = c - tile * S, G = p.mats[0].G;
+    u0 = tile * G + (rk * G) / S;
+    u1 = tile * G + ((rk + 1) * G) / S;
+  } else {
+    u0 = static_cast<int>(u_begin(c, p.U, p.C));
+    u1 = static_cast<int>(u_begin(c + 1, p.U, p.C));
+  }
   volatile int* abort_flag = &sb->abort_flag;
 
   if (threadIdx.x == 0) {
@@ -598,6 +607,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float o = xb[t * kTileRows + r];
             acc[t] = L == 0 ? acc[t] + o : o + acc[t];
           }
+          if (p.split > 1) {
+            // cluster split: the slice's sum stays in shared memory; rank 0 adds the ranks' sums
+            // after the cluster barrier at the end of the kernel
+#pragma unroll
+            for (int t = 0; t < NT; ++t) xb[t * kTileRows + r] = acc[t];
+          } else {
           const QmmMat& mt = p.mats[wk.mi];                     // read once per tile segment
           const int tile_u0 = mt.unit_off + wk.lt * mt.G;        // the tile's first global unit
           const int tile = mt.tile_off + wk.lt;                  // global tile (counter index)
@@ -652,6 +667,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             named_bar_sync(bar, kEpiThreads);
           }
+          }  // stream-K / whole tile
         }
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[t] = 0.f;
@@ -666,6 +682,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+  if (p.split > 1) {
+    // Cluster split-K: every rank's slice sum is in its exchange buffer (slot 0).  Rank 0's
+    // epilogue threads add them in rank order over distributed shared memory and write the tile;
+    // the second barrier keeps the peers' shared memory alive until then.
+    cluster_arrive_release();
+    cluster_wait_acquire();
+    const int S = p.split;
+    if (cluster_ctarank() == 0 && warp >= kEpiWarp0) {
+      const QmmMat& mt = p.mats[0];
+      const int tile = c / S;
+      const uint32_t xloc = smem_u32(reinterpret_cast<float*>(sb + 1));
+      pdl_wait_prior_grid();  // outputs may alias buffers an earlier kernel still reads
+      const bool live = !*abort_flag;
+      for (int idx = threadIdx.x - kEpiWarp0 * 32; idx < NT * kTileRows; idx += 2 * kEpiThreads) {
+        const int t = idx / kTileRows, row_g = tile * kTileRows + (idx - t * kTileRows);
+        float v = 0.f;
+        for (int q = 0; q < S; ++q) v += ld_cluster_f32(map_shared_rank(xloc + idx * 4, q));
+        if (live && t < p.M && row_g < mt.N) mt.out[static_cast<size_t>(t) * mt.ldo + row_g] = __float2bfloat16_rn(v);
+      }
+    }
+    cluster_arrive_relaxed();
+    cluster_wait_acquire();
   }
 }
 
@@ -768,24 +807,92 @@ static void pdl_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, bool 
 }
 
 template <int NT>
-static cudaError_t launch_tc(const QmmParams& prm, int dev, cudaStream_t stream, bool pdl) {
+static cudaError_t set_smem_attr(int dev) {
   constexpr int slot = NT == 2 ? 0 : NT == 4 ? 1 : NT == 8 ? 2 : 3;
-  constexpr size_t smem = qmm_smem_bytes(NT);
   if (dev >= 0 && dev < 64 && !g_attr_set[dev][slot]) {
     cudaError_t e = cudaFuncSetAttribute(qmm_w4g64_tc_kernel<NT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+                                         static_cast<int>(qmm_smem_bytes(NT)));
     if (e != cudaSuccess) return e;
     g_attr_set[dev][slot] = true;
   }
+  return cudaSuccess;
+}
+
+template <int NT>
+static cudaError_t launch_tc(const QmmParams& prm, int dev, cudaStream_t stream, bool pdl) {
+  const cudaError_t e = set_smem_attr<NT>(dev);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(prm.C);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = qmm_smem_bytes(NT);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   pdl_config(cfg, attr, pdl);
+  if (prm.split > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(prm.split);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   return cudaLaunchKernelEx(&cfg, qmm_w4g64_tc_kernel<NT>, prm);
+}
+
+// Clusters of S CTAs of the qmm kernel that can be resident at once on device `dev`: the
+// minimum over the four token-count variants, so that the split chosen from it is the same for
+// every M (the per-token results stay independent of M).  Cached per (device, S).
+static int g_max_clusters[64][9] = {};
+
+template <int NT>
+static int clusters_of(int S) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(S);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = qmm_smem_bytes(NT);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(S);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, qmm_w4g64_tc_kernel<NT>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+static int max_active_clusters(int dev, int S) {
+  if (dev < 0 || dev >= 64 || S < 2 || S > 8) return 0;
+  if (g_max_clusters[dev][S] == 0) {
+    if (set_smem_attr<2>(dev) != cudaSuccess || set_smem_attr<4>(dev) != cudaSuccess ||
+        set_smem_attr<8>(dev) != cudaSuccess || set_smem_attr<16>(dev) != cudaSuccess)
+      return 0;
+    int n = clusters_of<2>(S);
+    n = std::min(n, clusters_of<4>(S));
+    n = std::min(n, clusters_of<8>(S));
+    n = std::min(n, clusters_of<16>(S));
+    g_max_clusters[dev][S] = n > 0 ? n : -1;
+  }
+  return g_max_clusters[dev][S];
+}
+
+// Work split of a single-matrix call with `tiles` 128-row tiles of G groups on C CTAs.
+//   0      stream-K over all units (tiles >= C: every CTA streams whole tiles plus at most two
+//          partial ones; the split-K fix-up through global memory is paid a few times)
+//   S >= 1 S CTAs per tile, each a contiguous K slice; S > 1 CTAs form a cluster and rank 0 adds
+//          the slices over distributed shared memory (no global partials, atomics or fences).
+//          S is the largest split (<= 8) whose clusters are all resident at once.
+static int choose_split(int dev, int tiles, int G, int C) {
+  if (tiles >= C) return 0;
+  int S = std::min(std::min(C / tiles, 8), G);
+  for (; S > 1; --S)
+    if (max_active_clusters(dev, S) >= tiles) return S;
+  return 1;
 }
 
 static cudaError_t launch_xprep(const XPrepParams& xp, cudaStream_t stream, bool pdl) {
@@ -857,8 +964,46 @@ static cudaError_t launch_grouped_on(int n, const void* const* x, const int* ldx
   xp.total_groups = groups;
   prm.U = static_cast<int>(U);
   prm.C = static_cast<int>(U < C_cap ? U : C_cap);
+  prm.split = n == 1 ? choose_split(dev, static_cast<int>(T), prm.mats[0].G, C_cap) : 0;
+  if (prm.split > 0) prm.C = static_cast<int>(T) * prm.split;
   cudaError_t e = launch_xprep(xp, stream, pdl);
   if (e != cudaSuccess) return e;
+  if (M <= 2) return launch_tc<2>(prm, dev, stream, true);
+  if (M <= 4) return launch_tc<4>(prm, dev, stream, true);
+  if (M <= 8) return launch_tc<8>(prm, dev, stream, true);
+  return launch_tc<16>(prm, dev, stream, true);
+}
+
+// One matrix whose input was already written in the x-prep block format by a producer kernel
+// (prep.cu): no x-prep launch.  xq holds K/64 blocks for mpad(M) token rows.
+cudaError_t qmm_tc_launch_prepared(const void* xq, const void* w_tc, void* out, int ldo, int M, int N, int K,
+                                   void* ws, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int C_dev = device_sm_count(dev);
+  const WsLayout wl = ws_layout(C_dev);
+  uint8_t* wsb = static_cast<uint8_t*>(ws);
+  static thread_local QmmParams prm;
+  const QmmShape sh = qmm_shape(N, K);
+  prm.part = reinterpret_cast<float*>(wsb + wl.part_off);
+  prm.cnt = reinterpret_cast<uint32_t*>(wsb + wl.cnt_off);
+  prm.err = reinterpret_cast<uint32_t*>(wsb);
+  prm.xq = static_cast<const uint8_t*>(xq);
+  prm.M = M;
+  prm.n_mats = 1;
+  QmmMat& mt = prm.mats[0];
+  mt.w_tc = static_cast<const uint8_t*>(w_tc);
+  mt.out = static_cast<__nv_bfloat16*>(out);
+  mt.unit_off = 0;
+  mt.N = N;
+  mt.G = sh.G;
+  mt.tile_off = 0;
+  mt.xg_off = 0;
+  mt.ldo = ldo;
+  prm.U = static_cast<int>(sh.U);
+  prm.C = static_cast<int>(sh.U < C_dev ? sh.U : C_dev);
+  prm.split = choose_split(dev, static_cast<int>(sh.T), sh.G, C_dev);
+  if (prm.split > 0) prm.C = static_cast<int>(sh.T) * prm.split;
   if (M <= 2) return launch_tc<2>(prm, dev, stream, true);
   if (M <= 4) return launch_tc<4>(prm, dev, stream, true);
   if (M <= 8) return launch_tc<8>(prm, dev, stream, true);

@@ -1,0 +1,186 @@
+"""Fused verify step of a patched hybrid model (the B200 runtime for config 3 and 4).
+
+The module-by-module forward of `HybridModel` runs every small elementwise step as its own
+PyTorch kernel (dozens per layer).  `FusedStep` runs the same model with five kernel kinds and
+no intermediate activation round trips:
+
+    prep (residual add + RMSNorm -> qmm input digits)                  skinny_prep mode 0
+    qmm on prepared digits                                              skinny_qmm_w4g64_prepared
+    GDN mixer (conv .. gated norm -> out_proj digits)                   skinny_gdn_fused
+    attention mixer (norm, RoPE, KV append .. gate -> o_proj digits)    skinny_attn_fused
+    prep (SwiGLU -> down_proj digits)                                   skinny_prep mode 1
+
+Residual additions are deferred into the next prep.  The result equals the
+module-by-module patched forward up to the rounding of the fused reductions (norms, softplus,
+silu in f32), and the caches (`Cache`) are the same objects, so `HybridRollback` and the
+speculative loop work unchanged.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .model import AttnCache, GDNCache, HybridModel
+from .qmm import SkinnyWeight, get_workspace
+from .qmm import dequantize
+
+
+def _p(t) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+class FusedStep:
+    def __init__(self, model: HybridModel):
+        from .patch import FusedSliceLinear, SkinnyQuantizedLinear
+
+        self.model, self.cfg = model, model.cfg
+        emb = model.embed_tokens
+        if not hasattr(emb, "skinny_head"):
+            raise ValueError("FusedStep needs a patched model (skinny_mlx_b200.patch.patch_model)")
+        self.head = emb.skinny_head
+        self.layers = []
+        for layer in model.layers:
+            mlp = layer.mlp
+            assert isinstance(mlp.gate_proj, FusedSliceLinear) and isinstance(mlp.down_proj, SkinnyQuantizedLinear)
+            ent = {"gate_up": mlp.gate_proj._group.rw, "down": mlp.down_proj.rweight,
+                   "in_norm": layer.input_layernorm.weight, "post_norm": layer.post_attention_layernorm.weight}
+            if layer.is_linear:
+                g = layer.linear_attn
+                ent.update(kind="gdn", mod=g, proj=g.in_proj_qkv._group.rw, out=g.out_proj.rweight,
+                           conv_w=g.conv_weight.float().contiguous(), A_log=g.A_log.float().contiguous(),
+                           dt_bias=g.dt_bias.float().contiguous(), norm_w=g.norm.weight.float().contiguous())
+            else:
+                a = layer.self_attn
+                (q0, q1), (k0, k1), (v0, v1) = a.q_proj._group.bounds
+                D = self.cfg.head_dim
+                assert D == 128 and (q0, k0, v0) == (0, 2 * self.cfg.n_heads * D, 2 * self.cfg.n_heads * D
+                                                     + self.cfg.n_kv_heads * D), "q|gate, k, v fused in order"
+                half = self.cfg.rotary_dim // 2
+                dev = a.q_norm.weight.device
+                inv = self.cfg.rope_theta ** (-torch.arange(0, half, device=dev, dtype=torch.float32) / half)
+                ent.update(kind="attn", mod=a, proj=a.q_proj._group.rw, out=a.o_proj.rweight,
+                           qn=a.q_norm.weight.float().contiguous(), kn=a.k_norm.weight.float().contiguous(),
+                           inv=inv.contiguous())
+            self.layers.append(ent)
+        self.final_norm = model.norm.weight
+        self._bufs: dict[int, dict] = {}
+        self._attn_ws: dict[int, torch.Tensor] = {}
+
+    @property
+    def device(self):
+        return self.model.device
+
+    def make_cache(self, *a, **k):
+        return self.model.make_cache(*a, **k)
+
+    @property
+    def embed_tokens(self):
+        return self.model.embed_tokens
+
+    # ---------------------------------------------------------------- buffers per token count
+    def _buffers(self, m: int) -> dict:
+        b = self._bufs.get(m)
+        if b is None:
+            cfg, dev = self.cfg, self.model.device
+            L = _lib.lib()
+            xq = lambda k: torch.empty(int(L.skinny_xq_bytes(m, k)), dtype=torch.uint8, device=dev)
+            widths = {self.layers[i]["proj"].N for i in range(len(self.layers))}
+            b = {"h": [torch.empty(m, cfg.hidden, dtype=torch.bfloat16, device=dev) for _ in range(2)],
+                 "a": torch.empty(m, cfg.hidden, dtype=torch.bfloat16, device=dev),
+                 "xq_h": xq(cfg.hidden), "xq_i": xq(cfg.intermediate),
+                 "xq_o": xq(max(cfg.gdn_value_dim, cfg.n_heads * cfg.head_dim)),
+                 "proj": {n: torch.empty(m, n, dtype=torch.bfloat16, device=dev) for n in widths},
+                 "mix": torch.empty(m, cfg.hidden, dtype=torch.bfloat16, device=dev),
+                 "gu": torch.empty(m, 2 * cfg.intermediate, dtype=torch.bfloat16, device=dev),
+                 "down": torch.empty(m, cfg.hidden, dtype=torch.bfloat16, device=dev),
+                 "logits": torch.empty(m, self.head.N, dtype=torch.bfloat16, device=dev)}
+            self._bufs[m] = b
+        return b
+
+    @staticmethod
+    def _err_word(dev) -> torch.Tensor:
+        """Word 0 of the device's qmm workspace: device-side errors of every kernel of the step
+        land in one place (skinny_mlx_b200.qmm.device_errors reads it)."""
+        return get_workspace(dev, int(_lib.lib().skinny_qmm_workspace_bytes(128, 64)))
+
+    def _attention(self, ent, proj, c: AttnCache, m: int, xq, stream):
+        cfg = self.cfg
+        max_len = c.k.shape[0]
+        ws = self._attn_ws.get(max_len)
+        if ws is None:  # sized for 16 tokens; zero on first use, left zero by every call
+            n = int(_lib.lib().skinny_attn_workspace_bytes(16, cfg.n_heads, cfg.n_kv_heads, max_len))
+            ws = self._attn_ws[max_len] = torch.zeros(n, dtype=torch.uint8, device=proj.device)
+        L0 = c.length
+        _lib.call("skinny_attn_fused", _p(proj), proj.stride(0), _p(ent["qn"]), _p(ent["kn"]), _p(ent["inv"]),
+                  cfg.rotary_dim, cfg.rms_eps, _p(c.k), _p(c.v), L0, m, cfg.n_heads, cfg.n_kv_heads, max_len,
+                  _p(ws), ws.numel(), _p(xq), None, stream)
+        c.length = L0 + m
+
+    def _qmm(self, xq, w: SkinnyWeight, out, m: int, stream):
+        ws = get_workspace(out.device, int(_lib.lib().skinny_qmm_workspace_bytes(w.N, w.K)))
+        _lib.call("skinny_qmm_w4g64_prepared", _p(xq), _p(w.w_tc), _p(out), out.stride(0), m, w.N, w.K,
+                  _p(ws), ws.numel(), stream)
+
+    def _prep(self, mode, x, m, k, xq, stream, d=None, h_out=None, w=None, a_out=None):
+        _lib.call("skinny_prep", mode, _p(x), x.stride(0), _p(d), d.stride(0) if d is not None else 0,
+                  _p(h_out), h_out.stride(0) if h_out is not None else 0, _p(w), self.cfg.rms_eps, m, k,
+                  _p(xq), _p(a_out), stream)
+
+    # ---------------------------------------------------------------- the step
+    @torch.no_grad()
+    def __call__(self, ids: torch.Tensor, cache) -> tuple[torch.Tensor, torch.Tensor]:
+        """Same contract as HybridModel.forward for 1 <= len(ids) <= 16: (final normed hidden,
+        logits) as bf16 [T, H] and [T, V] (views of reused buffers: copy to keep)."""
+        cfg, m = self.cfg, ids.shape[0]
+        if m > 16:  # prefill: the module-by-module forward (qmm in 16-token chunks)
+            return self.model(ids, cache)
+        b = self._buffers(m)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.model.device).cuda_stream)
+        emb = self.model.embed_tokens
+        # the residual stream alternates between two buffers: a prep reads one and writes the other
+        hs = b["h"]
+        cur = 0
+        hs[0].copy_(dequantize(emb.weight[ids], emb.scales[ids], emb.biases[ids]).to(torch.bfloat16))
+        d = None
+
+        def add_norm(d, w, a_out=None):
+            nonlocal cur
+            if d is None:
+                self._prep(0, hs[cur], m, cfg.hidden, b["xq_h"], stream, w=w, a_out=a_out)
+            else:
+                self._prep(0, hs[cur], m, cfg.hidden, b["xq_h"], stream, d=d, h_out=hs[1 - cur], w=w, a_out=a_out)
+                cur = 1 - cur
+
+        for ent, c in zip(self.layers, cache.layers):
+            # x_l = x_{l-1} + down_{l-1}; digits of input_layernorm(x_l)
+            add_norm(d, ent["in_norm"])
+            proj = b["proj"][ent["proj"].N]
+            self._qmm(b["xq_h"], ent["proj"], proj, m, stream)
+            if ent["kind"] == "gdn":
+                c: GDNCache
+                rec = c.recording
+                if rec:
+                    c.fed = m
+                _lib.call("skinny_gdn_fused", _p(proj), proj.stride(0), _p(c.conv),
+                          _p(c.conv_full if rec else None), _p(ent["conv_w"]), _p(ent["A_log"]), _p(ent["dt_bias"]),
+                          _p(ent["norm_w"]), cfg.rms_eps, _p(c.state), _p(c.ckpt if rec and m > 1 else None),
+                          _p(b["xq_o"]), None, m, cfg.gdn_v_heads, cfg.gdn_k_heads, cfg.conv_kernel - 1,
+                          _p(self._err_word(proj.device)), stream)
+            else:
+                self._attention(ent, proj, c, m, b["xq_o"], stream)
+            self._qmm(b["xq_o"], ent["out"], b["mix"], m, stream)
+            # h = x_l + mixer; digits of post_attention_layernorm(h)
+            add_norm(b["mix"], ent["post_norm"])
+            self._qmm(b["xq_h"], ent["gate_up"], b["gu"], m, stream)
+            self._prep(1, b["gu"], m, cfg.intermediate, b["xq_i"], stream)
+            self._qmm(b["xq_i"], ent["down"], b["down"], m, stream)
+            d = b["down"]
+        add_norm(d, self.final_norm, a_out=b["a"])
+        self._qmm(b["xq_h"], self.head, b["logits"], m, stream)
+        return b["a"], b["logits"]
+
+
+__all__ = ["FusedStep"]

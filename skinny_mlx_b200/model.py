@@ -231,13 +231,18 @@ class Attention(nn.Module):
         self.k_norm = RMSNorm(D, cfg.rms_eps)
 
     def forward(self, x: torch.Tensor, cache: AttnCache) -> torch.Tensor:
+        return self.o_proj(self.attend(self.q_proj(x), self.k_proj(x), self.v_proj(x), cache))
+
+    def attend(self, qg: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cache: AttnCache) -> torch.Tensor:
+        """Everything between the projections and o_proj: q/k norm, partial RoPE, KV append,
+        causal GQA attention over the cache, output gate.  Returns o bf16 [T, n_heads * D]."""
         cfg = self.cfg
-        T, D, nh, nkv = x.shape[0], cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
-        qg = self.q_proj(x).reshape(T, nh, 2 * D)
+        T, D, nh, nkv = qg.shape[0], cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
+        qg = qg.reshape(T, nh, 2 * D)
         q, gate = qg[..., :D], qg[..., D:]
-        k = self.k_proj(x).reshape(T, nkv, D)
-        v = self.v_proj(x).reshape(T, nkv, D)
-        pos = torch.arange(cache.length, cache.length + T, device=x.device)
+        k = k.reshape(T, nkv, D)
+        v = v.reshape(T, nkv, D)
+        pos = torch.arange(cache.length, cache.length + T, device=qg.device)
         q = _rope(self.q_norm(q).float(), pos, cfg.rotary_dim, cfg.rope_theta)
         k = _rope(self.k_norm(k).float(), pos, cfg.rotary_dim, cfg.rope_theta)
         L0 = cache.length
@@ -245,12 +250,12 @@ class Attention(nn.Module):
         cache.v[L0:L0 + T] = v
         cache.length = L0 + T
         # queries sit at positions L0 .. L0+T-1 after L0 cached keys: bottom-right causal mask
-        causal = pos[:, None] >= torch.arange(L0 + T, device=x.device)[None, :]
+        causal = pos[:, None] >= torch.arange(L0 + T, device=qg.device)[None, :]
         o = F.scaled_dot_product_attention(
             q.to(torch.bfloat16).transpose(0, 1)[None], cache.k[:L0 + T].transpose(0, 1)[None],
             cache.v[:L0 + T].transpose(0, 1)[None], attn_mask=causal, enable_gqa=True)[0].transpose(0, 1)
         o = o.float() * torch.sigmoid(gate.float())
-        return self.o_proj(o.reshape(T, nh * D).to(torch.bfloat16))
+        return o.reshape(T, nh * D).to(torch.bfloat16)
 
 
 class GatedDeltaNet(nn.Module):
@@ -271,12 +276,17 @@ class GatedDeltaNet(nn.Module):
         self.out_proj = _qlinear(H, cfg.gdn_value_dim, gen, std, dev)
 
     def forward(self, x: torch.Tensor, cache: GDNCache) -> torch.Tensor:
+        return self.out_proj(self.mix(self.in_proj_qkv(x), self.in_proj_z(x), self.in_proj_b(x),
+                                      self.in_proj_a(x), cache))
+
+    def mix(self, qkv, z, b, a, cache: GDNCache) -> torch.Tensor:
+        """Everything between the input projections and out_proj (conv, gates, recurrence, gated
+        norm).  Returns o bf16 [T, value_dim]."""
         cfg = self.cfg
-        T, W, dk = x.shape[0], cfg.conv_kernel - 1, cfg.gdn_dim
-        qkv = self.in_proj_qkv(x)
-        z = self.in_proj_z(x).reshape(T, cfg.gdn_v_heads, dk)
-        b = self.in_proj_b(x).float()
-        a = self.in_proj_a(x).float()
+        T, W, dk = qkv.shape[0], cfg.conv_kernel - 1, cfg.gdn_dim
+        z = z.reshape(T, cfg.gdn_v_heads, dk)
+        b = b.float()
+        a = a.float()
         full = torch.cat([cache.conv, qkv], dim=0)                     # [W + T, C]
         if cache.recording:
             cache.conv_full[:W + T] = full
@@ -292,7 +302,7 @@ class GatedDeltaNet(nn.Module):
         g = torch.exp(-torch.exp(self.A_log.float()) * F.softplus(a + self.dt_bias.float()))
         beta = torch.sigmoid(b)
         qb, kb, vb = (t.to(torch.bfloat16).contiguous() for t in (q, k, v))
-        if x.is_cuda:  # the CUDA path always runs the kernel; CPU runs (tests) use torch
+        if qkv.is_cuda:  # the CUDA path always runs the kernel; CPU runs (tests) use torch
             from .gdn import recurrent
 
             y = recurrent(qb, kb, vb, g.contiguous(), beta.contiguous(), cache.state,
@@ -300,7 +310,7 @@ class GatedDeltaNet(nn.Module):
         else:
             y = _recurrent_torch(qb, kb, vb, g, beta, cache)
         o = self.norm(y).float() * F.silu(z.float())
-        return self.out_proj(o.reshape(T, cfg.gdn_value_dim).to(torch.bfloat16))
+        return o.reshape(T, cfg.gdn_value_dim).to(torch.bfloat16)
 
 
 def _recurrent_torch(q, k, v, g, beta, cache: GDNCache) -> torch.Tensor:

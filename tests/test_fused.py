@@ -1,0 +1,193 @@
+"""Fused step kernels (prep producers, prepared qmm, fused GDN mixer) and the fused verify step
+against the module-by-module path and the oracle."""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant
+from skinny_mlx_b200.model import SMALL, HybridModel
+
+pytestmark = pytest.mark.gpu
+PROMPT = [int(x) for x in np.random.default_rng(5).integers(0, SMALL.vocab, 24)]
+
+
+def _p(t):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _bf16(a, dev):
+    return torch.from_numpy(quant.f32_to_bf16_bits(np.asarray(a, np.float32)).view(np.int16)).view(torch.bfloat16).to(dev)
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("m", [1, 5, 8, 13])
+def test_prep_plain_is_the_xprep_format(cuda_lib, dev, m):
+    rng = np.random.default_rng(m)
+    x = quant.round_bf16(rng.standard_normal((m, 640)).astype(np.float32) * 3)
+    x[0, 64:128] = 0
+    xq = torch.zeros(int(cuda_lib.skinny_xq_bytes(m, 640)), dtype=torch.uint8, device=dev)
+    xt = _bf16(x, dev)
+    assert cuda_lib.skinny_prep(2, _p(xt), 640, None, 0, None, 0, None, ctypes.c_float(0), m, 640, _p(xq),
+                                None, _stream()) == 0
+    mpad = 8 if m <= 8 else 16
+    assert np.array_equal(xq.cpu().numpy().reshape(10, -1), quant.xq_blocks(x, mpad))
+
+
+@pytest.mark.parametrize("m", [1, 8, 16])
+def test_prep_norm_and_swiglu_feed_the_prepared_qmm(cuda_lib, dev, m):
+    from skinny_mlx_b200.qmm import get_workspace, quantize, repack_for_skinny, skinny_qmm
+
+    torch.manual_seed(m)
+    K, N = 1024, 768
+    w = repack_for_skinny(*quantize(torch.randn(N, K, device=dev) * 0.02))
+    ws = get_workspace(dev, int(cuda_lib.skinny_qmm_workspace_bytes(N, K)))
+    x = torch.randn(m, K, device=dev).to(torch.bfloat16)
+    d = torch.randn(m, K, device=dev).to(torch.bfloat16)
+    gw = torch.randn(K, device=dev) * 0.1
+    xq = torch.empty(int(cuda_lib.skinny_xq_bytes(m, K)), dtype=torch.uint8, device=dev)
+    h = torch.empty_like(x)
+    a = torch.empty(m, K, dtype=torch.bfloat16, device=dev)
+    # outputs overlapping the inputs are refused (chunks of a row are written while others read it)
+    assert cuda_lib.skinny_prep(0, _p(x), K, _p(d), K, _p(x), K, _p(gw), ctypes.c_float(1e-6), m, K, _p(xq),
+                                _p(a), _stream()) == -1
+    assert cuda_lib.skinny_prep(0, _p(x), K, _p(d), K, _p(h), K, _p(gw), ctypes.c_float(1e-6), m, K, _p(xq),
+                                _p(d), _stream()) == -1
+    assert cuda_lib.skinny_prep(0, _p(x), K, _p(d), K, _p(h), K, _p(gw), ctypes.c_float(1e-6), m, K, _p(xq),
+                                _p(a), _stream()) == 0
+    y = torch.empty(m, N, dtype=torch.bfloat16, device=dev)
+    assert cuda_lib.skinny_qmm_w4g64_prepared(_p(xq), _p(w.w_tc), _p(y), N, m, N, K, _p(ws), ws.numel(), _stream()) == 0
+    href = (x.float() + d.float()).to(torch.bfloat16)
+    assert torch.equal(h, href)
+    hf = href.float()
+    aref = (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-6) * (1 + gw)).to(torch.bfloat16)
+    assert (a.float() - aref.float()).abs().max().item() <= 2 ** -7 * aref.float().abs().max().item()
+    yref = skinny_qmm(a, w)  # same activation through the unprepared path: bit-identical
+    assert torch.equal(y, yref)
+    # SwiGLU
+    gu = torch.randn(m, 2 * K, device=dev).to(torch.bfloat16)
+    assert cuda_lib.skinny_prep(1, _p(gu), 2 * K, None, 0, None, 0, None, ctypes.c_float(0), m, K, _p(xq), None,
+                                _stream()) == 0
+    assert cuda_lib.skinny_qmm_w4g64_prepared(_p(xq), _p(w.w_tc), _p(y), N, m, N, K, _p(ws), ws.numel(), _stream()) == 0
+    sref = (torch.nn.functional.silu(gu[:, :K].float()) * gu[:, K:].float()).to(torch.bfloat16)
+    yref = skinny_qmm(sref, w).float()
+    assert ((y.float() - yref).abs().max() / yref.abs().max()).item() <= 1e-2
+
+
+@pytest.mark.parametrize("T", [1, 4, 8, 16])
+def test_gdn_fused_matches_module_mixer(cuda_lib, dev, T):
+    from skinny_mlx_b200.model import GDNCache
+
+    m = HybridModel(SMALL, seed=0, device=dev)
+    g = m.layers[0].linear_attn
+    cfg = SMALL
+    torch.manual_seed(T)
+    proj = (torch.randn(T, 3 * cfg.gdn_value_dim + cfg.gdn_value_dim + 2 * cfg.gdn_v_heads, device=dev) * 0.5).to(torch.bfloat16)
+    C = 3 * cfg.gdn_value_dim
+    ca, cb = GDNCache(cfg, 17, dev), GDNCache(cfg, 17, dev)
+    for c in (ca, cb):
+        c.conv.copy_((torch.randn_like(c.conv.float()) * 0.5).to(torch.bfloat16))
+        c.state.normal_().mul_(0.1)
+        c.recording = True
+    cb.conv.copy_(ca.conv)
+    cb.state.copy_(ca.state)
+    Hv = cfg.gdn_v_heads
+    ref = g.mix(proj[:, :C], proj[:, C:C + cfg.gdn_value_dim], proj[:, C + cfg.gdn_value_dim:C + cfg.gdn_value_dim + Hv],
+                proj[:, C + cfg.gdn_value_dim + Hv:], ca)
+    xq = torch.empty(int(cuda_lib.skinny_xq_bytes(T, cfg.gdn_value_dim)), dtype=torch.uint8, device=dev)
+    o = torch.empty(T, cfg.gdn_value_dim, dtype=torch.bfloat16, device=dev)
+    errw = torch.zeros(1, dtype=torch.int32, device=dev)
+    st = cuda_lib.skinny_gdn_fused(_p(proj), proj.stride(0), _p(cb.conv), _p(cb.conv_full), _p(g.conv_weight.float().contiguous()),
+                                   _p(g.A_log), _p(g.dt_bias), _p(g.norm.weight), ctypes.c_float(cfg.rms_eps),
+                                   _p(cb.state), _p(cb.ckpt), _p(xq), _p(o), T, Hv, cfg.gdn_k_heads, cfg.conv_kernel - 1,
+                                   _p(errw), _stream())
+    assert st == 0
+    torch.cuda.synchronize()
+    assert int(errw.item()) == 0
+    rel = lambda a, b: ((a.float() - b.float()).abs().max() / b.float().abs().max()).item()
+    assert rel(o, ref) <= 2e-2, rel(o, ref)
+    assert rel(cb.state, ca.state) <= 1e-2
+    assert torch.equal(cb.conv, ca.conv)
+    assert torch.equal(cb.conv_full[:3 + T], ca.conv_full[:3 + T])
+    if T > 1:
+        assert rel(cb.ckpt[:T - 1], ca.ckpt[:T - 1]) <= 1e-2
+
+
+def test_fused_step_matches_patched_model_and_keeps_spec_exact(cuda_lib, dev):
+    from skinny_mlx_b200.fused import FusedStep
+    from skinny_mlx_b200.patch import patch_model
+    from skinny_mlx_b200.spec import greedy, speculative
+    from test_model_patch import ReplayDrafter, _exact_or_near_tie
+
+    m = HybridModel(SMALL, seed=0, device=dev)
+    patch_model(m)
+    f = FusedStep(m)
+    ids = torch.tensor(PROMPT[:16], device=dev)
+    x = torch.tensor(PROMPT[16:24], device=dev)
+    ca, cb = m.make_cache(), m.make_cache()
+    m(ids, ca)
+    m(ids, cb)
+    ref = m(x, ca)[1].float()
+    got = f(x, cb)[1].float()
+    assert ((ref - got).abs().max() / ref.abs().max()).item() <= 1.5e-2
+    gaps = []
+    gref = greedy(f, PROMPT, 24, gaps)
+    d = ReplayDrafter(gref)
+    d.device = dev
+    st = {}
+    assert _exact_or_near_tie(gref, speculative(f, PROMPT, 24, d, 3, st), gaps)
+    assert st["accepted"] > 0
+
+
+@pytest.mark.parametrize("T,L0", [(1, 0), (1, 300), (5, 37), (8, 129), (16, 0), (16, 250)])
+def test_attn_fused_matches_module_attention(cuda_lib, dev, T, L0):
+    """Fused attention (norm, RoPE, KV append, split-KV softmax, gate, digits) against the module
+    path (torch RMSNorm/RoPE + SDPA) on the same projection output and cache."""
+    from skinny_mlx_b200.model import AttnCache
+
+    cfg = SMALL
+    m = HybridModel(cfg, seed=0, device=dev)
+    a = m.layers[cfg.attn_every - 1].self_attn
+    torch.manual_seed(T * 1000 + L0)
+    D, nh, nkv = cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
+    a.q_norm.weight.normal_().mul_(0.1)
+    a.k_norm.weight.normal_().mul_(0.1)
+    width = 2 * nh * D + 2 * nkv * D
+    proj = (torch.randn(T, width + 8, device=dev) * 2).to(torch.bfloat16)[:, :width]  # ldp > width
+    max_len = 400
+    ca, cb = AttnCache(cfg, max_len, dev), AttnCache(cfg, max_len, dev)
+    ca.k[:L0] = torch.randn(L0, nkv, D, device=dev).to(torch.bfloat16)
+    ca.v[:L0] = torch.randn(L0, nkv, D, device=dev).to(torch.bfloat16)
+    cb.k.copy_(ca.k)
+    cb.v.copy_(ca.v)
+    ca.length = cb.length = L0
+    q1, k1 = 2 * nh * D, 2 * nh * D + nkv * D
+    ref = a.attend(proj[:, :q1], proj[:, q1:k1], proj[:, k1:], ca)
+    half = cfg.rotary_dim // 2
+    inv = cfg.rope_theta ** (-torch.arange(0, half, device=dev, dtype=torch.float32) / half)
+    ws = torch.zeros(int(cuda_lib.skinny_attn_workspace_bytes(T, nh, nkv, max_len)), dtype=torch.uint8, device=dev)
+    xq = torch.empty(int(cuda_lib.skinny_xq_bytes(T, nh * D)), dtype=torch.uint8, device=dev)
+    o = torch.empty(T, nh * D, dtype=torch.bfloat16, device=dev)
+    for rep in range(2):  # twice: the workspace counters are left ready for the next call
+        cb.k[L0:].zero_()
+        cb.v[L0:].zero_()
+        st = cuda_lib.skinny_attn_fused(_p(proj), proj.stride(0), _p(a.q_norm.weight), _p(a.k_norm.weight), _p(inv),
+                                        cfg.rotary_dim, ctypes.c_float(cfg.rms_eps), _p(cb.k), _p(cb.v), L0, T, nh,
+                                        nkv, max_len, _p(ws), ws.numel(), _p(xq), _p(o), _stream())
+        assert st == 0
+        torch.cuda.synchronize()
+        err = ((o.float() - ref.float()).abs().max() / ref.float().abs().max()).item()
+        assert err <= 2e-2, err
+        assert torch.equal(cb.v[:L0 + T], ca.v[:L0 + T])
+        assert torch.equal(cb.k[:L0], ca.k[:L0])
+        kd = (cb.k[L0:L0 + T].float() - ca.k[L0:L0 + T].float()).abs()
+        assert (kd <= ca.k[L0:L0 + T].float().abs() * 2 ** -7 + 1e-6).all()  # within one bf16 ulp
+        assert int(ws[:2048].view(torch.int32).abs().sum()) == 0
+        mpad = 8 if T <= 8 else 16
+        got = xq.cpu().numpy().reshape(nh * D // 64, -1)
+        assert np.array_equal(got, quant.xq_blocks(o.float().cpu().numpy(), mpad))
