@@ -260,7 +260,7 @@ int skinny_gdn_fused(const void* proj, int ldp, void* conv, void* conv_full, con
   if (ldp < C + Hv * 128 + 2 * Hv) return SKINNY_ERR_INVALID_ARG;
   // conv window and projection rows are read as 16-byte vectors
   if (!aligned16(state) || (ckpt && !aligned16(ckpt)) || !aligned16(xq) || (ldp % 8) || !aligned16(proj) ||
-      !aligned16(conv) || !aligned4(o_out) || !aligned4(err_word))
+      !aligned16(conv) || !aligned16(conv_full) || !aligned4(o_out) || !aligned4(err_word))
     return SKINNY_ERR_ALIGNMENT;
   skinny::GdnFusedParamsHost prm{proj, ldp, conv, conv_full, conv_w, A_log, dt_bias, norm_w, eps, state,
                              T > 1 ? ckpt : nullptr, xq, o_out, static_cast<uint32_t*>(err_word), T, Hv, Hk, W};

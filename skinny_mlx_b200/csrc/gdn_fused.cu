@@ -13,7 +13,7 @@
 // Work split.  The recurrence is independent per state row (row = value channel): with
 // S_t = g_t S_{t-1} + beta_t (v_t - S_{t-1} k_t g_t) k_t^T a row needs only its own v entry and
 // the head's shared q_t, k_t.  A head is therefore one cluster of kRanks CTAs, each owning 16
-// state rows (16 x 128 f32 in registers: 8 threads per row, 16 columns each), so a layer runs
+// state rows (16 x 128 f32 in registers: 16 threads per row, 8 columns each), so a layer runs
 // on Hv * 8 SMs instead of Hv.  Every CTA recomputes the head's q and k (conv, norm: a few
 // hundred channels) rather than exchanging them.  The gated RMSNorm and the digits need whole
 // 64-row groups of y, so each CTA pushes its y rows into the shared memory of every CTA
@@ -35,14 +35,14 @@
 
 namespace skinny {
 
-constexpr int kGfThreads = 128;
+constexpr int kGfThreads = 256;
 constexpr int kGfD = 128;
 constexpr int kGfMaxT = 16;
 constexpr int kGfRanks = 8;                    // CTAs (cluster size) per head
 constexpr int kGfRows = kGfD / kGfRanks;       // state rows per CTA
-constexpr int kGfTpr = kGfThreads / kGfRows;   // threads per row (8)
-constexpr int kGfCols = kGfD / kGfTpr;         // state columns per thread (16)
-static_assert(kGfTpr == 8 && kGfCols == 16, "thread layout");
+constexpr int kGfTpr = kGfThreads / kGfRows;   // threads per row (16)
+constexpr int kGfCols = kGfD / kGfTpr;         // state columns per thread (8)
+static_assert(kGfTpr == 16 && kGfCols == 8, "thread layout");
 
 struct GdnFusedParams {
   const __nv_bfloat16* proj;  // [T, ldp]: q (Hk*128) | k (Hk*128) | v (Hv*128) | z (Hv*128) | b (Hv) | a (Hv)
@@ -109,7 +109,6 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
     abort_flag = 0;
     fence_mbar_init();
   }
-  cluster_arrive_relaxed();  // the mbarrier exists before any peer stores to it (waited below)
   pdl_launch_dependents();
   pdl_wait_prior_grid();
 
@@ -169,31 +168,27 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
     }
   }
   __syncthreads();
+  // Arrive once this CTA's mbarrier exists and its reads of the conv window are complete: a peer
+  // writes its share of the new window, and stores into this CTA's shared memory, only after the
+  // matching wait.
+  cluster_arrive_relaxed();
 
-  // ---- conv + silu; the window update (one writer per channel: v channels by their row owner,
-  // q/k channels spread over the ranks of the first value head that uses the k head)
+  // ---- conv + silu
 #pragma unroll
   for (int it = 0; it < kConvIt; ++it) {
     const int i = tid + it * kGfThreads;
     if (i < kCh) {
       const int part = i < kGfD ? 0 : i < 2 * kGfD ? 1 : 2;
       const int j = part == 0 ? i : part == 1 ? i - kGfD : i - 2 * kGfD;
+#pragma unroll 4
       for (int t = 0; t < T; ++t) {
         float acc = 0.f;
 #pragma unroll
         for (int q = 0; q <= W; ++q) acc = fmaf(__bfloat162float(fw[t + q][i]), cw[it][q], acc);
-        const float sv = acc / (1.f + __expf(-acc));
+        const float sv = __fdividef(acc, 1.f + __expf(-acc));
         if (part == 0) qs[t][j] = sv;
         else if (part == 1) ks[t][j] = sv;
         else vs[t][j] = bf16rf(sv);
-      }
-      const bool owner = part == 2 || ((h % rep) == 0 && (j / kGfRows) == static_cast<int>(rank));
-      if (owner) {
-        const int ch = chan(i);
-        if (p.conv_full)
-          for (int r = 0; r < W + T; ++r) p.conv_full[static_cast<size_t>(r) * C + ch] = fw[r][i];
-#pragma unroll
-        for (int r = 0; r < W; ++r) p.conv[static_cast<size_t>(r) * C + ch] = fw[T + r][i];  // last W rows
       }
     }
   }
@@ -269,7 +264,25 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
   __syncthreads();
   // ---- every rank receives the head's whole y: 16-byte asynchronous stores into each peer's
   // shared memory, counted on the peer's mbarrier (no cluster-wide release of global stores)
-  cluster_wait();  // all peers have initialised their mbarriers
+  cluster_wait();  // all peers have initialised their mbarriers and read the old window
+  // ---- conv_full (the verify's conv input) and the new window (its last W rows), 16-byte
+  // stores from the staged rows.  One writer per channel: this CTA's v channels, and q/k
+  // channels 16 rank .. 16 rank + 15 when h is the first value head of its k head.
+  {
+    const int runs = (h % rep) == 0 ? 3 : 1;  // 8-channel vectors per row: 2 per run
+    const int per_row = 2 * runs;
+    const int n_full = p.conv_full ? (W + T) * per_row : 0;
+    for (int e = tid; e < n_full + W * per_row; e += kGfThreads) {
+      const bool full = e < n_full;
+      const int e2 = full ? e : e - n_full;
+      const int r = e2 / per_row, v = e2 - r * per_row;
+      const int run = runs == 3 ? v >> 1 : 2;  // 0: q, 1: k, 2: v
+      const int slot = (run == 2 ? 2 * kGfD : run * kGfD + static_cast<int>(rank) * kGfRows) + (v & 1) * 8;
+      const uint4 val = *reinterpret_cast<const uint4*>(&fw[full ? r : T + r][slot]);
+      __nv_bfloat16* dst = full ? p.conv_full + static_cast<size_t>(r) * C : p.conv + static_cast<size_t>(r) * C;
+      *reinterpret_cast<uint4*>(dst + chan(slot)) = val;
+    }
+  }
   {
     const uint32_t ybase = smem_u32(&yall[0][0]), ybl = smem_u32(&ybar);
     for (int i = tid; i < T * (kGfRows / 4) * kGfRanks; i += kGfThreads) {

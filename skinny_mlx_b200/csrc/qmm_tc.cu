@@ -696,10 +696,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t xloc = smem_u32(reinterpret_cast<float*>(sb + 1));
       pdl_wait_prior_grid();  // outputs may alias buffers an earlier kernel still reads
       const bool live = !*abort_flag;
-      for (int idx = threadIdx.x - kEpiWarp0 * 32; idx < NT * kTileRows; idx += 2 * kEpiThreads) {
+      // NT * 128 sums over 256 threads; every remote load of a thread is issued before the adds
+      constexpr int kPer = (NT * kTileRows + 2 * kEpiThreads - 1) / (2 * kEpiThreads);
+      const int i0 = threadIdx.x - kEpiWarp0 * 32;
+      float part[kPer][8];
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const uint32_t a = xloc + (i0 + u * 2 * kEpiThreads) * 4;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) part[u][q] = q < S ? ld_cluster_f32(map_shared_rank(a, q)) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kPer; ++u) {
+        const int idx = i0 + u * 2 * kEpiThreads;
         const int t = idx / kTileRows, row_g = tile * kTileRows + (idx - t * kTileRows);
         float v = 0.f;
-        for (int q = 0; q < S; ++q) v += ld_cluster_f32(map_shared_rank(xloc + idx * 4, q));
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (q < S) v += part[u][q];  // rank order
         if (live && t < p.M && row_g < mt.N) mt.out[static_cast<size_t>(t) * mt.ldo + row_g] = __float2bfloat16_rn(v);
       }
     }
