@@ -148,7 +148,8 @@ size_t skinny_attn_workspace_bytes(int T, int n_heads, int n_kv_heads, int max_l
  *   o    = causal (bottom-right) grouped-query softmax(q k^T / sqrt(128)) v over positions
  *          0 .. L0+t, then bf16(bf16(o) sigmoid(gate)), written as qmm input digits to xq
  *          (K = n_heads*128) and, when o_out != NULL, as bf16 [T, n_heads*128].
- * proj [T, ldp] bf16 = per query head [q (128) | gate (128)] | k (n_kv*128) | v (n_kv*128).
+ * proj [T, ldp] bf16 (16-byte aligned, ldp % 8 == 0) = per query head [q (128) | gate (128)] |
+ * k (n_kv*128) | v (n_kv*128).
  * head_dim 128, T * n_heads / n_kv_heads <= 128.  The caller advances its cache length by T.
  * Launched with programmatic dependent launch.  No counterpart in the reference's own code. */
 int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,

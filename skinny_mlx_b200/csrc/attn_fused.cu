@@ -34,8 +34,9 @@ constexpr int kAtChunk = 128;        // keys per CTA
 constexpr int kAtRG = 16;            // query rows per CTA
 constexpr int kAtThreads = 256;
 constexpr int kAtWarps = kAtThreads / 32;
-constexpr int kAtKStride = kAtD + 2;  // bf16 per shared key row: 65 words, conflict-free by key
-constexpr int kAtPart = kAtD + 2;     // floats per published row: m, l, o[128]
+constexpr int kAtStride = kAtD + 8;   // bf16 per shared row: 272 bytes, ldmatrix conflict-free
+constexpr int kAtPart = kAtD + 4;     // floats per published row: m, l, (pad), o[128] (16-byte aligned)
+constexpr int kAtMergePass = 8;       // chunk partials whose loads a merging thread issues together
 constexpr int kAtMaxRG = 8;           // row groups per KV head (rep * T <= 128)
 constexpr int kAtCntWords = 64 * kAtMaxRG;
 constexpr size_t kAtPartOff = kAtCntWords * 4;
@@ -50,21 +51,42 @@ struct AttnParams {
   __nv_bfloat16* kc;          // [max_len, nkv, 128]
   __nv_bfloat16* vc;
   int T, L0, nh, nkv, rot, nchunks, nrg;
-  float* part;                // [nkv, nrg, nchunks, 16, kAtPart]
+  float* part;                // [nkv, nrg, nchunks, 16, kAtPart]: per row m, l, -, -, o[128]
   uint32_t* cnt;              // [nkv * kAtMaxRG], zero on entry, left zero
   uint8_t* xq;                // o_proj input digits (K = nh * 128)
   __nv_bfloat16* o_out;       // [T, nh * 128] or null
 };
 
 struct AttnSmem {
-  float q[kAtRG][kAtD];
-  float s[kAtRG][kAtChunk];
-  __nv_bfloat16 k[kAtChunk][kAtKStride];
-  __nv_bfloat16 v[kAtChunk][kAtD];
+  __nv_bfloat16 q[kAtRG][kAtStride];      // rotated queries of the row group
+  __nv_bfloat16 k[kAtChunk][kAtStride];   // keys of the chunk
+  __nv_bfloat16 v[kAtChunk][kAtStride];   // values of the chunk
+  __nv_bfloat16 pr[kAtRG][kAtStride];     // probabilities (bf16, as a flash kernel rounds them)
+  float s[kAtRG][kAtChunk];               // scores (log2 domain); reused for the merged rows
   float stage[kAtWarps][kAtD];
   float rowm[kAtRG], rowl[kAtRG];
   int last;
 };
+
+// ---- warp-level bf16 tensor-core tiles (m16n8k16, f32 accumulate)
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 
 __device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
@@ -117,6 +139,26 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
   pdl_launch_dependents();
   pdl_wait_prior_grid();
 
+  // output gates of the rows this thread finishes if this CTA merges (row tid / 16, 8 dims)
+  float gate_pre[8];
+  {
+    const int rr = tid / 16, d0 = (tid % 16) * 8;
+    if (rr < nrows) {
+      const int r = rbase + rr, t = r / rep, hq = kvh * rep + r % rep;
+      const uint4 gw = *reinterpret_cast<const uint4*>(p.proj + static_cast<size_t>(t) * p.ldp + hq * 2 * kAtD + kAtD + d0);
+      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(g2[i]);
+        gate_pre[2 * i] = f.x;
+        gate_pre[2 * i + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) gate_pre[i] = 0.f;
+    }
+  }
+
   // ---- cached keys and values of the chunk: every thread issues all its 16-byte loads first
   {
     constexpr int kPieces = kAtChunk * (kAtD / 8);  // 16-byte pieces per matrix
@@ -139,11 +181,7 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
     for (int u = 0; u < kPer; ++u) {
       const int e = tid + u * kAtThreads, j = e >> 4, pc = e & 15;
       if (j < nk && k0 + j >= p.L0) continue;  // a new key: written below by its warp
-      uint32_t* kd = reinterpret_cast<uint32_t*>(&sm.k[j][8 * pc]);  // 4-byte aligned rows
-      kd[0] = kw[u].x;
-      kd[1] = kw[u].y;
-      kd[2] = kw[u].z;
-      kd[3] = kw[u].w;
+      *reinterpret_cast<uint4*>(&sm.k[j][8 * pc]) = kw[u];
       *reinterpret_cast<uint4*>(&sm.v[j][8 * pc]) = vw[u];
     }
   }
@@ -156,8 +194,10 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
     for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(src[lane + 32 * i]);
     norm_rope(x, p.qn_w, p.eps, p.inv_freq, p.rot, p.L0 + t, sm.stage[warp], lane);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) sm.q[rr][lane + 32 * i] = x[i];
+    for (int i = 0; i < 4; ++i) sm.q[rr][lane + 32 * i] = __float2bfloat16_rn(x[i]);
   }
+  for (int i = tid; i < (kAtRG - nrows) * kAtD; i += kAtThreads)  // rows past the group: zero
+    sm.q[nrows + i / kAtD][i % kAtD] = __float2bfloat16_rn(0.f);
   // ---- new keys in the chunk (positions L0 .. L0+T-1): warp per key
   {
     const int jn0 = max(p.L0 - k0, 0);
@@ -187,31 +227,34 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
     }
   }
   __syncthreads();
-  // ---- scores (log2 domain): thread = (key j, row half)
+  // ---- scores on tensor cores (log2 domain): warp w takes keys 16w .. 16w+15 for the 16 rows
   {
-    const int j = tid % kAtChunk, h8 = (tid / kAtChunk) * 8;
-    float acc[8];
+    const int g = lane >> 2, cq = lane & 3;
+    const uint32_t a_addr =
+        smem_u32(&sm.q[0][0]) + (((lane & 7) + 8 * ((lane >> 3) & 1)) * kAtStride + 8 * (lane >> 4)) * 2;
+    const uint32_t b_addr =
+        smem_u32(&sm.k[0][0]) + ((16 * warp + (lane & 7) + 8 * (lane >> 4)) * kAtStride + 8 * ((lane >> 3) & 1)) * 2;
+    float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-#pragma unroll 4
-    for (int d = 0; d < kAtD; d += 2) {
-      const float2 kf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sm.k[j][d]));
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float2 qf = *reinterpret_cast<const float2*>(&sm.q[h8 + i][d]);
-        acc[i] = fmaf(qf.x, kf.x, fmaf(qf.y, kf.y, acc[i]));
-      }
+    for (int ks = 0; ks < kAtD / 16; ++ks) {
+      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+      ldsm_x4(a_addr + ks * 32, a0, a1, a2, a3);
+      ldsm_x4(b_addr + ks * 32, b0, b1, b2, b3);
+      mma_bf16(c[0], a0, a1, a2, a3, b0, b1);
+      mma_bf16(c[1], a0, a1, a2, a3, b2, b3);
     }
     const float sc = rsqrtf(static_cast<float>(kAtD)) * 1.4426950408889634f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int rr = h8 + i;
-      if (rr < nrows) {
-        const int t = (rbase + rr) / rep;
-        const bool vis = j < nk && k0 + j <= p.L0 + t;
-        sm.s[rr][j] = vis ? acc[i] * sc : -INFINITY;
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int rr = g + 8 * (e >> 1), j = 16 * warp + 8 * nt + 2 * cq + (e & 1);
+        if (rr < nrows) {
+          const int t = (rbase + rr) / rep;
+          const bool vis = j < nk && k0 + j <= p.L0 + t;
+          sm.s[rr][j] = vis ? c[nt][e] * sc : -INFINITY;
+        }
       }
-    }
   }
   __syncthreads();
   // ---- chunk softmax per row (warp per row)
@@ -228,9 +271,9 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
     float l = 0.f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float e = m == -INFINITY ? 0.f : exp2f(sv[i] - m);
-      sm.s[rr][lane + 32 * i] = e;
-      l += e;
+      const __nv_bfloat16 e = __float2bfloat16_rn(m == -INFINITY ? 0.f : exp2f(sv[i] - m));
+      sm.pr[rr][lane + 32 * i] = e;
+      l += __bfloat162float(e);  // the sum of the probabilities as the products use them
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
@@ -240,78 +283,107 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
     }
   }
   __syncthreads();
-  // ---- unnormalised outputs: thread = (dim pair, 4 rows); publish
+  for (int i = tid; i < (kAtRG - nrows) * kAtD; i += kAtThreads)
+    sm.pr[nrows + i / kAtD][i % kAtD] = __float2bfloat16_rn(0.f);
+  __syncthreads();
+  // ---- unnormalised outputs on tensor cores: warp w takes dims 16w .. 16w+15; publish
   {
-    const int dp = tid % 64, r4 = (tid / 64) * 4;
-    float o[4][2];
+    const int g = lane >> 2, cq = lane & 3;
+    const uint32_t a_addr =
+        smem_u32(&sm.pr[0][0]) + (((lane & 7) + 8 * ((lane >> 3) & 1)) * kAtStride + 8 * (lane >> 4)) * 2;
+    const uint32_t b_addr =
+        smem_u32(&sm.v[0][0]) + (((lane & 7) + 8 * ((lane >> 3) & 1)) * kAtStride + 16 * warp + 8 * (lane >> 4)) * 2;
+    float o[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = 0.f;
-    for (int j = 0; j < kAtChunk; ++j) {
-      const float2 vf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sm.v[j][2 * dp]));
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float pj = sm.s[r4 + i][j];
-        o[i][0] = fmaf(pj, vf.x, o[i][0]);
-        o[i][1] = fmaf(pj, vf.y, o[i][1]);
-      }
+    for (int ks = 0; ks < kAtChunk / 16; ++ks) {
+      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+      ldsm_x4(a_addr + ks * 32, a0, a1, a2, a3);
+      ldsm_x4_t(b_addr + ks * 16 * kAtStride * 2, b0, b1, b2, b3);
+      mma_bf16(o[0], a0, a1, a2, a3, b0, b1);
+      mma_bf16(o[1], a0, a1, a2, a3, b2, b3);
     }
     float* base = p.part + ((static_cast<size_t>(kvh) * p.nrg + rg) * p.nchunks + chunk) * kAtRG * kAtPart;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int rr = r4 + i;
-      if (rr < nrows) {
-        float* row = base + static_cast<size_t>(rr) * kAtPart;
-        if (dp == 0) {
-          row[0] = sm.rowm[rr];
-          row[1] = sm.rowl[rr];
-        }
-        *reinterpret_cast<float2*>(row + 2 + 2 * dp) = make_float2(o[i][0], o[i][1]);
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int rr = g + 8 * hf;
+        if (rr < nrows)
+          *reinterpret_cast<float2*>(base + static_cast<size_t>(rr) * kAtPart + 4 + 16 * warp + 8 * nt + 2 * cq) =
+              make_float2(o[nt][2 * hf], o[nt][2 * hf + 1]);
       }
+    if (tid < nrows) {
+      base[static_cast<size_t>(tid) * kAtPart] = sm.rowm[tid];
+      base[static_cast<size_t>(tid) * kAtPart + 1] = sm.rowl[tid];
     }
   }
-  __threadfence();
+  // Publish: the block's writes are ordered before thread 0's release-acquire increment (the
+  // barrier makes them visible to thread 0; the release is cumulative), and the last arriver's
+  // acquire makes every chunk's partials visible to it.
   __syncthreads();
   if (tid == 0) {
-    const uint32_t prev = atomicAdd(&p.cnt[kvh * kAtMaxRG + rg], 1u);
+    uint32_t prev;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;"
+                 : "=r"(prev)
+                 : "l"(p.cnt + kvh * kAtMaxRG + rg)
+                 : "memory");
     sm.last = prev == static_cast<uint32_t>(p.nchunks - 1);
   }
   __syncthreads();
   if (!sm.last) return;
-  __threadfence();
-  // ---- merge the chunks (chunk order), gate, digits
+  // ---- merge the chunks (chunk order, passes of kAtMergePass), gate, digits
   {
     const int rr = tid / 16, d0 = (tid % 16) * 8;
     if (rr < nrows) {
       const float* base = p.part + (static_cast<size_t>(kvh) * p.nrg + rg) * p.nchunks * kAtRG * kAtPart +
                           static_cast<size_t>(rr) * kAtPart;
       const size_t cstride = static_cast<size_t>(kAtRG) * kAtPart;
-      float M = -INFINITY;
-#pragma unroll 8
-      for (int c = 0; c < p.nchunks; ++c) M = fmaxf(M, __ldcg(base + c * cstride));
-      float L = 0.f, acc[8];
+      float M = -INFINITY, L = 0.f, acc[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-#pragma unroll 4
-      for (int c = 0; c < p.nchunks; ++c) {
-        const float* row = base + c * cstride;
-        const float mc = __ldcg(row);
-        const float wgt = mc == -INFINITY ? 0.f : exp2f(mc - M);
-        L = fmaf(wgt, __ldcg(row + 1), L);
+      for (int c0 = 0; c0 < p.nchunks; c0 += kAtMergePass) {
+        float mv[kAtMergePass], lv[kAtMergePass];
+        float4 ov[kAtMergePass][2];
 #pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-          const float2 ov = __ldcg(reinterpret_cast<const float2*>(row + 2 + d0 + i));
-          acc[i] = fmaf(wgt, ov.x, acc[i]);
-          acc[i + 1] = fmaf(wgt, ov.y, acc[i + 1]);
+        for (int u = 0; u < kAtMergePass; ++u) {
+          const int c = c0 + u;
+          if (c < p.nchunks) {
+            const float* row = base + c * cstride;
+            mv[u] = __ldcg(row);
+            lv[u] = __ldcg(row + 1);
+            ov[u][0] = __ldcg(reinterpret_cast<const float4*>(row + 4 + d0));
+            ov[u][1] = __ldcg(reinterpret_cast<const float4*>(row + 8 + d0));
+          } else {
+            mv[u] = -INFINITY;
+            lv[u] = 0.f;
+            ov[u][0] = ov[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
         }
+        float Mn = M;
+#pragma unroll
+        for (int u = 0; u < kAtMergePass; ++u) Mn = fmaxf(Mn, mv[u]);
+        const float alpha = M == -INFINITY ? 0.f : exp2f(M - Mn);
+        L *= alpha;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] *= alpha;
+#pragma unroll
+        for (int u = 0; u < kAtMergePass; ++u) {
+          const float wgt = mv[u] == -INFINITY ? 0.f : exp2f(mv[u] - Mn);
+          L = fmaf(wgt, lv[u], L);
+          acc[0] = fmaf(wgt, ov[u][0].x, acc[0]);
+          acc[1] = fmaf(wgt, ov[u][0].y, acc[1]);
+          acc[2] = fmaf(wgt, ov[u][0].z, acc[2]);
+          acc[3] = fmaf(wgt, ov[u][0].w, acc[3]);
+          acc[4] = fmaf(wgt, ov[u][1].x, acc[4]);
+          acc[5] = fmaf(wgt, ov[u][1].y, acc[5]);
+          acc[6] = fmaf(wgt, ov[u][1].z, acc[6]);
+          acc[7] = fmaf(wgt, ov[u][1].w, acc[7]);
+        }
+        M = Mn;
       }
-      const int r = rbase + rr, t = r / rep, hq = kvh * rep + r % rep;
-      const __nv_bfloat16* gate = p.proj + static_cast<size_t>(t) * p.ldp + hq * 2 * kAtD + kAtD;
       const float invL = 1.f / L;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float g = __bfloat162float(gate[d0 + i]);
-        sm.q[rr][d0 + i] = bfr(bfr(acc[i] * invL) * (1.f / (1.f + __expf(-g))));
-      }
+      for (int i = 0; i < 8; ++i) sm.s[rr][d0 + i] = bfr(bfr(acc[i] * invL) * (1.f / (1.f + __expf(-gate_pre[i]))));
     }
   }
   __syncthreads();
@@ -320,7 +392,7 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
     const int rr = job >> 1, hf = job & 1;
     const int r = rbase + rr, t = r / rep, hq = kvh * rep + r % rep;
     const int d = hf * 64 + 2 * lane;
-    const float a0 = sm.q[rr][d], a1 = sm.q[rr][d + 1];
+    const float a0 = sm.s[rr][d], a1 = sm.s[rr][d + 1];
     if (p.o_out) {
       __nv_bfloat16* op = p.o_out + static_cast<size_t>(t) * p.nh * kAtD + hq * kAtD + d;
       *reinterpret_cast<__nv_bfloat162*>(op) = __floats2bfloat162_rn(a0, a1);

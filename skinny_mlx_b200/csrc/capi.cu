@@ -284,7 +284,7 @@ int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const fl
     return SKINNY_ERR_SHAPE;
   if (ldp < (2 * n_heads + 2 * n_kv_heads) * 128) return SKINNY_ERR_INVALID_ARG;
   if (!aligned16(xq) || !aligned16(k_cache) || !aligned16(v_cache) ||
-      !aligned4(o_out) || (reinterpret_cast<uintptr_t>(proj) & 1u))
+      !aligned4(o_out) || !aligned16(proj) || (ldp % 8))
     return SKINNY_ERR_ALIGNMENT;
   if (!workspace || workspace_bytes < skinny::attn_ws_bytes(T, n_heads, n_kv_heads, max_len) ||
       !aligned16(workspace))
