@@ -151,11 +151,14 @@ size_t skinny_attn_workspace_bytes(int T, int n_heads, int n_kv_heads, int max_l
  * proj [T, ldp] bf16 (16-byte aligned, ldp % 8 == 0) = per query head [q (128) | gate (128)] |
  * k (n_kv*128) | v (n_kv*128).
  * head_dim 128, T * n_heads / n_kv_heads <= 128.  The caller advances its cache length by T.
+ * length_dev (may be NULL): when given, the cache length L0 is read from this device int32 when
+ * the kernel runs (L0 argument ignored), so that one captured launch (CUDA graph) serves every
+ * length; a device length outside [0, max_len - T] makes the launch touch nothing.
  * Launched with programmatic dependent launch.  No counterpart in the reference's own code. */
 int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
-                      const float* inv_freq, int rot, float eps, void* k_cache, void* v_cache, int L0, int T,
-                      int n_heads, int n_kv_heads, int max_len, void* workspace, size_t workspace_bytes, void* xq,
-                      void* o_out, void* stream);
+                      const float* inv_freq, int rot, float eps, void* k_cache, void* v_cache, int L0,
+                      const int32_t* length_dev, int T, int n_heads, int n_kv_heads, int max_len, void* workspace,
+                      size_t workspace_bytes, void* xq, void* o_out, void* stream);
 
 /* skinny_qmm_w4g64 on an input prepared by skinny_prep (same result as passing the bf16
  * activation itself), launched without the x-prep kernel. */

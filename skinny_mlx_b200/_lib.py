@@ -47,8 +47,8 @@ SIGNATURES = {
                                  c_int, c_void_p, c_void_p]),
     "skinny_attn_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "skinny_attn_fused": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, ctypes.c_float, c_void_p,
-                                  c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p,
-                                  c_void_p, c_void_p]),
+                                  c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t,
+                                  c_void_p, c_void_p, c_void_p]),
     "skinny_qmm_w4g64_prepared": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                           c_size_t, c_void_p]),
     "skinny_spec_accept_workspace_bytes": (c_size_t, []),

@@ -50,7 +50,8 @@ struct AttnParams {
   float eps;
   __nv_bfloat16* kc;          // [max_len, nkv, 128]
   __nv_bfloat16* vc;
-  int T, L0, nh, nkv, rot, nchunks, nrg;
+  int T, L0, nh, nkv, rot, nchunks, nrg, max_len;
+  const int* len_dev;         // if set: the cache length is read here (grid sized for max_len)
   float* part;                // [nkv, nrg, nchunks, 16, kAtPart]: per row m, l, -, -, o[128]
   uint32_t* cnt;              // [nkv * kAtMaxRG], zero on entry, left zero
   uint8_t* xq;                // o_proj input digits (K = nh * 128)
@@ -132,12 +133,18 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
   const int R = p.T * rep;
   const int rbase = rg * kAtRG;
   const int nrows = min(kAtRG, R - rbase);
-  const int Ltot = p.L0 + p.T;
-  const int k0 = chunk * kAtChunk;
-  const int nk = min(kAtChunk, Ltot - k0);
   const int qkw = p.nh * 2 * kAtD;  // column of k in proj
   pdl_launch_dependents();
   pdl_wait_prior_grid();
+  // the cache length: a kernel argument, or read from device memory so that one captured
+  // launch serves every length (the grid then covers max_len and the surplus chunks leave)
+  const int L0 = p.len_dev ? *p.len_dev : p.L0;
+  if (L0 < 0 || L0 + p.T > p.max_len) return;  // a device length out of range: no access at all
+  const int nchunks = p.len_dev ? (L0 + p.T + kAtChunk - 1) / kAtChunk : p.nchunks;
+  if (chunk >= nchunks) return;
+  const int Ltot = L0 + p.T;
+  const int k0 = chunk * kAtChunk;
+  const int nk = min(kAtChunk, Ltot - k0);
 
   // output gates of the rows this thread finishes if this CTA merges (row tid / 16, 8 dims)
   float gate_pre[8];
@@ -168,7 +175,7 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
     for (int u = 0; u < kPer; ++u) {
       const int e = tid + u * kAtThreads, j = e >> 4, pc = e & 15;
       const int pos = k0 + j;
-      if (j < nk && pos < p.L0) {
+      if (j < nk && pos < L0) {
         const size_t off = (static_cast<size_t>(pos) * p.nkv + kvh) * kAtD + 8 * pc;
         kw[u] = __ldg(reinterpret_cast<const uint4*>(p.kc + off));
         vw[u] = __ldg(reinterpret_cast<const uint4*>(p.vc + off));
@@ -180,7 +187,7 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
 #pragma unroll
     for (int u = 0; u < kPer; ++u) {
       const int e = tid + u * kAtThreads, j = e >> 4, pc = e & 15;
-      if (j < nk && k0 + j >= p.L0) continue;  // a new key: written below by its warp
+      if (j < nk && k0 + j >= L0) continue;  // a new key: written below by its warp
       *reinterpret_cast<uint4*>(&sm.k[j][8 * pc]) = kw[u];
       *reinterpret_cast<uint4*>(&sm.v[j][8 * pc]) = vw[u];
     }
@@ -192,7 +199,7 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
     float x[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(src[lane + 32 * i]);
-    norm_rope(x, p.qn_w, p.eps, p.inv_freq, p.rot, p.L0 + t, sm.stage[warp], lane);
+    norm_rope(x, p.qn_w, p.eps, p.inv_freq, p.rot, L0 + t, sm.stage[warp], lane);
 #pragma unroll
     for (int i = 0; i < 4; ++i) sm.q[rr][lane + 32 * i] = __float2bfloat16_rn(x[i]);
   }
@@ -200,9 +207,9 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
     sm.q[nrows + i / kAtD][i % kAtD] = __float2bfloat16_rn(0.f);
   // ---- new keys in the chunk (positions L0 .. L0+T-1): warp per key
   {
-    const int jn0 = max(p.L0 - k0, 0);
+    const int jn0 = max(L0 - k0, 0);
     for (int j = jn0 + warp; j < nk; j += kAtWarps) {
-      const int pos = k0 + j, t = pos - p.L0;
+      const int pos = k0 + j, t = pos - L0;
       const __nv_bfloat16* src = p.proj + static_cast<size_t>(t) * p.ldp + qkw;
       float x[4];
       __nv_bfloat16 vb[4];
@@ -251,7 +258,7 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
         const int rr = g + 8 * (e >> 1), j = 16 * warp + 8 * nt + 2 * cq + (e & 1);
         if (rr < nrows) {
           const int t = (rbase + rr) / rep;
-          const bool vis = j < nk && k0 + j <= p.L0 + t;
+          const bool vis = j < nk && k0 + j <= L0 + t;
           sm.s[rr][j] = vis ? c[nt][e] * sc : -INFINITY;
         }
       }
@@ -302,7 +309,7 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
       mma_bf16(o[0], a0, a1, a2, a3, b0, b1);
       mma_bf16(o[1], a0, a1, a2, a3, b2, b3);
     }
-    float* base = p.part + ((static_cast<size_t>(kvh) * p.nrg + rg) * p.nchunks + chunk) * kAtRG * kAtPart;
+    float* base = p.part + ((static_cast<size_t>(kvh) * p.nrg + rg) * nchunks + chunk) * kAtRG * kAtPart;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -327,7 +334,7 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
                  : "=r"(prev)
                  : "l"(p.cnt + kvh * kAtMaxRG + rg)
                  : "memory");
-    sm.last = prev == static_cast<uint32_t>(p.nchunks - 1);
+    sm.last = prev == static_cast<uint32_t>(nchunks - 1);
   }
   __syncthreads();
   if (!sm.last) return;
@@ -335,19 +342,19 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
   {
     const int rr = tid / 16, d0 = (tid % 16) * 8;
     if (rr < nrows) {
-      const float* base = p.part + (static_cast<size_t>(kvh) * p.nrg + rg) * p.nchunks * kAtRG * kAtPart +
+      const float* base = p.part + (static_cast<size_t>(kvh) * p.nrg + rg) * nchunks * kAtRG * kAtPart +
                           static_cast<size_t>(rr) * kAtPart;
       const size_t cstride = static_cast<size_t>(kAtRG) * kAtPart;
       float M = -INFINITY, L = 0.f, acc[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-      for (int c0 = 0; c0 < p.nchunks; c0 += kAtMergePass) {
+      for (int c0 = 0; c0 < nchunks; c0 += kAtMergePass) {
         float mv[kAtMergePass], lv[kAtMergePass];
         float4 ov[kAtMergePass][2];
 #pragma unroll
         for (int u = 0; u < kAtMergePass; ++u) {
           const int c = c0 + u;
-          if (c < p.nchunks) {
+          if (c < nchunks) {
             const float* row = base + c * cstride;
             mv[u] = __ldcg(row);
             lv[u] = __ldcg(row + 1);
@@ -420,8 +427,9 @@ bool attn_fits(int T, int nh, int nkv) {
 }
 
 cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, const float* kn_w,
-                              const float* inv_freq, int rot, float eps, void* kc, void* vc, int L0, int T,
-                              int nh, int nkv, void* ws, void* xq, void* o_out, cudaStream_t stream) {
+                              const float* inv_freq, int rot, float eps, void* kc, void* vc, int L0,
+                              const int* len_dev, int max_len, int T, int nh, int nkv, void* ws, void* xq,
+                              void* o_out, cudaStream_t stream) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -447,7 +455,9 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
   prm.nh = nh;
   prm.nkv = nkv;
   prm.rot = rot;
-  prm.nchunks = (L0 + T + kAtChunk - 1) / kAtChunk;
+  prm.len_dev = len_dev;
+  prm.max_len = max_len;
+  prm.nchunks = ((len_dev ? max_len : L0 + T) + kAtChunk - 1) / kAtChunk;  // grid; the kernel recomputes it from len_dev
   prm.nrg = (T * rep + kAtRG - 1) / kAtRG;
   prm.cnt = static_cast<uint32_t*>(ws);
   prm.part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kAtPartOff);

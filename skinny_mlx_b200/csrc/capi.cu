@@ -56,8 +56,9 @@ cudaError_t qmm_tc_launch_noalloc(const void* x, int ldx, const void* w_tc, void
 size_t attn_ws_bytes(int T, int nh, int nkv, int max_len);
 bool attn_fits(int T, int nh, int nkv);
 cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, const float* kn_w,
-                              const float* inv_freq, int rot, float eps, void* kc, void* vc, int L0, int T,
-                              int nh, int nkv, void* ws, void* xq, void* o_out, cudaStream_t stream);
+                              const float* inv_freq, int rot, float eps, void* kc, void* vc, int L0,
+                              const int* len_dev, int max_len, int T, int nh, int nkv, void* ws, void* xq,
+                              void* o_out, cudaStream_t stream);
 }  // namespace skinny
 
 namespace {
@@ -273,25 +274,26 @@ size_t skinny_attn_workspace_bytes(int T, int n_heads, int n_kv_heads, int max_l
 }
 
 int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
-                      const float* inv_freq, int rot, float eps, void* k_cache, void* v_cache, int L0, int T,
-                      int n_heads, int n_kv_heads, int max_len, void* workspace, size_t workspace_bytes, void* xq,
-                      void* o_out, void* stream) {
+                      const float* inv_freq, int rot, float eps, void* k_cache, void* v_cache, int L0,
+                      const int32_t* length_dev, int T, int n_heads, int n_kv_heads, int max_len, void* workspace,
+                      size_t workspace_bytes, void* xq, void* o_out, void* stream) {
   if (!proj || !q_norm_w || !k_norm_w || !k_cache || !v_cache || !xq || (rot > 0 && !inv_freq))
     return SKINNY_ERR_INVALID_ARG;
   if (T < 1 || T > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
+  // with length_dev the caller guarantees 0 <= *length_dev <= max_len - T when the launch runs
   if (!skinny::attn_fits(T, n_heads, n_kv_heads) || rot < 0 || rot > 128 || (rot % 2) || L0 < 0 ||
-      L0 + T > max_len)
+      (!length_dev && L0 + T > max_len) || max_len < T)
     return SKINNY_ERR_SHAPE;
   if (ldp < (2 * n_heads + 2 * n_kv_heads) * 128) return SKINNY_ERR_INVALID_ARG;
-  if (!aligned16(xq) || !aligned16(k_cache) || !aligned16(v_cache) ||
-      !aligned4(o_out) || !aligned16(proj) || (ldp % 8))
+  if (!aligned16(xq) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned4(o_out) || !aligned16(proj) ||
+      (ldp % 8) || !aligned4(length_dev))
     return SKINNY_ERR_ALIGNMENT;
   if (!workspace || workspace_bytes < skinny::attn_ws_bytes(T, n_heads, n_kv_heads, max_len) ||
       !aligned16(workspace))
     return SKINNY_ERR_WORKSPACE;
   return cuda_status(skinny::attn_fused_launch(proj, ldp, q_norm_w, k_norm_w, inv_freq, rot, eps, k_cache,
-                                               v_cache, L0, T, n_heads, n_kv_heads, workspace, xq, o_out,
-                                               static_cast<cudaStream_t>(stream)));
+                                               v_cache, L0, length_dev, max_len, T, n_heads, n_kv_heads,
+                                               workspace, xq, o_out, static_cast<cudaStream_t>(stream)));
 }
 
 int skinny_qmm_w4g64_prepared(const void* xq, const void* w_tc, void* out, int ldo, int M, int N, int K,

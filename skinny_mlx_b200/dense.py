@@ -22,9 +22,10 @@ import torch
 import torch.distributed as dist
 import torch.nn as nn
 import torch.nn.functional as F
+from torch.nn.attention import sdpa_kernel
 
 from .configs import DenseConfig
-from .model import AttnCache, QuantizedLinear, RMSNorm, _rope
+from .model import _SDPA_BACKENDS, AttnCache, QuantizedLinear, RMSNorm, _rope
 from .qmm import dequantize, quantize
 
 
@@ -96,9 +97,10 @@ class DenseLayer(nn.Module):
         cache.v[L0:L0 + T] = v
         cache.length = L0 + T
         causal = pos[:, None] >= torch.arange(L0 + T, device=x.device)[None, :]
-        o = F.scaled_dot_product_attention(q.transpose(0, 1)[None], cache.k[:L0 + T].transpose(0, 1)[None],
-                                           cache.v[:L0 + T].transpose(0, 1)[None], attn_mask=causal,
-                                           enable_gqa=True)[0].transpose(0, 1).reshape(T, nq * D)
+        with sdpa_kernel(_SDPA_BACKENDS):
+            o = F.scaled_dot_product_attention(q.transpose(0, 1)[None], cache.k[:L0 + T].transpose(0, 1)[None],
+                                               cache.v[:L0 + T].transpose(0, 1)[None], attn_mask=causal,
+                                               enable_gqa=True)[0].transpose(0, 1).reshape(T, nq * D)
         o = ex.gather(o.to(torch.bfloat16))
         h = (x.float() + ex.gather(self.o_proj(o)).float()).to(torch.bfloat16)
         gu = self.gate_up_proj(self.post_attention_layernorm(h))

@@ -106,7 +106,9 @@ class FusedStep:
         land in one place (skinny_mlx_b200.qmm.device_errors reads it)."""
         return get_workspace(dev, int(_lib.lib().skinny_qmm_workspace_bytes(128, 64)))
 
-    def _attention(self, ent, proj, c: AttnCache, m: int, xq, stream):
+    def _attention(self, ent, proj, c: AttnCache, m: int, xq, stream, len_dev=None):
+        """len_dev: a device int32 holding c.length when the launch runs (graph replay); the
+        caller then advances the host length itself."""
         cfg = self.cfg
         max_len = c.k.shape[0]
         ws = self._attn_ws.get(max_len)
@@ -115,9 +117,10 @@ class FusedStep:
             ws = self._attn_ws[max_len] = torch.zeros(n, dtype=torch.uint8, device=proj.device)
         L0 = c.length
         _lib.call("skinny_attn_fused", _p(proj), proj.stride(0), _p(ent["qn"]), _p(ent["kn"]), _p(ent["inv"]),
-                  cfg.rotary_dim, cfg.rms_eps, _p(c.k), _p(c.v), L0, m, cfg.n_heads, cfg.n_kv_heads, max_len,
-                  _p(ws), ws.numel(), _p(xq), None, stream)
-        c.length = L0 + m
+                  cfg.rotary_dim, cfg.rms_eps, _p(c.k), _p(c.v), L0, _p(len_dev), m, cfg.n_heads, cfg.n_kv_heads,
+                  max_len, _p(ws), ws.numel(), _p(xq), None, stream)
+        if len_dev is None:
+            c.length = L0 + m
 
     def _qmm(self, xq, w: SkinnyWeight, out, m: int, stream):
         ws = get_workspace(out.device, int(_lib.lib().skinny_qmm_workspace_bytes(w.N, w.K)))
@@ -131,9 +134,12 @@ class FusedStep:
 
     # ---------------------------------------------------------------- the step
     @torch.no_grad()
-    def __call__(self, ids: torch.Tensor, cache) -> tuple[torch.Tensor, torch.Tensor]:
+    def __call__(self, ids: torch.Tensor, cache, lens_dev: torch.Tensor | None = None
+                 ) -> tuple[torch.Tensor, torch.Tensor]:
         """Same contract as HybridModel.forward for 1 <= len(ids) <= 16: (final normed hidden,
-        logits) as bf16 [T, H] and [T, V] (views of reused buffers: copy to keep)."""
+        logits) as bf16 [T, H] and [T, V] (views of reused buffers: copy to keep).  lens_dev
+        (int32, one entry per attention layer): the attention kernels read the cache lengths there
+        and the host lengths are left to the caller (see GraphedStep)."""
         cfg, m = self.cfg, ids.shape[0]
         if m > 16:  # prefill: the module-by-module forward (qmm in 16-token chunks)
             return self.model(ids, cache)
@@ -154,6 +160,7 @@ class FusedStep:
                 self._prep(0, hs[cur], m, cfg.hidden, b["xq_h"], stream, d=d, h_out=hs[1 - cur], w=w, a_out=a_out)
                 cur = 1 - cur
 
+        ai = 0
         for ent, c in zip(self.layers, cache.layers):
             # x_l = x_{l-1} + down_{l-1}; digits of input_layernorm(x_l)
             add_norm(d, ent["in_norm"])
@@ -170,7 +177,9 @@ class FusedStep:
                           _p(b["xq_o"]), None, m, cfg.gdn_v_heads, cfg.gdn_k_heads, cfg.conv_kernel - 1,
                           _p(self._err_word(proj.device)), stream)
             else:
-                self._attention(ent, proj, c, m, b["xq_o"], stream)
+                self._attention(ent, proj, c, m, b["xq_o"], stream,
+                                None if lens_dev is None else lens_dev[ai:ai + 1])
+                ai += 1
             self._qmm(b["xq_o"], ent["out"], b["mix"], m, stream)
             # h = x_l + mixer; digits of post_attention_layernorm(h)
             add_norm(b["mix"], ent["post_norm"])
@@ -183,4 +192,89 @@ class FusedStep:
         return b["a"], b["logits"]
 
 
-__all__ = ["FusedStep"]
+class GraphedStep:
+    """FusedStep replayed from one CUDA graph per (cache, token count, recording state).
+
+    The step's launches are captured once; per call the host copies the token ids into the
+    graph's input buffer and the attention caches' lengths into a device array (one small copy
+    each, ordered on the stream before the replay), replays, and advances the host lengths.
+    Longer inputs (prefill) run FusedStep eagerly.  Attribute access falls through to the
+    FusedStep, so the greedy and speculative loops take either."""
+
+    def __init__(self, fused: FusedStep):
+        self.fused = fused
+        self._graphs: dict = {}
+        self._stream = torch.cuda.Stream(fused.device)
+
+    def __getattr__(self, name):
+        return getattr(self.fused, name)
+
+    @staticmethod
+    def _lens(cache):
+        if not hasattr(cache, "_lens_dev"):
+            attn = [c for c in cache.layers if isinstance(c, AttnCache)]
+            cache._attn = attn
+            cache._lens_dev = torch.zeros(max(len(attn), 1), dtype=torch.int32, device=attn[0].k.device)
+            cache._lens_host = torch.zeros(max(len(attn), 1), dtype=torch.int32).pin_memory()
+        return cache._attn, cache._lens_dev, cache._lens_host
+
+    def _capture(self, cache, m: int):
+        f, dev = self.fused, self.fused.device
+        attn, lens_dev, _ = self._lens(cache)
+        ids_buf = torch.zeros(m, dtype=torch.long, device=dev)
+        gdn = [c for c in cache.layers if isinstance(c, GDNCache)]
+        # warm-up on a scratch cache of the same shape, on the capture stream (buffers, the
+        # stream's qmm workspace and kernel attributes exist before capture)
+        scratch = f.make_cache(max_len=attn[0].k.shape[0], max_verify=gdn[0].max_verify if gdn else 17)
+        for c, s2 in zip(cache.layers, scratch.layers):
+            if isinstance(c, GDNCache):
+                s2.recording = c.recording
+        _, slens, _ = self._lens(scratch)
+        self._stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(self._stream):
+            f(ids_buf, scratch, slens)
+        self._stream.synchronize()
+        del scratch
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=self._stream):
+            f(ids_buf, cache, lens_dev)
+        # the entry keeps the cache alive: its id (the key) can then not be reused by another
+        # cache while the graph, which holds its buffers' addresses, exists
+        ent = (ids_buf, g, cache)
+        self._graphs[(id(cache), m, tuple(c.recording for c in gdn))] = ent
+        return ent
+
+    @torch.no_grad()
+    def __call__(self, ids: torch.Tensor, cache):
+        m = ids.shape[0]
+        if m > 16:
+            return self.fused(ids, cache)
+        gdn = [c for c in cache.layers if isinstance(c, GDNCache)]
+        key = (id(cache), m, tuple(c.recording for c in gdn))
+        ent = self._graphs.get(key) or self._capture(cache, m)
+        ids_buf, g, _ = ent
+        attn, lens_dev, lens_host = self._lens(cache)
+        if hasattr(cache, "_lens_evt"):
+            cache._lens_evt.synchronize()  # the previous copy out of the pinned buffer is done
+        for i, c in enumerate(attn):
+            lens_host[i] = c.length
+        ids_buf.copy_(ids, non_blocking=True)
+        lens_dev.copy_(lens_host, non_blocking=True)
+        if not hasattr(cache, "_lens_evt"):
+            cache._lens_evt = torch.cuda.Event()
+        cache._lens_evt.record()
+        g.replay()
+        for c in attn:
+            c.length += m
+        for c in gdn:
+            if c.recording:
+                c.fed = m
+        b = self.fused._bufs[m]
+        return b["a"], b["logits"]
+
+    def release(self) -> None:
+        """Drop the captured graphs (e.g. when their caches are discarded)."""
+        self._graphs.clear()
+
+
+__all__ = ["FusedStep", "GraphedStep"]

@@ -28,6 +28,7 @@ from dataclasses import dataclass, replace
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
+from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from .configs import HybridConfig
 from .qmm import dequantize, quantize
@@ -204,10 +205,27 @@ class Cache:
                 return c.length
         return 0
 
+    def reset(self) -> None:
+        """Empty the cache in place (same buffers: captured graphs that use it stay valid)."""
+        for c in self.layers:
+            if isinstance(c, AttnCache):
+                c.length = 0
+            else:
+                c.conv.zero_()
+                c.state.zero_()
+                c.recording = False
+                c.fed = 0
+
 
 # ---------------------------------------------------------------------------------------------
 # layers
 # ---------------------------------------------------------------------------------------------
+# Backends for the module path's attention: the memory-efficient kernel takes the explicit
+# bottom-right causal mask; the cuDNN backend is left out because it builds a new execution plan
+# for every new key length (tens of ms each time a decode loop's cache grows).
+_SDPA_BACKENDS = [SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
+
+
 def _rope(x: torch.Tensor, pos: torch.Tensor, rot: int, theta: float) -> torch.Tensor:
     """Partial rotary embedding (rotate-half) on the first `rot` dims; x [T, H, D] f32."""
     half = rot // 2
@@ -251,9 +269,10 @@ class Attention(nn.Module):
         cache.length = L0 + T
         # queries sit at positions L0 .. L0+T-1 after L0 cached keys: bottom-right causal mask
         causal = pos[:, None] >= torch.arange(L0 + T, device=qg.device)[None, :]
-        o = F.scaled_dot_product_attention(
-            q.to(torch.bfloat16).transpose(0, 1)[None], cache.k[:L0 + T].transpose(0, 1)[None],
-            cache.v[:L0 + T].transpose(0, 1)[None], attn_mask=causal, enable_gqa=True)[0].transpose(0, 1)
+        with sdpa_kernel(_SDPA_BACKENDS):
+            o = F.scaled_dot_product_attention(
+                q.to(torch.bfloat16).transpose(0, 1)[None], cache.k[:L0 + T].transpose(0, 1)[None],
+                cache.v[:L0 + T].transpose(0, 1)[None], attn_mask=causal, enable_gqa=True)[0].transpose(0, 1)
         o = o.float() * torch.sigmoid(gate.float())
         return o.reshape(T, nh * D).to(torch.bfloat16)
 

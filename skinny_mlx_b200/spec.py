@@ -157,10 +157,46 @@ class MTPDrafter:
         self.n_spec = 0
 
 
-def greedy(model, prompt: list[int], max_tokens: int, gaps: list | None = None) -> list[int]:
+class ScriptedDrafter:
+    """Drafts a known greedy continuation `ref`, each proposal replaced by a wrong token with
+    probability 1 - p (seeded): speculative decoding at a chosen acceptance rate.  With random
+    weights an MTP head accepts almost nothing, so this stands in for a trained head when the
+    speculative machinery is timed (K = 2 at p = 0.81 gives the reference's 2.51 tokens/step,
+    docs/flatspec-design.md:60-61)."""
+
+    def __init__(self, ref: list[int], p: float, vocab: int, device, seed: int = 0):
+        self.ref, self.p, self.vocab, self.device = ref, p, vocab, device
+        self.rng = torch.Generator().manual_seed(seed)
+
+    def begin(self, prompt, h, first) -> None:
+        self.pos = 1  # ref[0] is emitted by the prefill
+
+    def draft(self, k: int) -> torch.Tensor:
+        toks = []
+        for i in range(k):
+            j = self.pos + i
+            t = self.ref[j] if j < len(self.ref) else 0
+            if float(torch.rand((), generator=self.rng)) >= self.p:
+                t = (t + 1) % self.vocab
+            toks.append(t)
+        return torch.tensor(toks, dtype=torch.int32).to(self.device, non_blocking=True)
+
+    def update(self, h_kept, new_tokens) -> None:
+        self.pos += len(new_tokens)
+
+
+def _fresh_cache(model, cache):
+    if cache is None:
+        return model.make_cache()
+    cache.reset()
+    return cache
+
+
+def greedy(model, prompt: list[int], max_tokens: int, gaps: list | None = None, cache=None) -> list[int]:
     """Plain greedy decoding, one token per forward (skinny_mlx/spec.py:98-107).  `gaps`, when
-    given, receives each step's (top1 - top2 logit gap, top1 logit), for the near-tie check."""
-    cache = model.make_cache()
+    given, receives each step's (top1 - top2 logit gap, top1 logit), for the near-tie check.
+    `cache` (optional) is reset and reused, e.g. to keep a graph-replayed step's buffers."""
+    cache = _fresh_cache(model, cache)
     _, logits = model(torch.tensor(prompt, device=model.device), cache)
     out = []
     last = logits[-1]
@@ -177,11 +213,13 @@ def greedy(model, prompt: list[int], max_tokens: int, gaps: list | None = None) 
     return out
 
 
-def speculative(model, prompt: list[int], max_tokens: int, drafter, k: int, stats: dict | None = None) -> list[int]:
+def speculative(model, prompt: list[int], max_tokens: int, drafter, k: int, stats: dict | None = None,
+                cache=None) -> list[int]:
     """Greedy-exact speculative decoding (skinny_mlx/spec.py:110-156): each step verifies
     [last token] + K drafts in one forward (M = K+1), accepts the longest matching prefix on the
-    device, emits one bonus token and rolls the hybrid cache back to the accepted prefix."""
-    cache = model.make_cache()
+    device, emits one bonus token and rolls the hybrid cache back to the accepted prefix.
+    `cache` (optional) is reset and reused."""
+    cache = _fresh_cache(model, cache)
     rb = HybridRollback()
     h, logits = model(torch.tensor(prompt, device=model.device), cache)
     out = [int(torch.argmax(logits[-1].float()))]
@@ -203,4 +241,4 @@ def speculative(model, prompt: list[int], max_tokens: int, drafter, k: int, stat
     return out[:max_tokens]
 
 
-__all__ += ["HybridRollback", "MTPDrafter", "greedy", "speculative"]
+__all__ += ["HybridRollback", "MTPDrafter", "ScriptedDrafter", "greedy", "speculative"]

@@ -173,12 +173,14 @@ def test_attn_fused_matches_module_attention(cuda_lib, dev, T, L0):
     ws = torch.zeros(int(cuda_lib.skinny_attn_workspace_bytes(T, nh, nkv, max_len)), dtype=torch.uint8, device=dev)
     xq = torch.empty(int(cuda_lib.skinny_xq_bytes(T, nh * D)), dtype=torch.uint8, device=dev)
     o = torch.empty(T, nh * D, dtype=torch.bfloat16, device=dev)
-    for rep in range(2):  # twice: the workspace counters are left ready for the next call
+    len_dev = torch.tensor([L0], dtype=torch.int32, device=dev)
+    for rep in range(2):  # twice: the workspace counters are left ready; the second call reads L0 on the device
         cb.k[L0:].zero_()
         cb.v[L0:].zero_()
         st = cuda_lib.skinny_attn_fused(_p(proj), proj.stride(0), _p(a.q_norm.weight), _p(a.k_norm.weight), _p(inv),
-                                        cfg.rotary_dim, ctypes.c_float(cfg.rms_eps), _p(cb.k), _p(cb.v), L0, T, nh,
-                                        nkv, max_len, _p(ws), ws.numel(), _p(xq), _p(o), _stream())
+                                        cfg.rotary_dim, ctypes.c_float(cfg.rms_eps), _p(cb.k), _p(cb.v), L0,
+                                        _p(len_dev) if rep == 1 else None, T, nh, nkv, max_len, _p(ws), ws.numel(),
+                                        _p(xq), _p(o), _stream())
         assert st == 0
         torch.cuda.synchronize()
         err = ((o.float() - ref.float()).abs().max() / ref.float().abs().max()).item()
@@ -191,3 +193,27 @@ def test_attn_fused_matches_module_attention(cuda_lib, dev, T, L0):
         mpad = 8 if T <= 8 else 16
         got = xq.cpu().numpy().reshape(nh * D // 64, -1)
         assert np.array_equal(got, quant.xq_blocks(o.float().cpu().numpy(), mpad))
+
+
+def test_graphed_step_equals_eager_and_keeps_spec_exact(cuda_lib, dev):
+    """The CUDA-graph replay of the fused step (device-side cache lengths) reproduces the eager
+    fused step bit for bit over a greedy run, and speculative decoding through it equals greedy."""
+    from skinny_mlx_b200.fused import FusedStep, GraphedStep
+    from skinny_mlx_b200.patch import patch_model
+    from skinny_mlx_b200.spec import ScriptedDrafter, greedy, speculative
+    from test_model_patch import _exact_or_near_tie
+
+    m = HybridModel(SMALL, seed=0, device=dev)
+    patch_model(m)
+    f = FusedStep(m)
+    gs = GraphedStep(f)
+    gaps = []
+    ref = greedy(f, PROMPT, 24, gaps)
+    cache = gs.make_cache()
+    assert greedy(gs, PROMPT, 24, cache=cache) == ref
+    assert greedy(gs, PROMPT, 24, cache=cache) == ref  # same cache reset and replayed again
+    for k, p in ((2, 0.8), (3, 0.6)):
+        st = {}
+        got = speculative(gs, PROMPT, 24, ScriptedDrafter(ref, p, SMALL.vocab, dev, seed=k), k, st, cache=cache)
+        assert _exact_or_near_tie(ref, got, gaps)
+        assert st["accepted"] > 0
