@@ -179,6 +179,7 @@ class StackRunner:
         self.xs = {k: self.x_all[self.koff[k]: self.koff[k] + m * k].view(m, k) for k in ks}
         self.outs = [torch.empty(m, n, dtype=torch.bfloat16, device=dev) for _, n, _ in shapes]
         self.stream = torch.cuda.Stream(dev)
+        self.stream.wait_stream(torch.cuda.current_stream(dev))  # x was made on the current stream
         self._qmm = skinny_qmm
         with torch.cuda.stream(self.stream):
             for _ in range(2):
@@ -309,6 +310,7 @@ def config3_step_costs(model, dev, kv_len=2048, ms=(1, 6, 8, 16), steps=20):
                 c.recording = True
         ids = torch.randint(0, model.cfg.vocab, (m,), generator=gen, device=dev)
         s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))  # inputs were made on the current stream
 
         def step():
             for c in cache.layers:
@@ -386,17 +388,22 @@ def config4_spec(model, dev, n_tokens=256, prompt_len=512, fwd=None):
 
 
 def config5_steps(world: int, rank: int, dev, kv_len=4096, ms=(8, 16), steps=5, cfg=None):
-    """the 64-layer dense model, column-parallel over the job's ranks (NCCL
-    all-gather of every projection's output), one verify step at M tokens with `kv_len` cached
-    tokens, captured with its collectives in one CUDA graph when possible; max over ranks."""
+    """the 64-layer dense model, column-parallel over the job's ranks, one
+    verify step at M tokens with `kv_len` cached tokens: the fused step (DenseFusedStep: NCCL
+    all-gathers of digit blocks and output shards), and at the first M the module-by-module
+    forward for comparison; each captured with its collectives in one CUDA graph when possible;
+    max over ranks."""
     from skinny_mlx_b200.configs import DENSE_64L, packed_bytes
     from skinny_mlx_b200.dense import DenseModel
     from skinny_mlx_b200.patch import patch_model
+
+    from skinny_mlx_b200.dense_fused import DenseFusedStep
 
     cfg = cfg or DENSE_64L
     t0 = time.perf_counter()
     model = DenseModel(cfg, rank, world, seed=21, device=dev)
     patch_model(model)
+    fused = DenseFusedStep(model)
     torch.cuda.empty_cache()
     build_s = time.perf_counter() - t0
     per_layer = (packed_bytes((cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim, cfg.hidden)
@@ -407,18 +414,20 @@ def config5_steps(world: int, rank: int, dev, kv_len=4096, ms=(8, 16), steps=5, 
            "build_s": round(build_s, 1)}
     gen = torch.Generator(device=dev).manual_seed(9)
     peak, _ = measured_hbm_peak()
-    for m in ms:
+    runs = [(m, "fused", fused) for m in ms] + [(ms[0], "module_path", model)]
+    for m, kind, fwd in runs:
         caches = model.make_cache(kv_len + 32)
         for c in caches:
             c.k.normal_(generator=gen)
             c.v.normal_(generator=gen)
         ids = torch.randint(0, cfg.vocab, (m,), generator=gen, device=dev)
         s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))  # inputs were made on the current stream
 
         def step():
             for c in caches:
                 c.length = kv_len
-            model(ids, caches)
+            fwd(ids, caches)
 
         with torch.cuda.stream(s):
             step()
@@ -445,9 +454,10 @@ def config5_steps(world: int, rank: int, dev, kv_len=4096, ms=(8, 16), steps=5, 
             e1.record(s)
         e1.synchronize()
         ms_step = max_over_ranks(e0.elapsed_time(e1), world) / steps
-        out[f"M{m}"] = {"ms_per_step": round(ms_step, 4), "tok_s": round(m / (ms_step * 1e-3), 1),
-                        "cuda_graph": graph is not None,
-                        "hbm_frac_of_weight_floor": round(total / world / (ms_step * 1e-3) / 1e9 / peak, 4)}
+        out[f"M{m}" if kind == "fused" else f"M{m}_{kind}"] = {
+            "ms_per_step": round(ms_step, 4), "tok_s": round(m / (ms_step * 1e-3), 1),
+            "cuda_graph": graph is not None,
+            "hbm_frac_of_weight_floor": round(total / world / (ms_step * 1e-3) / 1e9 / peak, 4)}
         del graph, caches
         torch.cuda.empty_cache()
     del model

@@ -106,16 +106,20 @@ size_t skinny_xq_bytes(int M, int K);
  * qmm's input format, so a step's elementwise work and its next matmul need no x-prep launch or
  * activation round trip (the B200 form of the glue between the reference model's projections).
  *   mode 0: h = x (+ d if d != NULL; h written to h_out when given), a = bf16(h / rms(h) * (1 + w))
- *           with w f32 [K] (zero-centred RMSNorm, eps)
+ *           with w f32 [K] (zero-centred RMSNorm, eps); K <= 16384, x and d 16-byte aligned with
+ *           leading dimensions (and dseg_stride) multiples of 8
  *   mode 1: a = bf16(silu(g) * u), x = [g | u] with 2K columns (SwiGLU)
  *   mode 2: a = x
+ * d may be column-sharded as an all-gather of per-rank [M, N/G] outputs leaves it: with
+ * dseg_cols > 0 (a multiple of 64 dividing K), column c of token t is read at
+ * (c / dseg_cols) * dseg_stride + t * ldd + c % dseg_cols; dseg_cols = 0: plain rows.
  * x, d, h_out bf16 rows with leading dimensions ldx, ldd, ldh (even, 4-byte aligned); xq receives
  * skinny_xq_bytes(M, K) bytes (16-byte aligned); a_out (mode 0, may be NULL) receives a as bf16
  * [M, K].  h_out and a_out must not overlap x or d (SKINNY_ERR_INVALID_ARG): column chunks of a
  * row are written while other chunks of it are still being read.  Launched with programmatic
  * dependent launch: the next launch on the stream may start before this one ends. */
-int skinny_prep(int mode, const void* x, int ldx, const void* d, int ldd, void* h_out, int ldh,
-                const float* w, float eps, int M, int K, void* xq, void* a_out, void* stream);
+int skinny_prep(int mode, const void* x, int ldx, const void* d, int ldd, int dseg_cols, long long dseg_stride,
+                void* h_out, int ldh, const float* w, float eps, int M, int K, void* xq, void* a_out, void* stream);
 
 /* One Gated DeltaNet mixer from its fused input projection to the prepared input of out_proj,
  * in one launch: causal depthwise conv (window W <= 4, weights conv_w [C, W+1] f32) + SiLU,
@@ -136,7 +140,8 @@ int skinny_gdn_fused(const void* proj, int ldp, void* conv, void* conv_full, con
                      void* stream);
 
 /* Bytes of the workspace skinny_attn_fused needs for a KV cache of max_len positions (0 when the
- * shape is not supported).  Zero-filled before first use; a completed call leaves it reusable. */
+ * shape is not supported).  It holds per-chunk partial results between the call's two launches
+ * and no state between calls. */
 size_t skinny_attn_workspace_bytes(int T, int n_heads, int n_kv_heads, int max_len);
 
 /* One gated full-attention mixer from its fused projection to the prepared input of o_proj, in
@@ -146,17 +151,19 @@ size_t skinny_attn_workspace_bytes(int T, int n_heads, int n_kv_heads, int max_l
  *          positions L0 .. L0+T-1; k (bf16) and v are appended to k_cache / v_cache
  *          [max_len, n_kv_heads, 128] (16-byte aligned) at L0 .. L0+T-1;
  *   o    = causal (bottom-right) grouped-query softmax(q k^T / sqrt(128)) v over positions
- *          0 .. L0+t, then bf16(bf16(o) sigmoid(gate)), written as qmm input digits to xq
- *          (K = n_heads*128) and, when o_out != NULL, as bf16 [T, n_heads*128].
- * proj [T, ldp] bf16 (16-byte aligned, ldp % 8 == 0) = per query head [q (128) | gate (128)] |
- * k (n_kv*128) | v (n_kv*128).
+ *          0 .. L0+t, then (gated = 1) bf16(bf16(o) sigmoid(gate)) or (gated = 0) bf16(o),
+ *          written as qmm input digits to xq (K = n_heads*128) and, when o_out != NULL, as bf16
+ *          [T, n_heads*128].
+ * proj [T, ldp] bf16 (16-byte aligned, ldp % 8 == 0) = per query head [q (128) | gate (128)]
+ * (gated) or q (128) | k (n_kv*128) | v (n_kv*128).
  * head_dim 128, T * n_heads / n_kv_heads <= 128.  The caller advances its cache length by T.
  * length_dev (may be NULL): when given, the cache length L0 is read from this device int32 when
  * the kernel runs (L0 argument ignored), so that one captured launch (CUDA graph) serves every
  * length; a device length outside [0, max_len - T] makes the launch touch nothing.
- * Launched with programmatic dependent launch.  No counterpart in the reference's own code. */
+ * Two launches (per-chunk partials, then their merge), both with programmatic dependent launch.
+ * No counterpart in the reference's own code. */
 int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
-                      const float* inv_freq, int rot, float eps, void* k_cache, void* v_cache, int L0,
+                      const float* inv_freq, int rot, int gated, float eps, void* k_cache, void* v_cache, int L0,
                       const int32_t* length_dev, int T, int n_heads, int n_kv_heads, int max_len, void* workspace,
                       size_t workspace_bytes, void* xq, void* o_out, void* stream);
 

@@ -40,13 +40,13 @@ SIGNATURES = {
     "skinny_qmm_w4g64_grouped": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                          c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "skinny_xq_bytes": (c_size_t, [c_int, c_int]),
-    "skinny_prep": (c_int, [c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, ctypes.c_float,
-                            c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "skinny_prep": (c_int, [c_int, c_void_p, c_int, c_void_p, c_int, c_int, ctypes.c_longlong, c_void_p, c_int,
+                            c_void_p, ctypes.c_float, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "skinny_gdn_fused": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                  ctypes.c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                  c_int, c_void_p, c_void_p]),
     "skinny_attn_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
-    "skinny_attn_fused": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, ctypes.c_float, c_void_p,
+    "skinny_attn_fused": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, ctypes.c_float, c_void_p,
                                   c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t,
                                   c_void_p, c_void_p, c_void_p]),
     "skinny_qmm_w4g64_prepared": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,

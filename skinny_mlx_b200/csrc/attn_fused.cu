@@ -1,23 +1,24 @@
-// One gated full-attention mixer of the hybrid model, from its fused q|gate / k / v projection to
-// the prepared input of o_proj (the B200 form of the reference model's attention layer between
-// its projections, run during a verify step of T <= 16 tokens against a KV cache):
+// One full-attention mixer, from its fused projection to the prepared input of o_proj (the B200
+// form of the attention layers of the model the reference patches, run during a verify step of
+// T <= 16 tokens against a KV cache):
 //
 //   q, k  = RoPE( bf16(rmsnorm(q|k) * (1 + w)) )  on the first `rot` dims, positions L0 .. L0+T-1
 //   cache[L0 .. L0+T-1] = bf16(k), v                                (KV append)
 //   o     = softmax(q k^T / sqrt(128), causal bottom-right) v        (GQA: rep = n_heads / n_kv)
-//   o     = bf16( bf16(o) * sigmoid(gate) )  -> digits of o for o_proj (qmm input format)
+//   o     = bf16( bf16(o) * sigmoid(gate) )  (gated layers; else bf16(o))  -> digits of o for o_proj
 //
-// Split over keys (flash-decode style): CTA (chunk, row group, kv head) takes 128 keys of one KV
-// head and up to 16 query rows (row = t * rep + q head within the group), computes the chunk's
-// row maxima, sums and unnormalised outputs in f32 and publishes them; the CTA that finishes a
-// (row group, kv head) last merges the chunks in chunk order (deterministic) and finishes the
-// rows.  There is no waiting on other CTAs: the merge is done by whichever CTA arrives last.
-// Every CTA recomputes the normalised, rotated q of its rows and k of the new keys in its chunk;
-// the new keys are appended to the cache by the row-group-0 CTA of their chunk (positions >= L0
-// are only ever written, positions < L0 only read, so chunks never race).
-//
-// Launched with programmatic dependent launch (the next launch may start at once; this one waits
-// for the previous grid before its first global read).
+// Two launches, split over keys (flash-decode style):
+//   attn_chunk_kernel  CTA (128-key chunk, KV head): loads the chunk's keys and values once,
+//                      then for every group of 16 query rows (row = t * rep + q head in the
+//                      group) computes the chunk's row maxima, sums and unnormalised outputs on
+//                      bf16 tensor-core tiles and publishes them.  The new keys of the chunk are
+//                      normalised, rotated and appended to the cache by that CTA (positions >= L0
+//                      are only written, positions < L0 only read, so chunks never race).
+//   attn_merge_kernel  CTA (4 rows of a row group, KV head): merges the chunks (a fixed order:
+//                      deterministic), applies the gate and writes the digits.
+// No CTA waits on another; the merge launch waits for the chunk launch through programmatic
+// dependent launch, like every launch of the step (the next launch may start at once; a kernel
+// waits for the previous grid before its first global read).
 #include <cfloat>
 #include <cstdint>
 #include <cuda_bf16.h>
@@ -31,18 +32,17 @@ namespace skinny {
 
 constexpr int kAtD = 128;
 constexpr int kAtChunk = 128;        // keys per CTA
-constexpr int kAtRG = 16;            // query rows per CTA
+constexpr int kAtRG = 16;            // query rows per tensor-core tile
 constexpr int kAtThreads = 256;
 constexpr int kAtWarps = kAtThreads / 32;
 constexpr int kAtStride = kAtD + 8;   // bf16 per shared row: 272 bytes, ldmatrix conflict-free
 constexpr int kAtPart = kAtD + 4;     // floats per published row: m, l, (pad), o[128] (16-byte aligned)
-constexpr int kAtMergePass = 8;       // chunk partials whose loads a merging thread issues together
 constexpr int kAtMaxRG = 8;           // row groups per KV head (rep * T <= 128)
-constexpr int kAtCntWords = 64 * kAtMaxRG;
-constexpr size_t kAtPartOff = kAtCntWords * 4;
+constexpr int kAtMergePass = 9;       // chunk partials whose loads a merging thread issues together
+constexpr int kAtMaxT = 16;
 
 struct AttnParams {
-  const __nv_bfloat16* proj;  // [T, ldp]: q|gate (nh x 2 x 128, per head q then gate) | k (nkv x 128) | v
+  const __nv_bfloat16* proj;  // [T, ldp]: q heads (q | gate per head when gated) | k (nkv x 128) | v
   int ldp;
   const float* qn_w;          // [128] zero-centred RMSNorm weights
   const float* kn_w;
@@ -51,22 +51,26 @@ struct AttnParams {
   __nv_bfloat16* kc;          // [max_len, nkv, 128]
   __nv_bfloat16* vc;
   int T, L0, nh, nkv, rot, nchunks, nrg, max_len;
+  int gated;                  // 1: per head [q | gate] and o *= sigmoid(gate); 0: q heads only
   const int* len_dev;         // if set: the cache length is read here (grid sized for max_len)
   float* part;                // [nkv, nrg, nchunks, 16, kAtPart]: per row m, l, -, -, o[128]
-  uint32_t* cnt;              // [nkv * kAtMaxRG], zero on entry, left zero
   uint8_t* xq;                // o_proj input digits (K = nh * 128)
   __nv_bfloat16* o_out;       // [T, nh * 128] or null
 };
 
+constexpr int kAtMaxRows = kAtRG * kAtMaxRG;  // query rows of one KV head (T * rep)
+
+// followed in dynamic shared memory by the KV head's R query rows as projected, bf16 [R][128]
+// (staged once per CTA)
 struct AttnSmem {
+  float cs[kAtMaxT][kAtD / 2][2];         // cos / sin of (position, frequency), computed once
   __nv_bfloat16 q[kAtRG][kAtStride];      // rotated queries of the row group
   __nv_bfloat16 k[kAtChunk][kAtStride];   // keys of the chunk
   __nv_bfloat16 v[kAtChunk][kAtStride];   // values of the chunk
   __nv_bfloat16 pr[kAtRG][kAtStride];     // probabilities (bf16, as a flash kernel rounds them)
-  float s[kAtRG][kAtChunk];               // scores (log2 domain); reused for the merged rows
+  float s[kAtRG][kAtChunk];               // scores (log2 domain)
   float stage[kAtWarps][kAtD];
   float rowm[kAtRG], rowl[kAtRG];
-  int last;
 };
 
 // ---- warp-level bf16 tensor-core tiles (m16n8k16, f32 accumulate)
@@ -92,9 +96,10 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
 __device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 // Warp-collective: x holds dims lane + 32 i of one head row (bf16-exact).  Returns the row after
-// zero-centred RMSNorm (-> bf16) and RoPE at position pos on the first rot dims (-> bf16).
-__device__ __forceinline__ void norm_rope(float (&x)[4], const float* w, float eps, const float* inv_freq,
-                                          int rot, int pos, float* stage, int lane) {
+// zero-centred RMSNorm (-> bf16) and RoPE on the first rot dims (-> bf16), the rotation's cos /
+// sin taken from cs[j] = (cos, sin)(pos * inv_freq[j]) for the row's position.
+__device__ __forceinline__ void norm_rope_tab(float (&x)[4], const float* w, float eps, const float (*cs)[2], int rot,
+                                              float* stage, int lane) {
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) ss = fmaf(x[i], x[i], ss);
@@ -114,63 +119,61 @@ __device__ __forceinline__ void norm_rope(float (&x)[4], const float* w, float e
     const int d = lane + 32 * i;
     if (d < rot) {
       const int j = d < half ? d : d - half;
-      const float ang = static_cast<float>(pos) * inv_freq[j];
-      float sn, cs;
-      sincosf(ang, &sn, &cs);
-      x[i] = d < half ? x[i] * cs - stage[d + half] * sn : x[i] * cs + stage[d - half] * sn;
+      const float c = cs[j][0], sn = cs[j][1];
+      x[i] = d < half ? x[i] * c - stage[d + half] * sn : x[i] * c + stage[d - half] * sn;
     }
     x[i] = bfr(x[i]);
   }
   __syncwarp();
 }
 
-__global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_constant__ AttnParams p) {
+// The cache length: a kernel argument, or read from device memory so that one captured launch
+// serves every length (the chunk grid then covers max_len and the surplus chunks leave).
+// Returns -1 for a device length out of range (the launch then touches nothing).
+__device__ __forceinline__ int attn_length(const AttnParams& p) {
+  const int L0 = p.len_dev ? *p.len_dev : p.L0;
+  return (L0 < 0 || L0 + p.T > p.max_len) ? -1 : L0;
+}
+
+__device__ __forceinline__ float* part_row(const AttnParams& p, int kvh, int rg, int chunk, int rr) {
+  return p.part + (((static_cast<size_t>(kvh) * p.nrg + rg) * p.nchunks + chunk) * kAtRG + rr) * kAtPart;
+}
+
+__global__ void __launch_bounds__(kAtThreads) attn_chunk_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(16) uint8_t at_smem_raw[];
   AttnSmem& sm = *reinterpret_cast<AttnSmem*>(at_smem_raw);
-  const int chunk = blockIdx.x, rg = blockIdx.y, kvh = blockIdx.z;
+  const int chunk = blockIdx.x, kvh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rep = p.nh / p.nkv;
   const int R = p.T * rep;
-  const int rbase = rg * kAtRG;
-  const int nrows = min(kAtRG, R - rbase);
-  const int qkw = p.nh * 2 * kAtD;  // column of k in proj
+  const int qstride = p.gated ? 2 * kAtD : kAtD;  // proj columns per query head
+  const int qkw = p.nh * qstride;                  // column of k in proj
+  __nv_bfloat16 (*qraw)[kAtD] = reinterpret_cast<__nv_bfloat16 (*)[kAtD]>(at_smem_raw + sizeof(AttnSmem));
   pdl_launch_dependents();
   pdl_wait_prior_grid();
-  // the cache length: a kernel argument, or read from device memory so that one captured
-  // launch serves every length (the grid then covers max_len and the surplus chunks leave)
-  const int L0 = p.len_dev ? *p.len_dev : p.L0;
-  if (L0 < 0 || L0 + p.T > p.max_len) return;  // a device length out of range: no access at all
-  const int nchunks = p.len_dev ? (L0 + p.T + kAtChunk - 1) / kAtChunk : p.nchunks;
+  const int L0 = attn_length(p);
+  if (L0 < 0) return;
+  const int nchunks = (L0 + p.T + kAtChunk - 1) / kAtChunk;
   if (chunk >= nchunks) return;
   const int Ltot = L0 + p.T;
   const int k0 = chunk * kAtChunk;
   const int nk = min(kAtChunk, Ltot - k0);
 
-  // output gates of the rows this thread finishes if this CTA merges (row tid / 16, 8 dims)
-  float gate_pre[8];
-  {
-    const int rr = tid / 16, d0 = (tid % 16) * 8;
-    if (rr < nrows) {
-      const int r = rbase + rr, t = r / rep, hq = kvh * rep + r % rep;
-      const uint4 gw = *reinterpret_cast<const uint4*>(p.proj + static_cast<size_t>(t) * p.ldp + hq * 2 * kAtD + kAtD + d0);
-      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gw);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(g2[i]);
-        gate_pre[2 * i] = f.x;
-        gate_pre[2 * i + 1] = f.y;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) gate_pre[i] = 0.f;
-    }
-  }
-
-  // ---- cached keys and values of the chunk: every thread issues all its 16-byte loads first
+  // ---- cached keys and values of the chunk, and the KV head's query rows: every thread issues
+  // all its 16-byte loads first
   {
     constexpr int kPieces = kAtChunk * (kAtD / 8);  // 16-byte pieces per matrix
     constexpr int kPer = kPieces / kAtThreads;
-    uint4 kw[kPer], vw[kPer];
+    constexpr int kQPer = kAtMaxRows * (kAtD / 8) / kAtThreads;
+    uint4 kw[kPer], vw[kPer], qw[kQPer];
+#pragma unroll
+    for (int u = 0; u < kQPer; ++u) {
+      const int e = tid + u * kAtThreads, r = e >> 4, pc = e & 15;
+      if (r < R) {
+        const int t = r / rep, hq = kvh * rep + r % rep;
+        qw[u] = *reinterpret_cast<const uint4*>(p.proj + static_cast<size_t>(t) * p.ldp + hq * qstride + 8 * pc);
+      }
+    }
 #pragma unroll
     for (int u = 0; u < kPer; ++u) {
       const int e = tid + u * kAtThreads, j = e >> 4, pc = e & 15;
@@ -191,21 +194,22 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
       *reinterpret_cast<uint4*>(&sm.k[j][8 * pc]) = kw[u];
       *reinterpret_cast<uint4*>(&sm.v[j][8 * pc]) = vw[u];
     }
-  }
-  // ---- query rows: normalised, rotated, bf16
-  for (int rr = warp; rr < nrows; rr += kAtWarps) {
-    const int r = rbase + rr, t = r / rep, hq = kvh * rep + r % rep;
-    const __nv_bfloat16* src = p.proj + static_cast<size_t>(t) * p.ldp + hq * 2 * kAtD;
-    float x[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(src[lane + 32 * i]);
-    norm_rope(x, p.qn_w, p.eps, p.inv_freq, p.rot, L0 + t, sm.stage[warp], lane);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) sm.q[rr][lane + 32 * i] = __float2bfloat16_rn(x[i]);
+    for (int u = 0; u < kQPer; ++u) {
+      const int e = tid + u * kAtThreads, r = e >> 4, pc = e & 15;
+      if (r < R) *reinterpret_cast<uint4*>(&qraw[r][8 * pc]) = qw[u];
+    }
+    // rotation table for the T positions of the verify
+    for (int i = tid; i < p.T * (p.rot >> 1); i += kAtThreads) {
+      const int t = i / (p.rot >> 1), j = i - t * (p.rot >> 1);
+      float sn, c;
+      sincosf(static_cast<float>(L0 + t) * p.inv_freq[j], &sn, &c);
+      sm.cs[t][j][0] = c;
+      sm.cs[t][j][1] = sn;
+    }
   }
-  for (int i = tid; i < (kAtRG - nrows) * kAtD; i += kAtThreads)  // rows past the group: zero
-    sm.q[nrows + i / kAtD][i % kAtD] = __float2bfloat16_rn(0.f);
-  // ---- new keys in the chunk (positions L0 .. L0+T-1): warp per key
+  __syncthreads();
+  // ---- new keys in the chunk (positions L0 .. L0+T-1): warp per key, appended to the cache
   {
     const int jn0 = max(L0 - k0, 0);
     for (int j = jn0 + warp; j < nk; j += kAtWarps) {
@@ -218,7 +222,7 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
         x[i] = __bfloat162float(src[kvh * kAtD + lane + 32 * i]);
         vb[i] = src[p.nkv * kAtD + kvh * kAtD + lane + 32 * i];
       }
-      norm_rope(x, p.kn_w, p.eps, p.inv_freq, p.rot, pos, sm.stage[warp], lane);
+      norm_rope_tab(x, p.kn_w, p.eps, sm.cs[t], p.rot, sm.stage[warp], lane);
       const size_t off = (static_cast<size_t>(pos) * p.nkv + kvh) * kAtD;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -226,200 +230,252 @@ __global__ void __launch_bounds__(kAtThreads) attn_fused_kernel(const __grid_con
         const __nv_bfloat16 kb = __float2bfloat16_rn(x[i]);
         sm.k[j][d] = kb;
         sm.v[j][d] = vb[i];
-        if (rg == 0) {
-          p.kc[off + d] = kb;
-          p.vc[off + d] = vb[i];
-        }
+        p.kc[off + d] = kb;
+        p.vc[off + d] = vb[i];
       }
     }
   }
-  __syncthreads();
-  // ---- scores on tensor cores (log2 domain): warp w takes keys 16w .. 16w+15 for the 16 rows
-  {
-    const int g = lane >> 2, cq = lane & 3;
-    const uint32_t a_addr =
-        smem_u32(&sm.q[0][0]) + (((lane & 7) + 8 * ((lane >> 3) & 1)) * kAtStride + 8 * (lane >> 4)) * 2;
-    const uint32_t b_addr =
-        smem_u32(&sm.k[0][0]) + ((16 * warp + (lane & 7) + 8 * (lane >> 4)) * kAtStride + 8 * ((lane >> 3) & 1)) * 2;
-    float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+
+  const int g = lane >> 2, cq = lane & 3;
+  for (int rg = 0; rg * kAtRG < R; ++rg) {
+    const int rbase = rg * kAtRG;
+    const int nrows = min(kAtRG, R - rbase);
+    // ---- query rows of the group: normalised, rotated, bf16
+    for (int rr = warp; rr < nrows; rr += kAtWarps) {
+      const int r = rbase + rr, t = r / rep;
+      float x[4];
 #pragma unroll
-    for (int ks = 0; ks < kAtD / 16; ++ks) {
-      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-      ldsm_x4(a_addr + ks * 32, a0, a1, a2, a3);
-      ldsm_x4(b_addr + ks * 32, b0, b1, b2, b3);
-      mma_bf16(c[0], a0, a1, a2, a3, b0, b1);
-      mma_bf16(c[1], a0, a1, a2, a3, b2, b3);
+      for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(qraw[r][lane + 32 * i]);
+      norm_rope_tab(x, p.qn_w, p.eps, sm.cs[t], p.rot, sm.stage[warp], lane);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sm.q[rr][lane + 32 * i] = __float2bfloat16_rn(x[i]);
     }
-    const float sc = rsqrtf(static_cast<float>(kAtD)) * 1.4426950408889634f;
+    for (int i = tid; i < (kAtRG - nrows) * kAtD; i += kAtThreads) {  // rows past the group: zero
+      sm.q[nrows + i / kAtD][i % kAtD] = __float2bfloat16_rn(0.f);
+      sm.pr[nrows + i / kAtD][i % kAtD] = __float2bfloat16_rn(0.f);
+    }
+    __syncthreads();
+    // ---- scores on tensor cores (log2 domain): warp w takes keys 16w .. 16w+15 for the 16 rows
+    {
+      const uint32_t a_addr =
+          smem_u32(&sm.q[0][0]) + (((lane & 7) + 8 * ((lane >> 3) & 1)) * kAtStride + 8 * (lane >> 4)) * 2;
+      const uint32_t b_addr =
+          smem_u32(&sm.k[0][0]) + ((16 * warp + (lane & 7) + 8 * (lane >> 4)) * kAtStride + 8 * ((lane >> 3) & 1)) * 2;
+      float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int rr = g + 8 * (e >> 1), j = 16 * warp + 8 * nt + 2 * cq + (e & 1);
-        if (rr < nrows) {
-          const int t = (rbase + rr) / rep;
-          const bool vis = j < nk && k0 + j <= L0 + t;
-          sm.s[rr][j] = vis ? c[nt][e] * sc : -INFINITY;
-        }
+      for (int ks = 0; ks < kAtD / 16; ++ks) {
+        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+        ldsm_x4(a_addr + ks * 32, a0, a1, a2, a3);
+        ldsm_x4(b_addr + ks * 32, b0, b1, b2, b3);
+        mma_bf16(c[0], a0, a1, a2, a3, b0, b1);
+        mma_bf16(c[1], a0, a1, a2, a3, b2, b3);
       }
-  }
-  __syncthreads();
-  // ---- chunk softmax per row (warp per row)
-  for (int rr = warp; rr < nrows; rr += kAtWarps) {
-    float sv[4];
-    float m = -INFINITY;
+      const float sc = rsqrtf(static_cast<float>(kAtD)) * 1.4426950408889634f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      sv[i] = sm.s[rr][lane + 32 * i];
-      m = fmaxf(m, sv[i]);
-    }
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-    float l = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const __nv_bfloat16 e = __float2bfloat16_rn(m == -INFINITY ? 0.f : exp2f(sv[i] - m));
-      sm.pr[rr][lane + 32 * i] = e;
-      l += __bfloat162float(e);  // the sum of the probabilities as the products use them
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
-    if (lane == 0) {
-      sm.rowm[rr] = m;
-      sm.rowl[rr] = l;
-    }
-  }
-  __syncthreads();
-  for (int i = tid; i < (kAtRG - nrows) * kAtD; i += kAtThreads)
-    sm.pr[nrows + i / kAtD][i % kAtD] = __float2bfloat16_rn(0.f);
-  __syncthreads();
-  // ---- unnormalised outputs on tensor cores: warp w takes dims 16w .. 16w+15; publish
-  {
-    const int g = lane >> 2, cq = lane & 3;
-    const uint32_t a_addr =
-        smem_u32(&sm.pr[0][0]) + (((lane & 7) + 8 * ((lane >> 3) & 1)) * kAtStride + 8 * (lane >> 4)) * 2;
-    const uint32_t b_addr =
-        smem_u32(&sm.v[0][0]) + (((lane & 7) + 8 * ((lane >> 3) & 1)) * kAtStride + 16 * warp + 8 * (lane >> 4)) * 2;
-    float o[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-    for (int ks = 0; ks < kAtChunk / 16; ++ks) {
-      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-      ldsm_x4(a_addr + ks * 32, a0, a1, a2, a3);
-      ldsm_x4_t(b_addr + ks * 16 * kAtStride * 2, b0, b1, b2, b3);
-      mma_bf16(o[0], a0, a1, a2, a3, b0, b1);
-      mma_bf16(o[1], a0, a1, a2, a3, b2, b3);
-    }
-    float* base = p.part + ((static_cast<size_t>(kvh) * p.nrg + rg) * nchunks + chunk) * kAtRG * kAtPart;
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int rr = g + 8 * hf;
-        if (rr < nrows)
-          *reinterpret_cast<float2*>(base + static_cast<size_t>(rr) * kAtPart + 4 + 16 * warp + 8 * nt + 2 * cq) =
-              make_float2(o[nt][2 * hf], o[nt][2 * hf + 1]);
-      }
-    if (tid < nrows) {
-      base[static_cast<size_t>(tid) * kAtPart] = sm.rowm[tid];
-      base[static_cast<size_t>(tid) * kAtPart + 1] = sm.rowl[tid];
-    }
-  }
-  // Publish: the block's writes are ordered before thread 0's release-acquire increment (the
-  // barrier makes them visible to thread 0; the release is cumulative), and the last arriver's
-  // acquire makes every chunk's partials visible to it.
-  __syncthreads();
-  if (tid == 0) {
-    uint32_t prev;
-    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;"
-                 : "=r"(prev)
-                 : "l"(p.cnt + kvh * kAtMaxRG + rg)
-                 : "memory");
-    sm.last = prev == static_cast<uint32_t>(nchunks - 1);
-  }
-  __syncthreads();
-  if (!sm.last) return;
-  // ---- merge the chunks (chunk order, passes of kAtMergePass), gate, digits
-  {
-    const int rr = tid / 16, d0 = (tid % 16) * 8;
-    if (rr < nrows) {
-      const float* base = p.part + (static_cast<size_t>(kvh) * p.nrg + rg) * nchunks * kAtRG * kAtPart +
-                          static_cast<size_t>(rr) * kAtPart;
-      const size_t cstride = static_cast<size_t>(kAtRG) * kAtPart;
-      float M = -INFINITY, L = 0.f, acc[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-      for (int c0 = 0; c0 < nchunks; c0 += kAtMergePass) {
-        float mv[kAtMergePass], lv[kAtMergePass];
-        float4 ov[kAtMergePass][2];
-#pragma unroll
-        for (int u = 0; u < kAtMergePass; ++u) {
-          const int c = c0 + u;
-          if (c < nchunks) {
-            const float* row = base + c * cstride;
-            mv[u] = __ldcg(row);
-            lv[u] = __ldcg(row + 1);
-            ov[u][0] = __ldcg(reinterpret_cast<const float4*>(row + 4 + d0));
-            ov[u][1] = __ldcg(reinterpret_cast<const float4*>(row + 8 + d0));
-          } else {
-            mv[u] = -INFINITY;
-            lv[u] = 0.f;
-            ov[u][0] = ov[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int e = 0; e < 4; ++e) {
+          const int rr = g + 8 * (e >> 1), j = 16 * warp + 8 * nt + 2 * cq + (e & 1);
+          if (rr < nrows) {
+            const int t = (rbase + rr) / rep;
+            const bool vis = j < nk && k0 + j <= L0 + t;
+            sm.s[rr][j] = vis ? c[nt][e] * sc : -INFINITY;
           }
         }
-        float Mn = M;
+    }
+    __syncthreads();
+    // ---- chunk softmax per row (warp per row); probabilities rounded to bf16
+    for (int rr = warp; rr < nrows; rr += kAtWarps) {
+      float sv[4];
+      float m = -INFINITY;
 #pragma unroll
-        for (int u = 0; u < kAtMergePass; ++u) Mn = fmaxf(Mn, mv[u]);
-        const float alpha = M == -INFINITY ? 0.f : exp2f(M - Mn);
-        L *= alpha;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] *= alpha;
-#pragma unroll
-        for (int u = 0; u < kAtMergePass; ++u) {
-          const float wgt = mv[u] == -INFINITY ? 0.f : exp2f(mv[u] - Mn);
-          L = fmaf(wgt, lv[u], L);
-          acc[0] = fmaf(wgt, ov[u][0].x, acc[0]);
-          acc[1] = fmaf(wgt, ov[u][0].y, acc[1]);
-          acc[2] = fmaf(wgt, ov[u][0].z, acc[2]);
-          acc[3] = fmaf(wgt, ov[u][0].w, acc[3]);
-          acc[4] = fmaf(wgt, ov[u][1].x, acc[4]);
-          acc[5] = fmaf(wgt, ov[u][1].y, acc[5]);
-          acc[6] = fmaf(wgt, ov[u][1].z, acc[6]);
-          acc[7] = fmaf(wgt, ov[u][1].w, acc[7]);
-        }
-        M = Mn;
+      for (int i = 0; i < 4; ++i) {
+        sv[i] = sm.s[rr][lane + 32 * i];
+        m = fmaxf(m, sv[i]);
       }
-      const float invL = 1.f / L;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sm.s[rr][d0 + i] = bfr(bfr(acc[i] * invL) * (1.f / (1.f + __expf(-gate_pre[i]))));
+      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+      float l = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat16 e = __float2bfloat16_rn(m == -INFINITY ? 0.f : exp2f(sv[i] - m));
+        sm.pr[rr][lane + 32 * i] = e;
+        l += __bfloat162float(e);  // the sum of the probabilities as the products use them
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+      if (lane == 0) {
+        sm.rowm[rr] = m;
+        sm.rowl[rr] = l;
+      }
+    }
+    __syncthreads();
+    // ---- unnormalised outputs on tensor cores: warp w takes dims 16w .. 16w+15; publish
+    {
+      const uint32_t a_addr =
+          smem_u32(&sm.pr[0][0]) + (((lane & 7) + 8 * ((lane >> 3) & 1)) * kAtStride + 8 * (lane >> 4)) * 2;
+      const uint32_t b_addr =
+          smem_u32(&sm.v[0][0]) + (((lane & 7) + 8 * ((lane >> 3) & 1)) * kAtStride + 16 * warp + 8 * (lane >> 4)) * 2;
+      float o[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int ks = 0; ks < kAtChunk / 16; ++ks) {
+        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+        ldsm_x4(a_addr + ks * 32, a0, a1, a2, a3);
+        ldsm_x4_t(b_addr + ks * 16 * kAtStride * 2, b0, b1, b2, b3);
+        mma_bf16(o[0], a0, a1, a2, a3, b0, b1);
+        mma_bf16(o[1], a0, a1, a2, a3, b2, b3);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int rr = g + 8 * hf;
+          if (rr < nrows)
+            *reinterpret_cast<float2*>(part_row(p, kvh, rg, chunk, rr) + 4 + 16 * warp + 8 * nt + 2 * cq) =
+                make_float2(o[nt][2 * hf], o[nt][2 * hf + 1]);
+        }
+      if (tid < nrows) {
+        float* row = part_row(p, kvh, rg, chunk, tid);
+        row[0] = sm.rowm[tid];
+        row[1] = sm.rowl[tid];
+      }
+    }
+    __syncthreads();  // q, s, pr are reused by the next row group
+  }
+}
+
+// Merge: CTA (row quarter, row group, KV head) of 256 threads = 4 rows x 16 dim groups (8 dims
+// each) x 4 chunk subsets.  Thread subset s merges chunks s, s + 4, ... of its (row, dims),
+// issuing all of those loads at once (up to kAtMergePass chunks per pass); the 4 subsets' (max,
+// sum, output) are then combined in subset order in shared memory.  The result is a fixed
+// function of the partials (deterministic).
+__global__ void __launch_bounds__(kAtThreads) attn_merge_kernel(const __grid_constant__ AttnParams p) {
+  constexpr int kSub = 4, kRowsPer = 4;
+  __shared__ float os[kRowsPer][kAtD];
+  __shared__ float red[kSub - 1][kRowsPer][16][10];
+  const int rq = blockIdx.x & 3, rg = blockIdx.x >> 2, kvh = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rep = p.nh / p.nkv;
+  const int R = p.T * rep;
+  const int r0 = rg * kAtRG + rq * kRowsPer;          // first row of this CTA
+  const int nrows = max(0, min(kRowsPer, R - r0));
+  const int sub = tid >> 6, rr = (tid >> 4) & 3, dg = tid & 15, d0 = dg * 8;
+  pdl_launch_dependents();
+  pdl_wait_prior_grid();  // the chunk launch's partials (and the gates, written before it)
+  const int L0 = attn_length(p);
+  if (L0 < 0 || nrows == 0) return;
+  const int nchunks = (L0 + p.T + kAtChunk - 1) / kAtChunk;
+  const bool live = rr < nrows;
+  float M = -INFINITY, L = 0.f, acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  if (live) {
+    const float* base = part_row(p, kvh, rg, 0, rq * kRowsPer + rr);
+    const size_t cstride = static_cast<size_t>(kAtRG) * kAtPart;
+    for (int c0 = sub; c0 < nchunks; c0 += kSub * kAtMergePass) {
+      float mv[kAtMergePass], lv[kAtMergePass];
+      float4 ov[kAtMergePass][2];
+#pragma unroll
+      for (int u = 0; u < kAtMergePass; ++u) {  // unconditional loads (clamped), masked below
+        const float* row = base + min(c0 + kSub * u, nchunks - 1) * cstride;
+        mv[u] = __ldcg(row);
+        lv[u] = __ldcg(row + 1);
+        ov[u][0] = __ldcg(reinterpret_cast<const float4*>(row + 4 + d0));
+        ov[u][1] = __ldcg(reinterpret_cast<const float4*>(row + 8 + d0));
+      }
+#pragma unroll
+      for (int u = 0; u < kAtMergePass; ++u)
+        if (c0 + kSub * u >= nchunks) mv[u] = -INFINITY;
+      float Mn = M;
+#pragma unroll
+      for (int u = 0; u < kAtMergePass; ++u) Mn = fmaxf(Mn, mv[u]);
+      const float alpha = M == -INFINITY ? 0.f : exp2f(M - Mn);
+      L *= alpha;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] *= alpha;
+#pragma unroll
+      for (int u = 0; u < kAtMergePass; ++u) {
+        const float wgt = mv[u] == -INFINITY ? 0.f : exp2f(mv[u] - Mn);
+        L = fmaf(wgt, lv[u], L);
+        acc[0] = fmaf(wgt, ov[u][0].x, acc[0]);
+        acc[1] = fmaf(wgt, ov[u][0].y, acc[1]);
+        acc[2] = fmaf(wgt, ov[u][0].z, acc[2]);
+        acc[3] = fmaf(wgt, ov[u][0].w, acc[3]);
+        acc[4] = fmaf(wgt, ov[u][1].x, acc[4]);
+        acc[5] = fmaf(wgt, ov[u][1].y, acc[5]);
+        acc[6] = fmaf(wgt, ov[u][1].z, acc[6]);
+        acc[7] = fmaf(wgt, ov[u][1].w, acc[7]);
+      }
+      M = Mn;
+    }
+    if (sub > 0) {
+      float* dst = red[sub - 1][rr][dg];
+      dst[0] = M;
+      dst[1] = L;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dst[2 + i] = acc[i];
     }
   }
   __syncthreads();
+  if (live && sub == 0) {
+    // combine the subsets in order; the gate of this (row, dims)
+#pragma unroll
+    for (int q = 0; q < kSub - 1; ++q) {
+      const float* src = red[q][rr][dg];
+      const float Mn = fmaxf(M, src[0]);
+      const float a0 = M == -INFINITY ? 0.f : exp2f(M - Mn);
+      const float a1 = src[0] == -INFINITY ? 0.f : exp2f(src[0] - Mn);
+      L = fmaf(a1, src[1], L * a0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(a1, src[2 + i], acc[i] * a0);
+      M = Mn;
+    }
+    const int r = r0 + rr, t = r / rep, hq = kvh * rep + r % rep;
+    float gate[8];
+    if (p.gated) {
+      const uint4 gw = *reinterpret_cast<const uint4*>(p.proj + static_cast<size_t>(t) * p.ldp + hq * 2 * kAtD + kAtD + d0);
+      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(g2[i]);
+        gate[2 * i] = f.x;
+        gate[2 * i + 1] = f.y;
+      }
+    }
+    const float invL = 1.f / L;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float o = bfr(acc[i] * invL);
+      os[rr][d0 + i] = p.gated ? bfr(o * (1.f / (1.f + __expf(-gate[i])))) : o;
+    }
+  }
+  __syncthreads();
+  // ---- digits (and the optional bf16 copy) of the CTA's rows: warp per (row, 64 columns)
   const int mpad = p.T <= 8 ? 8 : 16;
-  for (int job = warp; job < 2 * nrows; job += kAtWarps) {
-    const int rr = job >> 1, hf = job & 1;
-    const int r = rbase + rr, t = r / rep, hq = kvh * rep + r % rep;
+  if (warp < 2 * nrows) {
+    const int jr = warp >> 1, hf = warp & 1;
+    const int r = r0 + jr, t = r / rep, hq = kvh * rep + r % rep;
     const int d = hf * 64 + 2 * lane;
-    const float a0 = sm.s[rr][d], a1 = sm.s[rr][d + 1];
+    const float a0 = os[jr][d], a1 = os[jr][d + 1];
     if (p.o_out) {
       __nv_bfloat16* op = p.o_out + static_cast<size_t>(t) * p.nh * kAtD + hq * kAtD + d;
       *reinterpret_cast<__nv_bfloat162*>(op) = __floats2bfloat162_rn(a0, a1);
     }
     write_digits(p.xq, mpad, t, 2 * hq + hf, lane, a0, a1);
   }
-  if (rg == 0) {  // padding tokens T .. mpad-1 of this KV head's query heads
+  if (rg == 0 && rq == 0) {  // padding tokens T .. mpad-1 of this KV head's query heads
     for (int job = warp; job < (mpad - p.T) * rep * 2; job += kAtWarps) {
       const int t = p.T + job / (rep * 2), rem = job % (rep * 2);
       write_digits(p.xq, mpad, t, 2 * (kvh * rep + rem / 2) + (rem & 1), lane, 0.f, 0.f);
     }
   }
-  if (tid == 0) p.cnt[kvh * kAtMaxRG + rg] = 0;  // ready for the next launch
 }
 
 size_t attn_ws_bytes(int T, int nh, int nkv, int max_len) {
   const int rep = nh / nkv;
   const int nrg = (T * rep + kAtRG - 1) / kAtRG;
   const int nchunks = (max_len + kAtChunk - 1) / kAtChunk;
-  return kAtPartOff + static_cast<size_t>(nkv) * nrg * nchunks * kAtRG * kAtPart * 4;
+  return static_cast<size_t>(nkv) * nrg * nchunks * kAtRG * kAtPart * 4;
 }
 
 bool attn_fits(int T, int nh, int nkv) {
@@ -427,7 +483,7 @@ bool attn_fits(int T, int nh, int nkv) {
 }
 
 cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, const float* kn_w,
-                              const float* inv_freq, int rot, float eps, void* kc, void* vc, int L0,
+                              const float* inv_freq, int rot, int gated, float eps, void* kc, void* vc, int L0,
                               const int* len_dev, int max_len, int T, int nh, int nkv, void* ws, void* xq,
                               void* o_out, cudaStream_t stream) {
   static bool attr_set[64] = {};
@@ -435,8 +491,8 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(attn_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(sizeof(AttnSmem)));
+    const cudaError_t e = cudaFuncSetAttribute(attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(sizeof(AttnSmem) + kAtMaxRows * kAtD * 2));
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
@@ -455,25 +511,36 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
   prm.nh = nh;
   prm.nkv = nkv;
   prm.rot = rot;
+  prm.gated = gated;
   prm.len_dev = len_dev;
   prm.max_len = max_len;
-  prm.nchunks = ((len_dev ? max_len : L0 + T) + kAtChunk - 1) / kAtChunk;  // grid; the kernel recomputes it from len_dev
+  // chunk grid (and the partials' chunk stride): the largest chunk count this cache can need
+  // with a device length, else the exact count
+  prm.nchunks = ((len_dev ? max_len : L0 + T) + kAtChunk - 1) / kAtChunk;
   prm.nrg = (T * rep + kAtRG - 1) / kAtRG;
-  prm.cnt = static_cast<uint32_t*>(ws);
-  prm.part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kAtPartOff);
+  prm.part = static_cast<float*>(ws);
   prm.xq = static_cast<uint8_t*>(xq);
   prm.o_out = static_cast<__nv_bfloat16*>(o_out);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(prm.nchunks, prm.nrg, nkv);
-  cfg.blockDim = dim3(kAtThreads);
-  cfg.dynamicSmemBytes = sizeof(AttnSmem);
-  cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(prm.nchunks, nkv);
+  cfg.blockDim = dim3(kAtThreads);
+  cfg.dynamicSmemBytes = sizeof(AttnSmem) + static_cast<size_t>(T) * rep * kAtD * 2;
+  cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, attn_fused_kernel, prm);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_chunk_kernel, prm);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t mcfg = {};
+  mcfg.gridDim = dim3(prm.nrg * 4, nkv);  // (row quarter, row group) x KV head
+  mcfg.blockDim = dim3(kAtThreads);
+  mcfg.dynamicSmemBytes = 0;
+  mcfg.stream = stream;
+  mcfg.attrs = attr;
+  mcfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&mcfg, attn_merge_kernel, prm);
 }
 
 }  // namespace skinny

@@ -21,8 +21,9 @@ bool qmm_noalloc_fits(int N, int K);
 size_t spec_accept_ws_bytes();
 cudaError_t qmm_tc_launch_prepared(const void* xq, const void* w_tc, void* out, int ldo, int M, int N, int K,
                                    void* ws, cudaStream_t stream);
-cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd, void* h_out, int ldh,
-                        const float* w, float eps, int K, int M, void* xq, void* a_out, cudaStream_t stream);
+cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd, int dseg_cols,
+                        long long dseg_stride, void* h_out, int ldh, const float* w, float eps, int K, int M,
+                        void* xq, void* a_out, cudaStream_t stream);
 struct GdnFusedParamsHost {
   const void* proj;
   int ldp;
@@ -56,7 +57,7 @@ cudaError_t qmm_tc_launch_noalloc(const void* x, int ldx, const void* w_tc, void
 size_t attn_ws_bytes(int T, int nh, int nkv, int max_len);
 bool attn_fits(int T, int nh, int nkv);
 cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, const float* kn_w,
-                              const float* inv_freq, int rot, float eps, void* kc, void* vc, int L0,
+                              const float* inv_freq, int rot, int gated, float eps, void* kc, void* vc, int L0,
                               const int* len_dev, int max_len, int T, int nh, int nkv, void* ws, void* xq,
                               void* o_out, cudaStream_t stream);
 }  // namespace skinny
@@ -219,35 +220,50 @@ size_t skinny_xq_bytes(int M, int K) {
   return static_cast<size_t>(K / skinny::kGroup) * skinny::xq_block_bytes(M <= 8 ? 8 : 16);
 }
 
-int skinny_prep(int mode, const void* x, int ldx, const void* d, int ldd, void* h_out, int ldh,
-                const float* w, float eps, int M, int K, void* xq, void* a_out, void* stream) {
+int skinny_prep(int mode, const void* x, int ldx, const void* d, int ldd, int dseg_cols, long long dseg_stride,
+                void* h_out, int ldh, const float* w, float eps, int M, int K, void* xq, void* a_out, void* stream) {
   if (!x || !xq || mode < 0 || mode > 2 || (mode == 0 && !w)) return SKINNY_ERR_INVALID_ARG;
   if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
   if (K < skinny::kGroup || K % skinny::kGroup) return SKINNY_ERR_SHAPE;
   const int need = mode == 1 ? 2 * K : K;
-  if (ldx < need || (d && ldd < K) || (h_out && ldh < K)) return SKINNY_ERR_INVALID_ARG;
+  if (ldx < need || (h_out && ldh < K)) return SKINNY_ERR_INVALID_ARG;
+  if (d && dseg_cols == 0 && ldd < K) return SKINNY_ERR_INVALID_ARG;
+  if (d && dseg_cols != 0 &&
+      (dseg_cols < 0 || dseg_cols % skinny::kGroup || K % dseg_cols || ldd < dseg_cols ||
+       dseg_stride < static_cast<long long>(M - 1) * ldd + dseg_cols))
+    return SKINNY_ERR_INVALID_ARG;
   // Outputs are written by one column chunk while other chunks of the row still read the inputs:
   // h_out and a_out must not overlap x or d.
   const auto span = [M](const void* p, int ld, int width) {
     const uintptr_t b = reinterpret_cast<uintptr_t>(p);
     return std::make_pair(b, b + (static_cast<uintptr_t>(M - 1) * ld + width) * 2);
   };
+  const auto dspan = [&]() {
+    if (dseg_cols == 0) return span(d, ldd, K);
+    const uintptr_t b = reinterpret_cast<uintptr_t>(d);
+    const uintptr_t n = static_cast<uintptr_t>(K / dseg_cols - 1) * dseg_stride +
+                        static_cast<uintptr_t>(M - 1) * ldd + dseg_cols;
+    return std::make_pair(b, b + n * 2);
+  };
   const auto overlap = [](std::pair<uintptr_t, uintptr_t> a, std::pair<uintptr_t, uintptr_t> b) {
     return a.first < b.second && b.first < a.second;
   };
   if (mode == 0) {
     const auto xs = span(x, ldx, K);
-    if (h_out && d && (overlap(span(h_out, ldh, K), xs) || overlap(span(h_out, ldh, K), span(d, ldd, K))))
+    if (h_out && d && (overlap(span(h_out, ldh, K), xs) || overlap(span(h_out, ldh, K), dspan())))
       return SKINNY_ERR_INVALID_ARG;
-    if (a_out && (overlap(span(a_out, K, K), xs) || (d && overlap(span(a_out, K, K), span(d, ldd, K)))))
+    if (a_out && (overlap(span(a_out, K, K), xs) || (d && overlap(span(a_out, K, K), dspan()))))
       return SKINNY_ERR_INVALID_ARG;
   }
-  // bf16 pairs are read and written as 4-byte words
-  if ((ldx % 2) || (d && ldd % 2) || (h_out && ldh % 2) || !aligned16(xq) || !aligned4(x) || !aligned4(d) ||
-      !aligned4(h_out) || !aligned4(a_out))
+  // bf16 pairs are read and written as 4-byte words; mode 0 reads its row as 16-byte vectors
+  if ((ldx % 2) || (d && ldd % 2) || (d && dseg_stride % 2) || (h_out && ldh % 2) || !aligned16(xq) ||
+      !aligned4(x) || !aligned4(d) || !aligned4(h_out) || !aligned4(a_out))
     return SKINNY_ERR_ALIGNMENT;
-  return cuda_status(skinny::prep_launch(mode, x, ldx, d, ldd, h_out, ldh, w, eps, K, M, xq, a_out,
-                                         static_cast<cudaStream_t>(stream)));
+  if (mode == 0 && (K > 16384)) return SKINNY_ERR_SHAPE;
+  if (mode == 0 && ((ldx % 8) || !aligned16(x) || (d && ((ldd % 8) || (dseg_stride % 8) || !aligned16(d)))))
+    return SKINNY_ERR_ALIGNMENT;
+  return cuda_status(skinny::prep_launch(mode, x, ldx, d, ldd, d ? dseg_cols : 0, dseg_stride, h_out, ldh, w, eps,
+                                         K, M, xq, a_out, static_cast<cudaStream_t>(stream)));
 }
 
 int skinny_gdn_fused(const void* proj, int ldp, void* conv, void* conv_full, const float* conv_w,
@@ -274,7 +290,7 @@ size_t skinny_attn_workspace_bytes(int T, int n_heads, int n_kv_heads, int max_l
 }
 
 int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
-                      const float* inv_freq, int rot, float eps, void* k_cache, void* v_cache, int L0,
+                      const float* inv_freq, int rot, int gated, float eps, void* k_cache, void* v_cache, int L0,
                       const int32_t* length_dev, int T, int n_heads, int n_kv_heads, int max_len, void* workspace,
                       size_t workspace_bytes, void* xq, void* o_out, void* stream) {
   if (!proj || !q_norm_w || !k_norm_w || !k_cache || !v_cache || !xq || (rot > 0 && !inv_freq))
@@ -284,14 +300,14 @@ int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const fl
   if (!skinny::attn_fits(T, n_heads, n_kv_heads) || rot < 0 || rot > 128 || (rot % 2) || L0 < 0 ||
       (!length_dev && L0 + T > max_len) || max_len < T)
     return SKINNY_ERR_SHAPE;
-  if (ldp < (2 * n_heads + 2 * n_kv_heads) * 128) return SKINNY_ERR_INVALID_ARG;
+  if ((gated != 0 && gated != 1) || ldp < ((1 + gated) * n_heads + 2 * n_kv_heads) * 128) return SKINNY_ERR_INVALID_ARG;
   if (!aligned16(xq) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned4(o_out) || !aligned16(proj) ||
       (ldp % 8) || !aligned4(length_dev))
     return SKINNY_ERR_ALIGNMENT;
   if (!workspace || workspace_bytes < skinny::attn_ws_bytes(T, n_heads, n_kv_heads, max_len) ||
       !aligned16(workspace))
     return SKINNY_ERR_WORKSPACE;
-  return cuda_status(skinny::attn_fused_launch(proj, ldp, q_norm_w, k_norm_w, inv_freq, rot, eps, k_cache,
+  return cuda_status(skinny::attn_fused_launch(proj, ldp, q_norm_w, k_norm_w, inv_freq, rot, gated, eps, k_cache,
                                                v_cache, L0, length_dev, max_len, T, n_heads, n_kv_heads,
                                                workspace, xq, o_out, static_cast<cudaStream_t>(stream)));
 }

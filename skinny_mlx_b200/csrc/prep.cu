@@ -2,7 +2,8 @@
 // x-prep block format the qmm kernel reads (qmm_layout.cuh), so that no separate x-prep launch
 // and no bf16 activation round trip sit between a step's elementwise work and its next matmul.
 //
-//   prep_rmsnorm : h = x (+ d)  [written to h_out as the next residual stream when d is given],
+//   prep_rmsnorm : h = x (+ d)  [written to h_out as the next residual stream when d is given;
+//                  d may be in the column-sharded layout of an all-gather, see d_off],
 //                  a = bf16( h / rms(h) * (1 + w) )            -> digits of a
 //   prep_swiglu  : a = bf16( silu(g) * u ) for gu = [g | u]     -> digits of a
 //   prep_plain   : a = x                                         -> digits of a
@@ -37,6 +38,7 @@ namespace skinny {
 
 constexpr int kPrepThreads = 256;
 constexpr int kPrepWarps = kPrepThreads / 32;
+constexpr int kPrepMaxK = 8 * 8 * kPrepThreads;  // mode 0 row length: 16-byte vectors per thread <= 8
 
 __device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
@@ -45,10 +47,20 @@ __device__ __forceinline__ float2 ld_bf2(const __nv_bfloat16* p) {
   return make_float2(__low2float(v), __high2float(v));
 }
 
+// d(t, c) in a column-sharded layout: column c of token t lives in shard c / seg_cols, at
+// shard * seg_stride + t * ldd + c % seg_cols (seg_cols = 0: plain rows).  This is the layout an
+// all-gather of per-rank [M, N/G] column shards produces, read without a transposing copy.
+__device__ __forceinline__ size_t d_off(int t, int c, int ldd, int seg_cols, long long seg_stride) {
+  if (seg_cols == 0) return static_cast<size_t>(t) * ldd + c;
+  const int sh = c / seg_cols;
+  return static_cast<size_t>(sh) * seg_stride + static_cast<size_t>(t) * ldd + (c - sh * seg_cols);
+}
+
 // mode 0: rmsnorm (optional residual add), 1: swiglu, 2: plain.
 template <int MODE>
 __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                                                             const __nv_bfloat16* __restrict__ d, int ldd,
+                                                            int dseg_cols, long long dseg_stride,
                                                             __nv_bfloat16* __restrict__ h_out, int ldh,
                                                             const float* __restrict__ w, float eps, int K, int M,
                                                             int mpad, uint8_t* __restrict__ xq,
@@ -62,37 +74,48 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16*
   pdl_launch_dependents();
   pdl_wait_prior_grid();  // x, d (and the buffers written below) belong to earlier launches
   const __nv_bfloat16* xr = x + static_cast<size_t>(t) * ldx;
-  const __nv_bfloat16* dr = d ? d + static_cast<size_t>(t) * ldd : nullptr;
+  const bool has_d = d != nullptr;
+  // mode 0: h = bf16(x + d) of the whole row, staged in shared memory by one round of 16-byte
+  // loads (the row's sum of squares and this chunk's groups both read it there)
+  extern __shared__ __align__(16) uint8_t prep_smem[];
+  float* hrow = reinterpret_cast<float*>(prep_smem);
   float rstd = 1.f;
   if (MODE == 0 && live) {
-    // row sum of squares of h = bf16(x + d): K/512 pairs per thread, loads batched by 4
-    float ss[4] = {0.f, 0.f, 0.f, 0.f};
-    const int npair = K / 2;
-    for (int base = tid; base < npair; base += 4 * kPrepThreads) {
-      float2 hv[4];
+    constexpr int kMaxPer = 8;  // 16-byte vectors per thread and tensor: K <= 8 * 8 * 256
+    const int nvec = K / 8;
+    uint4 xv[kMaxPer], dv[kMaxPer];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int c = 2 * (base + u * kPrepThreads);
-        hv[u] = c < K ? ld_bf2(xr + c) : make_float2(0.f, 0.f);
+    for (int u = 0; u < kMaxPer; ++u) {
+      const int v = tid + u * kPrepThreads;
+      if (v < nvec) {
+        xv[u] = *reinterpret_cast<const uint4*>(xr + 8 * v);
+        if (has_d) dv[u] = *reinterpret_cast<const uint4*>(d + d_off(t, 8 * v, ldd, dseg_cols, dseg_stride));
       }
-      if (dr) {
+    }
+    float ss = 0.f;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int c = 2 * (base + u * kPrepThreads);
-          if (c < K) {
-            const float2 dv = ld_bf2(dr + c);
-            hv[u].x = bf16r(hv[u].x + dv.x);
-            hv[u].y = bf16r(hv[u].y + dv.y);
+    for (int u = 0; u < kMaxPer; ++u) {
+      const int v = tid + u * kPrepThreads;
+      if (v < nvec) {
+        const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv[u]);
+        const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&dv[u]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float2 h = __bfloat1622float2(x2[i]);
+          if (has_d) {
+            const float2 dd = __bfloat1622float2(d2[i]);
+            h.x = bf16r(h.x + dd.x);
+            h.y = bf16r(h.y + dd.y);
           }
+          hrow[8 * v + 2 * i] = h.x;
+          hrow[8 * v + 2 * i + 1] = h.y;
+          ss = fmaf(h.x, h.x, fmaf(h.y, h.y, ss));
         }
       }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) ss[u] = fmaf(hv[u].x, hv[u].x, fmaf(hv[u].y, hv[u].y, ss[u]));
     }
-    float s = (ss[0] + ss[1]) + (ss[2] + ss[3]);
 #pragma unroll
-    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
-    if (lane == 0) red[warp] = s;
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    if (lane == 0) red[warp] = ss;
     __syncthreads();
     float tot = 0.f;
 #pragma unroll
@@ -104,15 +127,9 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16*
   float a0 = 0.f, a1 = 0.f;
   if (live) {
     if (MODE == 0) {
-      float2 hv = ld_bf2(xr + c);
-      if (dr) {
-        const float2 dv = ld_bf2(dr + c);
-        hv.x = bf16r(hv.x + dv.x);
-        hv.y = bf16r(hv.y + dv.y);
-        if (h_out)
-          *reinterpret_cast<__nv_bfloat162*>(h_out + static_cast<size_t>(t) * ldh + c) =
-              __floats2bfloat162_rn(hv.x, hv.y);
-      }
+      const float2 hv = make_float2(hrow[c], hrow[c + 1]);
+      if (has_d && h_out)
+        *reinterpret_cast<__nv_bfloat162*>(h_out + static_cast<size_t>(t) * ldh + c) = __floats2bfloat162_rn(hv.x, hv.y);
       a0 = bf16r(hv.x * rstd * (1.f + w[c]));
       a1 = bf16r(hv.y * rstd * (1.f + w[c + 1]));
       if (a_out)
@@ -130,39 +147,53 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16*
   write_digits(xq, mpad, t, g, lane, a0, a1);
 }
 
-static cudaError_t launch_pdl(void (*kern)(const __nv_bfloat16*, int, const __nv_bfloat16*, int, __nv_bfloat16*,
-                                           int, const float*, float, int, int, int, uint8_t*, __nv_bfloat16*),
-                              dim3 grid, cudaStream_t stream, const __nv_bfloat16* x, int ldx,
-                              const __nv_bfloat16* d, int ldd, __nv_bfloat16* h, int ldh, const float* w,
-                              float eps, int K, int M, int mpad, uint8_t* xq, __nv_bfloat16* a_out) {
+static cudaError_t launch_pdl(void (*kern)(const __nv_bfloat16*, int, const __nv_bfloat16*, int, int, long long,
+                                           __nv_bfloat16*, int, const float*, float, int, int, int, uint8_t*,
+                                           __nv_bfloat16*),
+                              dim3 grid, size_t smem, cudaStream_t stream, const __nv_bfloat16* x, int ldx,
+                              const __nv_bfloat16* d, int ldd, int dseg_cols, long long dseg_stride,
+                              __nv_bfloat16* h, int ldh, const float* w, float eps, int K, int M, int mpad,
+                              uint8_t* xq, __nv_bfloat16* a_out) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kPrepThreads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, x, ldx, d, ldd, h, ldh, w, eps, K, M, mpad, xq, a_out);
+  return cudaLaunchKernelEx(&cfg, kern, x, ldx, d, ldd, dseg_cols, dseg_stride, h, ldh, w, eps, K, M, mpad, xq,
+                            a_out);
 }
 
-cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd, void* h_out, int ldh,
-                        const float* w, float eps, int K, int M, void* xq, void* a_out, cudaStream_t stream) {
+cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd, int dseg_cols,
+                        long long dseg_stride, void* h_out, int ldh, const float* w, float eps, int K, int M,
+                        void* xq, void* a_out, cudaStream_t stream) {
   const int mpad = M <= 8 ? 8 : 16;
   const int G = K / 64;
   const dim3 grid((G + kPrepWarps - 1) / kPrepWarps, mpad);
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   auto* q = static_cast<uint8_t*>(xq);
-  if (mode == 0)
-    return launch_pdl(prep_kernel<0>, grid, stream, xb, ldx, static_cast<const __nv_bfloat16*>(d), ldd,
-                      static_cast<__nv_bfloat16*>(h_out), ldh, w, eps, K, M, mpad, q,
+  if (mode == 0) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      const cudaError_t e = cudaFuncSetAttribute(prep_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(kPrepMaxK * sizeof(float)));
+      if (e != cudaSuccess) return e;
+      attr_set[dev] = true;
+    }
+    return launch_pdl(prep_kernel<0>, grid, static_cast<size_t>(K) * sizeof(float), stream, xb, ldx, static_cast<const __nv_bfloat16*>(d), ldd, dseg_cols,
+                      dseg_stride, static_cast<__nv_bfloat16*>(h_out), ldh, w, eps, K, M, mpad, q,
                       static_cast<__nv_bfloat16*>(a_out));
+  }
   if (mode == 1)
-    return launch_pdl(prep_kernel<1>, grid, stream, xb, ldx, nullptr, 0, nullptr, 0, nullptr, 0.f, K, M, mpad, q,
-                      nullptr);
-  return launch_pdl(prep_kernel<2>, grid, stream, xb, ldx, nullptr, 0, nullptr, 0, nullptr, 0.f, K, M, mpad, q,
+    return launch_pdl(prep_kernel<1>, grid, 0, stream, xb, ldx, nullptr, 0, 0, 0, nullptr, 0, nullptr, 0.f, K, M, mpad,
+                      q, nullptr);
+  return launch_pdl(prep_kernel<2>, grid, 0, stream, xb, ldx, nullptr, 0, 0, 0, nullptr, 0, nullptr, 0.f, K, M, mpad, q,
                     nullptr);
 }
 

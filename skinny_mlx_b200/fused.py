@@ -117,7 +117,7 @@ class FusedStep:
             ws = self._attn_ws[max_len] = torch.zeros(n, dtype=torch.uint8, device=proj.device)
         L0 = c.length
         _lib.call("skinny_attn_fused", _p(proj), proj.stride(0), _p(ent["qn"]), _p(ent["kn"]), _p(ent["inv"]),
-                  cfg.rotary_dim, cfg.rms_eps, _p(c.k), _p(c.v), L0, _p(len_dev), m, cfg.n_heads, cfg.n_kv_heads,
+                  cfg.rotary_dim, 1, cfg.rms_eps, _p(c.k), _p(c.v), L0, _p(len_dev), m, cfg.n_heads, cfg.n_kv_heads,
                   max_len, _p(ws), ws.numel(), _p(xq), None, stream)
         if len_dev is None:
             c.length = L0 + m
@@ -128,7 +128,7 @@ class FusedStep:
                   _p(ws), ws.numel(), stream)
 
     def _prep(self, mode, x, m, k, xq, stream, d=None, h_out=None, w=None, a_out=None):
-        _lib.call("skinny_prep", mode, _p(x), x.stride(0), _p(d), d.stride(0) if d is not None else 0,
+        _lib.call("skinny_prep", mode, _p(x), x.stride(0), _p(d), d.stride(0) if d is not None else 0, 0, 0,
                   _p(h_out), h_out.stride(0) if h_out is not None else 0, _p(w), self.cfg.rms_eps, m, k,
                   _p(xq), _p(a_out), stream)
 

@@ -119,3 +119,79 @@ def test_column_parallel_nccl_two_gpus(cuda_lib, dev):
         assert p.exitcode == 0
     # per-row results of the same kernel; stream-K split points differ with the shard sizes
     assert ((ref - got).abs().max() / ref.abs().max()).item() <= 1e-2
+
+
+def _full(logits_shards: torch.Tensor) -> torch.Tensor:
+    """[G, M, V/G] rank-major vocabulary shards -> [M, V]."""
+    G, M, n = logits_shards.shape
+    return logits_shards.permute(1, 0, 2).reshape(M, G * n)
+
+
+@pytest.mark.gpu
+def test_dense_fused_step_matches_module_path(cuda_lib, dev):
+    """The fused dense step (prep / prepared qmm / ungated fused attention) against the patched
+    module-by-module forward of the same model, prefill then a 3-token verify."""
+    from skinny_mlx_b200.dense_fused import DenseFusedStep
+    from skinny_mlx_b200.patch import patch_model
+
+    m = DenseModel(small_dense(), 0, 1, seed=3, device=dev)
+    patch_model(m)
+    f = DenseFusedStep(m)
+    ca, cb = m.make_cache(64), m.make_cache(64)
+    for ids in (IDS[:5], IDS[5:]):
+        t = torch.tensor(ids, device=dev)
+        ref = m(t, ca).float()
+        got = _full(f(t, cb)).float()
+        assert ((ref - got).abs().max() / ref.abs().max()).item() <= 1.5e-2
+        assert (ref.argmax(-1) == got.argmax(-1)).float().mean().item() >= 0.75
+    assert [c.length for c in ca] == [c.length for c in cb]
+
+
+def _gpu_fused_rank(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from skinny_mlx_b200.dense_fused import DenseFusedStep
+        from skinny_mlx_b200.patch import patch_model
+
+        m = DenseModel(small_dense(), rank, world, seed=3, device=f"cuda:{rank}")
+        patch_model(m)
+        f = DenseFusedStep(m)
+        caches = m.make_cache(64)
+        f(torch.tensor(IDS[:5], device=f"cuda:{rank}"), caches)
+        logits = _full(f(torch.tensor(IDS[5:], device=f"cuda:{rank}"), caches)).float().cpu()
+        if rank == 0:
+            q.put(logits)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_dense_fused_step_two_gpus(cuda_lib, dev):
+    """2 ranks over NCCL (skipped on a 1-GPU box): the fused sharded step (digit-block and output
+    all-gathers) against the unsharded patched module path."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from skinny_mlx_b200.patch import patch_model
+
+    m = DenseModel(small_dense(), 0, 1, seed=3, device=dev)
+    patch_model(m)
+    caches = m.make_cache(64)
+    m(torch.tensor(IDS[:5], device=dev), caches)
+    ref = m(torch.tensor(IDS[5:], device=dev), caches).float().cpu()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gpu_fused_rank, args=(r, 2, 29657, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert ((ref - got).abs().max() / ref.abs().max()).item() <= 1.5e-2
