@@ -99,6 +99,37 @@ int skinny_qmm_w4g64_grouped(int n, const void* const* x, const int* ldx, const 
 int skinny_qmm_w4g64_simt(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
                           int N, int K, void* stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Peer memory for a sharded step (one GPU per rank): buffers allocated by one rank and opened by
+ * the others through CUDA IPC (NVLink loads and stores; no multicast), and the flags that order
+ * producers and consumers across ranks.  No counterpart in the reference (it runs on one GPU).
+ * ------------------------------------------------------------------------------------------- */
+
+/* cudaMalloc of `bytes` (zero-filled) and its 64-byte IPC handle. */
+int skinny_ipc_alloc(size_t bytes, void** ptr, void* handle64);
+/* Map another rank's buffer from its handle; unmap with skinny_ipc_close. */
+int skinny_ipc_open(const void* handle64, void** ptr);
+int skinny_ipc_close(void* ptr);
+int skinny_ipc_free(void* ptr);
+
+/* Synchronisation of one launch with the other ranks (all pointers device memory):
+ *   wait_flags  != NULL: before reading other ranks' data, wait (bounded, error bit 11) until
+ *                        wait_flags[0 .. n_ranks) >= *epoch;
+ *   counter     != NULL: after its last write, the launch's last CTA stores *epoch into
+ *                        signal_flags[r] for every rank r (this rank's word in each rank's
+ *                        flags), after a system-scope fence; the counter is zero between launches.
+ * epoch is a device counter the caller advances once per step (so a captured graph serves every
+ * step); err (required with an epoch) receives the error bits.  A NULL skinny_peer_sync pointer,
+ * or epoch == NULL, means no synchronisation. */
+typedef struct {
+  const uint32_t* epoch;
+  const uint32_t* wait_flags;
+  uint32_t* counter;
+  uint32_t* signal_flags[8];
+  uint32_t* err;
+  int n_ranks;
+} skinny_peer_sync;
+
 /* Bytes of one prepared qmm input (the digit blocks the qmm kernel reads) for M tokens, K columns. */
 size_t skinny_xq_bytes(int M, int K);
 
@@ -106,20 +137,24 @@ size_t skinny_xq_bytes(int M, int K);
  * qmm's input format, so a step's elementwise work and its next matmul need no x-prep launch or
  * activation round trip (the B200 form of the glue between the reference model's projections).
  *   mode 0: h = x (+ d if d != NULL; h written to h_out when given), a = bf16(h / rms(h) * (1 + w))
- *           with w f32 [K] (zero-centred RMSNorm, eps); K <= 16384, x and d 16-byte aligned with
- *           leading dimensions (and dseg_stride) multiples of 8
+ *           with w f32 [K] (zero-centred RMSNorm, eps); K <= 16384, x and d (or every shard)
+ *           16-byte aligned with leading dimensions multiples of 8
  *   mode 1: a = bf16(silu(g) * u), x = [g | u] with 2K columns (SwiGLU)
  *   mode 2: a = x
- * d may be column-sharded as an all-gather of per-rank [M, N/G] outputs leaves it: with
+ * d may be column-sharded, one [M, dseg_cols] shard per rank (e.g. the per-rank outputs of a
+ * column-parallel matmul, in an all-gather buffer or in the ranks' own memory): with
  * dseg_cols > 0 (a multiple of 64 dividing K), column c of token t is read at
- * (c / dseg_cols) * dseg_stride + t * ldd + c % dseg_cols; dseg_cols = 0: plain rows.
+ * dseg[c / dseg_cols] + t * ldd + c % dseg_cols (d is then ignored); dseg_cols = 0: plain rows.
+ * sync (may be NULL): wait for the shards' producers before reading d; signal after writing
+ * xq (a producer of this rank's digit groups).
  * x, d, h_out bf16 rows with leading dimensions ldx, ldd, ldh (even, 4-byte aligned); xq receives
  * skinny_xq_bytes(M, K) bytes (16-byte aligned); a_out (mode 0, may be NULL) receives a as bf16
  * [M, K].  h_out and a_out must not overlap x or d (SKINNY_ERR_INVALID_ARG): column chunks of a
  * row are written while other chunks of it are still being read.  Launched with programmatic
  * dependent launch: the next launch on the stream may start before this one ends. */
-int skinny_prep(int mode, const void* x, int ldx, const void* d, int ldd, int dseg_cols, long long dseg_stride,
-                void* h_out, int ldh, const float* w, float eps, int M, int K, void* xq, void* a_out, void* stream);
+int skinny_prep(int mode, const void* x, int ldx, const void* d, int ldd, int dseg_cols, const void* const* dseg,
+                void* h_out, int ldh, const float* w, float eps, int M, int K, void* xq, void* a_out,
+                const skinny_peer_sync* sync, void* stream);
 
 /* One Gated DeltaNet mixer from its fused input projection to the prepared input of out_proj,
  * in one launch: causal depthwise conv (window W <= 4, weights conv_w [C, W+1] f32) + SiLU,
@@ -160,17 +195,22 @@ size_t skinny_attn_workspace_bytes(int T, int n_heads, int n_kv_heads, int max_l
  * length_dev (may be NULL): when given, the cache length L0 is read from this device int32 when
  * the kernel runs (L0 argument ignored), so that one captured launch (CUDA graph) serves every
  * length; a device length outside [0, max_len - T] makes the launch touch nothing.
+ * sync (may be NULL; sharded step): the merge launch signals its completion.
  * Two launches (per-chunk partials, then their merge), both with programmatic dependent launch.
  * No counterpart in the reference's own code. */
 int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
                       const float* inv_freq, int rot, int gated, float eps, void* k_cache, void* v_cache, int L0,
                       const int32_t* length_dev, int T, int n_heads, int n_kv_heads, int max_len, void* workspace,
-                      size_t workspace_bytes, void* xq, void* o_out, void* stream);
+                      size_t workspace_bytes, void* xq, void* o_out, const skinny_peer_sync* sync, void* stream);
 
 /* skinny_qmm_w4g64 on an input prepared by skinny_prep (same result as passing the bf16
- * activation itself), launched without the x-prep kernel. */
+ * activation itself), launched without the x-prep kernel.  Sharded step: with xq_ranks != NULL
+ * the digit blocks of groups [r * xq_groups_per_rank, (r+1) * xq_groups_per_rank) are read from
+ * rank r's buffer xq_ranks[r] (at the offsets of a full K buffer; peer memory over NVLink), after
+ * waiting for the ranks' flags (sync), and the launch signals its completion (sync). */
 int skinny_qmm_w4g64_prepared(const void* xq, const void* w_tc, void* out, int ldo, int M, int N, int K,
-                              void* workspace, size_t workspace_bytes, void* stream);
+                              void* workspace, size_t workspace_bytes, const void* const* xq_ranks,
+                              int xq_groups_per_rank, const skinny_peer_sync* sync, void* stream);
 
 /* Bytes of the workspace skinny_spec_accept needs (zero-filled before first use; reusable). */
 size_t skinny_spec_accept_workspace_bytes(void);

@@ -40,17 +40,21 @@ SIGNATURES = {
     "skinny_qmm_w4g64_grouped": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                          c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "skinny_xq_bytes": (c_size_t, [c_int, c_int]),
-    "skinny_prep": (c_int, [c_int, c_void_p, c_int, c_void_p, c_int, c_int, ctypes.c_longlong, c_void_p, c_int,
-                            c_void_p, ctypes.c_float, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "skinny_prep": (c_int, [c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int,
+                            c_void_p, ctypes.c_float, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "skinny_gdn_fused": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                  ctypes.c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                                  c_int, c_void_p, c_void_p]),
     "skinny_attn_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "skinny_attn_fused": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, ctypes.c_float, c_void_p,
                                   c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t,
-                                  c_void_p, c_void_p, c_void_p]),
+                                  c_void_p, c_void_p, c_void_p, c_void_p]),
     "skinny_qmm_w4g64_prepared": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
-                                          c_size_t, c_void_p]),
+                                          c_size_t, c_void_p, c_int, c_void_p, c_void_p]),
+    "skinny_ipc_alloc": (c_int, [c_size_t, c_void_p, c_void_p]),
+    "skinny_ipc_open": (c_int, [c_void_p, c_void_p]),
+    "skinny_ipc_close": (c_int, [c_void_p]),
+    "skinny_ipc_free": (c_int, [c_void_p]),
     "skinny_spec_accept_workspace_bytes": (c_size_t, []),
     "skinny_spec_accept": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                    c_void_p, c_size_t, c_void_p]),
@@ -99,4 +103,11 @@ def call(name: str, *args) -> None:
     check(name, getattr(lib(), name)(*args))
 
 
-__all__ = ["lib", "call", "check", "SkinnyError", "SIGNATURES", "c_uint32"]
+class PeerSync(ctypes.Structure):
+    """Mirror of skinny_peer_sync (include/skinny_b200.h): device pointers as integers."""
+
+    _fields_ = [("epoch", c_void_p), ("wait_flags", c_void_p), ("counter", c_void_p),
+                ("signal_flags", c_void_p * 8), ("err", c_void_p), ("n_ranks", c_int)]
+
+
+__all__ = ["lib", "call", "check", "SkinnyError", "SIGNATURES", "c_uint32", "PeerSync"]

@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 
 #include "digits.cuh"
+#include "peer.cuh"
 #include "ptx.cuh"
 #include "qmm_layout.cuh"
 
@@ -56,6 +57,7 @@ struct AttnParams {
   float* part;                // [nkv, nrg, nchunks, 16, kAtPart]: per row m, l, -, -, o[128]
   uint8_t* xq;                // o_proj input digits (K = nh * 128)
   __nv_bfloat16* o_out;       // [T, nh * 128] or null
+  PeerSync sync;              // (sharded step) the merge launch signals its completion
 };
 
 constexpr int kAtMaxRows = kAtRG * kAtMaxRG;  // query rows of one KV head (T * rep)
@@ -353,6 +355,7 @@ __global__ void __launch_bounds__(kAtThreads) attn_merge_kernel(const __grid_con
   constexpr int kSub = 4, kRowsPer = 4;
   __shared__ float os[kRowsPer][kAtD];
   __shared__ float red[kSub - 1][kRowsPer][16][10];
+  __shared__ int sync_flag;
   const int rq = blockIdx.x & 3, rg = blockIdx.x >> 2, kvh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rep = p.nh / p.nkv;
@@ -363,9 +366,9 @@ __global__ void __launch_bounds__(kAtThreads) attn_merge_kernel(const __grid_con
   pdl_launch_dependents();
   pdl_wait_prior_grid();  // the chunk launch's partials (and the gates, written before it)
   const int L0 = attn_length(p);
-  if (L0 < 0 || nrows == 0) return;
-  const int nchunks = (L0 + p.T + kAtChunk - 1) / kAtChunk;
-  const bool live = rr < nrows;
+  const bool work = L0 >= 0 && nrows > 0;  // (no early exit: every CTA counts in the signal)
+  const int nchunks = work ? (L0 + p.T + kAtChunk - 1) / kAtChunk : 0;
+  const bool live = work && rr < nrows;
   float M = -INFINITY, L = 0.f, acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
@@ -452,7 +455,7 @@ __global__ void __launch_bounds__(kAtThreads) attn_merge_kernel(const __grid_con
   __syncthreads();
   // ---- digits (and the optional bf16 copy) of the CTA's rows: warp per (row, 64 columns)
   const int mpad = p.T <= 8 ? 8 : 16;
-  if (warp < 2 * nrows) {
+  if (work && warp < 2 * nrows) {
     const int jr = warp >> 1, hf = warp & 1;
     const int r = r0 + jr, t = r / rep, hq = kvh * rep + r % rep;
     const int d = hf * 64 + 2 * lane;
@@ -463,12 +466,13 @@ __global__ void __launch_bounds__(kAtThreads) attn_merge_kernel(const __grid_con
     }
     write_digits(p.xq, mpad, t, 2 * hq + hf, lane, a0, a1);
   }
-  if (rg == 0 && rq == 0) {  // padding tokens T .. mpad-1 of this KV head's query heads
+  if (work && rg == 0 && rq == 0) {  // padding tokens T .. mpad-1 of this KV head's query heads
     for (int job = warp; job < (mpad - p.T) * rep * 2; job += kAtWarps) {
       const int t = p.T + job / (rep * 2), rem = job % (rep * 2);
       write_digits(p.xq, mpad, t, 2 * (kvh * rep + rem / 2) + (rem & 1), lane, 0.f, 0.f);
     }
   }
+  peer_signal_done(p.sync, &sync_flag);  // (sharded step) this rank's digit groups are ready
 }
 
 size_t attn_ws_bytes(int T, int nh, int nkv, int max_len) {
@@ -485,7 +489,7 @@ bool attn_fits(int T, int nh, int nkv) {
 cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, const float* kn_w,
                               const float* inv_freq, int rot, int gated, float eps, void* kc, void* vc, int L0,
                               const int* len_dev, int max_len, int T, int nh, int nkv, void* ws, void* xq,
-                              void* o_out, cudaStream_t stream) {
+                              void* o_out, const skinny_peer_sync* sync, cudaStream_t stream) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -521,6 +525,7 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
   prm.part = static_cast<float*>(ws);
   prm.xq = static_cast<uint8_t*>(xq);
   prm.o_out = static_cast<__nv_bfloat16*>(o_out);
+  prm.sync = peer_sync_from(sync);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;

@@ -1,5 +1,6 @@
 // C-ABI entry points: host-side validation, then stream-ordered kernel launches.
 #include <cstdint>
+#include <cstring>
 #include <utility>
 #include <cuda_runtime.h>
 
@@ -20,10 +21,11 @@ cudaError_t qmm_simt_launch(const void* x, int ldx, const void* w_tc, void* out,
 bool qmm_noalloc_fits(int N, int K);
 size_t spec_accept_ws_bytes();
 cudaError_t qmm_tc_launch_prepared(const void* xq, const void* w_tc, void* out, int ldo, int M, int N, int K,
-                                   void* ws, cudaStream_t stream);
+                                   void* ws, const void* const* xq_ranks, int xq_gpr, const skinny_peer_sync* sync,
+                                   cudaStream_t stream);
 cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd, int dseg_cols,
-                        long long dseg_stride, void* h_out, int ldh, const float* w, float eps, int K, int M,
-                        void* xq, void* a_out, cudaStream_t stream);
+                        const void* const* dseg, void* h_out, int ldh, const float* w, float eps, int K, int M,
+                        void* xq, void* a_out, const skinny_peer_sync* sync, cudaStream_t stream);
 struct GdnFusedParamsHost {
   const void* proj;
   int ldp;
@@ -59,7 +61,7 @@ bool attn_fits(int T, int nh, int nkv);
 cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, const float* kn_w,
                               const float* inv_freq, int rot, int gated, float eps, void* kc, void* vc, int L0,
                               const int* len_dev, int max_len, int T, int nh, int nkv, void* ws, void* xq,
-                              void* o_out, cudaStream_t stream);
+                              void* o_out, const skinny_peer_sync* sync, cudaStream_t stream);
 }  // namespace skinny
 
 namespace {
@@ -215,55 +217,74 @@ int skinny_qmm_w4g64_noalloc(const void* x, int ldx, const void* w_tc, void* out
                                                    static_cast<cudaStream_t>(stream)));
 }
 
+// A peer-sync descriptor: absent, or a device epoch with an error word, 1..8 ranks, and for a
+// wait the local flag array, for a signal the local counter and one flag address per rank.
+static bool sync_ok(const skinny_peer_sync* s) {
+  if (!s || !s->epoch) return true;
+  if (s->n_ranks < 1 || s->n_ranks > 8 || !s->err) return false;
+  if (!s->wait_flags && !s->counter) return false;
+  if (s->counter)
+    for (int r = 0; r < s->n_ranks; ++r)
+      if (!s->signal_flags[r]) return false;
+  return true;
+}
+
 size_t skinny_xq_bytes(int M, int K) {
   if (M < 1 || M > skinny::kMaxTokens || K < skinny::kGroup || K % skinny::kGroup) return 0;
   return static_cast<size_t>(K / skinny::kGroup) * skinny::xq_block_bytes(M <= 8 ? 8 : 16);
 }
 
-int skinny_prep(int mode, const void* x, int ldx, const void* d, int ldd, int dseg_cols, long long dseg_stride,
-                void* h_out, int ldh, const float* w, float eps, int M, int K, void* xq, void* a_out, void* stream) {
+int skinny_prep(int mode, const void* x, int ldx, const void* d, int ldd, int dseg_cols, const void* const* dseg,
+                void* h_out, int ldh, const float* w, float eps, int M, int K, void* xq, void* a_out,
+                const skinny_peer_sync* sync, void* stream) {
   if (!x || !xq || mode < 0 || mode > 2 || (mode == 0 && !w)) return SKINNY_ERR_INVALID_ARG;
   if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
   if (K < skinny::kGroup || K % skinny::kGroup) return SKINNY_ERR_SHAPE;
+  if (!sync_ok(sync)) return SKINNY_ERR_INVALID_ARG;
   const int need = mode == 1 ? 2 * K : K;
   if (ldx < need || (h_out && ldh < K)) return SKINNY_ERR_INVALID_ARG;
-  if (d && dseg_cols == 0 && ldd < K) return SKINNY_ERR_INVALID_ARG;
-  if (d && dseg_cols != 0 &&
-      (dseg_cols < 0 || dseg_cols % skinny::kGroup || K % dseg_cols || ldd < dseg_cols ||
-       dseg_stride < static_cast<long long>(M - 1) * ldd + dseg_cols))
+  const bool segd = mode == 0 && dseg_cols > 0;
+  if (mode == 0 && dseg_cols < 0) return SKINNY_ERR_INVALID_ARG;
+  if (segd && (!dseg || dseg_cols % skinny::kGroup || K % dseg_cols || K / dseg_cols > 8 || ldd < dseg_cols))
     return SKINNY_ERR_INVALID_ARG;
+  if (mode == 0 && d && !segd && ldd < K) return SKINNY_ERR_INVALID_ARG;
+  const bool has_d = mode == 0 && (d || segd);
   // Outputs are written by one column chunk while other chunks of the row still read the inputs:
-  // h_out and a_out must not overlap x or d.
+  // h_out and a_out must not overlap x or d (or a shard of d).
   const auto span = [M](const void* p, int ld, int width) {
     const uintptr_t b = reinterpret_cast<uintptr_t>(p);
     return std::make_pair(b, b + (static_cast<uintptr_t>(M - 1) * ld + width) * 2);
   };
-  const auto dspan = [&]() {
-    if (dseg_cols == 0) return span(d, ldd, K);
-    const uintptr_t b = reinterpret_cast<uintptr_t>(d);
-    const uintptr_t n = static_cast<uintptr_t>(K / dseg_cols - 1) * dseg_stride +
-                        static_cast<uintptr_t>(M - 1) * ldd + dseg_cols;
-    return std::make_pair(b, b + n * 2);
-  };
   const auto overlap = [](std::pair<uintptr_t, uintptr_t> a, std::pair<uintptr_t, uintptr_t> b) {
     return a.first < b.second && b.first < a.second;
   };
+  const auto hits_d = [&](std::pair<uintptr_t, uintptr_t> o) {
+    if (!has_d) return false;
+    if (!segd) return overlap(o, span(d, ldd, K));
+    for (int i = 0; i < K / dseg_cols; ++i)
+      if (overlap(o, span(dseg[i], ldd, dseg_cols))) return true;
+    return false;
+  };
   if (mode == 0) {
     const auto xs = span(x, ldx, K);
-    if (h_out && d && (overlap(span(h_out, ldh, K), xs) || overlap(span(h_out, ldh, K), dspan())))
+    if (h_out && has_d && (overlap(span(h_out, ldh, K), xs) || hits_d(span(h_out, ldh, K))))
       return SKINNY_ERR_INVALID_ARG;
-    if (a_out && (overlap(span(a_out, K, K), xs) || (d && overlap(span(a_out, K, K), dspan()))))
-      return SKINNY_ERR_INVALID_ARG;
+    if (a_out && (overlap(span(a_out, K, K), xs) || hits_d(span(a_out, K, K)))) return SKINNY_ERR_INVALID_ARG;
   }
   // bf16 pairs are read and written as 4-byte words; mode 0 reads its row as 16-byte vectors
-  if ((ldx % 2) || (d && ldd % 2) || (d && dseg_stride % 2) || (h_out && ldh % 2) || !aligned16(xq) ||
-      !aligned4(x) || !aligned4(d) || !aligned4(h_out) || !aligned4(a_out))
+  if ((ldx % 2) || (has_d && ldd % 2) || (h_out && ldh % 2) || !aligned16(xq) || !aligned4(x) ||
+      !aligned4(h_out) || !aligned4(a_out))
     return SKINNY_ERR_ALIGNMENT;
-  if (mode == 0 && (K > 16384)) return SKINNY_ERR_SHAPE;
-  if (mode == 0 && ((ldx % 8) || !aligned16(x) || (d && ((ldd % 8) || (dseg_stride % 8) || !aligned16(d)))))
+  if (mode == 0 && K > 16384) return SKINNY_ERR_SHAPE;
+  if (mode == 0 && ((ldx % 8) || !aligned16(x) || (has_d && (ldd % 8))))
     return SKINNY_ERR_ALIGNMENT;
-  return cuda_status(skinny::prep_launch(mode, x, ldx, d, ldd, d ? dseg_cols : 0, dseg_stride, h_out, ldh, w, eps,
-                                         K, M, xq, a_out, static_cast<cudaStream_t>(stream)));
+  if (mode == 0 && has_d && !segd && !aligned16(d)) return SKINNY_ERR_ALIGNMENT;
+  if (segd)
+    for (int i = 0; i < K / dseg_cols; ++i)
+      if (!dseg[i] || !aligned16(dseg[i])) return SKINNY_ERR_ALIGNMENT;
+  return cuda_status(skinny::prep_launch(mode, x, ldx, mode == 0 ? d : nullptr, ldd, segd ? dseg_cols : 0, dseg,
+                                         h_out, ldh, w, eps, K, M, xq, a_out, sync,
+                                         static_cast<cudaStream_t>(stream)));
 }
 
 int skinny_gdn_fused(const void* proj, int ldp, void* conv, void* conv_full, const float* conv_w,
@@ -292,7 +313,7 @@ size_t skinny_attn_workspace_bytes(int T, int n_heads, int n_kv_heads, int max_l
 int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
                       const float* inv_freq, int rot, int gated, float eps, void* k_cache, void* v_cache, int L0,
                       const int32_t* length_dev, int T, int n_heads, int n_kv_heads, int max_len, void* workspace,
-                      size_t workspace_bytes, void* xq, void* o_out, void* stream) {
+                      size_t workspace_bytes, void* xq, void* o_out, const skinny_peer_sync* sync, void* stream) {
   if (!proj || !q_norm_w || !k_norm_w || !k_cache || !v_cache || !xq || (rot > 0 && !inv_freq))
     return SKINNY_ERR_INVALID_ARG;
   if (T < 1 || T > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
@@ -300,7 +321,8 @@ int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const fl
   if (!skinny::attn_fits(T, n_heads, n_kv_heads) || rot < 0 || rot > 128 || (rot % 2) || L0 < 0 ||
       (!length_dev && L0 + T > max_len) || max_len < T)
     return SKINNY_ERR_SHAPE;
-  if ((gated != 0 && gated != 1) || ldp < ((1 + gated) * n_heads + 2 * n_kv_heads) * 128) return SKINNY_ERR_INVALID_ARG;
+  if ((gated != 0 && gated != 1) || ldp < ((1 + gated) * n_heads + 2 * n_kv_heads) * 128 || !sync_ok(sync))
+    return SKINNY_ERR_INVALID_ARG;
   if (!aligned16(xq) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned4(o_out) || !aligned16(proj) ||
       (ldp % 8) || !aligned4(length_dev))
     return SKINNY_ERR_ALIGNMENT;
@@ -309,22 +331,61 @@ int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const fl
     return SKINNY_ERR_WORKSPACE;
   return cuda_status(skinny::attn_fused_launch(proj, ldp, q_norm_w, k_norm_w, inv_freq, rot, gated, eps, k_cache,
                                                v_cache, L0, length_dev, max_len, T, n_heads, n_kv_heads,
-                                               workspace, xq, o_out, static_cast<cudaStream_t>(stream)));
+                                               workspace, xq, o_out, sync, static_cast<cudaStream_t>(stream)));
 }
 
 int skinny_qmm_w4g64_prepared(const void* xq, const void* w_tc, void* out, int ldo, int M, int N, int K,
-                              void* workspace, size_t workspace_bytes, void* stream) {
-  if (!xq || !w_tc || !out) return SKINNY_ERR_INVALID_ARG;
+                              void* workspace, size_t workspace_bytes, const void* const* xq_ranks,
+                              int xq_groups_per_rank, const skinny_peer_sync* sync, void* stream) {
+  if ((!xq && !xq_ranks) || !w_tc || !out) return SKINNY_ERR_INVALID_ARG;
   const int st = check_qmm_shape(N, K);
   if (st != SKINNY_OK) return st;
   if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
   if (ldo < N) return SKINNY_ERR_INVALID_ARG;
-  if (!aligned16(xq) || !aligned16(w_tc)) return SKINNY_ERR_ALIGNMENT;
+  if (xq_ranks) {
+    const int G = K / skinny::kGroup;
+    if (xq_groups_per_rank < 1 || G % xq_groups_per_rank || G / xq_groups_per_rank > 8) return SKINNY_ERR_INVALID_ARG;
+    for (int r = 0; r < G / xq_groups_per_rank; ++r)
+      if (!xq_ranks[r] || !aligned16(xq_ranks[r])) return SKINNY_ERR_ALIGNMENT;
+  } else if (!aligned16(xq)) {
+    return SKINNY_ERR_ALIGNMENT;
+  }
+  if (!sync_ok(sync)) return SKINNY_ERR_INVALID_ARG;
+  if (!aligned16(w_tc)) return SKINNY_ERR_ALIGNMENT;
   const skinny::WsLayout wl = skinny::ws_layout(skinny::device_sm_count(current_device()));
   if (!workspace || workspace_bytes < wl.total || !aligned16(workspace)) return SKINNY_ERR_WORKSPACE;
-  return cuda_status(skinny::qmm_tc_launch_prepared(xq, w_tc, out, ldo, M, N, K, workspace,
-                                                    static_cast<cudaStream_t>(stream)));
+  return cuda_status(skinny::qmm_tc_launch_prepared(xq, w_tc, out, ldo, M, N, K, workspace, xq_ranks,
+                                                    xq_groups_per_rank, sync, static_cast<cudaStream_t>(stream)));
 }
+
+// ---- peer memory (CUDA IPC) ----
+static_assert(sizeof(cudaIpcMemHandle_t) == 64, "64-byte IPC handles");
+int skinny_ipc_alloc(size_t bytes, void** ptr, void* handle64) {
+  if (!ptr || !handle64 || bytes == 0) return SKINNY_ERR_INVALID_ARG;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_status(e);
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();  // zeroed before any rank can map it
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle64), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_status(e);
+  }
+  *ptr = p;
+  return SKINNY_OK;
+}
+
+int skinny_ipc_open(const void* handle64, void** ptr) {
+  if (!handle64 || !ptr) return SKINNY_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int skinny_ipc_close(void* ptr) { return ptr ? cuda_status(cudaIpcCloseMemHandle(ptr)) : SKINNY_ERR_INVALID_ARG; }
+
+int skinny_ipc_free(void* ptr) { return ptr ? cuda_status(cudaFree(ptr)) : SKINNY_ERR_INVALID_ARG; }
 
 size_t skinny_spec_accept_workspace_bytes(void) { return skinny::spec_accept_ws_bytes(); }
 

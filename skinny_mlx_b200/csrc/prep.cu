@@ -31,6 +31,7 @@
 #include <cuda_runtime.h>
 
 #include "digits.cuh"
+#include "peer.cuh"
 #include "ptx.cuh"
 #include "qmm_layout.cuh"
 
@@ -47,34 +48,41 @@ __device__ __forceinline__ float2 ld_bf2(const __nv_bfloat16* p) {
   return make_float2(__low2float(v), __high2float(v));
 }
 
-// d(t, c) in a column-sharded layout: column c of token t lives in shard c / seg_cols, at
-// shard * seg_stride + t * ldd + c % seg_cols (seg_cols = 0: plain rows).  This is the layout an
-// all-gather of per-rank [M, N/G] column shards produces, read without a transposing copy.
-__device__ __forceinline__ size_t d_off(int t, int c, int ldd, int seg_cols, long long seg_stride) {
-  if (seg_cols == 0) return static_cast<size_t>(t) * ldd + c;
+// d(t, c): plain rows, or column-sharded with one [M, seg_cols] shard per rank (column c of
+// token t in shard c / seg_cols at t * ldd + c % seg_cols): the per-rank outputs of a
+// column-parallel matmul, in an all-gather buffer or read in place from the ranks' memory.
+struct DSegs {
+  const __nv_bfloat16* p[kMaxPeers];
+};
+__device__ __forceinline__ const __nv_bfloat16* d_at(const __nv_bfloat16* d, const DSegs& segs, int t, int c, int ldd,
+                                                     int seg_cols) {
+  if (seg_cols == 0) return d + static_cast<size_t>(t) * ldd + c;
   const int sh = c / seg_cols;
-  return static_cast<size_t>(sh) * seg_stride + static_cast<size_t>(t) * ldd + (c - sh * seg_cols);
+  return segs.p[sh] + static_cast<size_t>(t) * ldd + (c - sh * seg_cols);
 }
 
 // mode 0: rmsnorm (optional residual add), 1: swiglu, 2: plain.
 template <int MODE>
 __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                                                             const __nv_bfloat16* __restrict__ d, int ldd,
-                                                            int dseg_cols, long long dseg_stride,
+                                                            int dseg_cols, const __grid_constant__ DSegs segs,
                                                             __nv_bfloat16* __restrict__ h_out, int ldh,
                                                             const float* __restrict__ w, float eps, int K, int M,
                                                             int mpad, uint8_t* __restrict__ xq,
-                                                            __nv_bfloat16* __restrict__ a_out) {
+                                                            __nv_bfloat16* __restrict__ a_out,
+                                                            const __grid_constant__ PeerSync sync) {
   const int t = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = K / 64;
   const int g = blockIdx.x * kPrepWarps + warp;
   const bool live = t < M;
   __shared__ float red[kPrepWarps];
+  __shared__ int sync_flag;
   pdl_launch_dependents();
   pdl_wait_prior_grid();  // x, d (and the buffers written below) belong to earlier launches
+  peer_wait_all(sync, &sync_flag);  // d's shards from the other ranks (a timeout is recorded)
   const __nv_bfloat16* xr = x + static_cast<size_t>(t) * ldx;
-  const bool has_d = d != nullptr;
+  const bool has_d = d != nullptr || dseg_cols > 0;
   // mode 0: h = bf16(x + d) of the whole row, staged in shared memory by one round of 16-byte
   // loads (the row's sum of squares and this chunk's groups both read it there)
   extern __shared__ __align__(16) uint8_t prep_smem[];
@@ -89,7 +97,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16*
       const int v = tid + u * kPrepThreads;
       if (v < nvec) {
         xv[u] = *reinterpret_cast<const uint4*>(xr + 8 * v);
-        if (has_d) dv[u] = *reinterpret_cast<const uint4*>(d + d_off(t, 8 * v, ldd, dseg_cols, dseg_stride));
+        if (has_d) dv[u] = *reinterpret_cast<const uint4*>(d_at(d, segs, t, 8 * v, ldd, dseg_cols));
       }
     }
     float ss = 0.f;
@@ -122,7 +130,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16*
     for (int i = 0; i < kPrepWarps; ++i) tot += red[i];  // fixed order, the same in every chunk
     rstd = rsqrtf(tot / static_cast<float>(K) + eps);
   }
-  if (g >= G) return;
+  if (g < G) {
   const int c = g * 64 + 2 * lane;
   float a0 = 0.f, a1 = 0.f;
   if (live) {
@@ -145,15 +153,17 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16*
     }
   }
   write_digits(xq, mpad, t, g, lane, a0, a1);
+  }
+  peer_signal_done(sync, &sync_flag);  // this rank's digit groups are ready for the other ranks
 }
 
-static cudaError_t launch_pdl(void (*kern)(const __nv_bfloat16*, int, const __nv_bfloat16*, int, int, long long,
+static cudaError_t launch_pdl(void (*kern)(const __nv_bfloat16*, int, const __nv_bfloat16*, int, int, DSegs,
                                            __nv_bfloat16*, int, const float*, float, int, int, int, uint8_t*,
-                                           __nv_bfloat16*),
+                                           __nv_bfloat16*, PeerSync),
                               dim3 grid, size_t smem, cudaStream_t stream, const __nv_bfloat16* x, int ldx,
-                              const __nv_bfloat16* d, int ldd, int dseg_cols, long long dseg_stride,
-                              __nv_bfloat16* h, int ldh, const float* w, float eps, int K, int M, int mpad,
-                              uint8_t* xq, __nv_bfloat16* a_out) {
+                              const __nv_bfloat16* d, int ldd, int dseg_cols, const DSegs& segs, __nv_bfloat16* h,
+                              int ldh, const float* w, float eps, int K, int M, int mpad, uint8_t* xq,
+                              __nv_bfloat16* a_out, const PeerSync& sync) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kPrepThreads);
@@ -164,18 +174,21 @@ static cudaError_t launch_pdl(void (*kern)(const __nv_bfloat16*, int, const __nv
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, x, ldx, d, ldd, dseg_cols, dseg_stride, h, ldh, w, eps, K, M, mpad, xq,
-                            a_out);
+  return cudaLaunchKernelEx(&cfg, kern, x, ldx, d, ldd, dseg_cols, segs, h, ldh, w, eps, K, M, mpad, xq, a_out, sync);
 }
 
 cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd, int dseg_cols,
-                        long long dseg_stride, void* h_out, int ldh, const float* w, float eps, int K, int M,
-                        void* xq, void* a_out, cudaStream_t stream) {
+                        const void* const* dseg, void* h_out, int ldh, const float* w, float eps, int K, int M,
+                        void* xq, void* a_out, const skinny_peer_sync* sync, cudaStream_t stream) {
   const int mpad = M <= 8 ? 8 : 16;
   const int G = K / 64;
   const dim3 grid((G + kPrepWarps - 1) / kPrepWarps, mpad);
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   auto* q = static_cast<uint8_t*>(xq);
+  DSegs segs{};
+  if (dseg_cols > 0)
+    for (int i = 0; i < K / dseg_cols && i < kMaxPeers; ++i) segs.p[i] = static_cast<const __nv_bfloat16*>(dseg[i]);
+  const PeerSync ps = peer_sync_from(sync);
   if (mode == 0) {
     static bool attr_set[64] = {};
     int dev = 0;
@@ -186,15 +199,15 @@ cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd
       if (e != cudaSuccess) return e;
       attr_set[dev] = true;
     }
-    return launch_pdl(prep_kernel<0>, grid, static_cast<size_t>(K) * sizeof(float), stream, xb, ldx, static_cast<const __nv_bfloat16*>(d), ldd, dseg_cols,
-                      dseg_stride, static_cast<__nv_bfloat16*>(h_out), ldh, w, eps, K, M, mpad, q,
-                      static_cast<__nv_bfloat16*>(a_out));
+    return launch_pdl(prep_kernel<0>, grid, static_cast<size_t>(K) * sizeof(float), stream, xb, ldx,
+                      static_cast<const __nv_bfloat16*>(d), ldd, dseg_cols, segs, static_cast<__nv_bfloat16*>(h_out),
+                      ldh, w, eps, K, M, mpad, q, static_cast<__nv_bfloat16*>(a_out), ps);
   }
   if (mode == 1)
-    return launch_pdl(prep_kernel<1>, grid, 0, stream, xb, ldx, nullptr, 0, 0, 0, nullptr, 0, nullptr, 0.f, K, M, mpad,
-                      q, nullptr);
-  return launch_pdl(prep_kernel<2>, grid, 0, stream, xb, ldx, nullptr, 0, 0, 0, nullptr, 0, nullptr, 0.f, K, M, mpad, q,
-                    nullptr);
+    return launch_pdl(prep_kernel<1>, grid, 0, stream, xb, ldx, nullptr, 0, 0, segs, nullptr, 0, nullptr, 0.f, K, M,
+                      mpad, q, nullptr, ps);
+  return launch_pdl(prep_kernel<2>, grid, 0, stream, xb, ldx, nullptr, 0, 0, segs, nullptr, 0, nullptr, 0.f, K, M,
+                    mpad, q, nullptr, ps);
 }
 
 }  // namespace skinny

@@ -61,6 +61,7 @@
 
 #include <mutex>
 
+#include "peer.cuh"
 #include "ptx.cuh"
 #include "qmm_layout.cuh"
 #include "skinny_status.h"
@@ -116,6 +117,12 @@ struct QmmParams {
   int M, C, n_mats;
   int U;                // total units
   int split;            // 0: stream-K over all units; S >= 1: one matrix, S CTAs (a cluster) per tile
+  // One-matrix calls of a sharded step: the x-prep blocks of groups [r * xq_gpr, (r+1) * xq_gpr)
+  // are read from rank r's buffer xq_rank[r] (at the same offsets as in a full buffer) after
+  // waiting for the ranks' flags; the launch signals its completion (sync).  xq_gpr = 0: xq.
+  const uint8_t* xq_rank[kMaxPeers];
+  int xq_gpr;
+  PeerSync sync;
   QmmMat mats[kMaxMats];
 };
 
@@ -298,6 +305,24 @@ __global__ void __launch_bounds__(256) qmm_xprep_kernel(const __grid_constant__ 
   }
 }
 
+// x-prep blocks of n consecutive groups starting at global group `g` into one stage: one bulk
+// copy, or (sharded step) one per rank whose slice the groups cross.
+__device__ __forceinline__ void copy_x_blocks(const QmmParams& p, uint32_t dst, int g, int n, uint32_t xb,
+                                              uint32_t bar) {
+  if (p.xq_gpr == 0) {
+    bulk_g2s(dst, p.xq + static_cast<size_t>(g) * xb, static_cast<uint32_t>(n) * xb, bar);
+    return;
+  }
+  while (n > 0) {
+    const int r = g / p.xq_gpr;
+    const int m = min(n, (r + 1) * p.xq_gpr - g);
+    bulk_g2s(dst, p.xq_rank[r] + static_cast<size_t>(g) * xb, static_cast<uint32_t>(m) * xb, bar);
+    dst += static_cast<uint32_t>(m) * xb;
+    g += m;
+    n -= m;
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 // The qmm kernel.  NT: token columns read back per unit (2, 4, 8 or 16).
 // ---------------------------------------------------------------------------------------------
@@ -393,13 +418,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++k;
       }
       pdl_wait_prior_grid();  // the x-prep blocks are written by the previous kernel
+      if (p.sync.wait_flags) {  // (sharded step) and by the other ranks; a timeout is recorded
+        peer_wait_flags(p.sync);
+        fence_proxy_async_global();  // the bulk copies below read what the acquire made visible
+      }
       {
         UnitWalk w2;
         w2.init(p, u0);
         for (int f = 0; f < k; ++f) {
           const int n = w2.stage_n(u1);
-          bulk_g2s(smem_u32(xring + f * XSTAGE), p.xq + static_cast<size_t>(p.mats[w2.mi].xg_off + w2.g) * XB,
-                   static_cast<uint32_t>(n) * XB, smem_u32(&sb->full[f]));
+          copy_x_blocks(p, smem_u32(xring + f * XSTAGE), p.mats[w2.mi].xg_off + w2.g, n, XB, smem_u32(&sb->full[f]));
           w2.advance(p, n);
         }
         cmi = wk.mi;
@@ -421,8 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bulk_g2s_hint(smem_u32(wring + s * kWStageBytes),
                       w_tc + static_cast<size_t>(wk.u - wk.uoff) * kUnitWBytes,
                       static_cast<uint32_t>(n) * kUnitWBytes, smem_u32(&sb->full[s]), pol_w);
-        bulk_g2s(smem_u32(xring + s * XSTAGE), p.xq + static_cast<size_t>(xg_off + wk.g) * XB,
-                 static_cast<uint32_t>(n) * XB, smem_u32(&sb->full[s]));
+        copy_x_blocks(p, smem_u32(xring + s * XSTAGE), xg_off + wk.g, n, XB, smem_u32(&sb->full[s]));
         wk.advance(p, n);
         ++k;
       }
@@ -541,9 +568,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     float* xchg = reinterpret_cast<float*>(sb + 1);  // [2][NT][128] partial-sum exchange
-    float acc[NT];
+    // f32 sums of the segment's groups, token pairs packed (2i, 2i + 1) for f32x2 arithmetic
+    uint64_t acc2[NT / 2];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+    for (int i = 0; i < NT / 2; ++i) acc2[i] = 0ull;
     bool dep_waited = false;
     int seg = 0;  // tile segments finished by this CTA
     UnitWalk wk;
@@ -562,23 +590,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           {
             const QmmMeta& mm = sb->meta[qa][j];
             const uint32_t sbw = mm.sb[r];
-            float xs[NT], xsum[NT];
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              xs[t] = mm.x[t];
-              xsum[t] = mm.x[kMaxTokens + t];
-            }
+            // (xs, xsum) of token pairs, read as packed pairs
+            const uint64_t* xs2 = reinterpret_cast<const uint64_t*>(mm.x);
+            const uint64_t* xsum2 = reinterpret_cast<const uint64_t*>(mm.x + kMaxTokens);
             float dh[NT], dl[NT];
             const uint32_t dbase = tmem + lane_off + kDCol0 + (qd * kUPS + j) * DW;
-            tmem_ld<NT>(dbase, dh);
-            tmem_ld<NT>(dbase + MP, dl);
+            if constexpr (NT == MP && NT == 8) {
+              float d[2 * NT];  // hi columns then lo columns: one load
+              tmem_ld<2 * NT>(dbase, d);
+#pragma unroll
+              for (int t = 0; t < NT; ++t) {
+                dh[t] = d[t];
+                dl[t] = d[NT + t];
+              }
+            } else {
+              tmem_ld<NT>(dbase, dh);
+              tmem_ld<NT>(dbase + MP, dl);
+            }
             tc_wait_ld();
             const float sc = __uint_as_float(sbw << 16);
             const float bo = fmaf(8.0f, sc, __uint_as_float(sbw & 0xFFFF0000u));  // b + 8 s
+            const uint64_t sc2 = f2_pack(sc, sc), bo2 = f2_pack(bo, bo);
+            // acc += (s xs) G + (b + 8 s) xsum per token, as fmaf(s * xs, G, fmaf(bo, xsum, acc))
 #pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              const int G = __float_as_int(dh[t]) * 256 + __float_as_int(dl[t]);
-              acc[t] = fmaf(sc * xs[t], static_cast<float>(G), fmaf(bo, xsum[t], acc[t]));
+            for (int i = 0; i < NT / 2; ++i) {
+              const float g0 = static_cast<float>(__float_as_int(dh[2 * i]) * 256 + __float_as_int(dl[2 * i]));
+              const float g1 =
+                  static_cast<float>(__float_as_int(dh[2 * i + 1]) * 256 + __float_as_int(dl[2 * i + 1]));
+              const uint64_t part = f2_fma(bo2, xsum2[i], acc2[i]);
+              acc2[i] = f2_fma(f2_mul(sc2, xs2[i]), f2_pack(g0, g1), part);
             }
           }
         }
@@ -594,6 +634,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int g = wk.g + n - 1;  // group of the stage's last unit
       if (g == wk.G - 1 || wk.u + n == u1) {
         // ---- end of a tile segment: combine the lanes, then write the tile or publish a partial
+        float acc[NT];
+#pragma unroll
+        for (int i = 0; i < NT / 2; ++i) f2_unpack(acc2[i], acc[2 * i], acc[2 * i + 1]);
         const int own = k & 1;  // the warpgroup that holds the segment's last stage finishes it
         float* xb = xchg + (seg & 1) * NT * kTileRows;
         if (L != own) {
@@ -670,7 +713,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }  // stream-K / whole tile
         }
 #pragma unroll
-        for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+        for (int i = 0; i < NT / 2; ++i) acc2[i] = 0ull;
         ++seg;
       }
       wk.advance(p, n);
@@ -720,6 +763,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     cluster_arrive_relaxed();
     cluster_wait_acquire();
   }
+  peer_signal_done(p.sync, &sb->last_flag[0]);  // (sharded step) this rank's output is complete
 }
 
 // One-time relayout: MLX packs + bf16 scales/biases -> units (see qmm_layout.cuh).
@@ -941,6 +985,8 @@ static cudaError_t launch_grouped_on(int n, const void* const* x, const int* ldx
   prm.xq = xq;
   prm.M = M;
   prm.n_mats = n;
+  prm.xq_gpr = 0;
+  prm.sync = PeerSync{};
   xp.xq = xq;
   xp.M = M;
   xp.mpad = mpad;
@@ -991,7 +1037,8 @@ static cudaError_t launch_grouped_on(int n, const void* const* x, const int* ldx
 // One matrix whose input was already written in the x-prep block format by a producer kernel
 // (prep.cu): no x-prep launch.  xq holds K/64 blocks for mpad(M) token rows.
 cudaError_t qmm_tc_launch_prepared(const void* xq, const void* w_tc, void* out, int ldo, int M, int N, int K,
-                                   void* ws, cudaStream_t stream) {
+                                   void* ws, const void* const* xq_ranks, int xq_gpr, const skinny_peer_sync* sync,
+                                   cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   const int C_dev = device_sm_count(dev);
@@ -1005,6 +1052,11 @@ cudaError_t qmm_tc_launch_prepared(const void* xq, const void* w_tc, void* out, 
   prm.xq = static_cast<const uint8_t*>(xq);
   prm.M = M;
   prm.n_mats = 1;
+  prm.xq_gpr = xq_ranks ? xq_gpr : 0;
+  for (int r = 0; r < kMaxPeers; ++r) prm.xq_rank[r] = nullptr;
+  if (xq_ranks)
+    for (int r = 0; r < kMaxPeers && r * xq_gpr < K / kGroup; ++r) prm.xq_rank[r] = static_cast<const uint8_t*>(xq_ranks[r]);
+  prm.sync = peer_sync_from(sync);
   QmmMat& mt = prm.mats[0];
   mt.w_tc = static_cast<const uint8_t*>(w_tc);
   mt.out = static_cast<__nv_bfloat16*>(out);

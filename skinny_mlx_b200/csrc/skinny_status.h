@@ -25,4 +25,5 @@ constexpr unsigned kErrBitWaitDrain = 1u << 6;
 constexpr unsigned kErrBitXOverflow = 1u << 8;  // an activation exceeded the f16 range
 constexpr unsigned kErrBitBadInput = 1u << 9;   // e.g. a token id outside the vocabulary
 constexpr unsigned kErrBitWaitCluster = 1u << 10;  // a CTA's wait for its cluster peers' data
+constexpr unsigned kErrBitWaitPeer = 1u << 11;     // a launch's wait for the other ranks' flags
 }  // namespace skinny

@@ -118,19 +118,19 @@ class FusedStep:
         L0 = c.length
         _lib.call("skinny_attn_fused", _p(proj), proj.stride(0), _p(ent["qn"]), _p(ent["kn"]), _p(ent["inv"]),
                   cfg.rotary_dim, 1, cfg.rms_eps, _p(c.k), _p(c.v), L0, _p(len_dev), m, cfg.n_heads, cfg.n_kv_heads,
-                  max_len, _p(ws), ws.numel(), _p(xq), None, stream)
+                  max_len, _p(ws), ws.numel(), _p(xq), None, None, stream)
         if len_dev is None:
             c.length = L0 + m
 
     def _qmm(self, xq, w: SkinnyWeight, out, m: int, stream):
         ws = get_workspace(out.device, int(_lib.lib().skinny_qmm_workspace_bytes(w.N, w.K)))
         _lib.call("skinny_qmm_w4g64_prepared", _p(xq), _p(w.w_tc), _p(out), out.stride(0), m, w.N, w.K,
-                  _p(ws), ws.numel(), stream)
+                  _p(ws), ws.numel(), None, 0, None, stream)
 
     def _prep(self, mode, x, m, k, xq, stream, d=None, h_out=None, w=None, a_out=None):
-        _lib.call("skinny_prep", mode, _p(x), x.stride(0), _p(d), d.stride(0) if d is not None else 0, 0, 0,
+        _lib.call("skinny_prep", mode, _p(x), x.stride(0), _p(d), d.stride(0) if d is not None else 0, 0, None,
                   _p(h_out), h_out.stride(0) if h_out is not None else 0, _p(w), self.cfg.rms_eps, m, k,
-                  _p(xq), _p(a_out), stream)
+                  _p(xq), _p(a_out), None, stream)
 
     # ---------------------------------------------------------------- the step
     @torch.no_grad()

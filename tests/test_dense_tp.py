@@ -147,7 +147,7 @@ def test_dense_fused_step_matches_module_path(cuda_lib, dev):
     assert [c.length for c in ca] == [c.length for c in cb]
 
 
-def _gpu_fused_rank(rank, world, port, q):
+def _gpu_fused_rank(rank, world, port, q, exchange):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import datetime
 
@@ -156,26 +156,34 @@ def _gpu_fused_rank(rank, world, port, q):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
+    f = None
     try:
         from skinny_mlx_b200.dense_fused import DenseFusedStep
         from skinny_mlx_b200.patch import patch_model
 
         m = DenseModel(small_dense(), rank, world, seed=3, device=f"cuda:{rank}")
         patch_model(m)
-        f = DenseFusedStep(m)
+        f = DenseFusedStep(m, exchange=exchange)
         caches = m.make_cache(64)
-        f(torch.tensor(IDS[:5], device=f"cuda:{rank}"), caches)
-        logits = _full(f(torch.tensor(IDS[5:], device=f"cuda:{rank}"), caches)).float().cpu()
+        out = []
+        # prefill, then verify steps of 3, 1 and 16 tokens: every step advances the epoch
+        for ids in (IDS[:5], IDS[5:], IDS[:1], (IDS * 2)[:16]):
+            out.append(_full(f(torch.tensor(ids, device=f"cuda:{rank}"), caches)).float().cpu())
+        errs = f.errors()
         if rank == 0:
-            q.put(logits)
+            q.put((out, errs))
     finally:
+        if f is not None:
+            f.release()
         dist.destroy_process_group()
 
 
 @pytest.mark.gpu
-def test_dense_fused_step_two_gpus(cuda_lib, dev):
-    """2 ranks over NCCL (skipped on a 1-GPU box): the fused sharded step (digit-block and output
-    all-gathers) against the unsharded patched module path."""
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+def test_dense_fused_step_two_gpus(cuda_lib, dev, exchange):
+    """2 ranks (skipped on a 1-GPU box): the fused sharded step against the unsharded patched
+    module path, with the peer-memory exchange (other ranks' digit blocks and output shards read
+    in place over NVLink after per-layer flags) and with NCCL all-gathers."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from skinny_mlx_b200.patch import patch_model
@@ -183,15 +191,47 @@ def test_dense_fused_step_two_gpus(cuda_lib, dev):
     m = DenseModel(small_dense(), 0, 1, seed=3, device=dev)
     patch_model(m)
     caches = m.make_cache(64)
-    m(torch.tensor(IDS[:5], device=dev), caches)
-    ref = m(torch.tensor(IDS[5:], device=dev), caches).float().cpu()
+    refs = [m(torch.tensor(ids, device=dev), caches).float().cpu()
+            for ids in (IDS[:5], IDS[5:], IDS[:1], (IDS * 2)[:16])]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_gpu_fused_rank, args=(r, 2, 29657, q)) for r in range(2)]
+    port = 29657 if exchange == "peer" else 29667
+    procs = [ctx.Process(target=_gpu_fused_rank, args=(r, 2, port, q, exchange)) for r in range(2)]
     for p in procs:
         p.start()
-    got = q.get(timeout=300)
+    got, errs = q.get(timeout=300)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert ((ref - got).abs().max() / ref.abs().max()).item() <= 1.5e-2
+    assert errs == 0
+    for ref, g in zip(refs, got):
+        assert ((ref - g).abs().max() / ref.abs().max()).item() <= 1.5e-2
+        assert (ref.argmax(-1) == g.argmax(-1)).float().mean().item() >= 0.75
+
+
+@pytest.mark.gpu
+def test_peer_wait_gives_up_and_records(cuda_lib, dev):
+    """A consumer whose flag no producer sets: the bounded wait gives up (about a second), sets
+    its error bit, and the context stays usable (the digits are still written)."""
+    import ctypes
+
+    from skinny_mlx_b200 import _lib
+
+    K, M = 256, 4
+    x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+    xq = torch.zeros(int(_lib.lib().skinny_xq_bytes(M, K)), dtype=torch.uint8, device=dev)
+    epoch = torch.ones(1, dtype=torch.int32, device=dev)
+    flags = torch.zeros(2, dtype=torch.int32, device=dev)  # nothing ever stores the epoch here
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    s = _lib.PeerSync()
+    s.epoch, s.wait_flags, s.err, s.n_ranks = epoch.data_ptr(), flags.data_ptr(), err.data_ptr(), 2
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    _lib.call("skinny_prep", 2, ctypes.c_void_p(x.data_ptr()), K, None, 0, 0, None, None, 0, None, 0.0, M, K,
+              ctypes.c_void_p(xq.data_ptr()), None, ctypes.byref(s), stream)
+    torch.cuda.synchronize(dev)
+    assert int(err.item()) & (1 << 11)
+    ref = torch.zeros_like(xq)
+    _lib.call("skinny_prep", 2, ctypes.c_void_p(x.data_ptr()), K, None, 0, 0, None, None, 0, None, 0.0, M, K,
+              ctypes.c_void_p(ref.data_ptr()), None, None, stream)
+    torch.cuda.synchronize(dev)
+    assert torch.equal(xq, ref)

@@ -33,8 +33,8 @@ def test_prep_plain_is_the_xprep_format(cuda_lib, dev, m):
     x[0, 64:128] = 0
     xq = torch.zeros(int(cuda_lib.skinny_xq_bytes(m, 640)), dtype=torch.uint8, device=dev)
     xt = _bf16(x, dev)
-    assert cuda_lib.skinny_prep(2, _p(xt), 640, None, 0, 0, 0, None, 0, None, ctypes.c_float(0), m, 640, _p(xq),
-                                None, _stream()) == 0
+    assert cuda_lib.skinny_prep(2, _p(xt), 640, None, 0, 0, None, None, 0, None, ctypes.c_float(0), m, 640, _p(xq),
+                                None, None, _stream()) == 0
     mpad = 8 if m <= 8 else 16
     assert np.array_equal(xq.cpu().numpy().reshape(10, -1), quant.xq_blocks(x, mpad))
 
@@ -54,14 +54,15 @@ def test_prep_norm_and_swiglu_feed_the_prepared_qmm(cuda_lib, dev, m):
     h = torch.empty_like(x)
     a = torch.empty(m, K, dtype=torch.bfloat16, device=dev)
     # outputs overlapping the inputs are refused (chunks of a row are written while others read it)
-    assert cuda_lib.skinny_prep(0, _p(x), K, _p(d), K, 0, 0, _p(x), K, _p(gw), ctypes.c_float(1e-6), m, K, _p(xq),
-                                _p(a), _stream()) == -1
-    assert cuda_lib.skinny_prep(0, _p(x), K, _p(d), K, 0, 0, _p(h), K, _p(gw), ctypes.c_float(1e-6), m, K, _p(xq),
-                                _p(d), _stream()) == -1
-    assert cuda_lib.skinny_prep(0, _p(x), K, _p(d), K, 0, 0, _p(h), K, _p(gw), ctypes.c_float(1e-6), m, K, _p(xq),
-                                _p(a), _stream()) == 0
+    assert cuda_lib.skinny_prep(0, _p(x), K, _p(d), K, 0, None, _p(x), K, _p(gw), ctypes.c_float(1e-6), m, K, _p(xq),
+                                _p(a), None, _stream()) == -1
+    assert cuda_lib.skinny_prep(0, _p(x), K, _p(d), K, 0, None, _p(h), K, _p(gw), ctypes.c_float(1e-6), m, K, _p(xq),
+                                _p(d), None, _stream()) == -1
+    assert cuda_lib.skinny_prep(0, _p(x), K, _p(d), K, 0, None, _p(h), K, _p(gw), ctypes.c_float(1e-6), m, K, _p(xq),
+                                _p(a), None, _stream()) == 0
     y = torch.empty(m, N, dtype=torch.bfloat16, device=dev)
-    assert cuda_lib.skinny_qmm_w4g64_prepared(_p(xq), _p(w.w_tc), _p(y), N, m, N, K, _p(ws), ws.numel(), _stream()) == 0
+    assert cuda_lib.skinny_qmm_w4g64_prepared(_p(xq), _p(w.w_tc), _p(y), N, m, N, K, _p(ws), ws.numel(), None, 0, None,
+                                                 _stream()) == 0
     href = (x.float() + d.float()).to(torch.bfloat16)
     assert torch.equal(h, href)
     hf = href.float()
@@ -71,9 +72,10 @@ def test_prep_norm_and_swiglu_feed_the_prepared_qmm(cuda_lib, dev, m):
     assert torch.equal(y, yref)
     # SwiGLU
     gu = torch.randn(m, 2 * K, device=dev).to(torch.bfloat16)
-    assert cuda_lib.skinny_prep(1, _p(gu), 2 * K, None, 0, 0, 0, None, 0, None, ctypes.c_float(0), m, K, _p(xq), None,
-                                _stream()) == 0
-    assert cuda_lib.skinny_qmm_w4g64_prepared(_p(xq), _p(w.w_tc), _p(y), N, m, N, K, _p(ws), ws.numel(), _stream()) == 0
+    assert cuda_lib.skinny_prep(1, _p(gu), 2 * K, None, 0, 0, None, None, 0, None, ctypes.c_float(0), m, K, _p(xq), None,
+                                None, _stream()) == 0
+    assert cuda_lib.skinny_qmm_w4g64_prepared(_p(xq), _p(w.w_tc), _p(y), N, m, N, K, _p(ws), ws.numel(), None, 0, None,
+                                                 _stream()) == 0
     sref = (torch.nn.functional.silu(gu[:, :K].float()) * gu[:, K:].float()).to(torch.bfloat16)
     yref = skinny_qmm(sref, w).float()
     assert ((y.float() - yref).abs().max() / yref.abs().max()).item() <= 1e-2
@@ -180,7 +182,7 @@ def test_attn_fused_matches_module_attention(cuda_lib, dev, T, L0):
         st = cuda_lib.skinny_attn_fused(_p(proj), proj.stride(0), _p(a.q_norm.weight), _p(a.k_norm.weight), _p(inv),
                                         cfg.rotary_dim, 1, ctypes.c_float(cfg.rms_eps), _p(cb.k), _p(cb.v), L0,
                                         _p(len_dev) if rep == 1 else None, T, nh, nkv, max_len, _p(ws), ws.numel(),
-                                        _p(xq), _p(o), _stream())
+                                        _p(xq), _p(o), None, _stream())
         assert st == 0
         torch.cuda.synchronize()
         err = ((o.float() - ref.float()).abs().max() / ref.float().abs().max()).item()
@@ -260,7 +262,7 @@ def test_attn_fused_ungated_dense_shape(cuda_lib, dev):
     o = torch.empty(T, nh * D, dtype=torch.bfloat16, device=dev)
     st = cuda_lib.skinny_attn_fused(_p(proj), proj.stride(0), _p(qn), _p(kn), _p(inv), 128, 0, ctypes.c_float(1e-6),
                                     _p(kc), _p(vc), L0, None, T, nh, nkv, max_len, _p(ws), ws.numel(), _p(xq), _p(o),
-                                    _stream())
+                                    None, _stream())
     assert st == 0
     torch.cuda.synchronize()
     err = ((o.float() - ref).abs().max() / ref.abs().max()).item()
