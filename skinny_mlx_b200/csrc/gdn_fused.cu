@@ -226,21 +226,39 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
   // ---- recurrence: thread = (row, sub); columns sub + 8 i in registers.  Per token the three
   // dot products a = S k, b = S q (of the previous state) and c = k q share one reduction round:
   //   u = beta (v - g a),   S <- g S + u k^T,   y = S q = g b + u c.
+  // The next token's operands are loaded while the current token's reductions run; the
+  // arithmetic per token is the same whatever T is, so a token's results do not depend on how
+  // many tokens share the launch.
+  float kn[kGfCols], qn[kGfCols], gn = 0.f, bn = 0.f, vn = 0.f;
+  const auto load_tok = [&](int t) {
+    gn = gs[t];
+    bn = bs[t];
+    vn = vs[t][row];
+#pragma unroll
+    for (int i = 0; i < kGfCols; ++i) {
+      kn[i] = ks[t][sub + kGfTpr * i];
+      qn[i] = qs[t][sub + kGfTpr * i];
+    }
+  };
+  if (T > 0) load_tok(0);
   for (int t = 0; t < T; ++t) {
-    const float gt = gs[t], bt = bs[t], vt = vs[t][row];
-    float kk[kGfCols];
+    const float gt = gn, bt = bn, vt = vn;
+    float kk[kGfCols], qq[kGfCols];
+#pragma unroll
+    for (int i = 0; i < kGfCols; ++i) {
+      kk[i] = kn[i];
+      qq[i] = qn[i];
+    }
+    if (t + 1 < T) load_tok(t + 1);
     float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f, c0 = 0.f, c1 = 0.f;
 #pragma unroll
     for (int i = 0; i < kGfCols; i += 2) {
-      kk[i] = ks[t][sub + kGfTpr * i];
-      kk[i + 1] = ks[t][sub + kGfTpr * (i + 1)];
-      const float q0 = qs[t][sub + kGfTpr * i], q1 = qs[t][sub + kGfTpr * (i + 1)];
       a0 = fmaf(S[i], kk[i], a0);
       a1 = fmaf(S[i + 1], kk[i + 1], a1);
-      b0 = fmaf(S[i], q0, b0);
-      b1 = fmaf(S[i + 1], q1, b1);
-      c0 = fmaf(kk[i], q0, c0);
-      c1 = fmaf(kk[i + 1], q1, c1);
+      b0 = fmaf(S[i], qq[i], b0);
+      b1 = fmaf(S[i + 1], qq[i + 1], b1);
+      c0 = fmaf(kk[i], qq[i], c0);
+      c1 = fmaf(kk[i + 1], qq[i + 1], c1);
     }
     float a = a0 + a1, b = b0 + b1, c = c0 + c1;
 #pragma unroll

@@ -120,6 +120,52 @@ def test_gdn_fused_matches_module_mixer(cuda_lib, dev, T):
         assert rel(cb.ckpt[:T - 1], ca.ckpt[:T - 1]) <= 1e-2
 
 
+def test_gdn_fused_prefix_reproduces_checkpoints(cuda_lib, dev):
+    """Rollback through the fused mixer: a verify of the first n of 12 tokens from the same state
+    yields the 12-token verify's checkpoint n - 1 as its state, and the same outputs, bit for bit;
+    so do n single-token steps (a token's results depend only on the tokens before it, not on
+    how many tokens share the launch: speculative decoding then reproduces greedy decoding)."""
+    from skinny_mlx_b200.model import GDNCache
+
+    m = HybridModel(SMALL, seed=0, device=dev)
+    g = m.layers[0].linear_attn
+    cfg = SMALL
+    torch.manual_seed(12)
+    Tl, Hv = 12, cfg.gdn_v_heads
+    proj = (torch.randn(Tl, 4 * cfg.gdn_value_dim + 2 * Hv, device=dev) * 0.5).to(torch.bfloat16)
+    base = GDNCache(cfg, 17, dev)
+    base.conv.copy_((torch.randn_like(base.conv.float()) * 0.5).to(torch.bfloat16))
+    base.state.normal_().mul_(0.1)
+
+    def run(T, c=None, row=0):
+        if c is None:
+            c = GDNCache(cfg, 17, dev)
+            c.conv.copy_(base.conv)
+            c.state.copy_(base.state)
+        xq = torch.empty(int(cuda_lib.skinny_xq_bytes(T, cfg.gdn_value_dim)), dtype=torch.uint8, device=dev)
+        o = torch.empty(T, cfg.gdn_value_dim, dtype=torch.bfloat16, device=dev)
+        errw = torch.zeros(1, dtype=torch.int32, device=dev)
+        assert cuda_lib.skinny_gdn_fused(_p(proj[row:]), proj.stride(0), _p(c.conv), _p(c.conv_full),
+                                         _p(g.conv_weight.float().contiguous()), _p(g.A_log), _p(g.dt_bias),
+                                         _p(g.norm.weight), ctypes.c_float(cfg.rms_eps), _p(c.state), _p(c.ckpt),
+                                         _p(xq), _p(o), T, Hv, cfg.gdn_k_heads, cfg.conv_kernel - 1, _p(errw),
+                                         _stream()) == 0
+        torch.cuda.synchronize()
+        assert int(errw.item()) == 0
+        return c, o
+
+    full, o_full = run(Tl)
+    for n in (1, 3, 7, 11):
+        c, o = run(n)
+        assert torch.equal(c.state, full.ckpt[n - 1])
+        assert torch.equal(o, o_full[:n])
+    c = None
+    for t in range(4):  # single-token steps
+        c, o = run(1, c, t)
+        assert torch.equal(c.state, full.ckpt[t])
+        assert torch.equal(o, o_full[t:t + 1])
+
+
 def test_fused_step_matches_patched_model_and_keeps_spec_exact(cuda_lib, dev):
     from skinny_mlx_b200.fused import FusedStep
     from skinny_mlx_b200.patch import patch_model
