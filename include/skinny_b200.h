@@ -182,7 +182,8 @@ size_t skinny_attn_workspace_bytes(int T, int n_heads, int n_kv_heads, int max_l
 /* One gated full-attention mixer from its fused projection to the prepared input of o_proj, in
  * one launch (the attention layers inside the verify forward of skinny_mlx/spec.py:23-28, which
  * runs the mlx_lm Qwen3.5 model; that layer code is mlx_lm's, not the reference's own):
- *   q, k = RoPE(bf16(rmsnorm(q|k) (1 + w))) on the first rot dims (inv_freq [rot/2] f32) at
+ *   q, k = RoPE(bf16(rmsnorm(q|k) (1 + w))) on the first rot dims (rot in {0, 16, 32, 64, 128};
+ *          inv_freq [rot/2] f32) at
  *          positions L0 .. L0+T-1; k (bf16) and v are appended to k_cache / v_cache
  *          [max_len, n_kv_heads, 128] (16-byte aligned) at L0 .. L0+T-1;
  *   o    = causal (bottom-right) grouped-query softmax(q k^T / sqrt(128)) v over positions

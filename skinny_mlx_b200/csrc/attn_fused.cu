@@ -63,20 +63,46 @@ struct AttnParams {
 
 constexpr int kAtMaxRows = kAtRG * kAtMaxRG;  // query rows of one KV head (T * rep)
 
-// followed in dynamic shared memory by the KV head's R query rows as projected, bf16 [R][128]
-// (staged once per CTA)
+constexpr int kAtPassTiles = 3;                      // 16-row tiles of one pass of a chunk CTA
+constexpr int kAtPassRows = kAtRG * kAtPassTiles;    // query rows per pass
+
 struct AttnSmem {
-  float cs[kAtMaxT][kAtD / 2][2];         // cos / sin of (position, frequency), computed once
-  __nv_bfloat16 q[kAtRG][kAtStride];      // rotated queries of the row group
-  __nv_bfloat16 k[kAtChunk][kAtStride];   // keys of the chunk
-  __nv_bfloat16 v[kAtChunk][kAtStride];   // values of the chunk
-  __nv_bfloat16 pr[kAtRG][kAtStride];     // probabilities (bf16, as a flash kernel rounds them)
-  float s[kAtRG][kAtChunk];               // scores (log2 domain)
+  float cs[kAtMaxT][kAtD / 2][2];            // cos / sin of (position, frequency), computed once
+  float qw[kAtD], kw[kAtD];                  // q / k norm weights
+  __nv_bfloat16 q[kAtPassRows][kAtStride];   // normalised, rotated query rows of the pass
+  __nv_bfloat16 k[kAtChunk][kAtStride];      // keys of the chunk
+  __nv_bfloat16 v[kAtChunk][kAtStride];      // values of the chunk
+  __nv_bfloat16 pr[kAtPassRows][kAtStride];  // probabilities (bf16, as a flash kernel rounds them)
+  float redm[kAtWarps][kAtPassRows];         // per (warp = 16-key block, row): max of the block
+  float redl[kAtWarps][kAtPassRows];         //                                sum of its probabilities
   float stage[kAtWarps][kAtD];
-  float rowm[kAtRG], rowl[kAtRG];
 };
 
 __device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// Loads issued where they stand (volatile: the compiler neither sinks them towards their first
+// use nor splits a batch of them into several round trips).  nc: data that no launch writes while
+// this one runs; cg: data written by the previous launch (read from L2).
+__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ float ld_nc_f32(const float* p) {
+  float r;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(r) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cg_v4(const float* p) {
+  float4 r;
+  asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ float2 ld_cg_v2(const float* p) {
+  float2 r;
+  asm volatile("ld.global.cg.v2.f32 {%0, %1}, [%2];" : "=f"(r.x), "=f"(r.y) : "l"(p));
+  return r;
+}
 
 // Warp-collective: x holds dims lane + 32 i of one head row (bf16-exact).  Returns the row after
 // zero-centred RMSNorm (-> bf16) and RoPE on the first rot dims (-> bf16), the rotation's cos /
@@ -110,6 +136,37 @@ __device__ __forceinline__ void norm_rope_tab(float (&x)[4], const float* w, flo
   __syncwarp();
 }
 
+// Half-warp collective (16 lanes; lane pc holds dims 8 pc .. 8 pc + 7 of one head row, bf16-exact;
+// both halves of the warp call it together, each for its own row): zero-centred RMSNorm (-> bf16)
+// and RoPE on the first rot dims (-> bf16), rot in {0, 16, 32, 64, 128}, so the partner dims
+// d +- rot/2 sit in lane pc ^ (rot / 16).
+__device__ __forceinline__ void norm_rope_hw(float (&x)[8], const float* w, float eps, const float (*cs)[2], int rot,
+                                             int pc) {
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
+#pragma unroll
+  for (int o = 8; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+  const float rstd = rsqrtf(ss / kAtD + eps);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = bfr(x[i] * rstd * (1.f + w[8 * pc + i]));
+  const int half = rot >> 1;
+  const int px = rot >= 16 ? rot >> 4 : 0;
+  float y[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) y[i] = __shfl_xor_sync(0xFFFFFFFFu, x[i], px);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int d = 8 * pc + i;
+    if (d < rot) {
+      const int j = d < half ? d : d - half;
+      const float c = cs[j][0], sn = cs[j][1];
+      x[i] = d < half ? x[i] * c - y[i] * sn : x[i] * c + y[i] * sn;
+    }
+    x[i] = bfr(x[i]);
+  }
+}
+
 // The cache length: a kernel argument, or read from device memory so that one captured launch
 // serves every length (the chunk grid then covers max_len and the surplus chunks leave).
 // Returns -1 for a device length out of range (the launch then touches nothing).
@@ -122,7 +179,7 @@ __device__ __forceinline__ float* part_row(const AttnParams& p, int kvh, int rg,
   return p.part + (((static_cast<size_t>(kvh) * p.nrg + rg) * p.nchunks + chunk) * kAtRG + rr) * kAtPart;
 }
 
-__global__ void __launch_bounds__(kAtThreads) attn_chunk_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kAtThreads, 2) attn_chunk_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(16) uint8_t at_smem_raw[];
   AttnSmem& sm = *reinterpret_cast<AttnSmem*>(at_smem_raw);
   const int chunk = blockIdx.x, kvh = blockIdx.y;
@@ -131,7 +188,6 @@ __global__ void __launch_bounds__(kAtThreads) attn_chunk_kernel(const __grid_con
   const int R = p.T * rep;
   const int qstride = p.gated ? 2 * kAtD : kAtD;  // proj columns per query head
   const int qkw = p.nh * qstride;                  // column of k in proj
-  __nv_bfloat16 (*qraw)[kAtD] = reinterpret_cast<__nv_bfloat16 (*)[kAtD]>(at_smem_raw + sizeof(AttnSmem));
   pdl_launch_dependents();
   pdl_wait_prior_grid();
   const int L0 = attn_length(p);
@@ -141,54 +197,68 @@ __global__ void __launch_bounds__(kAtThreads) attn_chunk_kernel(const __grid_con
   const int Ltot = L0 + p.T;
   const int k0 = chunk * kAtChunk;
   const int nk = min(kAtChunk, Ltot - k0);
+  const int half = p.rot >> 1;
 
-  // ---- cached keys and values of the chunk, and the KV head's query rows: every thread issues
-  // all its 16-byte loads first
+  // ---- every load of the CTA issued together: cached keys and values of the chunk, the KV head's
+  // query rows (kept in registers: thread = (row (tid >> 4) + 16 u, dims 8 (tid & 15) ..)), the
+  // norm weights and the rotary frequencies of the position table
+  constexpr int kPieces = kAtChunk * (kAtD / 8);  // 16-byte pieces per matrix
+  constexpr int kPer = kPieces / kAtThreads;
+  constexpr int kQPer = kAtMaxRows * (kAtD / 8) / kAtThreads;
+  constexpr int kTabPer = kAtMaxT * (kAtD / 2) / kAtThreads;
+  const int pc = tid & 15;
+  uint4 qv[kQPer];
   {
-    constexpr int kPieces = kAtChunk * (kAtD / 8);  // 16-byte pieces per matrix
-    constexpr int kPer = kPieces / kAtThreads;
-    constexpr int kQPer = kAtMaxRows * (kAtD / 8) / kAtThreads;
-    uint4 kw[kPer], vw[kPer], qw[kQPer];
+    uint4 kw[kPer], vw[kPer];
 #pragma unroll
-    for (int u = 0; u < kQPer; ++u) {
-      const int e = tid + u * kAtThreads, r = e >> 4, pc = e & 15;
-      if (r < R) {
+    for (int u = 0; u < kQPer; ++u) {  // rows of the first pass now, the others when their pass starts
+      const int r = (tid >> 4) + 16 * u;
+      qv[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (u < kAtPassTiles && r < R) {
         const int t = r / rep, hq = kvh * rep + r % rep;
-        qw[u] = *reinterpret_cast<const uint4*>(p.proj + static_cast<size_t>(t) * p.ldp + hq * qstride + 8 * pc);
+        qv[u] = ld_nc_v4(p.proj + static_cast<size_t>(t) * p.ldp + hq * qstride + 8 * pc);
       }
     }
 #pragma unroll
     for (int u = 0; u < kPer; ++u) {
-      const int e = tid + u * kAtThreads, j = e >> 4, pc = e & 15;
+      const int e = tid + u * kAtThreads, j = e >> 4, pce = e & 15;
       const int pos = k0 + j;
       if (j < nk && pos < L0) {
-        const size_t off = (static_cast<size_t>(pos) * p.nkv + kvh) * kAtD + 8 * pc;
-        kw[u] = __ldg(reinterpret_cast<const uint4*>(p.kc + off));
-        vw[u] = __ldg(reinterpret_cast<const uint4*>(p.vc + off));
+        const size_t off = (static_cast<size_t>(pos) * p.nkv + kvh) * kAtD + 8 * pce;
+        kw[u] = ld_nc_v4(p.kc + off);
+        vw[u] = ld_nc_v4(p.vc + off);
       } else {
         kw[u] = make_uint4(0u, 0u, 0u, 0u);
         vw[u] = kw[u];
       }
     }
+    const float nwv = ld_nc_f32(tid < kAtD ? p.qn_w + tid : p.kn_w + (tid - kAtD));
+    float fr[kTabPer];
+#pragma unroll
+    for (int u = 0; u < kTabPer; ++u) {
+      const int i = tid + u * kAtThreads;
+      fr[u] = 0.f;
+      if (half > 0 && i < p.T * half) fr[u] = ld_nc_f32(p.inv_freq + i % half);
+    }
 #pragma unroll
     for (int u = 0; u < kPer; ++u) {
-      const int e = tid + u * kAtThreads, j = e >> 4, pc = e & 15;
+      const int e = tid + u * kAtThreads, j = e >> 4, pce = e & 15;
       if (j < nk && k0 + j >= L0) continue;  // a new key: written below by its warp
-      *reinterpret_cast<uint4*>(&sm.k[j][8 * pc]) = kw[u];
-      *reinterpret_cast<uint4*>(&sm.v[j][8 * pc]) = vw[u];
+      *reinterpret_cast<uint4*>(&sm.k[j][8 * pce]) = kw[u];
+      *reinterpret_cast<uint4*>(&sm.v[j][8 * pce]) = vw[u];
     }
+    if (tid < kAtD) sm.qw[tid] = nwv;
+    else sm.kw[tid - kAtD] = nwv;
 #pragma unroll
-    for (int u = 0; u < kQPer; ++u) {
-      const int e = tid + u * kAtThreads, r = e >> 4, pc = e & 15;
-      if (r < R) *reinterpret_cast<uint4*>(&qraw[r][8 * pc]) = qw[u];
-    }
-    // rotation table for the T positions of the verify
-    for (int i = tid; i < p.T * (p.rot >> 1); i += kAtThreads) {
-      const int t = i / (p.rot >> 1), j = i - t * (p.rot >> 1);
-      float sn, c;
-      sincosf(static_cast<float>(L0 + t) * p.inv_freq[j], &sn, &c);
-      sm.cs[t][j][0] = c;
-      sm.cs[t][j][1] = sn;
+    for (int u = 0; u < kTabPer; ++u) {
+      const int i = tid + u * kAtThreads;
+      if (half > 0 && i < p.T * half) {
+        const int t = i / half, j = i - t * half;
+        float sn, c;
+        sincosf(static_cast<float>(L0 + t) * fr[u], &sn, &c);
+        sm.cs[t][j][0] = c;
+        sm.cs[t][j][1] = sn;
+      }
     }
   }
   __syncthreads();
@@ -205,7 +275,7 @@ __global__ void __launch_bounds__(kAtThreads) attn_chunk_kernel(const __grid_con
         x[i] = __bfloat162float(src[kvh * kAtD + lane + 32 * i]);
         vb[i] = src[p.nkv * kAtD + kvh * kAtD + lane + 32 * i];
       }
-      norm_rope_tab(x, p.kn_w, p.eps, sm.cs[t], p.rot, sm.stage[warp], lane);
+      norm_rope_tab(x, sm.kw, p.eps, sm.cs[t], p.rot, sm.stage[warp], lane);
       const size_t off = (static_cast<size_t>(pos) * p.nkv + kvh) * kAtD;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -219,111 +289,178 @@ __global__ void __launch_bounds__(kAtThreads) attn_chunk_kernel(const __grid_con
     }
   }
 
+  // ---- passes of up to three 16-row tiles: scores, softmax and outputs of all the pass's rows
+  // together (warp w: keys 16w .. 16w+15 for the scores, dims 16w .. 16w+15 for the outputs)
   const int g = lane >> 2, cq = lane & 3;
-  for (int rg = 0; rg * kAtRG < R; ++rg) {
-    const int rbase = rg * kAtRG;
-    const int nrows = min(kAtRG, R - rbase);
-    // ---- query rows of the group: normalised, rotated, bf16
-    for (int rr = warp; rr < nrows; rr += kAtWarps) {
-      const int r = rbase + rr, t = r / rep;
-      float x[4];
+  const float sc = rsqrtf(static_cast<float>(kAtD)) * 1.4426950408889634f;
+  for (int rbase = 0; rbase < R; rbase += kAtPassRows) {
+    const int nrows = min(kAtPassRows, R - rbase);
+    const int ntiles = (nrows + kAtRG - 1) / kAtRG;
+    // query rows of the pass: normalised and rotated from registers (half-warp per row); rows
+    // past R inside the pass's tiles are zero
 #pragma unroll
-      for (int i = 0; i < 4; ++i) x[i] = __bfloat162float(qraw[r][lane + 32 * i]);
-      norm_rope_tab(x, p.qn_w, p.eps, sm.cs[t], p.rot, sm.stage[warp], lane);
+    for (int u = 0; u < kQPer; ++u) {
+      const int r = (tid >> 4) + 16 * u;  // rows 16u .. 16u+15 are in one pass: warp-uniform test
+      if (r >= rbase && r < rbase + ntiles * kAtRG) {
+        if (u >= kAtPassTiles && r < R) {
+          const int t = r / rep, hq = kvh * rep + r % rep;
+          qv[u] = ld_nc_v4(p.proj + static_cast<size_t>(t) * p.ldp + hq * qstride + 8 * pc);
+        }
+        float x[8];
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&qv[u]);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) sm.q[rr][lane + 32 * i] = __float2bfloat16_rn(x[i]);
-    }
-    for (int i = tid; i < (kAtRG - nrows) * kAtD; i += kAtThreads) {  // rows past the group: zero
-      sm.q[nrows + i / kAtD][i % kAtD] = __float2bfloat16_rn(0.f);
-      sm.pr[nrows + i / kAtD][i % kAtD] = __float2bfloat16_rn(0.f);
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(h2[i]);
+          x[2 * i] = f.x;
+          x[2 * i + 1] = f.y;
+        }
+        const int t = min(r / rep, p.T - 1);
+        norm_rope_hw(x, sm.qw, p.eps, sm.cs[t], p.rot, pc);
+        uint4 packed;
+        __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&packed);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          o2[i] = r < R ? __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]) : __floats2bfloat162_rn(0.f, 0.f);
+        *reinterpret_cast<uint4*>(&sm.q[r - rbase][8 * pc]) = packed;
+      }
     }
     __syncthreads();
-    // ---- scores on tensor cores (log2 domain): warp w takes keys 16w .. 16w+15 for the 16 rows
+    // scores (log2 domain), masked; each warp's 16-key maximum per row
+    float c[kAtPassTiles][2][4];
+#pragma unroll
+    for (int rt = 0; rt < kAtPassTiles; ++rt)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) c[rt][nt][e] = 0.f;
     {
       const uint32_t a_addr =
           smem_u32(&sm.q[0][0]) + (((lane & 7) + 8 * ((lane >> 3) & 1)) * kAtStride + 8 * (lane >> 4)) * 2;
       const uint32_t b_addr =
           smem_u32(&sm.k[0][0]) + ((16 * warp + (lane & 7) + 8 * (lane >> 4)) * kAtStride + 8 * ((lane >> 3) & 1)) * 2;
-      float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
       for (int ks = 0; ks < kAtD / 16; ++ks) {
-        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-        ldsm_x4(a_addr + ks * 32, a0, a1, a2, a3);
+        uint32_t b0, b1, b2, b3;
         ldsm_x4(b_addr + ks * 32, b0, b1, b2, b3);
-        mma_bf16(c[0], a0, a1, a2, a3, b0, b1);
-        mma_bf16(c[1], a0, a1, a2, a3, b2, b3);
-      }
-      const float sc = rsqrtf(static_cast<float>(kAtD)) * 1.4426950408889634f;
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int rr = g + 8 * (e >> 1), j = 16 * warp + 8 * nt + 2 * cq + (e & 1);
-          if (rr < nrows) {
-            const int t = (rbase + rr) / rep;
-            const bool vis = j < nk && k0 + j <= L0 + t;
-            sm.s[rr][j] = vis ? c[nt][e] * sc : -INFINITY;
+        for (int rt = 0; rt < kAtPassTiles; ++rt) {
+          if (rt < ntiles) {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(a_addr + (rt * kAtRG * kAtStride) * 2 + ks * 32, a0, a1, a2, a3);
+            mma_bf16(c[rt][0], a0, a1, a2, a3, b0, b1);
+            mma_bf16(c[rt][1], a0, a1, a2, a3, b2, b3);
           }
         }
-    }
-    __syncthreads();
-    // ---- chunk softmax per row (warp per row); probabilities rounded to bf16
-    for (int rr = warp; rr < nrows; rr += kAtWarps) {
-      float sv[4];
-      float m = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        sv[i] = sm.s[rr][lane + 32 * i];
-        m = fmaxf(m, sv[i]);
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-      float l = 0.f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const __nv_bfloat16 e = __float2bfloat16_rn(m == -INFINITY ? 0.f : exp2f(sv[i] - m));
-        sm.pr[rr][lane + 32 * i] = e;
-        l += __bfloat162float(e);  // the sum of the probabilities as the products use them
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
-      if (lane == 0) {
-        sm.rowm[rr] = m;
-        sm.rowl[rr] = l;
       }
     }
+#pragma unroll
+    for (int rt = 0; rt < kAtPassTiles; ++rt) {
+      if (rt < ntiles) {
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int rr = rt * kAtRG + g + 8 * hf;
+          const int t = min((rbase + rr) / rep, p.T - 1);
+          float m = -INFINITY;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int j = 16 * warp + 8 * nt + 2 * cq + e;
+              const bool vis = j < nk && k0 + j <= L0 + t;
+              const float v = vis ? c[rt][nt][2 * hf + e] * sc : -INFINITY;
+              c[rt][nt][2 * hf + e] = v;
+              m = fmaxf(m, v);
+            }
+          m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+          m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
+          if (cq == 0) sm.redm[warp][rr] = m;
+        }
+      }
+    }
     __syncthreads();
-    // ---- unnormalised outputs on tensor cores: warp w takes dims 16w .. 16w+15; publish
+    // probabilities (bf16) with the row maximum over the chunk; each warp's partial sums
+#pragma unroll
+    for (int rt = 0; rt < kAtPassTiles; ++rt) {
+      if (rt < ntiles) {
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int rr = rt * kAtRG + g + 8 * hf;
+          float m = sm.redm[0][rr];
+#pragma unroll
+          for (int w = 1; w < kAtWarps; ++w) m = fmaxf(m, sm.redm[w][rr]);
+          float l = 0.f;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const float e0 = m == -INFINITY ? 0.f : exp2f(c[rt][nt][2 * hf] - m);
+            const float e1 = m == -INFINITY ? 0.f : exp2f(c[rt][nt][2 * hf + 1] - m);
+            const __nv_bfloat162 pb = __floats2bfloat162_rn(e0, e1);
+            *reinterpret_cast<__nv_bfloat162*>(&sm.pr[rr][16 * warp + 8 * nt + 2 * cq]) = pb;
+            const float2 pf = __bfloat1622float2(pb);  // the probabilities as the products use them
+            l += pf.x;
+            l += pf.y;
+          }
+          l += __shfl_xor_sync(0xFFFFFFFFu, l, 1);
+          l += __shfl_xor_sync(0xFFFFFFFFu, l, 2);
+          if (cq == 0) sm.redl[warp][rr] = l;
+        }
+      }
+    }
+    __syncthreads();
+    // unnormalised outputs on tensor cores; publish them with each row's (max, sum)
     {
+      float o[kAtPassTiles][2][4];
+#pragma unroll
+      for (int rt = 0; rt < kAtPassTiles; ++rt)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[rt][nt][e] = 0.f;
       const uint32_t a_addr =
           smem_u32(&sm.pr[0][0]) + (((lane & 7) + 8 * ((lane >> 3) & 1)) * kAtStride + 8 * (lane >> 4)) * 2;
       const uint32_t b_addr =
           smem_u32(&sm.v[0][0]) + (((lane & 7) + 8 * ((lane >> 3) & 1)) * kAtStride + 16 * warp + 8 * (lane >> 4)) * 2;
-      float o[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
       for (int ks = 0; ks < kAtChunk / 16; ++ks) {
-        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-        ldsm_x4(a_addr + ks * 32, a0, a1, a2, a3);
+        uint32_t b0, b1, b2, b3;
         ldsm_x4_t(b_addr + ks * 16 * kAtStride * 2, b0, b1, b2, b3);
-        mma_bf16(o[0], a0, a1, a2, a3, b0, b1);
-        mma_bf16(o[1], a0, a1, a2, a3, b2, b3);
+#pragma unroll
+        for (int rt = 0; rt < kAtPassTiles; ++rt) {
+          if (rt < ntiles) {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(a_addr + (rt * kAtRG * kAtStride) * 2 + ks * 32, a0, a1, a2, a3);
+            mma_bf16(o[rt][0], a0, a1, a2, a3, b0, b1);
+            mma_bf16(o[rt][1], a0, a1, a2, a3, b2, b3);
+          }
+        }
       }
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
+      for (int rt = 0; rt < kAtPassTiles; ++rt) {
+        if (rt < ntiles) {
+          const int rg = (rbase + rt * kAtRG) / kAtRG;
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          const int rr = g + 8 * hf;
-          if (rr < nrows)
-            *reinterpret_cast<float2*>(part_row(p, kvh, rg, chunk, rr) + 4 + 16 * warp + 8 * nt + 2 * cq) =
-                make_float2(o[nt][2 * hf], o[nt][2 * hf + 1]);
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              const int rr = g + 8 * hf;
+              if (rt * kAtRG + rr < nrows)
+                *reinterpret_cast<float2*>(part_row(p, kvh, rg, chunk, rr) + 4 + 16 * warp + 8 * nt + 2 * cq) =
+                    make_float2(o[rt][nt][2 * hf], o[rt][nt][2 * hf + 1]);
+            }
         }
+      }
       if (tid < nrows) {
-        float* row = part_row(p, kvh, rg, chunk, tid);
-        row[0] = sm.rowm[tid];
-        row[1] = sm.rowl[tid];
+        float m = sm.redm[0][tid], l = sm.redl[0][tid];
+#pragma unroll
+        for (int w = 1; w < kAtWarps; ++w) {
+          m = fmaxf(m, sm.redm[w][tid]);
+          l += sm.redl[w][tid];
+        }
+        float* row = part_row(p, kvh, (rbase + tid) / kAtRG, chunk, (rbase + tid) % kAtRG);
+        row[0] = m;
+        row[1] = l;
       }
     }
-    __syncthreads();  // q, s, pr are reused by the next row group
+    __syncthreads();  // q, pr and the reductions are reused by the next pass
   }
 }
 
@@ -350,6 +487,11 @@ __global__ void __launch_bounds__(kAtThreads) attn_merge_kernel(const __grid_con
   const bool work = L0 >= 0 && nrows > 0;  // (no early exit: every CTA counts in the signal)
   const int nchunks = work ? (L0 + p.T + kAtChunk - 1) / kAtChunk : 0;
   const bool live = work && rr < nrows;
+  uint4 gw = make_uint4(0u, 0u, 0u, 0u);  // the gate of this (row, dims), loaded with the partials
+  if (live && sub == 0 && p.gated) {
+    const int r = r0 + rr, t = r / rep, hq = kvh * rep + r % rep;
+    gw = ld_nc_v4(p.proj + static_cast<size_t>(t) * p.ldp + hq * 2 * kAtD + kAtD + d0);
+  }
   float M = -INFINITY, L = 0.f, acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
@@ -362,10 +504,11 @@ __global__ void __launch_bounds__(kAtThreads) attn_merge_kernel(const __grid_con
 #pragma unroll
       for (int u = 0; u < kAtMergePass; ++u) {  // unconditional loads (clamped), masked below
         const float* row = base + min(c0 + kSub * u, nchunks - 1) * cstride;
-        mv[u] = __ldcg(row);
-        lv[u] = __ldcg(row + 1);
-        ov[u][0] = __ldcg(reinterpret_cast<const float4*>(row + 4 + d0));
-        ov[u][1] = __ldcg(reinterpret_cast<const float4*>(row + 8 + d0));
+        const float2 ml = ld_cg_v2(row);
+        mv[u] = ml.x;
+        lv[u] = ml.y;
+        ov[u][0] = ld_cg_v4(row + 4 + d0);
+        ov[u][1] = ld_cg_v4(row + 8 + d0);
       }
 #pragma unroll
       for (int u = 0; u < kAtMergePass; ++u)
@@ -414,10 +557,8 @@ __global__ void __launch_bounds__(kAtThreads) attn_merge_kernel(const __grid_con
       for (int i = 0; i < 8; ++i) acc[i] = fmaf(a1, src[2 + i], acc[i] * a0);
       M = Mn;
     }
-    const int r = r0 + rr, t = r / rep, hq = kvh * rep + r % rep;
     float gate[8];
     if (p.gated) {
-      const uint4 gw = *reinterpret_cast<const uint4*>(p.proj + static_cast<size_t>(t) * p.ldp + hq * 2 * kAtD + kAtD + d0);
       const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gw);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -477,7 +618,7 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
     const cudaError_t e = cudaFuncSetAttribute(attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(sizeof(AttnSmem) + kAtMaxRows * kAtD * 2));
+                                               static_cast<int>(sizeof(AttnSmem)));
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
@@ -513,7 +654,7 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(prm.nchunks, nkv);
   cfg.blockDim = dim3(kAtThreads);
-  cfg.dynamicSmemBytes = sizeof(AttnSmem) + static_cast<size_t>(T) * rep * kAtD * 2;
+  cfg.dynamicSmemBytes = sizeof(AttnSmem);
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;

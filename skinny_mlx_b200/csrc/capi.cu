@@ -318,7 +318,8 @@ int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const fl
     return SKINNY_ERR_INVALID_ARG;
   if (T < 1 || T > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
   // with length_dev the caller guarantees 0 <= *length_dev <= max_len - T when the launch runs
-  if (!skinny::attn_fits(T, n_heads, n_kv_heads) || rot < 0 || rot > 128 || (rot % 2) || L0 < 0 ||
+  if (!skinny::attn_fits(T, n_heads, n_kv_heads) || (rot != 0 && rot != 16 && rot != 32 && rot != 64 && rot != 128) ||
+      L0 < 0 ||
       (!length_dev && L0 + T > max_len) || max_len < T)
     return SKINNY_ERR_SHAPE;
   if ((gated != 0 && gated != 1) || ldp < ((1 + gated) * n_heads + 2 * n_kv_heads) * 128 || !sync_ok(sync))

@@ -32,39 +32,82 @@ def _p(t) -> ctypes.c_void_p:
     return ctypes.c_void_p(0 if t is None else t.data_ptr())
 
 
-class FusedStep:
-    def __init__(self, model: HybridModel):
-        from .patch import FusedSliceLinear, SkinnyQuantizedLinear
+def layer_entry(layer, cfg) -> dict:
+    """The weights one decoder layer of a patched hybrid model runs with in the fused step."""
+    from .patch import FusedSliceLinear, SkinnyQuantizedLinear
 
+    mlp = layer.mlp
+    assert isinstance(mlp.gate_proj, FusedSliceLinear) and isinstance(mlp.down_proj, SkinnyQuantizedLinear)
+    ent = {"gate_up": mlp.gate_proj._group.rw, "down": mlp.down_proj.rweight,
+           "in_norm": layer.input_layernorm.weight, "post_norm": layer.post_attention_layernorm.weight}
+    if layer.is_linear:
+        g = layer.linear_attn
+        ent.update(kind="gdn", mod=g, proj=g.in_proj_qkv._group.rw, out=g.out_proj.rweight,
+                   conv_w=g.conv_weight.float().contiguous(), A_log=g.A_log.float().contiguous(),
+                   dt_bias=g.dt_bias.float().contiguous(), norm_w=g.norm.weight.float().contiguous())
+    else:
+        a = layer.self_attn
+        (q0, q1), (k0, k1), (v0, v1) = a.q_proj._group.bounds
+        D = cfg.head_dim
+        assert D == 128 and (q0, k0, v0) == (0, 2 * cfg.n_heads * D, 2 * cfg.n_heads * D
+                                             + cfg.n_kv_heads * D), "q|gate, k, v fused in order"
+        half = cfg.rotary_dim // 2
+        dev = a.q_norm.weight.device
+        inv = cfg.rope_theta ** (-torch.arange(0, half, device=dev, dtype=torch.float32) / half)
+        ent.update(kind="attn", mod=a, proj=a.q_proj._group.rw, out=a.o_proj.rweight,
+                   qn=a.q_norm.weight.float().contiguous(), kn=a.k_norm.weight.float().contiguous(),
+                   inv=inv.contiguous())
+    return ent
+
+
+class FusedOps:
+    """The launches the fused step is made of (prep, prepared qmm, fused attention), for a
+    hybrid-model config `cfg`; subclasses run a model or a draft head with them."""
+
+    cfg = None
+    _attn_ws: dict
+
+    @staticmethod
+    def _err_word(dev) -> torch.Tensor:
+        """Word 0 of the device's qmm workspace: device-side errors of every kernel of the step
+        land in one place (skinny_mlx_b200.qmm.device_errors reads it)."""
+        return get_workspace(dev, int(_lib.lib().skinny_qmm_workspace_bytes(128, 64)))
+
+    def _attention(self, ent, proj, c: AttnCache, m: int, xq, stream, len_dev=None):
+        """len_dev: a device int32 holding c.length when the launch runs (graph replay); the
+        caller then advances the host length itself."""
+        cfg = self.cfg
+        max_len = c.k.shape[0]
+        ws = self._attn_ws.get(max_len)
+        if ws is None:  # sized for 16 tokens; zero on first use, left zero by every call
+            n = int(_lib.lib().skinny_attn_workspace_bytes(16, cfg.n_heads, cfg.n_kv_heads, max_len))
+            ws = self._attn_ws[max_len] = torch.zeros(n, dtype=torch.uint8, device=proj.device)
+        L0 = c.length
+        _lib.call("skinny_attn_fused", _p(proj), proj.stride(0), _p(ent["qn"]), _p(ent["kn"]), _p(ent["inv"]),
+                  cfg.rotary_dim, 1, cfg.rms_eps, _p(c.k), _p(c.v), L0, _p(len_dev), m, cfg.n_heads, cfg.n_kv_heads,
+                  max_len, _p(ws), ws.numel(), _p(xq), None, None, stream)
+        if len_dev is None:
+            c.length = L0 + m
+
+    def _qmm(self, xq, w: SkinnyWeight, out, m: int, stream):
+        ws = get_workspace(out.device, int(_lib.lib().skinny_qmm_workspace_bytes(w.N, w.K)))
+        _lib.call("skinny_qmm_w4g64_prepared", _p(xq), _p(w.w_tc), _p(out), out.stride(0), m, w.N, w.K,
+                  _p(ws), ws.numel(), None, 0, None, stream)
+
+    def _prep(self, mode, x, m, k, xq, stream, d=None, h_out=None, w=None, a_out=None):
+        _lib.call("skinny_prep", mode, _p(x), x.stride(0), _p(d), d.stride(0) if d is not None else 0, 0, None,
+                  _p(h_out), h_out.stride(0) if h_out is not None else 0, _p(w), self.cfg.rms_eps, m, k,
+                  _p(xq), _p(a_out), None, stream)
+
+
+class FusedStep(FusedOps):
+    def __init__(self, model: HybridModel):
         self.model, self.cfg = model, model.cfg
         emb = model.embed_tokens
         if not hasattr(emb, "skinny_head"):
             raise ValueError("FusedStep needs a patched model (skinny_mlx_b200.patch.patch_model)")
         self.head = emb.skinny_head
-        self.layers = []
-        for layer in model.layers:
-            mlp = layer.mlp
-            assert isinstance(mlp.gate_proj, FusedSliceLinear) and isinstance(mlp.down_proj, SkinnyQuantizedLinear)
-            ent = {"gate_up": mlp.gate_proj._group.rw, "down": mlp.down_proj.rweight,
-                   "in_norm": layer.input_layernorm.weight, "post_norm": layer.post_attention_layernorm.weight}
-            if layer.is_linear:
-                g = layer.linear_attn
-                ent.update(kind="gdn", mod=g, proj=g.in_proj_qkv._group.rw, out=g.out_proj.rweight,
-                           conv_w=g.conv_weight.float().contiguous(), A_log=g.A_log.float().contiguous(),
-                           dt_bias=g.dt_bias.float().contiguous(), norm_w=g.norm.weight.float().contiguous())
-            else:
-                a = layer.self_attn
-                (q0, q1), (k0, k1), (v0, v1) = a.q_proj._group.bounds
-                D = self.cfg.head_dim
-                assert D == 128 and (q0, k0, v0) == (0, 2 * self.cfg.n_heads * D, 2 * self.cfg.n_heads * D
-                                                     + self.cfg.n_kv_heads * D), "q|gate, k, v fused in order"
-                half = self.cfg.rotary_dim // 2
-                dev = a.q_norm.weight.device
-                inv = self.cfg.rope_theta ** (-torch.arange(0, half, device=dev, dtype=torch.float32) / half)
-                ent.update(kind="attn", mod=a, proj=a.q_proj._group.rw, out=a.o_proj.rweight,
-                           qn=a.q_norm.weight.float().contiguous(), kn=a.k_norm.weight.float().contiguous(),
-                           inv=inv.contiguous())
-            self.layers.append(ent)
+        self.layers = [layer_entry(layer, self.cfg) for layer in model.layers]
         self.final_norm = model.norm.weight
         self._bufs: dict[int, dict] = {}
         self._attn_ws: dict[int, torch.Tensor] = {}
@@ -99,38 +142,6 @@ class FusedStep:
                  "logits": torch.empty(m, self.head.N, dtype=torch.bfloat16, device=dev)}
             self._bufs[m] = b
         return b
-
-    @staticmethod
-    def _err_word(dev) -> torch.Tensor:
-        """Word 0 of the device's qmm workspace: device-side errors of every kernel of the step
-        land in one place (skinny_mlx_b200.qmm.device_errors reads it)."""
-        return get_workspace(dev, int(_lib.lib().skinny_qmm_workspace_bytes(128, 64)))
-
-    def _attention(self, ent, proj, c: AttnCache, m: int, xq, stream, len_dev=None):
-        """len_dev: a device int32 holding c.length when the launch runs (graph replay); the
-        caller then advances the host length itself."""
-        cfg = self.cfg
-        max_len = c.k.shape[0]
-        ws = self._attn_ws.get(max_len)
-        if ws is None:  # sized for 16 tokens; zero on first use, left zero by every call
-            n = int(_lib.lib().skinny_attn_workspace_bytes(16, cfg.n_heads, cfg.n_kv_heads, max_len))
-            ws = self._attn_ws[max_len] = torch.zeros(n, dtype=torch.uint8, device=proj.device)
-        L0 = c.length
-        _lib.call("skinny_attn_fused", _p(proj), proj.stride(0), _p(ent["qn"]), _p(ent["kn"]), _p(ent["inv"]),
-                  cfg.rotary_dim, 1, cfg.rms_eps, _p(c.k), _p(c.v), L0, _p(len_dev), m, cfg.n_heads, cfg.n_kv_heads,
-                  max_len, _p(ws), ws.numel(), _p(xq), None, None, stream)
-        if len_dev is None:
-            c.length = L0 + m
-
-    def _qmm(self, xq, w: SkinnyWeight, out, m: int, stream):
-        ws = get_workspace(out.device, int(_lib.lib().skinny_qmm_workspace_bytes(w.N, w.K)))
-        _lib.call("skinny_qmm_w4g64_prepared", _p(xq), _p(w.w_tc), _p(out), out.stride(0), m, w.N, w.K,
-                  _p(ws), ws.numel(), None, 0, None, stream)
-
-    def _prep(self, mode, x, m, k, xq, stream, d=None, h_out=None, w=None, a_out=None):
-        _lib.call("skinny_prep", mode, _p(x), x.stride(0), _p(d), d.stride(0) if d is not None else 0, 0, None,
-                  _p(h_out), h_out.stride(0) if h_out is not None else 0, _p(w), self.cfg.rms_eps, m, k,
-                  _p(xq), _p(a_out), None, stream)
 
     # ---------------------------------------------------------------- the step
     @torch.no_grad()

@@ -10,9 +10,13 @@ all projections 4-bit g64.  It runs on the same qmm as the trunk once patched.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.nn as nn
 
+from . import _lib
+from .fused import FusedOps, layer_entry
 from .model import AttnCache, DecoderLayer, HybridModel, RMSNorm, _qlinear
 
 
@@ -41,4 +45,67 @@ class MTPHead(nn.Module):
         return AttnCache(self.cfg, max_len, self.device)
 
 
-__all__ = ["MTPHead"]
+class FusedMTPHead(FusedOps):
+    """MTPHead.forward for 1..16 tokens on the fused step's kernels: the two input norms write
+    the digits of the two halves of fc's input, then fc, the decoder layer (prep, qkv, fused
+    attention on the head's cache, o_proj, residual + norm, gate|up, SwiGLU, down) and the final
+    residual + norm, 12 launches under programmatic dependent launch instead of the
+    module-by-module forward.  More tokens (the prompt) run the module forward.  The result is a
+    reused buffer, valid until the next call with the same token count."""
+
+    def __init__(self, head: MTPHead):
+        from .patch import SkinnyQuantizedLinear
+
+        if not isinstance(head.fc, SkinnyQuantizedLinear):
+            raise ValueError("FusedMTPHead needs a patched head (skinny_mlx_b200.patch.patch_model(head))")
+        self.head, self.cfg = head, head.cfg
+        self.fc = head.fc.rweight
+        self.ent = layer_entry(head.layer, head.cfg)
+        self._attn_ws: dict = {}
+        self._bufs: dict = {}
+
+    def make_cache(self, max_len: int = 4096) -> AttnCache:
+        return self.head.make_cache(max_len)
+
+    def _buffers(self, m: int) -> dict:
+        b = self._bufs.get(m)
+        if b is None:
+            cfg, dev, L = self.cfg, self.head.device, _lib.lib()
+            H = cfg.hidden
+            xq = lambda k: torch.empty(int(L.skinny_xq_bytes(m, k)), dtype=torch.uint8, device=dev)
+            bf = lambda n: torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+            b = {"xq_fc": xq(2 * H), "xq_h": xq(H), "xq_o": xq(cfg.n_heads * cfg.head_dim),
+                 "xq_i": xq(cfg.intermediate), "x": bf(H), "proj": bf(self.ent["proj"].N), "mix": bf(H),
+                 "gu": bf(2 * cfg.intermediate), "down": bf(H), "h2": bf(H), "h3": bf(H), "out": bf(H),
+                 "xb": int(L.skinny_xq_bytes(m, 64))}
+            self._bufs[m] = b
+        return b
+
+    @torch.no_grad()
+    def __call__(self, emb: torch.Tensor, hidden: torch.Tensor, cache: AttnCache) -> torch.Tensor:
+        m = emb.shape[0]
+        if m > 16:
+            return self.head(emb, hidden, cache)
+        cfg, head, ent = self.cfg, self.head, self.ent
+        H = cfg.hidden
+        b = self._buffers(m)
+        emb, hidden = emb.contiguous(), hidden.contiguous()
+        stream = ctypes.c_void_p(torch.cuda.current_stream(head.device).cuda_stream)
+        # fc input [norm_e(emb) | norm_h(hidden)]: digit groups [0, H/64) and [H/64, 2H/64)
+        self._prep(0, emb, m, H, b["xq_fc"], stream, w=head.pre_fc_norm_embedding.weight)
+        self._prep(0, hidden, m, H, b["xq_fc"][(H // 64) * b["xb"]:], stream, w=head.pre_fc_norm_hidden.weight)
+        self._qmm(b["xq_fc"], self.fc, b["x"], m, stream)
+        self._prep(0, b["x"], m, H, b["xq_h"], stream, w=ent["in_norm"])
+        self._qmm(b["xq_h"], ent["proj"], b["proj"], m, stream)
+        self._attention(ent, b["proj"], cache, m, b["xq_o"], stream)
+        self._qmm(b["xq_o"], ent["out"], b["mix"], m, stream)
+        self._prep(0, b["x"], m, H, b["xq_h"], stream, d=b["mix"], h_out=b["h2"], w=ent["post_norm"])
+        self._qmm(b["xq_h"], ent["gate_up"], b["gu"], m, stream)
+        self._prep(1, b["gu"], m, cfg.intermediate, b["xq_i"], stream)
+        self._qmm(b["xq_i"], ent["down"], b["down"], m, stream)
+        self._prep(0, b["h2"], m, H, b["xq_h"], stream, d=b["down"], h_out=b["h3"], w=head.norm.weight,
+                   a_out=b["out"])
+        return b["out"]
+
+
+__all__ = ["MTPHead", "FusedMTPHead"]

@@ -113,7 +113,16 @@ class MTPDrafter:
     def __init__(self, model, head, vocab: int | None = 32768, seed: int = 0):
         from .model import QuantizedLinear
 
+        from .patch import SkinnyQuantizedLinear
+
         self.model, self.head = model, head
+        # a patched head runs on the fused kernels (its module forward is kept for the prompt)
+        if isinstance(head.fc, SkinnyQuantizedLinear):
+            from .mtp import FusedMTPHead
+
+            self._fwd = FusedMTPHead(head)
+        else:
+            self._fwd = head
         emb = model.embed_tokens
         V = emb.weight.shape[0]
         if vocab and vocab < V:
@@ -133,7 +142,7 @@ class MTPDrafter:
             self._logits = ql
 
     def _step(self, tokens: torch.Tensor, hidden: torch.Tensor) -> torch.Tensor:
-        return self.head(self.model.embed_tokens(tokens), hidden, self.cache)
+        return self._fwd(self.model.embed_tokens(tokens), hidden, self.cache)
 
     def begin(self, prompt: list[int], h: torch.Tensor, first: int) -> None:
         self.cache = self.head.make_cache()

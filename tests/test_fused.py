@@ -315,3 +315,30 @@ def test_attn_fused_ungated_dense_shape(cuda_lib, dev):
     assert err <= 2e-2, err
     assert torch.equal(vc[L0:L0 + T], v_new)
     assert ((kc[L0:L0 + T].float() - k_new.float()).abs() <= k_new.float().abs() * 2 ** -7 + 1e-6).all()
+
+
+def test_fused_mtp_head_matches_module_head(cuda_lib, dev):
+    """The MTP draft head on the fused kernels against its patched module forward: a 20-token
+    prompt through the module path into both caches, then draft steps of 1, 3 and 1 tokens."""
+    from skinny_mlx_b200.mtp import FusedMTPHead, MTPHead
+    from skinny_mlx_b200.patch import patch_model
+
+    m = HybridModel(SMALL, seed=0, device=dev)
+    patch_model(m)
+    head = MTPHead(m, seed=13)
+    patch_model(head)
+    fused = FusedMTPHead(head)
+    ca, cb = head.make_cache(64), fused.make_cache(64)
+    g = torch.Generator(device="cpu").manual_seed(3)
+    ids = torch.randint(0, SMALL.vocab, (25,), generator=g).to(dev)
+    hid = (torch.randn(25, SMALL.hidden, generator=g) * 2).to(torch.bfloat16).to(dev)
+    emb = m.embed_tokens(ids)
+    ref = head(emb[:20], hid[:20], ca)
+    got = fused(emb[:20], hid[:20], cb)  # more than 16 tokens: the module forward
+    assert torch.equal(ref, got)
+    rel = lambda a, b: ((a.float() - b.float()).abs().max() / b.float().abs().max()).item()
+    for a, b in ((20, 21), (21, 24), (24, 25)):
+        ref = head(emb[a:b], hid[a:b], ca)
+        got = fused(emb[a:b], hid[a:b], cb).clone()
+        assert rel(got, ref) <= 2e-2, (a, b, rel(got, ref))
+        assert ca.length == cb.length == b
