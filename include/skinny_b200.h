@@ -118,6 +118,11 @@ int skinny_ipc_free(void* ptr);
  *   counter     != NULL: after its last write, the launch's last CTA stores *epoch into
  *                        signal_flags[r] for every rank r (this rank's word in each rank's
  *                        flags), after a system-scope fence; the counter is zero between launches.
+ *   n_mirror > 0:        a launch that writes qmm input digits (skinny_prep, skinny_attn_fused)
+ *                        also writes them to mirror[0 .. n_mirror): other ranks' buffers, each
+ *                        the address that corresponds to xq there (same block offsets), so that
+ *                        consumers read every rank's digits from their own memory; the signal
+ *                        above is stored after these writes.
  * epoch is a device counter the caller advances once per step (so a captured graph serves every
  * step); err (required with an epoch) receives the error bits.  A NULL skinny_peer_sync pointer,
  * or epoch == NULL, means no synchronisation. */
@@ -128,6 +133,8 @@ typedef struct {
   uint32_t* signal_flags[8];
   uint32_t* err;
   int n_ranks;
+  void* mirror[8];
+  int n_mirror;
 } skinny_peer_sync;
 
 /* Bytes of one prepared qmm input (the digit blocks the qmm kernel reads) for M tokens, K columns. */

@@ -107,7 +107,8 @@ class PeerSync(ctypes.Structure):
     """Mirror of skinny_peer_sync (include/skinny_b200.h): device pointers as integers."""
 
     _fields_ = [("epoch", c_void_p), ("wait_flags", c_void_p), ("counter", c_void_p),
-                ("signal_flags", c_void_p * 8), ("err", c_void_p), ("n_ranks", c_int)]
+                ("signal_flags", c_void_p * 8), ("err", c_void_p), ("n_ranks", c_int),
+                ("mirror", c_void_p * 8), ("n_mirror", c_int)]
 
 
 __all__ = ["lib", "call", "check", "SkinnyError", "SIGNATURES", "c_uint32", "PeerSync"]

@@ -586,12 +586,13 @@ __global__ void __launch_bounds__(kAtThreads) attn_merge_kernel(const __grid_con
       __nv_bfloat16* op = p.o_out + static_cast<size_t>(t) * p.nh * kAtD + hq * kAtD + d;
       *reinterpret_cast<__nv_bfloat162*>(op) = __floats2bfloat162_rn(a0, a1);
     }
-    write_digits(p.xq, mpad, t, 2 * hq + hf, lane, a0, a1);
+    write_digits(p.xq, mpad, t, 2 * hq + hf, lane, a0, a1, p.sync.mirror, p.sync.n_mirror);
   }
   if (work && rg == 0 && rq == 0) {  // padding tokens T .. mpad-1 of this KV head's query heads
     for (int job = warp; job < (mpad - p.T) * rep * 2; job += kAtWarps) {
       const int t = p.T + job / (rep * 2), rem = job % (rep * 2);
-      write_digits(p.xq, mpad, t, 2 * (kvh * rep + rem / 2) + (rem & 1), lane, 0.f, 0.f);
+      write_digits(p.xq, mpad, t, 2 * (kvh * rep + rem / 2) + (rem & 1), lane, 0.f, 0.f, p.sync.mirror,
+                   p.sync.n_mirror);
     }
   }
   peer_signal_done(p.sync, &sync_flag);  // (sharded step) this rank's digit groups are ready

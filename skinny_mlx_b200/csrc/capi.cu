@@ -218,7 +218,8 @@ int skinny_qmm_w4g64_noalloc(const void* x, int ldx, const void* w_tc, void* out
 }
 
 // A peer-sync descriptor: absent, or a device epoch with an error word, 1..8 ranks, and for a
-// wait the local flag array, for a signal the local counter and one flag address per rank.
+// wait the local flag array, for a signal the local counter and one flag address per rank;
+// 0..8 mirror destinations, 16-byte aligned.
 static bool sync_ok(const skinny_peer_sync* s) {
   if (!s || !s->epoch) return true;
   if (s->n_ranks < 1 || s->n_ranks > 8 || !s->err) return false;
@@ -226,6 +227,9 @@ static bool sync_ok(const skinny_peer_sync* s) {
   if (s->counter)
     for (int r = 0; r < s->n_ranks; ++r)
       if (!s->signal_flags[r]) return false;
+  if (s->n_mirror < 0 || s->n_mirror > 8) return false;
+  for (int i = 0; i < s->n_mirror; ++i)
+    if (!s->mirror[i] || (reinterpret_cast<uintptr_t>(s->mirror[i]) & 15)) return false;
   return true;
 }
 

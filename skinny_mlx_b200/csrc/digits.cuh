@@ -9,8 +9,10 @@
 namespace skinny {
 
 // Writes the digits of two values (columns 2*lane, 2*lane+1 of group g, token t) and, from lane 0,
-// the group's xs and xsum.  a0, a1 are bf16-exact floats.  Warp-collective.
-__device__ __forceinline__ void write_digits(uint8_t* xq, int mpad, int t, int g, int lane, float a0, float a1) {
+// the group's xs and xsum.  a0, a1 are bf16-exact floats.  Warp-collective.  The same words are
+// also written to mirror[0 .. n_mirror) (other ranks' copies of xq, same layout), if any.
+__device__ __forceinline__ void write_digits(uint8_t* xq, int mpad, int t, int g, int lane, float a0, float a1,
+                                             uint8_t* const* mirror = nullptr, int n_mirror = 0) {
   float amax = fmaxf(fabsf(a0), fabsf(a1));
 #pragma unroll
   for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
@@ -35,18 +37,21 @@ __device__ __forceinline__ void write_digits(uint8_t* xq, int mpad, int t, int g
   }
   const int hi0 = (v0 + 128) >> 8, hi1 = (v1 + 128) >> 8;
   const int lo0 = v0 - 256 * hi0, lo1 = v1 - 256 * hi1;
-  uint8_t* blk = xq + static_cast<size_t>(g) * xq_block_bytes(mpad);
+  const size_t boff = static_cast<size_t>(g) * xq_block_bytes(mpad);
   const int k = 2 * lane;
   const int kofs = (k >> 5) * (mpad * 64) + ((k >> 4) & 1) * 128 + (k & 15);
   const int rh = t, rl = mpad + t;
-  *reinterpret_cast<uint16_t*>(blk + kofs + (rh >> 3) * 256 + (rh & 7) * 16) =
-      static_cast<uint16_t>((hi0 & 0xFF) | ((hi1 & 0xFF) << 8));
-  *reinterpret_cast<uint16_t*>(blk + kofs + (rl >> 3) * 256 + (rl & 7) * 16) =
-      static_cast<uint16_t>((lo0 & 0xFF) | ((lo1 & 0xFF) << 8));
-  if (lane == 0) {
-    float* xf = reinterpret_cast<float*>(blk + 2 * mpad * 64);
-    xf[t] = xs;
-    xf[mpad + t] = xsum;
+  const uint16_t whi = static_cast<uint16_t>((hi0 & 0xFF) | ((hi1 & 0xFF) << 8));
+  const uint16_t wlo = static_cast<uint16_t>((lo0 & 0xFF) | ((lo1 & 0xFF) << 8));
+  for (int d = -1; d < n_mirror; ++d) {
+    uint8_t* blk = (d < 0 ? xq : mirror[d]) + boff;
+    *reinterpret_cast<uint16_t*>(blk + kofs + (rh >> 3) * 256 + (rh & 7) * 16) = whi;
+    *reinterpret_cast<uint16_t*>(blk + kofs + (rl >> 3) * 256 + (rl & 7) * 16) = wlo;
+    if (lane == 0) {
+      float* xf = reinterpret_cast<float*>(blk + 2 * mpad * 64);
+      xf[t] = xs;
+      xf[mpad + t] = xsum;
+    }
   }
 }
 

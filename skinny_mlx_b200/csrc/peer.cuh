@@ -28,6 +28,8 @@ struct PeerSync {
   uint32_t* signal_flags[kMaxPeers];
   uint32_t* err;
   int n_ranks;
+  uint8_t* mirror[kMaxPeers];  // other ranks' copies of the launch's digit output (xq)
+  int n_mirror;
 };
 
 inline PeerSync peer_sync_from(const skinny_peer_sync* s) {
@@ -39,6 +41,8 @@ inline PeerSync peer_sync_from(const skinny_peer_sync* s) {
   for (int i = 0; i < kMaxPeers; ++i) p.signal_flags[i] = s->signal_flags[i];
   p.err = s->err;
   p.n_ranks = s->n_ranks;
+  p.n_mirror = s->epoch ? s->n_mirror : 0;
+  for (int i = 0; i < kMaxPeers; ++i) p.mirror[i] = i < p.n_mirror ? static_cast<uint8_t*>(s->mirror[i]) : nullptr;
   return p;
 }
 

@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16*
       a1 = xv.y;
     }
   }
-  write_digits(xq, mpad, t, g, lane, a0, a1);
+  write_digits(xq, mpad, t, g, lane, a0, a1, sync.mirror, sync.n_mirror);
   }
   peer_signal_done(sync, &sync_flag);  // this rank's digit groups are ready for the other ranks
 }

@@ -16,12 +16,14 @@ Per layer, rank g of G:
 
 Two exchanges (G > 1):
 
-* "peer" (default): each rank keeps its slices in a buffer the other ranks map through CUDA IPC
-  (NVLink peer memory).  Consumers read the other ranks' digit blocks and output shards in
-  place -- the qmm's bulk copies of x blocks and the prep's 16-byte row loads go to whichever
-  rank owns the data -- after a bounded wait on per-(layer, kind) flags that each producer
-  launch sets on every rank when its last CTA finishes (skinny_peer_sync).  No collective runs
-  inside a layer; one NCCL all-gather of the logits ends the step.
+* "peer" (default): each rank keeps a buffer the other ranks map through CUDA IPC (NVLink peer
+  memory).  The digit producers (attention, SwiGLU prep) write their digit blocks into every
+  rank's buffer (skinny_peer_sync mirrors), so each qmm reads its whole input from local memory
+  however often its tiles re-read it; the output shards of o_proj and down are read in place
+  from their owners by the next prep (one 16-byte load per element group).  Consumers start
+  after a bounded wait on per-(layer, kind) flags that each producer launch sets on every rank
+  when its last CTA finishes.  No collective runs inside a layer; one NCCL all-gather of the
+  logits ends the step.
 * "nccl": an all_gather_into_tensor after each of the four producers (the baseline).
 
 With G = 1 there is no exchange.  The logits come back as [G, M, V/G] (rank-major shards).
@@ -198,8 +200,32 @@ class DenseFusedStep:
     # ---------------------------------------------------------------- launches
     def _qmm(self, w, out_ptr, ldo, m, stream, xq=None, xq_ranks=None, gpr=0, sync=None):
         ws = get_workspace(self.model.device, int(_lib.lib().skinny_qmm_workspace_bytes(w.N, w.K)))
-        _lib.call("skinny_qmm_w4g64_prepared", _p(xq), _p(w.w_tc), ctypes.c_void_p(out_ptr), ldo, m, w.N, w.K,
+        xq_arg = xq if isinstance(xq, ctypes.c_void_p) else _p(xq)
+        _lib.call("skinny_qmm_w4g64_prepared", xq_arg, _p(w.w_tc), ctypes.c_void_p(out_ptr), ldo, m, w.N, w.K,
                   _p(ws), ws.numel(), xq_ranks, gpr, sync, stream)
+
+    def _own(self, region: str, offset: int = 0) -> ctypes.c_void_p:
+        """Address of `region` (+ offset bytes) in this rank's peer buffer."""
+        return ctypes.c_void_p(self._peer["bases"][self.rank] + self._peer["off"][region] + offset)
+
+    def _signal_mirrored(self, layer, kind, region, offset):
+        """The signal of a digit producer that also writes its digits into every other rank's
+        copy of `region` (at the same offset): consumers then read all digits locally."""
+        key = ("m", layer, kind, region, offset)
+        cache = self._peer.setdefault("mirrored", {})
+        s = cache.get(key)
+        if s is None:
+            base = self._peer["syncs"][layer][kind][0]
+            s = _lib.PeerSync()
+            ctypes.pointer(s)[0] = base  # copy of the plain signal
+            n = 0
+            for r, b in enumerate(self._peer["bases"]):
+                if r != self.rank:
+                    s.mirror[n] = b + self._peer["off"][region] + offset
+                    n += 1
+            s.n_mirror = n
+            cache[key] = s
+        return ctypes.byref(s)
 
     def _prep0(self, x, h_out, w, m, xq, stream, segs=None, a_out=None, sync=None):
         """Residual add of every rank's [m, H/G] shard (segs: their addresses) and RMSNorm."""
@@ -246,10 +272,9 @@ class DenseFusedStep:
             if ws is None:
                 n = int(_lib.lib().skinny_attn_workspace_bytes(16, self.nq, self.nkv, max_len))
                 ws = self._attn_ws[max_len] = torch.zeros(n, dtype=torch.uint8, device=dev)
-            if peer:
-                xq_o_mine = ctypes.c_void_p(self._peer["bases"][self.rank] + self._peer["off"]["xq_o"]
-                                            + self.rank * gpr_o * xb)
-                asig = self._sync(li, 0, "signal")
+            if peer:  # this rank's heads' digits, written here and in every other rank's buffer
+                xq_o_mine = self._own("xq_o", self.rank * gpr_o * xb)
+                asig = self._signal_mirrored(li, 0, "xq_o", self.rank * gpr_o * xb)
             else:
                 xq_o_mine = _p(b["xq_o_loc"] if self.exchange == "nccl" else b["xq_o"])
                 asig = None
@@ -260,8 +285,7 @@ class DenseFusedStep:
             # ---- o_proj -> this rank's shard of the hidden
             if peer:
                 o_ptr = self._peer["bases"][self.rank] + self._peer["off"]["o"]
-                self._qmm(ent["o"], o_ptr, H // G, m, stream, xq_ranks=self._ranks("xq_o"), gpr=gpr_o,
-                          sync=self._combined(li, 0, 1))
+                self._qmm(ent["o"], o_ptr, H // G, m, stream, xq=self._own("xq_o"), sync=self._combined(li, 0, 1))
                 o_segs, o_wait = self._ranks("o"), self._sync(li, 1, "wait")
             else:
                 if self.exchange == "nccl":
@@ -278,9 +302,8 @@ class DenseFusedStep:
             # ---- MLP
             self._qmm(ent["gu"], b["gu"].data_ptr(), b["gu"].stride(0), m, stream, xq=b["xq_h"])
             if peer:
-                xq_i_mine = ctypes.c_void_p(self._peer["bases"][self.rank] + self._peer["off"]["xq_i"]
-                                            + self.rank * gpr_i * xb)
-                psig = self._sync(li, 2, "signal")
+                xq_i_mine = self._own("xq_i", self.rank * gpr_i * xb)
+                psig = self._signal_mirrored(li, 2, "xq_i", self.rank * gpr_i * xb)
             else:
                 xq_i_mine = _p(b["xq_i_loc"] if self.exchange == "nccl" else b["xq_i"])
                 psig = None
@@ -288,8 +311,7 @@ class DenseFusedStep:
                       I // G, xq_i_mine, None, psig, stream)
             if peer:
                 dn_ptr = self._peer["bases"][self.rank] + self._peer["off"]["dn"]
-                self._qmm(ent["down"], dn_ptr, H // G, m, stream, xq_ranks=self._ranks("xq_i"), gpr=gpr_i,
-                          sync=self._combined(li, 2, 3))
+                self._qmm(ent["down"], dn_ptr, H // G, m, stream, xq=self._own("xq_i"), sync=self._combined(li, 2, 3))
                 prev = (self._ranks("dn"), self._sync(li, 3, "wait"))
             else:
                 if self.exchange == "nccl":

@@ -235,3 +235,36 @@ def test_peer_wait_gives_up_and_records(cuda_lib, dev):
               ctypes.c_void_p(ref.data_ptr()), None, None, stream)
     torch.cuda.synchronize(dev)
     assert torch.equal(xq, ref)
+
+
+@pytest.mark.gpu
+def test_prep_mirrors_digits_and_signals(cuda_lib, dev):
+    """A digit producer with mirror destinations (the sharded step's push of digit blocks into
+    the other ranks' buffers), here two local buffers: every copy equals the plain output, and
+    the launch's last CTA stores the epoch into every signal flag."""
+    import ctypes
+
+    from skinny_mlx_b200 import _lib
+
+    K, M = 1024, 5
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    x = torch.randn(M, 2 * K, device=dev).to(torch.bfloat16)
+    n = int(_lib.lib().skinny_xq_bytes(M, K))
+    ref, own, m1, m2 = (torch.zeros(n, dtype=torch.uint8, device=dev) for _ in range(4))
+    epoch = torch.full((1,), 7, dtype=torch.int32, device=dev)
+    counter = torch.zeros(1, dtype=torch.int32, device=dev)
+    flags = torch.zeros(3, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    s = _lib.PeerSync()
+    s.epoch, s.counter, s.err, s.n_ranks = epoch.data_ptr(), counter.data_ptr(), err.data_ptr(), 3
+    for r in range(3):
+        s.signal_flags[r] = flags.data_ptr() + 4 * r
+    s.mirror[0], s.mirror[1], s.n_mirror = m1.data_ptr(), m2.data_ptr(), 2
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    _lib.call("skinny_prep", 1, P(x), 2 * K, None, 0, 0, None, None, 0, None, 0.0, M, K, P(ref), None, None, stream)
+    _lib.call("skinny_prep", 1, P(x), 2 * K, None, 0, 0, None, None, 0, None, 0.0, M, K, P(own), None,
+              ctypes.byref(s), stream)
+    torch.cuda.synchronize(dev)
+    for buf in (own, m1, m2):
+        assert torch.equal(buf, ref)
+    assert flags.tolist() == [7, 7, 7] and int(counter.item()) == 0 and int(err.item()) == 0
