@@ -369,9 +369,11 @@ def config4_spec(model, dev, n_tokens=256, prompt_len=512, fwd=None):
         torch.cuda.synchronize()
         return r, time.perf_counter() - t0
 
-    gaps = []
-    ref, t_g = timed(lambda n: greedy(step, prompt, n, gaps if n == n_tokens else None, cache=cache))
-    out = {"greedy_tok_s": round(n_tokens / t_g, 1), "tokens": n_tokens, "prompt": prompt_len}
+    gaps = []  # the reference continuation and its near-tie gaps, from an untimed run
+    ref = greedy(step, prompt, n_tokens, gaps, cache=cache)
+    got_g, t_g = timed(lambda n: greedy(step, prompt, n, cache=cache))
+    out = {"greedy_tok_s": round(n_tokens / t_g, 1), "tokens": n_tokens, "prompt": prompt_len,
+           "greedy_identical": got_g == ref}
 
     def record(name, k, mk):
         st, d = {}, mk()  # one drafter for the untimed and the timed run (its state resets in begin)

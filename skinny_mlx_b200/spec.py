@@ -207,19 +207,21 @@ def greedy(model, prompt: list[int], max_tokens: int, gaps: list | None = None, 
     `cache` (optional) is reset and reused, e.g. to keep a graph-replayed step's buffers."""
     cache = _fresh_cache(model, cache)
     _, logits = model(torch.tensor(prompt, device=model.device), cache)
-    out = []
+    toks = []
     last = logits[-1]
-    for _ in range(max_tokens):
+    for i in range(max_tokens):
         if gaps is not None:
             t2 = torch.topk(last.float(), 2).values
             gaps.append((float(t2[0] - t2[1]), float(t2[0])))
-        y = int(torch.argmax(last.float()))
-        out.append(y)
-        if len(out) == max_tokens:
+        # the token stays on the device and feeds the next step there: no host round trip per
+        # token (argmax returns the first maximal index, as the reference's does)
+        y = torch.argmax(last).view(1)
+        toks.append(y)
+        if i + 1 == max_tokens:
             break
-        _, logits = model(torch.tensor([y], device=model.device), cache)
+        _, logits = model(y, cache)
         last = logits[-1]
-    return out
+    return torch.cat(toks).tolist()
 
 
 def speculative(model, prompt: list[int], max_tokens: int, drafter, k: int, stats: dict | None = None,
