@@ -40,7 +40,9 @@ constexpr int kAtWarps = kAtThreads / 32;
 constexpr int kAtStride = kAtD + 8;   // bf16 per shared row: 272 bytes, ldmatrix conflict-free
 constexpr int kAtPart = kAtD + 4;     // floats per published row: m, l, (pad), o[128] (16-byte aligned)
 constexpr int kAtMaxRG = 8;           // row groups per KV head (rep * T <= 128)
-constexpr int kAtMergePass = 9;       // chunk partials whose loads a merging thread issues together
+constexpr int kAtMergeRows = 1;       // query rows per merge CTA
+constexpr int kAtMergeSub = 16;       // chunk subsets per row (threads per (row, 8 dims))
+constexpr int kAtMergePass = 3;       // chunk partials whose loads a merging thread issues together
 constexpr int kAtMaxT = 16;
 
 struct AttnParams {
@@ -208,6 +210,36 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_chunk_kernel(const __grid_
   constexpr int kTabPer = kAtMaxT * (kAtD / 2) / kAtThreads;
   const int pc = tid & 15;
   uint4 qv[kQPer];
+  // Query rows of the pass starting at row rbase (ntiles 16-row tiles): normalised and rotated from
+  // registers (half-warp per row) into sm.q; rows past R inside the pass's tiles are zero.
+  const auto norm_pass = [&](int rbase, int ntiles) {
+#pragma unroll
+    for (int u = 0; u < kQPer; ++u) {
+      const int r = (tid >> 4) + 16 * u;  // rows 16u .. 16u+15 are in one pass: warp-uniform test
+      if (r >= rbase && r < rbase + ntiles * kAtRG) {
+        if (u >= kAtPassTiles && r < R) {
+          const int t = r / rep, hq = kvh * rep + r % rep;
+          qv[u] = ld_nc_v4(p.proj + static_cast<size_t>(t) * p.ldp + hq * qstride + 8 * pc);
+        }
+        float x[8];
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&qv[u]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(h2[i]);
+          x[2 * i] = f.x;
+          x[2 * i + 1] = f.y;
+        }
+        const int t = min(r / rep, p.T - 1);
+        norm_rope_hw(x, sm.qw, p.eps, sm.cs[t], p.rot, pc);
+        uint4 packed;
+        __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&packed);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          o2[i] = r < R ? __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]) : __floats2bfloat162_rn(0.f, 0.f);
+        *reinterpret_cast<uint4*>(&sm.q[r - rbase][8 * pc]) = packed;
+      }
+    }
+  };
   {
     uint4 kw[kPer], vw[kPer];
 #pragma unroll
@@ -240,13 +272,6 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_chunk_kernel(const __grid_
       fr[u] = 0.f;
       if (half > 0 && i < p.T * half) fr[u] = ld_nc_f32(p.inv_freq + i % half);
     }
-#pragma unroll
-    for (int u = 0; u < kPer; ++u) {
-      const int e = tid + u * kAtThreads, j = e >> 4, pce = e & 15;
-      if (j < nk && k0 + j >= L0) continue;  // a new key: written below by its warp
-      *reinterpret_cast<uint4*>(&sm.k[j][8 * pce]) = kw[u];
-      *reinterpret_cast<uint4*>(&sm.v[j][8 * pce]) = vw[u];
-    }
     if (tid < kAtD) sm.qw[tid] = nwv;
     else sm.kw[tid - kAtD] = nwv;
 #pragma unroll
@@ -259,6 +284,17 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_chunk_kernel(const __grid_
         sm.cs[t][j][0] = c;
         sm.cs[t][j][1] = sn;
       }
+    }
+    __syncthreads();  // the position table and the norm weights
+    // the first pass's query rows are normalised while the cached keys and values are still
+    // arriving; then those are stored
+    norm_pass(0, min(kAtPassTiles, (R + kAtRG - 1) / kAtRG));
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int e = tid + u * kAtThreads, j = e >> 4, pce = e & 15;
+      if (j < nk && k0 + j >= L0) continue;  // a new key: written below by its warp
+      *reinterpret_cast<uint4*>(&sm.k[j][8 * pce]) = kw[u];
+      *reinterpret_cast<uint4*>(&sm.v[j][8 * pce]) = vw[u];
     }
   }
   __syncthreads();
@@ -296,34 +332,7 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_chunk_kernel(const __grid_
   for (int rbase = 0; rbase < R; rbase += kAtPassRows) {
     const int nrows = min(kAtPassRows, R - rbase);
     const int ntiles = (nrows + kAtRG - 1) / kAtRG;
-    // query rows of the pass: normalised and rotated from registers (half-warp per row); rows
-    // past R inside the pass's tiles are zero
-#pragma unroll
-    for (int u = 0; u < kQPer; ++u) {
-      const int r = (tid >> 4) + 16 * u;  // rows 16u .. 16u+15 are in one pass: warp-uniform test
-      if (r >= rbase && r < rbase + ntiles * kAtRG) {
-        if (u >= kAtPassTiles && r < R) {
-          const int t = r / rep, hq = kvh * rep + r % rep;
-          qv[u] = ld_nc_v4(p.proj + static_cast<size_t>(t) * p.ldp + hq * qstride + 8 * pc);
-        }
-        float x[8];
-        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&qv[u]);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = __bfloat1622float2(h2[i]);
-          x[2 * i] = f.x;
-          x[2 * i + 1] = f.y;
-        }
-        const int t = min(r / rep, p.T - 1);
-        norm_rope_hw(x, sm.qw, p.eps, sm.cs[t], p.rot, pc);
-        uint4 packed;
-        __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&packed);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          o2[i] = r < R ? __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]) : __floats2bfloat162_rn(0.f, 0.f);
-        *reinterpret_cast<uint4*>(&sm.q[r - rbase][8 * pc]) = packed;
-      }
-    }
+    if (rbase > 0) norm_pass(rbase, ntiles);  // (the first pass's rows were done while staging)
     __syncthreads();
     // scores (log2 domain), masked; each warp's 16-key maximum per row
     float c[kAtPassTiles][2][4];
@@ -464,23 +473,26 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_chunk_kernel(const __grid_
   }
 }
 
-// Merge: CTA (row quarter, row group, KV head) of 256 threads = 4 rows x 16 dim groups (8 dims
-// each) x 4 chunk subsets.  Thread subset s merges chunks s, s + 4, ... of its (row, dims),
-// issuing all of those loads at once (up to kAtMergePass chunks per pass); the 4 subsets' (max,
-// sum, output) are then combined in subset order in shared memory.  The result is a fixed
-// function of the partials (deterministic).
+// Merge: CTA (row, KV head) of 256 threads = 16 dim groups (8 dims each) x 16 chunk subsets: one
+// row per CTA spreads the partials' reads over many SMs (with 4 rows per CTA the reads of 96 CTAs
+// took ~5 us for 6.7 MB).  Thread subset s merges chunks s, s + 16, ... of its dims, issuing all
+// of those loads at once (up to kAtMergePass chunks per pass); the 16 subsets' (max, sum, output)
+// are then combined in subset order in shared memory.  The result is a fixed function of the
+// partials (deterministic), and chunks past a row's last visible key change nothing.
 __global__ void __launch_bounds__(kAtThreads) attn_merge_kernel(const __grid_constant__ AttnParams p) {
-  constexpr int kSub = 4, kRowsPer = 4;
+  constexpr int kSub = kAtMergeSub, kRowsPer = kAtMergeRows;
+  static_assert(kSub * kRowsPer * 16 == kAtThreads, "thread layout");
+  constexpr int kQuarters = kAtRG / kRowsPer;  // CTAs per row group
   __shared__ float os[kRowsPer][kAtD];
   __shared__ float red[kSub - 1][kRowsPer][16][10];
   __shared__ int sync_flag;
-  const int rq = blockIdx.x & 3, rg = blockIdx.x >> 2, kvh = blockIdx.y;
+  const int rq = blockIdx.x % kQuarters, rg = blockIdx.x / kQuarters, kvh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rep = p.nh / p.nkv;
   const int R = p.T * rep;
   const int r0 = rg * kAtRG + rq * kRowsPer;          // first row of this CTA
   const int nrows = max(0, min(kRowsPer, R - r0));
-  const int sub = tid >> 6, rr = (tid >> 4) & 3, dg = tid & 15, d0 = dg * 8;
+  const int sub = tid / (16 * kRowsPer), rr = (tid >> 4) % kRowsPer, dg = tid & 15, d0 = dg * 8;
   pdl_launch_dependents();
   pdl_wait_prior_grid();  // the chunk launch's partials (and the gates, written before it)
   const int L0 = attn_length(p);
@@ -662,7 +674,7 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
   cudaError_t e = cudaLaunchKernelEx(&cfg, attn_chunk_kernel, prm);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t mcfg = {};
-  mcfg.gridDim = dim3(prm.nrg * 4, nkv);  // (row quarter, row group) x KV head
+  mcfg.gridDim = dim3(prm.nrg * (kAtRG / kAtMergeRows), nkv);  // (rows, row group) x KV head
   mcfg.blockDim = dim3(kAtThreads);
   mcfg.dynamicSmemBytes = 0;
   mcfg.stream = stream;
