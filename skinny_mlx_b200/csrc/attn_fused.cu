@@ -77,7 +77,6 @@ struct AttnSmem {
   __nv_bfloat16 pr[kAtPassRows][kAtStride];  // probabilities (bf16, as a flash kernel rounds them)
   float redm[kAtWarps][kAtPassRows];         // per (warp = 16-key block, row): max of the block
   float redl[kAtWarps][kAtPassRows];         //                                sum of its probabilities
-  float stage[kAtWarps][kAtD];
 };
 
 __device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
@@ -104,38 +103,6 @@ __device__ __forceinline__ float2 ld_cg_v2(const float* p) {
   float2 r;
   asm volatile("ld.global.cg.v2.f32 {%0, %1}, [%2];" : "=f"(r.x), "=f"(r.y) : "l"(p));
   return r;
-}
-
-// Warp-collective: x holds dims lane + 32 i of one head row (bf16-exact).  Returns the row after
-// zero-centred RMSNorm (-> bf16) and RoPE on the first rot dims (-> bf16), the rotation's cos /
-// sin taken from cs[j] = (cos, sin)(pos * inv_freq[j]) for the row's position.
-__device__ __forceinline__ void norm_rope_tab(float (&x)[4], const float* w, float eps, const float (*cs)[2], int rot,
-                                              float* stage, int lane) {
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) ss = fmaf(x[i], x[i], ss);
-#pragma unroll
-  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-  const float rstd = rsqrtf(ss / kAtD + eps);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int d = lane + 32 * i;
-    x[i] = bfr(x[i] * rstd * (1.f + w[d]));
-    stage[d] = x[i];
-  }
-  __syncwarp();
-  const int half = rot >> 1;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int d = lane + 32 * i;
-    if (d < rot) {
-      const int j = d < half ? d : d - half;
-      const float c = cs[j][0], sn = cs[j][1];
-      x[i] = d < half ? x[i] * c - stage[d + half] * sn : x[i] * c + stage[d - half] * sn;
-    }
-    x[i] = bfr(x[i]);
-  }
-  __syncwarp();
 }
 
 // Half-warp collective (16 lanes; lane pc holds dims 8 pc .. 8 pc + 7 of one head row, bf16-exact;
@@ -264,6 +231,15 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_chunk_kernel(const __grid_
         vw[u] = kw[u];
       }
     }
+    // the chunk's new keys (positions L0 .. L0+T-1 that fall in it, at most 16): half-warp per key
+    const int jnew = max(L0 - k0, 0) + (tid >> 4);
+    const bool has_new = jnew < nk;
+    uint4 knew = make_uint4(0u, 0u, 0u, 0u), vnew = knew;
+    if (has_new) {
+      const __nv_bfloat16* src = p.proj + static_cast<size_t>(k0 + jnew - L0) * p.ldp + qkw;
+      knew = ld_nc_v4(src + kvh * kAtD + 8 * pc);
+      vnew = ld_nc_v4(src + p.nkv * kAtD + kvh * kAtD + 8 * pc);
+    }
     const float nwv = ld_nc_f32(tid < kAtD ? p.qn_w + tid : p.kn_w + (tid - kAtD));
     float fr[kTabPer];
 #pragma unroll
@@ -289,6 +265,30 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_chunk_kernel(const __grid_
     // the first pass's query rows are normalised while the cached keys and values are still
     // arriving; then those are stored
     norm_pass(0, min(kAtPassTiles, (R + kAtRG - 1) / kAtRG));
+    // new keys: normalised, rotated (every warp takes part in the shuffles), appended to the cache
+    if (__any_sync(0xFFFFFFFFu, has_new)) {
+      float x[8];
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&knew);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h2[i]);
+        x[2 * i] = f.x;
+        x[2 * i + 1] = f.y;
+      }
+      const int t = has_new ? k0 + jnew - L0 : 0;
+      norm_rope_hw(x, sm.kw, p.eps, sm.cs[t], p.rot, pc);
+      if (has_new) {
+        uint4 kb;
+        __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&kb);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o2[i] = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+        *reinterpret_cast<uint4*>(&sm.k[jnew][8 * pc]) = kb;
+        *reinterpret_cast<uint4*>(&sm.v[jnew][8 * pc]) = vnew;
+        const size_t off = (static_cast<size_t>(k0 + jnew) * p.nkv + kvh) * kAtD + 8 * pc;
+        *reinterpret_cast<uint4*>(p.kc + off) = kb;
+        *reinterpret_cast<uint4*>(p.vc + off) = vnew;
+      }
+    }
 #pragma unroll
     for (int u = 0; u < kPer; ++u) {
       const int e = tid + u * kAtThreads, j = e >> 4, pce = e & 15;
@@ -298,33 +298,6 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_chunk_kernel(const __grid_
     }
   }
   __syncthreads();
-  // ---- new keys in the chunk (positions L0 .. L0+T-1): warp per key, appended to the cache
-  {
-    const int jn0 = max(L0 - k0, 0);
-    for (int j = jn0 + warp; j < nk; j += kAtWarps) {
-      const int pos = k0 + j, t = pos - L0;
-      const __nv_bfloat16* src = p.proj + static_cast<size_t>(t) * p.ldp + qkw;
-      float x[4];
-      __nv_bfloat16 vb[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        x[i] = __bfloat162float(src[kvh * kAtD + lane + 32 * i]);
-        vb[i] = src[p.nkv * kAtD + kvh * kAtD + lane + 32 * i];
-      }
-      norm_rope_tab(x, sm.kw, p.eps, sm.cs[t], p.rot, sm.stage[warp], lane);
-      const size_t off = (static_cast<size_t>(pos) * p.nkv + kvh) * kAtD;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int d = lane + 32 * i;
-        const __nv_bfloat16 kb = __float2bfloat16_rn(x[i]);
-        sm.k[j][d] = kb;
-        sm.v[j][d] = vb[i];
-        p.kc[off + d] = kb;
-        p.vc[off + d] = vb[i];
-      }
-    }
-  }
-
   // ---- passes of up to three 16-row tiles: scores, softmax and outputs of all the pass's rows
   // together (warp w: keys 16w .. 16w+15 for the scores, dims 16w .. 16w+15 for the outputs)
   const int g = lane >> 2, cq = lane & 3;
