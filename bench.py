@@ -628,6 +628,66 @@ def run_head_case(args):
                       "packed_bytes": packed_bytes(151936, 2560)}), flush=True)
 
 
+def run_verify_case(args):
+    """--case verify: the config-3 fused verify step at M = 1 and M = 8 (2048 cached tokens,
+    checkpoints recorded), each captured in a CUDA graph; after warm replays, one replay of each
+    inside the NVTX ranges "m1" and "m8", so that a profiler can list every launch of both steps
+    (ncu --nvtx --nvtx-include m1/ --nvtx-include m8/)."""
+    from skinny_mlx_b200.fused import FusedStep
+    from skinny_mlx_b200.model import AttnCache
+
+    dev = torch.device("cuda", 0)
+    model = build_config3(dev)
+    fused = FusedStep(model)
+    gen = torch.Generator(device=dev).manual_seed(5)
+    graphs, out = {}, {"case": "verify"}
+    for m in (1, 8):
+        cache = fused.make_cache(max_len=2048 + 32, max_verify=17)
+        for c in cache.layers:
+            if isinstance(c, AttnCache):
+                c.k.normal_(generator=gen)
+                c.v.normal_(generator=gen)
+            else:
+                c.state.normal_(generator=gen).mul_(0.05)
+                c.recording = True
+        ids = torch.randint(0, model.cfg.vocab, (m,), generator=gen, device=dev)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+
+        def step(cache=cache, ids=ids):
+            for c in cache.layers:
+                if isinstance(c, AttnCache):
+                    c.length = 2048
+            fused(ids, cache)
+
+        with torch.cuda.stream(s):
+            step()
+            step()
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            step()
+        graphs[m] = (g, s, cache)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            for _ in range(max(args.warmup, 3)):
+                g.replay()
+            e0.record(s)
+            for _ in range(args.steps):
+                g.replay()
+            e1.record(s)
+        e1.synchronize()
+        out[f"ms_M{m}"] = round(e0.elapsed_time(e1) / args.steps, 4)
+    for m in (1, 8):
+        g, s, _ = graphs[m]
+        torch.cuda.nvtx.range_push(f"m{m}")
+        with torch.cuda.stream(s):
+            g.replay()
+        s.synchronize()
+        torch.cuda.nvtx.range_pop()
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -638,13 +698,17 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the config-3/4 model measurements")
     ap.add_argument("--no-dense", action="store_true", help="skip the config-5 column-parallel model")
-    ap.add_argument("--case", default="stack", choices=["stack", "head"],
-                    help="head: single-matrix profiling case instead of the bench line")
+    ap.add_argument("--case", default="stack", choices=["stack", "head", "verify"],
+                    help="head: single-matrix profiling case; verify: the config-3 step at M = 1 and 8 "
+                         "in NVTX ranges; both instead of the bench line")
     ap.add_argument("--m", type=int, default=M_STACK, help="tokens for --case head")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.case == "head":
         run_head_case(args)
+        return
+    if args.case == "verify":
+        run_verify_case(args)
         return
     world, rank, local = init_dist()
     try:
