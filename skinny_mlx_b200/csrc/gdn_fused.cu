@@ -80,7 +80,6 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
   constexpr int kVec = kCh / 8;            // 16-byte vectors per row of them
   constexpr int kRowsMax = W + kGfMaxT;
   constexpr int kStg = (kRowsMax * kVec + kGfThreads - 1) / kGfThreads;
-  constexpr int kConvIt = (kCh + kGfThreads - 1) / kGfThreads;
   const int h = blockIdx.x / kGfRanks;
   const uint32_t rank = cluster_ctarank();
   const int r0 = static_cast<int>(rank) * kGfRows;
@@ -95,7 +94,7 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
   __shared__ float vs[kGfMaxT][kGfRows];
   __shared__ __align__(16) float yl[kGfMaxT][kGfRows];
   __shared__ __align__(16) float yall[kGfMaxT][kGfD];  // the head's y, pushed by every rank
-  __shared__ float gs[kGfMaxT], bs[kGfMaxT];
+  __shared__ float gs[kGfMaxT], bs[kGfMaxT], kq[kGfMaxT];  // gates; k_t . q_t
   __shared__ __align__(8) uint64_t ybar;
   __shared__ int abort_flag;
 
@@ -137,12 +136,13 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
     nw0 = p.norm_w[j0];
     nw1 = p.norm_w[j0 + 1];
   }
-  float cw[kConvIt][W + 1];
+  // conv weights: channel tid (a q or k channel) and v channel 2*128 + (tid & 15)
+  static_assert(kGfThreads == 2 * kGfD && kGfRows * kGfMaxT == kGfThreads, "conv work split");
+  float cw[W + 1], cwv[W + 1];
 #pragma unroll
-  for (int it = 0; it < kConvIt; ++it) {
-    const int i = tid + it * kGfThreads;
-#pragma unroll
-    for (int q = 0; q <= W; ++q) cw[it][q] = i < kCh ? p.conv_w[static_cast<size_t>(chan(i)) * (W + 1) + q] : 0.f;
+  for (int q = 0; q <= W; ++q) {
+    cw[q] = p.conv_w[static_cast<size_t>(chan(tid)) * (W + 1) + q];
+    cwv[q] = p.conv_w[static_cast<size_t>(chan(2 * kGfD + (tid & 15))) * (W + 1) + q];
   }
   {
     const int nvec = (W + T) * kVec;
@@ -173,23 +173,26 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
   // matching wait.
   cluster_arrive_relaxed();
 
-  // ---- conv + silu
-#pragma unroll
-  for (int it = 0; it < kConvIt; ++it) {
-    const int i = tid + it * kGfThreads;
-    if (i < kCh) {
-      const int part = i < kGfD ? 0 : i < 2 * kGfD ? 1 : 2;
-      const int j = part == 0 ? i : part == 1 ? i - kGfD : i - 2 * kGfD;
+  // ---- conv + silu.  Thread tid: q/k channel tid for every token, and v channel tid & 15 for
+  // token tid >> 4, so that no thread has more than T + 1 outputs.
+  {
+    const int part = tid < kGfD ? 0 : 1;
+    const int j = tid - part * kGfD;
 #pragma unroll 4
-      for (int t = 0; t < T; ++t) {
-        float acc = 0.f;
+    for (int t = 0; t < T; ++t) {
+      float acc = 0.f;
 #pragma unroll
-        for (int q = 0; q <= W; ++q) acc = fmaf(__bfloat162float(fw[t + q][i]), cw[it][q], acc);
-        const float sv = __fdividef(acc, 1.f + __expf(-acc));
-        if (part == 0) qs[t][j] = sv;
-        else if (part == 1) ks[t][j] = sv;
-        else vs[t][j] = bf16rf(sv);
-      }
+      for (int q = 0; q <= W; ++q) acc = fmaf(__bfloat162float(fw[t + q][tid]), cw[q], acc);
+      const float sv = __fdividef(acc, 1.f + __expf(-acc));
+      if (part == 0) qs[t][j] = sv;
+      else ks[t][j] = sv;
+    }
+    const int tv = tid >> 4, jv = tid & 15;
+    if (tv < T) {
+      float acc = 0.f;
+#pragma unroll
+      for (int q = 0; q <= W; ++q) acc = fmaf(__bfloat162float(fw[tv + q][2 * kGfD + jv]), cwv[q], acc);
+      vs[tv][jv] = bf16rf(__fdividef(acc, 1.f + __expf(-acc)));
     }
   }
   __syncthreads();
@@ -223,17 +226,38 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
     bs[tid] = 1.f / (1.f + expf(-gb));
   }
   __syncthreads();
-  // ---- recurrence: thread = (row, sub); columns sub + 8 i in registers.  Per token the three
-  // dot products a = S k, b = S q (of the previous state) and c = k q share one reduction round:
+  // ---- k_t . q_t of every token (the same for every state row): thread (t, sub) forms the partial
+  // over the columns it takes in the recurrence and the 16 partials are summed by the same
+  // butterfly, so the value is the one the per-token reduction would give.
+  {
+    const int t = tid >> 4, sb = tid & 15;
+    float c0 = 0.f, c1 = 0.f;
+    if (t < T) {
+#pragma unroll
+      for (int i = 0; i < kGfCols; i += 2) {
+        c0 = fmaf(ks[t][sb + kGfTpr * i], qs[t][sb + kGfTpr * i], c0);
+        c1 = fmaf(ks[t][sb + kGfTpr * (i + 1)], qs[t][sb + kGfTpr * (i + 1)], c1);
+      }
+    }
+    float c = c0 + c1;
+#pragma unroll
+    for (int o = 1; o < kGfTpr; o <<= 1) c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
+    if (sb == 0 && t < T) kq[t] = c;
+  }
+  __syncthreads();
+  // ---- recurrence: thread = (row, sub); columns sub + 8 i in registers.  Per token the two
+  // dot products a = S k, b = S q (of the previous state) share one reduction round (c = k q
+  // comes from above):
   //   u = beta (v - g a),   S <- g S + u k^T,   y = S q = g b + u c.
   // The next token's operands are loaded while the current token's reductions run; the
   // arithmetic per token is the same whatever T is, so a token's results do not depend on how
   // many tokens share the launch.
-  float kn[kGfCols], qn[kGfCols], gn = 0.f, bn = 0.f, vn = 0.f;
+  float kn[kGfCols], qn[kGfCols], gn = 0.f, bn = 0.f, vn = 0.f, cn = 0.f;
   const auto load_tok = [&](int t) {
     gn = gs[t];
     bn = bs[t];
     vn = vs[t][row];
+    cn = kq[t];
 #pragma unroll
     for (int i = 0; i < kGfCols; ++i) {
       kn[i] = ks[t][sub + kGfTpr * i];
@@ -242,7 +266,7 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
   };
   if (T > 0) load_tok(0);
   for (int t = 0; t < T; ++t) {
-    const float gt = gn, bt = bn, vt = vn;
+    const float gt = gn, bt = bn, vt = vn, c = cn;
     float kk[kGfCols], qq[kGfCols];
 #pragma unroll
     for (int i = 0; i < kGfCols; ++i) {
@@ -250,22 +274,19 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
       qq[i] = qn[i];
     }
     if (t + 1 < T) load_tok(t + 1);
-    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f, c0 = 0.f, c1 = 0.f;
+    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
     for (int i = 0; i < kGfCols; i += 2) {
       a0 = fmaf(S[i], kk[i], a0);
       a1 = fmaf(S[i + 1], kk[i + 1], a1);
       b0 = fmaf(S[i], qq[i], b0);
       b1 = fmaf(S[i + 1], qq[i + 1], b1);
-      c0 = fmaf(kk[i], qq[i], c0);
-      c1 = fmaf(kk[i + 1], qq[i + 1], c1);
     }
-    float a = a0 + a1, b = b0 + b1, c = c0 + c1;
+    float a = a0 + a1, b = b0 + b1;
 #pragma unroll
     for (int o = 1; o < kGfTpr; o <<= 1) {
       a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
       b += __shfl_xor_sync(0xFFFFFFFFu, b, o);
-      c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
     }
     const float u = bt * (vt - gt * a);
 #pragma unroll
