@@ -97,6 +97,10 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
   __shared__ float gs[kGfMaxT], bs[kGfMaxT], kq[kGfMaxT];  // gates; k_t . q_t
   __shared__ __align__(8) uint64_t ybar;
   __shared__ int abort_flag;
+  // dynamic: the per-thread partials of S q for every token (summed after the recurrence) and u
+  extern __shared__ __align__(16) float gdn_dyn[];
+  float* bpart = gdn_dyn;                        // [kGfMaxT][kGfThreads]
+  float* ust = gdn_dyn + kGfMaxT * kGfThreads;   // [kGfMaxT][kGfRows]
 
   // channel of CTA-local conv slot i: q (0..127) and k (128..255) of head hk, v rows r0..r0+15 of h
   const auto chan = [&](int i) {
@@ -245,19 +249,18 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
     if (sb == 0 && t < T) kq[t] = c;
   }
   __syncthreads();
-  // ---- recurrence: thread = (row, sub); columns sub + 8 i in registers.  Per token the two
-  // dot products a = S k, b = S q (of the previous state) share one reduction round (c = k q
-  // comes from above):
+  // ---- recurrence: thread = (row, sub); columns sub + 8 i in registers.  Per token only a = S k
+  // (of the previous state) is reduced across the row's lanes; the partials of b = S q are kept
+  // and summed after the loop, and c = k q comes from above:
   //   u = beta (v - g a),   S <- g S + u k^T,   y = S q = g b + u c.
   // The next token's operands are loaded while the current token's reductions run; the
   // arithmetic per token is the same whatever T is, so a token's results do not depend on how
   // many tokens share the launch.
-  float kn[kGfCols], qn[kGfCols], gn = 0.f, bn = 0.f, vn = 0.f, cn = 0.f;
+  float kn[kGfCols], qn[kGfCols], gn = 0.f, bn = 0.f, vn = 0.f;
   const auto load_tok = [&](int t) {
     gn = gs[t];
     bn = bs[t];
     vn = vs[t][row];
-    cn = kq[t];
 #pragma unroll
     for (int i = 0; i < kGfCols; ++i) {
       kn[i] = ks[t][sub + kGfTpr * i];
@@ -266,7 +269,7 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
   };
   if (T > 0) load_tok(0);
   for (int t = 0; t < T; ++t) {
-    const float gt = gn, bt = bn, vt = vn, c = cn;
+    const float gt = gn, bt = bn, vt = vn;
     float kk[kGfCols], qq[kGfCols];
 #pragma unroll
     for (int i = 0; i < kGfCols; ++i) {
@@ -282,16 +285,14 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
       b0 = fmaf(S[i], qq[i], b0);
       b1 = fmaf(S[i + 1], qq[i + 1], b1);
     }
-    float a = a0 + a1, b = b0 + b1;
+    float a = a0 + a1;
+    bpart[t * kGfThreads + tid] = b0 + b1;  // reduced after the recurrence: off the token chain
 #pragma unroll
-    for (int o = 1; o < kGfTpr; o <<= 1) {
-      a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
-      b += __shfl_xor_sync(0xFFFFFFFFu, b, o);
-    }
+    for (int o = 1; o < kGfTpr; o <<= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, o);
     const float u = bt * (vt - gt * a);
 #pragma unroll
     for (int i = 0; i < kGfCols; ++i) S[i] = fmaf(u, kk[i], gt * S[i]);
-    if (sub == 0) yl[t][row] = bf16rf(fmaf(gt, b, u * c));
+    if (sub == 0) ust[t * kGfRows + row] = u;
     if (p.ckpt && t + 1 < T) {
       float* cp = p.ckpt + static_cast<size_t>(t) * p.Hv * kGfD * kGfD + srow;
 #pragma unroll
@@ -300,6 +301,30 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
   }
 #pragma unroll
   for (int i = 0; i < kGfCols; ++i) p.state[srow + kGfTpr * i] = S[i];
+  __syncthreads();
+  // y = g b + u c per (token, row): b summed from the 16 column partials in the order of the
+  // lane butterfly (pairs, then pairs of pairs, ...), which is the same value in every lane
+  {
+    const int t = tid >> 4, rw = tid & 15;
+    if (t < T) {
+      const float4* pb = reinterpret_cast<const float4*>(bpart + t * kGfThreads + rw * kGfTpr);
+      float pv[16];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 v = pb[i];
+        pv[4 * i] = v.x;
+        pv[4 * i + 1] = v.y;
+        pv[4 * i + 2] = v.z;
+        pv[4 * i + 3] = v.w;
+      }
+      float s1[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s1[i] = pv[2 * i] + pv[2 * i + 1];
+      const float s2a = s1[0] + s1[1], s2b = s1[2] + s1[3], s2c = s1[4] + s1[5], s2d = s1[6] + s1[7];
+      const float b = (s2a + s2b) + (s2c + s2d);
+      yl[t][rw] = bf16rf(fmaf(gs[t], b, ust[t * kGfRows + rw] * kq[t]));
+    }
+  }
   __syncthreads();
   // ---- every rank receives the head's whole y: 16-byte asynchronous stores into each peer's
   // shared memory, counted on the peer's mbarrier (no cluster-wide release of global stores)
@@ -377,12 +402,24 @@ struct GdnFusedParamsHost {
   int T, Hv, Hk, W;
 };
 
+constexpr size_t kGfDynBytes = (kGfMaxT * kGfThreads + kGfMaxT * kGfRows) * sizeof(float);
+
 template <int W>
 static cudaError_t launch_gdn_fused(const GdnFusedParams& prm, cudaStream_t stream) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(gdn_fused_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(kGfDynBytes));
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(prm.Hv * kGfRanks);
   cfg.blockDim = dim3(kGfThreads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = kGfDynBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
