@@ -391,11 +391,11 @@ def config4_spec(model, dev, n_tokens=256, prompt_len=512, fwd=None):
 
 def config5_steps(world: int, rank: int, dev, kv_len=4096, ms=(8, 16), steps=5, cfg=None):
     """the 64-layer dense model, column-parallel over the job's ranks, one
-    verify step at M tokens with `kv_len` cached tokens: the fused step (DenseFusedStep; with
-    more than one rank the other ranks' digit blocks and output shards are read in place from
-    their memory over NVLink), and at the first M, for comparison, the fused step with NCCL
-    all-gathers instead (more than one rank) and the module-by-module forward; each captured
-    with its collectives in one CUDA graph when possible; max over ranks."""
+    verify step at M tokens with `kv_len` cached tokens: the fused step (DenseFusedStep with its
+    default exchange for this many ranks: peer memory over NVLink at 2, NCCL all-gathers from 4),
+    and at the first M, for comparison, the fused step with the other exchange (more than one
+    rank) and the module-by-module forward; each captured with its collectives in one CUDA graph
+    when possible; max over ranks."""
     from skinny_mlx_b200.configs import DENSE_64L, packed_bytes
     from skinny_mlx_b200.dense import DenseModel
     from skinny_mlx_b200.patch import patch_model
@@ -406,8 +406,9 @@ def config5_steps(world: int, rank: int, dev, kv_len=4096, ms=(8, 16), steps=5, 
     t0 = time.perf_counter()
     model = DenseModel(cfg, rank, world, seed=21, device=dev)
     patch_model(model)
-    fused = DenseFusedStep(model)
-    fused_nccl = DenseFusedStep(model, exchange="nccl") if world > 1 else None
+    fused = DenseFusedStep(model)  # the default exchange for this many ranks
+    other = {"peer": "nccl", "nccl": "peer"}.get(fused.exchange)
+    fused_alt = DenseFusedStep(model, exchange=other) if other else None
     torch.cuda.empty_cache()
     build_s = time.perf_counter() - t0
     per_layer = (packed_bytes((cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim, cfg.hidden)
@@ -419,8 +420,9 @@ def config5_steps(world: int, rank: int, dev, kv_len=4096, ms=(8, 16), steps=5, 
     gen = torch.Generator(device=dev).manual_seed(9)
     peak, _ = measured_hbm_peak()
     runs = [(m, "fused", fused) for m in ms] + [(ms[0], "module_path", model)]
-    if fused_nccl is not None:
-        runs.insert(len(ms), (ms[0], "fused_nccl", fused_nccl))
+    if fused_alt is not None:
+        runs.insert(len(ms), (ms[0], f"fused_{other}", fused_alt))
+        out["exchange"] = fused.exchange
     for m, kind, fwd in runs:
         caches = model.make_cache(kv_len + 32)
         for c in caches:
@@ -467,8 +469,10 @@ def config5_steps(world: int, rank: int, dev, kv_len=4096, ms=(8, 16), steps=5, 
         del graph, caches
         torch.cuda.empty_cache()
     if world > 1:
-        out["peer_wait_errors"] = fused.errors()
+        out["peer_wait_errors"] = fused.errors() + (fused_alt.errors() if fused_alt is not None else 0)
     fused.release()  # every rank, after the last step (unmaps the other ranks' buffers)
+    if fused_alt is not None:
+        fused_alt.release()
     del model
     torch.cuda.empty_cache()
     return out

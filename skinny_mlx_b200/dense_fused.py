@@ -16,7 +16,7 @@ Per layer, rank g of G:
 
 Two exchanges (G > 1):
 
-* "peer" (default): each rank keeps a buffer the other ranks map through CUDA IPC (NVLink peer
+* "peer" (the default for 2 ranks): each rank keeps a buffer the other ranks map through CUDA IPC (NVLink peer
   memory).  The digit producers (attention, SwiGLU prep) write their digit blocks into every
   rank's buffer (skinny_peer_sync mirrors), so each qmm reads its whole input from local memory
   however often its tiles re-read it; the output shards of o_proj and down are read in place
@@ -24,7 +24,7 @@ Two exchanges (G > 1):
   after a bounded wait on per-(layer, kind) flags that each producer launch sets on every rank
   when its last CTA finishes.  No collective runs inside a layer; one NCCL all-gather of the
   logits ends the step.
-* "nccl": an all_gather_into_tensor after each of the four producers (the baseline).
+* "nccl" (the default from 4 ranks): an all_gather_into_tensor after each of the four producers.
 
 With G = 1 there is no exchange.  The logits come back as [G, M, V/G] (rank-major shards).
 """
@@ -52,11 +52,17 @@ def _align(n: int, a: int = 256) -> int:
 
 
 class DenseFusedStep:
-    def __init__(self, model: DenseModel, exchange: str = "peer"):
+    """exchange: "peer", "nccl", or "auto" (peer memory for 2 ranks, NCCL from 4: measured on B200,
+    the peer exchange ties NCCL's all-gathers at 2 ranks and trails them at 4, where every
+    producer writes its digit blocks to three other GPUs and every consumer polls four flags)."""
+
+    def __init__(self, model: DenseModel, exchange: str = "auto"):
         from .patch import SkinnyQuantizedLinear
 
         self.model, self.cfg, self.G, self.rank = model, model.cfg, model.world, model.rank
         self.group = model.ex.group
+        if exchange == "auto":
+            exchange = "peer" if self.G == 2 else "nccl"
         self.exchange = exchange if self.G > 1 else "none"
         assert self.exchange in ("none", "peer", "nccl")
         cfg = self.cfg
