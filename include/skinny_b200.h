@@ -137,6 +137,16 @@ typedef struct {
   int n_mirror;
 } skinny_peer_sync;
 
+/* Token embedding rows of a 4-bit group-64 table in MLX packing (the embedding lookup of the
+ * verify forward, skinny_mlx/spec.py:23-28 via mlx_lm's QuantizedEmbedding; the dequantisation
+ * is skinny_mlx/qmm.py:8-9's affine rule):
+ *   out[t, k] = bf16(q * scale + bias), q = nibble k % 8 of word k / 8 of row ids[t]
+ * (f32 product then f32 sum, each rounded).  ids: M int64 (device), rows outside [0, V) are
+ * written as zeros.  w_packed [V, K/8] u32, scales / biases [V, K/64] bf16, out [M, ldo] bf16
+ * (16-byte aligned rows).  One launch (programmatic dependent launch). */
+int skinny_embed_w4g64(const int64_t* ids, int M, const void* w_packed, const void* scales, const void* biases,
+                       int V, int K, void* out, int ldo, void* stream);
+
 /* Bytes of one prepared qmm input (the digit blocks the qmm kernel reads) for M tokens, K columns. */
 size_t skinny_xq_bytes(int M, int K);
 

@@ -51,6 +51,8 @@ SIGNATURES = {
                                   c_void_p, c_void_p, c_void_p, c_void_p]),
     "skinny_qmm_w4g64_prepared": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                           c_size_t, c_void_p, c_int, c_void_p, c_void_p]),
+    "skinny_embed_w4g64": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_int,
+                                   c_void_p]),
     "skinny_ipc_alloc": (c_int, [c_size_t, c_void_p, c_void_p]),
     "skinny_ipc_open": (c_int, [c_void_p, c_void_p]),
     "skinny_ipc_close": (c_int, [c_void_p]),

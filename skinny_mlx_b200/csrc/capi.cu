@@ -26,6 +26,8 @@ cudaError_t qmm_tc_launch_prepared(const void* xq, const void* w_tc, void* out, 
 cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd, int dseg_cols,
                         const void* const* dseg, void* h_out, int ldh, const float* w, float eps, int K, int M,
                         void* xq, void* a_out, const skinny_peer_sync* sync, cudaStream_t stream);
+cudaError_t embed_launch(const int64_t* ids, int M, const void* w, const void* sc, const void* bi, int V, int K,
+                         void* out, int ldo, cudaStream_t stream);
 struct GdnFusedParamsHost {
   const void* proj;
   int ldp;
@@ -231,6 +233,19 @@ static bool sync_ok(const skinny_peer_sync* s) {
   for (int i = 0; i < s->n_mirror; ++i)
     if (!s->mirror[i] || (reinterpret_cast<uintptr_t>(s->mirror[i]) & 15)) return false;
   return true;
+}
+
+int skinny_embed_w4g64(const int64_t* ids, int M, const void* w_packed, const void* scales, const void* biases,
+                       int V, int K, void* out, int ldo, void* stream) {
+  if (!ids || !w_packed || !scales || !biases || !out || V < 1) return SKINNY_ERR_INVALID_ARG;
+  if (M < 1 || M > 65535) return SKINNY_ERR_TOKENS;
+  if (K < skinny::kGroup || K % skinny::kGroup || ldo < K) return SKINNY_ERR_SHAPE;
+  if (!aligned16(out) || (ldo % 8) || (reinterpret_cast<uintptr_t>(w_packed) & 3) ||
+      (reinterpret_cast<uintptr_t>(scales) & 1) || (reinterpret_cast<uintptr_t>(biases) & 1) ||
+      (reinterpret_cast<uintptr_t>(ids) & 7))
+    return SKINNY_ERR_ALIGNMENT;
+  return cuda_status(skinny::embed_launch(ids, M, w_packed, scales, biases, V, K, out, ldo,
+                                          static_cast<cudaStream_t>(stream)));
 }
 
 size_t skinny_xq_bytes(int M, int K) {

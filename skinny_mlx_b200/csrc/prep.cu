@@ -210,4 +210,55 @@ cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd
                     mpad, q, nullptr, ps);
 }
 
+// Token embedding rows of a 4-bit group-64 table (MLX packing: word j of a row holds columns
+// 8j .. 8j+7, nibble i = column 8j + i; bf16 scale and bias per 64 columns):
+//   out[t, k] = bf16( q * s + b )  (f32 product, then f32 sum, each rounded: the same two
+//   operations as the reference's dequantize), rows of ids outside [0, V) written as zeros.
+// CTA per token, thread per packed word: one 4-byte load, eight values, one 16-byte store.
+__global__ void __launch_bounds__(kPrepThreads) embed_w4g64_kernel(const int64_t* __restrict__ ids,
+                                                                   const uint32_t* __restrict__ w,
+                                                                   const __nv_bfloat16* __restrict__ sc,
+                                                                   const __nv_bfloat16* __restrict__ bi, int V, int K,
+                                                                   __nv_bfloat16* __restrict__ out, int ldo) {
+  pdl_launch_dependents();
+  pdl_wait_prior_grid();  // the ids (and the rows this launch overwrites) belong to earlier work
+  const int t = blockIdx.x;
+  const int64_t id = ids[t];
+  const bool ok = id >= 0 && id < V;
+  const int nw = K / 8;
+  const size_t row = ok ? static_cast<size_t>(id) : 0;
+  for (int j = threadIdx.x; j < nw; j += kPrepThreads) {
+    uint4 o = make_uint4(0u, 0u, 0u, 0u);
+    if (ok) {
+      const uint32_t word = w[row * nw + j];
+      const float s = __bfloat162float(sc[row * (K / 64) + j / 8]);
+      const float b = __bfloat162float(bi[row * (K / 64) + j / 8]);
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float q0 = static_cast<float>((word >> (8 * i)) & 0xF);
+        const float q1 = static_cast<float>((word >> (8 * i + 4)) & 0xF);
+        o2[i] = __floats2bfloat162_rn(__fadd_rn(__fmul_rn(q0, s), b), __fadd_rn(__fmul_rn(q1, s), b));
+      }
+    }
+    *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * ldo + 8 * j) = o;
+  }
+}
+
+cudaError_t embed_launch(const int64_t* ids, int M, const void* w, const void* sc, const void* bi, int V, int K,
+                         void* out, int ldo, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M);
+  cfg.blockDim = dim3(kPrepThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, embed_w4g64_kernel, ids, static_cast<const uint32_t*>(w),
+                            static_cast<const __nv_bfloat16*>(sc), static_cast<const __nv_bfloat16*>(bi), V, K,
+                            static_cast<__nv_bfloat16*>(out), ldo);
+}
+
 }  // namespace skinny

@@ -38,7 +38,7 @@ import torch.distributed as dist
 
 from . import _lib
 from .dense import DenseModel
-from .qmm import dequantize, get_workspace
+from .qmm import get_workspace
 
 _KINDS = 4  # attention digits, o_proj shard, SwiGLU digits, down shard
 
@@ -257,7 +257,9 @@ class DenseFusedStep:
             self._peer["epoch"].add_(1)  # one step: every flag of this step carries the new epoch
         w, s, bb = self.model.embed
         hs, cur = b["h"], 0
-        hs[0].copy_(dequantize(w[ids], s[ids], bb[ids]).to(torch.bfloat16))
+        ids = ids.to(torch.long).contiguous()
+        _lib.call("skinny_embed_w4g64", _p(ids), m, _p(w), _p(s), _p(bb), w.shape[0], cfg.hidden, _p(hs[0]),
+                  hs[0].stride(0), stream)
         D, H, I = cfg.head_dim, cfg.hidden, cfg.intermediate
         xb = b["xb"]
         gpr_o, gpr_i = 2 * self.nq, I // G // 64

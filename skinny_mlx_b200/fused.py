@@ -25,7 +25,7 @@ import torch
 from . import _lib
 from .model import AttnCache, GDNCache, HybridModel
 from .qmm import SkinnyWeight, get_workspace
-from .qmm import dequantize
+
 
 
 def _p(t) -> ctypes.c_void_p:
@@ -160,7 +160,9 @@ class FusedStep(FusedOps):
         # the residual stream alternates between two buffers: a prep reads one and writes the other
         hs = b["h"]
         cur = 0
-        hs[0].copy_(dequantize(emb.weight[ids], emb.scales[ids], emb.biases[ids]).to(torch.bfloat16))
+        ids = ids.to(torch.long).contiguous()
+        _lib.call("skinny_embed_w4g64", _p(ids), m, _p(emb.weight), _p(emb.scales), _p(emb.biases),
+                  emb.weight.shape[0], cfg.hidden, _p(hs[0]), hs[0].stride(0), stream)
         d = None
 
         def add_norm(d, w, a_out=None):

@@ -342,3 +342,19 @@ def test_fused_mtp_head_matches_module_head(cuda_lib, dev):
         got = fused(emb[a:b], hid[a:b], cb).clone()
         assert rel(got, ref) <= 2e-2, (a, b, rel(got, ref))
         assert ca.length == cb.length == b
+
+
+def test_embedding_gather_matches_module_lookup(cuda_lib, dev):
+    """skinny_embed_w4g64 against the module embedding (dequantise then bf16), bit for bit, with
+    repeated ids; an id outside the table gives a zero row."""
+    m = HybridModel(SMALL, seed=0, device=dev)
+    emb = m.embed_tokens
+    V, H = emb.weight.shape[0], SMALL.hidden
+    ids = torch.tensor([3, 0, V - 1, 3, 77, 1000 % V, 5, 6, 7], device=dev)
+    out = torch.full((ids.numel() + 1, H), 7.0, dtype=torch.bfloat16, device=dev)
+    ids_bad = torch.cat([ids, torch.tensor([V], device=dev)])
+    assert cuda_lib.skinny_embed_w4g64(_p(ids_bad), ids_bad.numel(), _p(emb.weight), _p(emb.scales), _p(emb.biases), V,
+                                       H, _p(out), H, _stream()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(out[:-1], emb(ids))
+    assert torch.count_nonzero(out[-1]).item() == 0
