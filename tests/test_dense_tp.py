@@ -268,3 +268,42 @@ def test_prep_mirrors_digits_and_signals(cuda_lib, dev):
     for buf in (own, m1, m2):
         assert torch.equal(buf, ref)
     assert flags.tolist() == [7, 7, 7] and int(counter.item()) == 0 and int(err.item()) == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m", [3, 12])
+def test_prepared_qmm_reads_digit_blocks_from_rank_buffers(cuda_lib, dev, m):
+    """The prepared qmm's per-rank input (xq_ranks, groups_per_rank): group g's digit block comes
+    from buffer g / groups_per_rank, at the offset it has in a full buffer.  Two local buffers
+    stand in for two ranks, each holding only its own slice (the rest zero): the result equals
+    the call on the full buffer bit for bit."""
+    import ctypes
+
+    from skinny_mlx_b200 import _lib
+    from skinny_mlx_b200.qmm import get_workspace, quantize, repack_for_skinny
+
+    torch.manual_seed(m)
+    K, N = 1024, 640
+    G, gpr = K // 64, K // 64 // 2
+    w = repack_for_skinny(*quantize(torch.randn(N, K, device=dev) * 0.02))
+    ws = get_workspace(dev, int(cuda_lib.skinny_qmm_workspace_bytes(N, K)))
+    x = torch.randn(m, K, device=dev).to(torch.bfloat16)
+    xq = torch.zeros(int(cuda_lib.skinny_xq_bytes(m, K)), dtype=torch.uint8, device=dev)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    assert cuda_lib.skinny_prep(2, P(x), K, None, 0, 0, None, None, 0, None, ctypes.c_float(0), m, K, P(xq), None, None,
+                                stream) == 0
+    xb = int(cuda_lib.skinny_xq_bytes(m, 64))
+    r0, r1 = torch.zeros_like(xq), torch.zeros_like(xq)
+    r0[:gpr * xb] = xq[:gpr * xb]
+    r1[gpr * xb:] = xq[gpr * xb:]
+    y_full = torch.empty(m, N, dtype=torch.bfloat16, device=dev)
+    y_ranks = torch.empty_like(y_full)
+    assert cuda_lib.skinny_qmm_w4g64_prepared(P(xq), P(w.w_tc), P(y_full), N, m, N, K, P(ws), ws.numel(), None, 0,
+                                                 None, stream) == 0
+    ranks = (ctypes.c_void_p * 8)(r0.data_ptr(), r1.data_ptr())
+    assert cuda_lib.skinny_qmm_w4g64_prepared(None, P(w.w_tc), P(y_ranks), N, m, N, K, P(ws), ws.numel(), ranks, gpr,
+                                                 None, stream) == 0
+    torch.cuda.synchronize(dev)
+    assert torch.equal(y_full, y_ranks)
+    assert G == 2 * gpr
