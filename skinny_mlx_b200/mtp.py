@@ -53,12 +53,13 @@ class FusedMTPHead(FusedOps):
     module-by-module forward.  More tokens (the prompt) run the module forward.  The result is a
     reused buffer, valid until the next call with the same token count."""
 
-    def __init__(self, head: MTPHead):
+    def __init__(self, head: MTPHead, embed=None):
+        """embed: the model's token embedding (QuantizedEmbedding), for step_ids."""
         from .patch import SkinnyQuantizedLinear
 
         if not isinstance(head.fc, SkinnyQuantizedLinear):
             raise ValueError("FusedMTPHead needs a patched head (skinny_mlx_b200.patch.patch_model(head))")
-        self.head, self.cfg = head, head.cfg
+        self.head, self.cfg, self.embed = head, head.cfg, embed
         self.fc = head.fc.rweight
         self.ent = layer_entry(head.layer, head.cfg)
         self._attn_ws: dict = {}
@@ -74,7 +75,7 @@ class FusedMTPHead(FusedOps):
             H = cfg.hidden
             xq = lambda k: torch.empty(int(L.skinny_xq_bytes(m, k)), dtype=torch.uint8, device=dev)
             bf = lambda n: torch.empty(m, n, dtype=torch.bfloat16, device=dev)
-            b = {"xq_fc": xq(2 * H), "xq_h": xq(H), "xq_o": xq(cfg.n_heads * cfg.head_dim),
+            b = {"emb": bf(H), "xq_fc": xq(2 * H), "xq_h": xq(H), "xq_o": xq(cfg.n_heads * cfg.head_dim),
                  "xq_i": xq(cfg.intermediate), "x": bf(H), "proj": bf(self.ent["proj"].N), "mix": bf(H),
                  "gu": bf(2 * cfg.intermediate), "down": bf(H), "h2": bf(H), "h3": bf(H), "out": bf(H),
                  "xb": int(L.skinny_xq_bytes(m, 64))}
@@ -82,7 +83,24 @@ class FusedMTPHead(FusedOps):
         return b
 
     @torch.no_grad()
-    def __call__(self, emb: torch.Tensor, hidden: torch.Tensor, cache: AttnCache) -> torch.Tensor:
+    def step_ids(self, ids: torch.Tensor, hidden: torch.Tensor, cache: AttnCache, len_dev=None) -> torch.Tensor:
+        """The forward from token ids (int64, on the device): the embedding rows are gathered by
+        one launch (skinny_embed_w4g64) into a reused buffer."""
+        m = ids.numel()
+        if m > 16:
+            return self(self.embed(ids), hidden, cache)
+        b = self._buffers(m)
+        e = self.embed
+        _lib.call("skinny_embed_w4g64", ctypes.c_void_p(ids.data_ptr()), m, ctypes.c_void_p(e.weight.data_ptr()),
+                  ctypes.c_void_p(e.scales.data_ptr()), ctypes.c_void_p(e.biases.data_ptr()), e.weight.shape[0],
+                  self.cfg.hidden, ctypes.c_void_p(b["emb"].data_ptr()), b["emb"].stride(0),
+                  ctypes.c_void_p(torch.cuda.current_stream(self.head.device).cuda_stream))
+        return self(b["emb"], hidden, cache, len_dev)
+
+    @torch.no_grad()
+    def __call__(self, emb: torch.Tensor, hidden: torch.Tensor, cache: AttnCache, len_dev=None) -> torch.Tensor:
+        """len_dev: a device int32 holding cache.length when the launches run (graph replay); the
+        caller then advances the host length itself."""
         m = emb.shape[0]
         if m > 16:
             return self.head(emb, hidden, cache)
@@ -97,7 +115,7 @@ class FusedMTPHead(FusedOps):
         self._qmm(b["xq_fc"], self.fc, b["x"], m, stream)
         self._prep(0, b["x"], m, H, b["xq_h"], stream, w=ent["in_norm"])
         self._qmm(b["xq_h"], ent["proj"], b["proj"], m, stream)
-        self._attention(ent, b["proj"], cache, m, b["xq_o"], stream)
+        self._attention(ent, b["proj"], cache, m, b["xq_o"], stream, len_dev)
         self._qmm(b["xq_o"], ent["out"], b["mix"], m, stream)
         self._prep(0, b["x"], m, H, b["xq_h"], stream, d=b["mix"], h_out=b["h2"], w=ent["post_norm"])
         self._qmm(b["xq_h"], ent["gate_up"], b["gu"], m, stream)

@@ -120,7 +120,7 @@ class MTPDrafter:
         if isinstance(head.fc, SkinnyQuantizedLinear):
             from .mtp import FusedMTPHead
 
-            self._fwd = FusedMTPHead(head)
+            self._fwd = FusedMTPHead(head, model.embed_tokens)
         else:
             self._fwd = head
         emb = model.embed_tokens
@@ -163,6 +163,104 @@ class MTPDrafter:
     def update(self, h_kept: torch.Tensor, new_tokens: list[int]) -> None:
         self.cache.trim(self.n_spec)
         self.h_last = self._step(torch.tensor(new_tokens, device=self.model.device), h_kept)[-1:]
+        self.n_spec = 0
+
+
+class GraphedMTPDrafter(MTPDrafter):
+    """MTPDrafter whose draft chain (K logits, argmaxes and K - 1 head steps) and whose update
+    step (one per accepted count) are replayed from CUDA graphs, so a speculative step costs the
+    host two replays instead of some 40 launches.  Needs a patched head (fused kernels).  The
+    head's cache length lives on the device while a graph runs (advanced there between draft
+    steps); the host copy is kept in step.  The prompt (begin) runs eagerly."""
+
+    def __init__(self, model, head, vocab: int | None = 32768, seed: int = 0):
+        from .mtp import FusedMTPHead
+
+        super().__init__(model, head, vocab, seed)
+        if not isinstance(self._fwd, FusedMTPHead):
+            raise ValueError("GraphedMTPDrafter needs a patched head")
+        dev, H = model.device, model.cfg.hidden
+        self._h = torch.zeros(1, H, dtype=torch.bfloat16, device=dev)      # h_last
+        self._hk = torch.zeros(17, H, dtype=torch.bfloat16, device=dev)    # kept hidden rows
+        self._ids_in = torch.zeros(17, dtype=torch.long, device=dev)
+        self._ids_host = torch.zeros(17, dtype=torch.long).pin_memory()
+        self._toks = torch.zeros(16, dtype=torch.int32, device=dev)
+        self._len = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._len_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self._evt = torch.cuda.Event()
+        self._stream = torch.cuda.Stream(dev)
+        self._graphs: dict = {}
+
+    def begin(self, prompt: list[int], h: torch.Tensor, first: int) -> None:
+        # one head cache for every run of this drafter: the graphs hold its buffers
+        if getattr(self, "cache", None) is None:
+            self.cache = self.head.make_cache()
+        self.cache.length = 0
+        ids = torch.tensor(list(prompt[1:]) + [first], device=self.model.device)
+        self.h_last = self._step(ids, h)[-1:]
+        self.n_spec = 0
+        self._h.copy_(self.h_last)
+
+    # -- graph bodies (captured on self._stream; cache = the head's cache)
+    def _draft_body(self, k: int, cache) -> None:
+        h = self._h
+        for i in range(k):
+            t = self.ids[torch.argmax(self._logits(h).float(), dim=-1)]
+            self._toks[i:i + 1].copy_(t)
+            if i < k - 1:
+                h = self._fwd.step_ids(t, h, cache, self._len)[-1:]
+                self._len.add_(1)
+
+    def _update_body(self, m: int, cache) -> None:
+        out = self._fwd.step_ids(self._ids_in[:m], self._hk[:m], cache, self._len)
+        self._h.copy_(out[-1:])
+
+    def _capture(self, key, body):
+        # warm-up on a scratch cache of the same size (buffers, workspaces), then capture
+        scratch = self.head.make_cache(self.cache.k.shape[0])
+        self._stream.wait_stream(torch.cuda.current_stream(self.model.device))
+        saved = self._h.clone()
+        with torch.cuda.stream(self._stream):
+            body(scratch)
+        self._stream.synchronize()
+        self._h.copy_(saved)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=self._stream):
+            body(self.cache)
+        self._graphs[key] = (g, self.cache)
+        return g
+
+    def _graph(self, key, body):
+        ent = self._graphs.get(key)
+        if ent is not None and ent[1] is self.cache:
+            return ent[0]
+        return self._capture(key, body)
+
+    def _set_len(self) -> None:
+        self._evt.synchronize()  # the previous copy out of the pinned word is done
+        self._len_host[0] = self.cache.length
+        self._len.copy_(self._len_host, non_blocking=True)
+        self._evt.record()
+
+    def draft(self, k: int) -> torch.Tensor:
+        g = self._graph(("d", k), lambda c: self._draft_body(k, c))
+        self._set_len()
+        g.replay()
+        self.cache.length += k - 1
+        self.n_spec = k - 1
+        return self._toks[:k]
+
+    def update(self, h_kept: torch.Tensor, new_tokens: list[int]) -> None:
+        self.cache.trim(self.n_spec)
+        m = len(new_tokens)
+        self._evt.synchronize()
+        self._ids_host[:m] = torch.tensor(new_tokens, dtype=torch.long)
+        self._ids_in[:m].copy_(self._ids_host[:m], non_blocking=True)
+        self._hk[:m].copy_(h_kept)
+        g = self._graph(("u", m), lambda c: self._update_body(m, c))
+        self._set_len()
+        g.replay()
+        self.cache.length += m
         self.n_spec = 0
 
 
@@ -252,4 +350,4 @@ def speculative(model, prompt: list[int], max_tokens: int, drafter, k: int, stat
     return out[:max_tokens]
 
 
-__all__ += ["HybridRollback", "MTPDrafter", "ScriptedDrafter", "greedy", "speculative"]
+__all__ += ["HybridRollback", "MTPDrafter", "GraphedMTPDrafter", "ScriptedDrafter", "greedy", "speculative"]

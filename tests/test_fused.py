@@ -358,3 +358,39 @@ def test_embedding_gather_matches_module_lookup(cuda_lib, dev):
     torch.cuda.synchronize()
     assert torch.equal(out[:-1], emb(ids))
     assert torch.count_nonzero(out[-1]).item() == 0
+
+
+def test_graphed_mtp_drafter_equals_eager_drafter(cuda_lib, dev):
+    """The MTP drafter replayed from CUDA graphs proposes the same tokens as the eager drafter on
+    the fused kernels through begin, draft and update steps, and speculative decoding with it
+    reproduces greedy decoding."""
+    from skinny_mlx_b200.fused import FusedStep, GraphedStep
+    from skinny_mlx_b200.mtp import MTPHead
+    from skinny_mlx_b200.patch import patch_model
+    from skinny_mlx_b200.spec import GraphedMTPDrafter, MTPDrafter, greedy, speculative
+    from test_model_patch import _exact_or_near_tie
+
+    m = HybridModel(SMALL, seed=0, device=dev)
+    patch_model(m)
+    head = MTPHead(m, seed=13)
+    patch_model(head)
+    f = FusedStep(m)
+    cache = f.make_cache()
+    h, _ = f(torch.tensor(PROMPT, device=dev), cache)
+    eager, graphed = MTPDrafter(m, head, vocab=None), GraphedMTPDrafter(m, head, vocab=None)
+    for d in (eager, graphed):
+        d.begin(PROMPT, h, 5)
+    g = torch.Generator(device="cpu").manual_seed(1)
+    for k, keep in ((2, 1), (3, 3), (2, 2), (3, 1)):
+        a, b = eager.draft(k).clone(), graphed.draft(k).clone()
+        assert torch.equal(a, b), (k, a, b)
+        hk = (torch.randn(keep, SMALL.hidden, generator=g) * 2).to(torch.bfloat16).to(dev)
+        new = torch.randint(0, SMALL.vocab, (keep,), generator=g).tolist()
+        eager.update(hk, new)
+        graphed.update(hk, new)
+        assert eager.cache.length == graphed.cache.length
+    gs = GraphedStep(f)
+    gaps = []
+    ref = greedy(f, PROMPT, 20, gaps)
+    got = speculative(gs, PROMPT, 20, GraphedMTPDrafter(m, head, vocab=None), 2, cache=gs.make_cache())
+    assert _exact_or_near_tie(ref, got, gaps)
