@@ -94,6 +94,12 @@ int skinny_qmm_w4g64_grouped(int n, const void* const* x, const int* ldx, const 
                              void* const* out, const int* ldo, const int* N, const int* K, int M,
                              void* workspace, size_t workspace_bytes, void* stream);
 
+/* The relaid weight back as bf16 W[N, K] (row stride ldo, 16-byte aligned rows):
+ * W = bf16(q * scale + bias), the f32 product then the f32 sum, each rounded (the dequantisation
+ * of skinny_mlx/qmm.py:8-9).  For many-token inputs (a prompt), which a dense GEMM serves
+ * better than the token-streaming qmm; skinny_qmm (Python) uses it from 64 tokens.  One launch. */
+int skinny_dequant_w4g64(const void* w_tc, int N, int K, void* out, int ldo, void* stream);
+
 /* Same contract with plain CUDA cores (no tcgen05), one thread per output.  A slow cross-check
  * used by the tests to localise a mismatch; it has no counterpart in the reference. */
 int skinny_qmm_w4g64_simt(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,

@@ -51,6 +51,7 @@ SIGNATURES = {
                                   c_void_p, c_void_p, c_void_p, c_void_p]),
     "skinny_qmm_w4g64_prepared": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                           c_size_t, c_void_p, c_int, c_void_p, c_void_p]),
+    "skinny_dequant_w4g64": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p]),
     "skinny_embed_w4g64": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_int,
                                    c_void_p]),
     "skinny_ipc_alloc": (c_int, [c_size_t, c_void_p, c_void_p]),

@@ -18,6 +18,7 @@ cudaError_t qmm_repack_launch(const uint32_t* w, const uint16_t* s, const uint16
                               int N, int K, cudaStream_t stream);
 cudaError_t qmm_simt_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
                             int N, int K, cudaStream_t stream);
+cudaError_t qmm_dequant_launch(const void* w_tc, int N, int K, void* out, int ldo, cudaStream_t stream);
 bool qmm_noalloc_fits(int N, int K);
 size_t spec_accept_ws_bytes();
 cudaError_t qmm_tc_launch_prepared(const void* xq, const void* w_tc, void* out, int ldo, int M, int N, int K,
@@ -193,6 +194,14 @@ int skinny_qmm_w4g64_grouped(int n, const void* const* x, const int* ldx, const 
   if (!workspace || workspace_bytes < wl.total || !aligned16(workspace)) return SKINNY_ERR_WORKSPACE;
   return cuda_status(skinny::qmm_tc_launch_grouped(n, x, ldx, w_tc, out, ldo, N, K, M, workspace,
                                                    static_cast<cudaStream_t>(stream), true));
+}
+
+int skinny_dequant_w4g64(const void* w_tc, int N, int K, void* out, int ldo, void* stream) {
+  if (!w_tc || !out) return SKINNY_ERR_INVALID_ARG;
+  const int st = check_qmm_shape(N, K);
+  if (st != SKINNY_OK) return st;
+  if (ldo < K || (ldo % 8) || !aligned16(out) || !aligned16(w_tc)) return SKINNY_ERR_ALIGNMENT;
+  return cuda_status(skinny::qmm_dequant_launch(w_tc, N, K, out, ldo, static_cast<cudaStream_t>(stream)));
 }
 
 int skinny_qmm_w4g64_simt(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,

@@ -1188,6 +1188,47 @@ cudaError_t qmm_repack_launch(const uint32_t* w, const uint16_t* s, const uint16
   return cudaGetLastError();
 }
 
+// Relaid units -> bf16 W[N, K] (row stride ldo): w = bf16(q * s + b), the f32 product then the f32
+// sum, each rounded (the MLX dequantisation).  CTA per unit, thread per (row, 32-column chunk):
+// one 16-byte load of 32 nibbles, four 16-byte stores.  For callers that hand many tokens to a
+// dense GEMM instead of the token-streaming qmm.
+__global__ void __launch_bounds__(256) qmm_dequant_kernel(const uint8_t* __restrict__ w_tc, int N, int K,
+                                                         __nv_bfloat16* __restrict__ out, int ldo) {
+  const int G = K / kGroup;
+  const long long u = blockIdx.x;
+  const int tile = static_cast<int>(u / G), g = static_cast<int>(u % G);
+  const int r = threadIdx.x & (kTileRows - 1), c = threadIdx.x >> 7;
+  const int n = tile * kTileRows + r;
+  if (n >= N) return;
+  const uint8_t* unit = w_tc + u * kUnitWBytes;
+  const uint4 nib = *reinterpret_cast<const uint4*>(unit + c * 2048 + r * 16);
+  const uint32_t sb = *reinterpret_cast<const uint32_t*>(unit + kUnitNibBytes + r * 4);
+  const float s = __uint_as_float(sb << 16), b = __uint_as_float(sb & 0xFFFF0000u);
+  const uint32_t words[4] = {nib.x, nib.y, nib.z, nib.w};
+  // nibble of column k0 + i inside a word: i = 0..3 at bits 4 + 8i, i = 4..7 at bits 8(i - 4)
+  __nv_bfloat16* dst = out + static_cast<size_t>(n) * ldo + g * kGroup + 32 * c;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 o;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      const int sh0 = i < 4 ? 4 + 8 * i : 8 * (i - 4), sh1 = i + 1 < 4 ? 4 + 8 * (i + 1) : 8 * (i - 3);
+      const float q0 = static_cast<float>(((words[j] >> sh0) & 0xF) ^ 8);
+      const float q1 = static_cast<float>(((words[j] >> sh1) & 0xF) ^ 8);
+      o2[i / 2] = __floats2bfloat162_rn(__fadd_rn(__fmul_rn(q0, s), b), __fadd_rn(__fmul_rn(q1, s), b));
+    }
+    *reinterpret_cast<uint4*>(dst + 8 * j) = o;
+  }
+}
+
+cudaError_t qmm_dequant_launch(const void* w_tc, int N, int K, void* out, int ldo, cudaStream_t stream) {
+  const QmmShape sh = qmm_shape(N, K);
+  qmm_dequant_kernel<<<static_cast<unsigned>(sh.U), 256, 0, stream>>>(static_cast<const uint8_t*>(w_tc), N, K,
+                                                                    static_cast<__nv_bfloat16*>(out), ldo);
+  return cudaGetLastError();
+}
+
 cudaError_t qmm_simt_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
                             int N, int K, cudaStream_t stream) {
   const QmmShape sh = qmm_shape(N, K);

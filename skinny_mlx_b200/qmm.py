@@ -27,6 +27,7 @@ from . import _lib
 GROUP = 64
 BITS = 4
 MAX_TOKENS = 16
+PREFILL_TOKENS = 64  # from this many tokens skinny_qmm dequantises once and runs a dense GEMM
 
 
 # ---------------------------------------------------------------------------------------------
@@ -182,7 +183,10 @@ def skinny_qmm(x: torch.Tensor, w: SkinnyWeight, out: torch.Tensor | None = None
     """x [..., K] (bf16) @ dequant(W)^T -> [..., N] bf16 through the tcgen05 kernel.
 
     Token counts above 16 are processed in 16-token chunks by the same kernel (each token's
-    result does not depend on the chunking).  Replaces skinny_mlx/qmm.py:132.
+    result does not depend on the chunking); from PREFILL_TOKENS tokens (a prompt) the weight is
+    instead dequantised to bf16 once (skinny_dequant_w4g64) and multiplied by a dense GEMM, which
+    rounds the weights to bf16 and so differs from the small-M results in the last bits.
+    Replaces skinny_mlx/qmm.py:132.
     """
     _require_cuda(x, "x")
     if x.shape[-1] != w.K:
@@ -202,6 +206,13 @@ def skinny_qmm(x: torch.Tensor, w: SkinnyWeight, out: torch.Tensor | None = None
     elif out.shape != (m, w.N) or out.dtype != torch.bfloat16 or not out.is_contiguous():
         raise ValueError("out must be a contiguous bf16 [M, N] tensor")
     L = _lib.lib()
+    if m >= PREFILL_TOKENS:
+        with torch.cuda.device(dev):
+            wd = torch.empty(w.N, w.K, dtype=torch.bfloat16, device=dev)
+            _lib.check("skinny_dequant_w4g64", L.skinny_dequant_w4g64(
+                w.w_tc.data_ptr(), w.N, w.K, wd.data_ptr(), w.K, _stream_handle(dev)))
+            torch.matmul(x2, wd.t(), out=out)
+        return out.reshape(*lead, w.N)
     with torch.cuda.device(dev):
         need = L.skinny_qmm_workspace_bytes(w.N, w.K)
         ws = get_workspace(dev, need)

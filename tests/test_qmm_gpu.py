@@ -192,3 +192,29 @@ def test_qmm_grouped_matches_single_calls(cuda_lib, dev, m):
         assert quant.rel_err(single, o.float().cpu().numpy()) <= TIGHT
         assert quant.rel_err(ref, o.float().cpu().numpy()) <= TIGHT
     assert device_errors(dev) == 0
+
+
+def test_dequant_and_many_token_path(cuda_lib, dev):
+    """skinny_dequant_w4g64 gives the MLX dequantisation bit for bit (bf16 of q * s + b), and
+    skinny_qmm from PREFILL_TOKENS tokens (dequantise + dense GEMM) agrees with the f32 reference
+    and with the token-streaming kernel within the bf16 tolerance."""
+    import ctypes
+
+    from skinny_mlx_b200.qmm import PREFILL_TOKENS, dequantize, quantize, repack_for_skinny, skinny_qmm
+
+    torch.manual_seed(7)
+    N, K = 8224, 1024  # a partial last row tile
+    wp, s, b = quantize(torch.randn(N, K, device=dev) * 0.02)
+    sw = repack_for_skinny(wp, s, b)
+    wd = torch.empty(N, K, dtype=torch.bfloat16, device=dev)
+    assert cuda_lib.skinny_dequant_w4g64(ctypes.c_void_p(sw.w_tc.data_ptr()), N, K, ctypes.c_void_p(wd.data_ptr()), K,
+                                         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
+    ref_w = dequantize(wp, s, b)
+    assert torch.equal(wd, ref_w.to(torch.bfloat16))
+    m = PREFILL_TOKENS + 8
+    x = torch.randn(m, K, device=dev).to(torch.bfloat16)
+    y = skinny_qmm(x, sw).float()
+    ref = x.float() @ ref_w.t()
+    assert ((y - ref).abs().max() / ref.abs().max()).item() <= 1e-2
+    small = torch.cat([skinny_qmm(x[i:i + 16], sw) for i in range(0, m, 16)]).float()
+    assert ((y - small).abs().max() / small.abs().max()).item() <= 1e-2
