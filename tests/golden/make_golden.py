@@ -71,7 +71,9 @@ def make_qmm_small() -> None:
 
 
 def main() -> None:
-    ref_root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    if len(sys.argv) < 2:
+        sys.exit("usage: python tests/golden/make_golden.py <checkout of the reference skinny-mlx>")
+    ref_root = Path(sys.argv[1])
     ref_qmm = load_reference_module(ref_root, "skinny_mlx.qmm")
     make_repack(ref_qmm)
     make_config(ref_qmm)
