@@ -633,6 +633,50 @@ def run_head_case(args):
                       "packed_bytes": packed_bytes(151936, 2560)}), flush=True)
 
 
+def run_attn_case(args):
+    """--case attn: the fused attention of the config-5 dense model (40 query heads, 8 KV heads,
+    rotary on all 128 dims, no gate) at --m tokens against 4096 cached tokens, 8 layers' caches
+    back to back per step: a small case for profilers (about 0.3 GB on the device)."""
+    import ctypes
+
+    from skinny_mlx_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    D, nh, nkv, L0, layers, T = 128, 40, 8, 4096, 8, args.m
+    max_len = L0 + 32
+    g = torch.Generator(device=dev).manual_seed(3)
+    proj = torch.randn(T, (nh + 2 * nkv) * D, device=dev, generator=g).to(torch.bfloat16)
+    caches = [(torch.randn(max_len, nkv, D, device=dev, generator=g).to(torch.bfloat16),
+               torch.randn(max_len, nkv, D, device=dev, generator=g).to(torch.bfloat16)) for _ in range(layers)]
+    qn = torch.zeros(D, device=dev)
+    kn = torch.zeros(D, device=dev)
+    inv = (1e6 ** (-torch.arange(0, 64, device=dev, dtype=torch.float32) / 64)).contiguous()
+    L = _lib.lib()
+    ws = torch.zeros(int(L.skinny_attn_workspace_bytes(16, nh, nkv, max_len)), dtype=torch.uint8, device=dev)
+    xq = torch.zeros(int(L.skinny_xq_bytes(16, nh * D)), dtype=torch.uint8, device=dev)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+
+    def step():
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        for kc, vc in caches:
+            _lib.call("skinny_attn_fused", P(proj), proj.stride(0), P(qn), P(kn), P(inv), 128, 0, 1e-6, P(kc), P(vc), L0,
+                      None, T, nh, nkv, max_len, P(ws), ws.numel(), P(xq), None, None, stream)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps / layers
+    kv = L0 * nkv * D * 2 * 2
+    print(json.dumps({"case": "attn", "tokens": T, "us_per_layer": round(us, 2), "kv_bytes": kv,
+                      "GBps": round(kv / (us * 1e-6) / 1e9, 1)}), flush=True)
+
+
 def run_verify_case(args):
     """--case verify: the config-3 fused verify step at M = 1 and M = 8 (2048 cached tokens,
     checkpoints recorded), each captured in a CUDA graph; after warm replays, one replay of each
@@ -703,10 +747,11 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the config-3/4 model measurements")
     ap.add_argument("--no-dense", action="store_true", help="skip the config-5 column-parallel model")
-    ap.add_argument("--case", default="stack", choices=["stack", "head", "verify"],
+    ap.add_argument("--case", default="stack", choices=["stack", "head", "verify", "attn"],
                     help="head: single-matrix profiling case; verify: the config-3 step at M = 1 and 8 "
-                         "in NVTX ranges; both instead of the bench line")
-    ap.add_argument("--m", type=int, default=M_STACK, help="tokens for --case head")
+                         "in NVTX ranges; attn: the dense model's attention at --m tokens; all instead "
+                         "of the bench line")
+    ap.add_argument("--m", type=int, default=M_STACK, help="tokens for --case head and --case attn")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.case == "head":
@@ -714,6 +759,9 @@ def main():
         return
     if args.case == "verify":
         run_verify_case(args)
+        return
+    if args.case == "attn":
+        run_attn_case(args)
         return
     world, rank, local = init_dist()
     try:
