@@ -408,7 +408,8 @@ def config5_steps(world: int, rank: int, dev, kv_len=4096, ms=(8, 16), steps=5, 
     model = DenseModel(cfg, rank, world, seed=21, device=dev)
     patch_model(model)
     fused = DenseFusedStep(model)  # the default exchange for this many ranks
-    other = {"peer": "nccl", "nccl": "peer"}.get(fused.exchange)
+    # the other exchange beside it, for the rank counts where both were validated (2 and 4)
+    other = {"peer": "nccl", "nccl": "peer"}.get(fused.exchange) if world <= 4 else None
     fused_alt = DenseFusedStep(model, exchange=other) if other else None
     torch.cuda.empty_cache()
     build_s = time.perf_counter() - t0
