@@ -217,11 +217,17 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
     }
     const float nq = rsqrtf(static_cast<float>(kGfD)) / fmaxf(sqrtf(sq), 1e-12f);
     const float nk = 1.f / fmaxf(sqrtf(sk), 1e-12f);
+    float c = 0.f;  // k_t . q_t of the rounded vectors (the same for every state row)
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      qs[t][lane + 32 * u] = bf16rf(qv[u] * nq);
-      ks[t][lane + 32 * u] = bf16rf(kv[u] * nk);
+      const float qr = bf16rf(qv[u] * nq), kr = bf16rf(kv[u] * nk);
+      qs[t][lane + 32 * u] = qr;
+      ks[t][lane + 32 * u] = kr;
+      c = fmaf(kr, qr, c);
     }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
+    if (lane == 0) kq[t] = c;
   }
   if (tid < T) {
     const float xa = ga + gdt;
@@ -230,28 +236,9 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
     bs[tid] = 1.f / (1.f + expf(-gb));
   }
   __syncthreads();
-  // ---- k_t . q_t of every token (the same for every state row): thread (t, sub) forms the partial
-  // over the columns it takes in the recurrence and the 16 partials are summed by the same
-  // butterfly, so the value is the one the per-token reduction would give.
-  {
-    const int t = tid >> 4, sb = tid & 15;
-    float c0 = 0.f, c1 = 0.f;
-    if (t < T) {
-#pragma unroll
-      for (int i = 0; i < kGfCols; i += 2) {
-        c0 = fmaf(ks[t][sb + kGfTpr * i], qs[t][sb + kGfTpr * i], c0);
-        c1 = fmaf(ks[t][sb + kGfTpr * (i + 1)], qs[t][sb + kGfTpr * (i + 1)], c1);
-      }
-    }
-    float c = c0 + c1;
-#pragma unroll
-    for (int o = 1; o < kGfTpr; o <<= 1) c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
-    if (sb == 0 && t < T) kq[t] = c;
-  }
-  __syncthreads();
   // ---- recurrence: thread = (row, sub); columns sub + 8 i in registers.  Per token only a = S k
   // (of the previous state) is reduced across the row's lanes; the partials of b = S q are kept
-  // and summed after the loop, and c = k q comes from above:
+  // and summed after the loop, and c = k q comes from the norm phase:
   //   u = beta (v - g a),   S <- g S + u k^T,   y = S q = g b + u c.
   // The next token's operands are loaded while the current token's reductions run; the
   // arithmetic per token is the same whatever T is, so a token's results do not depend on how
