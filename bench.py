@@ -202,6 +202,25 @@ class StackRunner:
     def replay(self):
         self.graph.replay()
 
+    def add_second_buffers(self):
+        """A second graph over a second input buffer and a second result buffer (the other
+        projections' outputs are shared): consecutive steps then use different host-visible
+        buffers, so one step's copies can overlap its neighbours' compute."""
+        ks = sorted(self.xs)
+        self.x_all2 = self.x_all.clone()
+        xs2 = {k: self.x_all2[self.koff[k]: self.koff[k] + self.m * k].view(self.m, k) for k in ks}
+        self.out_last2 = torch.empty_like(self.outs[-1])
+        saved = self.xs, self.outs
+        self.xs, self.outs = xs2, self.outs[:-1] + [self.out_last2]
+        with torch.cuda.stream(self.stream):
+            self.run_eager()
+        self.stream.synchronize()
+        self.graph2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph2, stream=self.stream):
+            self.run_eager()
+        self.stream.synchronize()
+        self.xs, self.outs = saved
+
     def algorithmic_bytes(self) -> int:
         from skinny_mlx_b200.configs import packed_bytes
 
@@ -233,31 +252,79 @@ def time_replays(runner: StackRunner, steps: int, warmup: int, world: int, sampl
 
 
 def time_e2e(runner: StackRunner, steps: int, warmup: int):
-    """Public-API step with host buffers: H2D of the step's activations from pinned memory,
-    graph replay of the 129 projections, D2H of the logits (the step's result)."""
-    s = runner.stream
-    host_x = torch.empty(runner.x_all.numel(), dtype=torch.bfloat16, pin_memory=True)
-    host_x.copy_(runner.x_all.cpu())
-    logits = runner.outs[-1]
-    host_y = torch.empty(logits.shape, dtype=logits.dtype, pin_memory=True)
+    """Public-API steps with host buffers: every step copies its activations in from pinned host
+    memory, replays the 129 projections (one grouped call, CUDA graph) and copies the logits (the
+    step's result) out to pinned host memory.  The copies run on a second stream against double
+    buffers, so step i's input copy and step i-1's result copy overlap the neighbouring steps'
+    compute; the timed region runs from before the first input copy to the end of the last
+    result copy.  Returns (ms for `steps` steps, H2D bytes per step, D2H bytes per step, ms for
+    the same steps with every copy serialised on the compute stream)."""
+    if not hasattr(runner, "graph2"):
+        runner.add_second_buffers()
+    main = runner.stream
+    copy = torch.cuda.Stream(main.device)
+    xbuf = [runner.x_all, runner.x_all2]
+    ybuf = [runner.outs[-1], runner.out_last2]
+    graphs = [runner.graph, runner.graph2]
+    host_x = [torch.empty(runner.x_all.numel(), dtype=torch.bfloat16, pin_memory=True) for _ in range(2)]
+    for h in host_x:
+        h.copy_(runner.x_all.cpu())
+    host_y = [torch.empty(ybuf[0].shape, dtype=ybuf[0].dtype, pin_memory=True) for _ in range(2)]
+    h2d = [torch.cuda.Event(), torch.cuda.Event()]
+    d2h = [torch.cuda.Event(), torch.cuda.Event()]
+    done = [torch.cuda.Event(), torch.cuda.Event()]
+    start = torch.cuda.Event()
 
-    def one():
-        runner.x_all.copy_(host_x, non_blocking=True)
-        runner.replay()
-        host_y.copy_(logits, non_blocking=True)
+    def pipelined(n, e0=None, e1=None):
+        if e0 is not None:
+            e0.record(main)
+        start.record(main)
+        copy.wait_event(start)
+        with torch.cuda.stream(copy):
+            xbuf[0].copy_(host_x[0], non_blocking=True)
+            h2d[0].record(copy)
+        for i in range(n):
+            b = i & 1
+            main.wait_event(h2d[b])
+            if i >= 2:
+                main.wait_event(d2h[b])  # result buffer b was copied out
+            with torch.cuda.stream(main):
+                graphs[b].replay()
+            done[b].record(main)
+            with torch.cuda.stream(copy):
+                if i + 1 < n:
+                    if i >= 1:
+                        copy.wait_event(done[1 - b])  # step i-1 has read input buffer 1-b
+                    xbuf[1 - b].copy_(host_x[1 - b], non_blocking=True)
+                    h2d[1 - b].record(copy)
+                copy.wait_event(done[b])
+                host_y[b].copy_(ybuf[b], non_blocking=True)
+                d2h[b].record(copy)
+        main.wait_event(d2h[(n - 1) & 1])
+        if e1 is not None:
+            e1.record(main)
 
-    with torch.cuda.stream(s):
-        for _ in range(warmup):
-            one()
-    s.synchronize()
+    def serial(n):
+        with torch.cuda.stream(main):
+            for _ in range(n):
+                runner.x_all.copy_(host_x[0], non_blocking=True)
+                runner.replay()
+                host_y[0].copy_(ybuf[0], non_blocking=True)
+
+    pipelined(max(warmup, 3))
+    main.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(s):
-        e0.record(s)
-        for _ in range(steps):
-            one()
-        e1.record(s)
+    pipelined(steps, e0, e1)
     e1.synchronize()
-    return e0.elapsed_time(e1), host_x.numel() * 2, host_y.numel() * 2
+    ms = e0.elapsed_time(e1)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    serial(max(warmup, 3))
+    main.synchronize()
+    f0.record(main)
+    serial(steps)
+    f1.record(main)
+    f1.synchronize()
+    return ms, host_x[0].numel() * 2, host_y[0].numel() * 2, f0.elapsed_time(f1)
 
 
 def config1_sweep(dev, copies=40):
@@ -541,8 +608,9 @@ def run_skinny(args, world, rank, local):
     msl_step = max_over_ranks(msl, world) / args.steps
     del rl
 
-    e2e_ms, h2d, d2h = time_e2e(runner, args.steps, args.warmup)
+    e2e_ms, h2d, d2h, e2e_serial_ms = time_e2e(runner, args.steps, args.warmup)
     e2e_ms = max_over_ranks(e2e_ms, world) / args.steps
+    e2e_serial_ms = max_over_ranks(e2e_serial_ms, world) / args.steps
     e2e_value = per_step_bytes * world / (e2e_ms * 1e-3) / 1e9
 
     sweep = config1_sweep(dev) if (rank == 0 and not args.no_sweep) else None
@@ -550,6 +618,8 @@ def run_skinny(args, world, rank, local):
     c5 = config5_steps(world, rank, dev) if not args.no_dense else None
     if rank == 0 and not args.no_model:
         del runner.graph
+        if hasattr(runner, "graph2"):
+            del runner.graph2
         model = build_config3(dev)
         from skinny_mlx_b200.fused import FusedStep, GraphedStep
 
@@ -600,7 +670,10 @@ def run_skinny(args, world, rank, local):
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
-                    "path": "pinned H2D of activations, CUDA-graph replay of the skinny_qmm_grouped call, D2H of logits"},
+                    "ms_per_step_copies_serialised": round(e2e_serial_ms, 4),
+                    "path": "pinned H2D of each step's activations and D2H of its logits on a copy stream, "
+                            "double-buffered so they overlap the neighbouring steps' CUDA-graph replay of the "
+                            "skinny_qmm_grouped call"},
             "gpu_launches": KERNELS_PER_CALL * args.steps,
             "per_projection_launches": {"ms_per_step": round(msl_step, 4),
                                         "GBps": round(per_step_bytes / (msl_step * 1e-3) / 1e9, 1),
