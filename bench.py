@@ -414,13 +414,13 @@ def config4_spec(model, dev, n_tokens=256, prompt_len=512, fwd=None):
     """greedy vs speculative decoding from a 512-token seeded prompt, tok/s
     and token-exactness against greedy.  Drafters: the MTP head (random weights: it accepts
     almost nothing; its draft chain and update replayed from CUDA graphs) over 32768 seeded ids at
-    K = 2, 3, and a scripted drafter that proposes the
+    K = 2, 3, the model-free prompt-lookup drafter (K = 3), and a scripted drafter that proposes the
     greedy continuation at the reference's acceptance (K = 2, 2.51 tokens/step).  `fwd` (default
     the model) runs the verify and decode forwards, replayed from CUDA graphs when it is a
     GraphedStep; every run reuses one cache, and each configuration runs once untimed first."""
     from skinny_mlx_b200.mtp import MTPHead
     from skinny_mlx_b200.patch import patch_model
-    from skinny_mlx_b200.spec import GraphedMTPDrafter, ScriptedDrafter, greedy, speculative
+    from skinny_mlx_b200.spec import GraphedMTPDrafter, PromptLookupDrafter, ScriptedDrafter, greedy, speculative
 
     g = torch.Generator().manual_seed(512)
     prompt = torch.randint(0, model.cfg.vocab, (prompt_len,), generator=g).tolist()
@@ -454,6 +454,7 @@ def config4_spec(model, dev, n_tokens=256, prompt_len=512, fwd=None):
     for k in (2, 3):
         record(f"K{k}", k, lambda: GraphedMTPDrafter(model, head, vocab=32768, seed=3))
     record("K2_scripted_p0.81", 2, lambda: ScriptedDrafter(ref, 0.81, model.cfg.vocab, dev, seed=5))
+    record("K3_prompt_lookup", 3, lambda: PromptLookupDrafter(3, dev))
     return out
 
 

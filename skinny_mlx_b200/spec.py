@@ -264,6 +264,47 @@ class GraphedMTPDrafter(MTPDrafter):
         self.n_spec = 0
 
 
+class PromptLookupDrafter:
+    """Model-free drafter (skinny_mlx/spec.py:32-51): proposes the up to K tokens that followed the
+    latest earlier occurrence of the context's trailing n-gram, for n = ngram down to 1 (none if
+    no n-gram recurs).  Every n-gram's two latest start positions are indexed as tokens arrive,
+    so a draft costs O(ngram) instead of a scan of the context."""
+
+    def __init__(self, ngram: int = 3, device=None):
+        self.ngram, self.device = ngram, device
+
+    def begin(self, prompt, h, first) -> None:
+        if self.device is None and h is not None:
+            self.device = h.device
+        self.ctx: list[int] = []
+        self.pos = [dict() for _ in range(self.ngram + 1)]  # n -> {n-gram: (latest start, previous)}
+        for t in list(prompt) + [int(first)]:
+            self._push(t)
+
+    def _push(self, tok: int) -> None:
+        self.ctx.append(int(tok))
+        L = len(self.ctx)
+        for n in range(1, min(self.ngram, L) + 1):
+            key = tuple(self.ctx[L - n:])
+            prev = self.pos[n].get(key)
+            self.pos[n][key] = (L - n, prev[0] if prev else None)
+
+    def draft(self, k: int) -> torch.Tensor:
+        ctx, L = self.ctx, len(self.ctx)
+        for n in range(self.ngram, 0, -1):
+            if L < n + 1:
+                continue
+            ent = self.pos[n].get(tuple(ctx[L - n:]))  # ent[0] is the trailing n-gram itself
+            if ent is not None and ent[1] is not None:
+                s = ent[1]
+                return torch.tensor(ctx[s + n: s + n + k], dtype=torch.int32).to(self.device, non_blocking=True)
+        return torch.empty(0, dtype=torch.int32, device=self.device)
+
+    def update(self, h_kept, new_tokens) -> None:
+        for t in new_tokens:
+            self._push(t)
+
+
 class ScriptedDrafter:
     """Drafts a known greedy continuation `ref`, each proposal replaced by a wrong token with
     probability 1 - p (seeded): speculative decoding at a chosen acceptance rate.  With random
@@ -335,12 +376,12 @@ def speculative(model, prompt: list[int], max_tokens: int, drafter, k: int, stat
     drafter.begin(prompt, h, out[0])
     steps = accepted = 0
     while len(out) < max_tokens:
-        draft = drafter.draft(k)
+        draft = drafter.draft(k)  # up to k tokens (a model-free drafter may propose fewer)
         x = torch.cat([torch.tensor([out[-1]], dtype=torch.int32, device=model.device), draft])
         rb.record(cache)
         h, logits = model(x.long(), cache)
         n, new = _accept_any(logits, draft)
-        rb.rollback(cache, fed=k + 1, keep=n + 1)
+        rb.rollback(cache, fed=x.numel(), keep=n + 1)
         drafter.update(h[: n + 1], new)
         out += new
         steps += 1
@@ -350,4 +391,5 @@ def speculative(model, prompt: list[int], max_tokens: int, drafter, k: int, stat
     return out[:max_tokens]
 
 
-__all__ += ["HybridRollback", "MTPDrafter", "GraphedMTPDrafter", "ScriptedDrafter", "greedy", "speculative"]
+__all__ += ["HybridRollback", "MTPDrafter", "GraphedMTPDrafter", "PromptLookupDrafter", "ScriptedDrafter", "greedy",
+            "speculative"]

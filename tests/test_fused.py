@@ -394,3 +394,25 @@ def test_graphed_mtp_drafter_equals_eager_drafter(cuda_lib, dev):
     ref = greedy(f, PROMPT, 20, gaps)
     got = speculative(gs, PROMPT, 20, GraphedMTPDrafter(m, head, vocab=None), 2, cache=gs.make_cache())
     assert _exact_or_near_tie(ref, got, gaps)
+
+
+def test_prompt_lookup_speculation_reproduces_greedy(cuda_lib, dev):
+    """Speculative decoding with the model-free prompt-lookup drafter (drafts of any length,
+    including none) through the graph-replayed fused step reproduces greedy decoding, on a
+    prompt with repeats so that drafts are proposed."""
+    from skinny_mlx_b200.fused import FusedStep, GraphedStep
+    from skinny_mlx_b200.patch import patch_model
+    from skinny_mlx_b200.spec import PromptLookupDrafter, greedy, speculative
+    from test_model_patch import _exact_or_near_tie
+
+    m = HybridModel(SMALL, seed=0, device=dev)
+    patch_model(m)
+    f = FusedStep(m)
+    gs = GraphedStep(f)
+    prompt = (PROMPT[:8] * 3)[:20]
+    gaps = []
+    ref = greedy(f, prompt, 24, gaps)
+    st = {}
+    got = speculative(gs, prompt, 24, PromptLookupDrafter(3), 3, st, cache=gs.make_cache())
+    assert _exact_or_near_tie(ref, got, gaps)
+    assert st["steps"] > 0
