@@ -614,10 +614,10 @@ def run_skinny(args, world, rank, local):
     e2e_serial_ms = max_over_ranks(e2e_serial_ms, world) / args.steps
     e2e_value = per_step_bytes * world / (e2e_ms * 1e-3) / 1e9
 
-    sweep = config1_sweep(dev) if (rank == 0 and not args.no_sweep) else None
+    sweep = config1_sweep(dev) if (world == 1 and not args.no_sweep) else None
     c3 = c3m = c4 = None
     c5 = config5_steps(world, rank, dev) if not args.no_dense else None
-    if rank == 0 and not args.no_model:
+    if world == 1 and not args.no_model:  # configs 3 and 4 are single-GPU workloads
         del runner.graph
         if hasattr(runner, "graph2"):
             del runner.graph2
@@ -636,7 +636,7 @@ def run_skinny(args, world, rank, local):
     achieved = qmm_bytes / (ms_step * 1e-3) / 1e9
 
     cpu = None
-    if rank == 0 and not args.no_cpu:
+    if world == 1 and not args.no_cpu:  # the CPU baseline is reported at N = 1 only
         from oracle import cpu_baseline
 
         torch.set_num_threads(os.cpu_count() or 1)
