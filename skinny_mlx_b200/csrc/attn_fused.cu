@@ -9,12 +9,13 @@
 //
 // Two launches, split over keys (flash-decode style):
 //   attn_chunk_kernel  CTA (128-key chunk, KV head): loads the chunk's keys and values once,
-//                      then for every group of 16 query rows (row = t * rep + q head in the
-//                      group) computes the chunk's row maxima, sums and unnormalised outputs on
-//                      bf16 tensor-core tiles and publishes them.  The new keys of the chunk are
-//                      normalised, rotated and appended to the cache by that CTA (positions >= L0
-//                      are only written, positions < L0 only read, so chunks never race).
-//   attn_merge_kernel  CTA (4 rows of a row group, KV head): merges the chunks (a fixed order:
+//                      then in passes of up to three 16-row tiles of query rows (row = t * rep +
+//                      q head in the group) computes the chunk's row maxima, sums and
+//                      unnormalised outputs on bf16 tensor-core tiles and publishes them.  The
+//                      new keys of the chunk are normalised, rotated and appended to the cache by
+//                      that CTA (positions >= L0 are only written, positions < L0 only read, so
+//                      chunks never race).
+//   attn_merge_kernel  CTA (one query row, KV head): merges the chunks (a fixed order:
 //                      deterministic), applies the gate and writes the digits.
 // No CTA waits on another; the merge launch waits for the chunk launch through programmatic
 // dependent launch, like every launch of the step (the next launch may start at once; a kernel
