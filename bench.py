@@ -9,11 +9,16 @@ CUDA graph) is reported beside it.  Weights total 2.0 GB, far above the 126 MB L
 is needed between steps.
 
 metric: qmm HBM GB/s over the step (algorithmic bytes = packed weights + bf16 activations in
-and out, per step, divided by the device time of the step).  Extra keys report the config-1
-per-M sweep (40 rotated copies of the 9728 x 2560 matrix per M), the M=1 stack cost (cost of
-M=8 vs M=1) and the CPU baseline.
+and out, per step, divided by the device time of the step).  `e2e` is the same steps with every
+step's activations copied in from pinned host memory and its logits copied out (copy stream,
+double buffers).  Extra keys (N = 1) report the config-1 per-M sweep (40 rotated copies of the
+9728 x 2560 matrix per M), the M=1 stack cost (cost of M=8 vs M=1), the CPU baseline, the
+config-3 verify step at M = 1/6/8/16 (fused kernels, CUDA graphs), config-4 decoding (greedy,
+MTP, prompt-lookup and scripted drafters); at every N, config 5 (the 64-layer dense model split
+over the ranks).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl skinny|reference]
+    python bench.py --case head|verify|attn ...   (small cases for profilers)
 
 With N > 1 (torchrun) every rank runs an independent replica of the stack (the path has no
 exchange step at this configuration): value = bytes of all ranks / max-over-ranks time.
