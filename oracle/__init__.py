@@ -14,8 +14,13 @@ pinned two ways:
     (skinny_mlx/qmm.py:96-115), executed in this container over a numpy stand-in for
     `mlx.core` (tests/golden/make_golden.py), which also pins the reference kernel's decode
     order and affine identity (skinny_mlx/qmm.py:21-86) through `qmm_metal_order` below;
-  * the speculative loop protocol is pinned by running the reference's own `speculative` and
-    `greedy` loops (skinny_mlx/spec.py:98-156) over this oracle's model.
+  * the decode-loop protocol is pinned by running the reference's own `greedy` and
+    `speculative` loops (skinny_mlx/spec.py:98-156), its `MTPDrafter` and `PromptLookupDrafter`
+    and its `HybridRollback` (skinny_mlx/rollback.py:19-73) over this oracle's float64 model
+    (oracle/model.py), through numpy stand-ins for mlx.core / mlx_lm; the token streams are the
+    fixture tests/golden/spec_streams.json (tests/golden/make_golden.py), which
+    tests/test_spec_golden.py holds this repository's loops to on the CPU and on the GPU.
+`qmm_small.npz` is oracle-generated (oracle.quant.qmm_ref), not reference output.
 The MLX CPU accumulation order itself is unpinned; every float comparison therefore uses the
 reference's own relative-error metric (skinny_mlx/qmm.py:185) with the tolerance BASELINE
 states (1.5e-2), never bit equality.

@@ -278,6 +278,10 @@ class Attention(nn.Module):
 
 
 class GatedDeltaNet(nn.Module):
+    # True: the recurrence runs in torch on CUDA too, so a module forward uses no kernel of this
+    # library besides the patched projections (an independent reference for the fused step)
+    torch_recurrence = False
+
     def __init__(self, cfg: ModelConfig, gen, dev):
         super().__init__()
         H, std = cfg.hidden, cfg.weight_std
@@ -321,7 +325,7 @@ class GatedDeltaNet(nn.Module):
         g = torch.exp(-torch.exp(self.A_log.float()) * F.softplus(a + self.dt_bias.float()))
         beta = torch.sigmoid(b)
         qb, kb, vb = (t.to(torch.bfloat16).contiguous() for t in (q, k, v))
-        if qkv.is_cuda:  # the CUDA path always runs the kernel; CPU runs (tests) use torch
+        if qkv.is_cuda and not GatedDeltaNet.torch_recurrence:  # CPU runs (tests) use torch
             from .gdn import recurrent
 
             y = recurrent(qb, kb, vb, g.contiguous(), beta.contiguous(), cache.state,
@@ -382,15 +386,19 @@ class DecoderLayer(nn.Module):
 class HybridModel(nn.Module):
     """forward(ids [T] int64, cache) -> (final normed hidden [T, H] bf16, logits [T, V] bf16)."""
 
-    def __init__(self, cfg: ModelConfig = SMALL, seed: int = 0, device="cuda"):
+    def __init__(self, cfg: ModelConfig = SMALL, seed: int = 0, device="cuda", init_device=None):
+        """init_device: where the seeded weights are drawn and quantized (default `device`).  The
+        CPU generator gives the same weights on every machine, so a model drawn on "cpu" and moved
+        to the GPU matches fixtures made from the same seed on a CPU-only host."""
         super().__init__()
         self.cfg = cfg
         self.device = torch.device(device)
-        gen = torch.Generator(device=self.device).manual_seed(seed)
-        ew = torch.randn(cfg.vocab, cfg.hidden, generator=gen, device=self.device) * cfg.weight_std
+        idev = torch.device(init_device) if init_device is not None else self.device
+        gen = torch.Generator(device=idev).manual_seed(seed)
+        ew = torch.randn(cfg.vocab, cfg.hidden, generator=gen, device=idev) * cfg.weight_std
         self.embed_tokens = QuantizedEmbedding(*quantize(ew))
         del ew
-        self.layers = nn.ModuleList([DecoderLayer(cfg, i, gen, self.device) for i in range(cfg.layers)])
+        self.layers = nn.ModuleList([DecoderLayer(cfg, i, gen, idev) for i in range(cfg.layers)])
         self.norm = RMSNorm(cfg.hidden, cfg.rms_eps)
         self.to(self.device)
 

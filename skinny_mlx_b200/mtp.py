@@ -21,17 +21,19 @@ from .model import AttnCache, DecoderLayer, HybridModel, RMSNorm, _qlinear
 
 
 class MTPHead(nn.Module):
-    def __init__(self, model: HybridModel, seed: int = 1):
+    def __init__(self, model: HybridModel, seed: int = 1, init_device=None):
+        """init_device: where the seeded weights are drawn (default the model's device)."""
         super().__init__()
         cfg = model.cfg
-        gen = torch.Generator(device=model.device).manual_seed(seed)
+        idev = torch.device(init_device) if init_device is not None else model.device
+        gen = torch.Generator(device=idev).manual_seed(seed)
         H = cfg.hidden
         self.cfg = cfg
         self.device = model.device
         self.pre_fc_norm_embedding = RMSNorm(H, cfg.rms_eps).to(model.device)
         self.pre_fc_norm_hidden = RMSNorm(H, cfg.rms_eps).to(model.device)
-        self.fc = _qlinear(H, 2 * H, gen, cfg.weight_std, model.device)
-        self.layer = DecoderLayer(cfg, cfg.attn_every - 1, gen, model.device)  # full attention
+        self.fc = _qlinear(H, 2 * H, gen, cfg.weight_std, idev)
+        self.layer = DecoderLayer(cfg, cfg.attn_every - 1, gen, idev)  # full attention
         assert not self.layer.is_linear
         self.norm = RMSNorm(H, cfg.rms_eps)
         self.to(model.device)

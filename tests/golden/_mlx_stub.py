@@ -1,8 +1,11 @@
-"""A numpy stand-in for the parts of `mlx.core` that the reference's pure-host code touches.
+"""A numpy stand-in for the parts of `mlx.core` and `mlx_lm` that the reference's pure-host code
+touches.
 
 Used only by tests/golden/make_golden.py, in the build container, to execute the reference's
-own Python (skinny_mlx/qmm.py `repack_for_skinny` and `config_for`, skinny_mlx/spec.py loops)
-and record golden vectors.  MLX itself is not installable here; nothing that needs Metal runs.
+own Python (skinny_mlx/qmm.py `repack_for_skinny` and `config_for`; skinny_mlx/spec.py `greedy`,
+`speculative`, `MTPDrafter` and skinny_mlx/rollback.py `HybridRollback` over the float64 oracle
+model, oracle/model.py) and record golden vectors.  MLX and mlx-lm are not installable here;
+nothing that needs Metal runs.
 """
 
 from __future__ import annotations
@@ -55,3 +58,23 @@ def install(quantized_matmul=None, extra: dict | None = None) -> types.ModuleTyp
     sys.modules["mlx.core"] = core
     sys.modules["mlx.nn"] = nn
     return core
+
+
+def install_mlx_lm(cache_mod, gated_delta_update) -> None:
+    """Register fake `mlx_lm.models.cache` (KVCache, make_prompt_cache) and
+    `mlx_lm.models.qwen3_5` (gated_delta_update), backed by the oracle's cache classes and
+    recurrence.  make_prompt_cache(model) returns model.make_cache(), as mlx_lm does for models
+    that define it."""
+    lm = types.ModuleType("mlx_lm")
+    models = types.ModuleType("mlx_lm.models")
+    cache = types.ModuleType("mlx_lm.models.cache")
+    cache.KVCache = cache_mod.KVCache
+    cache.ArraysCache = cache_mod.ArraysCache
+    cache.make_prompt_cache = lambda model, max_kv_size=None: model.make_cache()
+    q35 = types.ModuleType("mlx_lm.models.qwen3_5")
+    q35.gated_delta_update = gated_delta_update
+    lm.models = models
+    models.cache = cache
+    models.qwen3_5 = q35
+    sys.modules.update({"mlx_lm": lm, "mlx_lm.models": models, "mlx_lm.models.cache": cache,
+                        "mlx_lm.models.qwen3_5": q35})

@@ -7,6 +7,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
+from oracle.checks import argmax_violations
 from skinny_mlx_b200.dense import DenseModel, small_dense
 
 IDS = [5, 17, 300, 4000, 9, 2222, 123, 77]
@@ -119,6 +120,7 @@ def test_column_parallel_nccl_two_gpus(cuda_lib, dev):
         assert p.exitcode == 0
     # per-row results of the same kernel; stream-K split points differ with the shard sizes
     assert ((ref - got).abs().max() / ref.abs().max()).item() <= 1e-2
+    assert not argmax_violations(ref.numpy(), got.numpy())
 
 
 def _full(logits_shards: torch.Tensor) -> torch.Tensor:
@@ -143,7 +145,7 @@ def test_dense_fused_step_matches_module_path(cuda_lib, dev):
         ref = m(t, ca).float()
         got = _full(f(t, cb)).float()
         assert ((ref - got).abs().max() / ref.abs().max()).item() <= 1.5e-2
-        assert (ref.argmax(-1) == got.argmax(-1)).float().mean().item() >= 0.75
+        assert not argmax_violations(ref.cpu().numpy(), got.cpu().numpy())
     assert [c.length for c in ca] == [c.length for c in cb]
 
 
@@ -206,7 +208,7 @@ def test_dense_fused_step_two_gpus(cuda_lib, dev, exchange):
     assert errs == 0
     for ref, g in zip(refs, got):
         assert ((ref - g).abs().max() / ref.abs().max()).item() <= 1.5e-2
-        assert (ref.argmax(-1) == g.argmax(-1)).float().mean().item() >= 0.75
+        assert not argmax_violations(ref.numpy(), g.numpy())
 
 
 @pytest.mark.gpu
