@@ -2,14 +2,18 @@
  * skinny_b200 — C ABI of the B200 (sm_100a) flat multi-token verify path.
  *
  * Plain pointers and sizes only; every device pointer is caller-owned CUDA memory, `stream` is a
- * cudaStream_t passed as void*, and every call is stream-ordered on it.  No entry point allocates
- * device memory, synchronises the stream, or retains a pointer after it returns.
+ * cudaStream_t passed as void*, and every call is stream-ordered on it.  No compute entry point
+ * allocates device memory, synchronises the stream, or retains a pointer after it returns.  The
+ * exceptions are the peer-memory set-up calls (skinny_ipc_alloc allocates, zero-fills and
+ * synchronises the device once, before the buffer is shared; skinny_ipc_free frees), which a
+ * sharded step makes once at start-up, never per step.
  *
  * Return value: SKINNY_OK (0) or a negative status (see skinny_strerror).  Argument errors are
  * detected on the host before anything is launched.  Kernel-side errors (a bounded wait that ran
- * out, an activation outside the f16 range) are OR-ed into 32-bit word 0 of the workspace; read
- * it after the stream work completes.  A workspace that recorded an error must be zero-filled
- * again before reuse.
+ * out; an out-of-range token id in the embedding lookup) are OR-ed into 32-bit word 0 of the
+ * workspace; read it after the stream work completes.  A workspace that recorded an error must
+ * be zero-filled again before reuse.  Non-finite activations are not errors: they propagate to
+ * the affected outputs as NaN, as f32 arithmetic would.
  *
  * Reference interfaces replaced (paths inside rachittshah/skinny-mlx):
  *   skinny_repack_w4g64  <- skinny_mlx/qmm.py:96  repack_for_skinny(w)
@@ -100,10 +104,12 @@ int skinny_qmm_w4g64_grouped(int n, const void* const* x, const int* ldx, const 
  * better than the token-streaming qmm; skinny_qmm (Python) uses it from 64 tokens.  One launch. */
 int skinny_dequant_w4g64(const void* w_tc, int N, int K, void* out, int ldo, void* stream);
 
-/* Same contract with plain CUDA cores (no tcgen05), one thread per output.  A slow cross-check
- * used by the tests to localise a mismatch; it has no counterpart in the reference. */
-int skinny_qmm_w4g64_simt(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
-                          int N, int K, void* stream);
+/* The launch skinny_qmm_w4g64 makes for M tokens of an N x K weight on the current device:
+ * *token_cols = token columns read back per 128 x 64 unit (2, 4, 8 or 16), *split = 0 for the
+ * persistent stream-K grid over all units or S >= 1 for S CTAs per 128-row tile (a thread-block
+ * cluster summing S K-slices), *ctas = the grid size.  Replaces skinny_mlx/qmm.py:118
+ * config_for(m, k) -> (RF, SK), the Metal kernel's row-fragment and K-split choice. */
+int skinny_qmm_launch_config(int M, int N, int K, int* token_cols, int* split, int* ctas);
 
 /* ---------------------------------------------------------------------------------------------
  * Peer memory for a sharded step (one GPU per rank): buffers allocated by one rank and opened by
@@ -287,6 +293,13 @@ int skinny_gdn_rollback(int n_layers, float* const* state, const float* const* c
  * `stream` and then launches, without programmatic dependent launch. */
 int skinny_qmm_w4g64_noalloc(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
                              int N, int K, void* stream);
+/* The device error bits of the latest skinny_qmm_w4g64_noalloc call ordered before this one on
+ * `stream` (a bounded wait inside the kernel that ran out; 0 = none), copied as one uint32 to dst
+ * (device, pinned or pageable host memory) with a stream-ordered copy: read dst after the stream
+ * reaches it (a pageable destination makes the copy wait for the stream).  Enqueue it before the
+ * next no-alloc call on the device, which clears the word.  No counterpart in the reference; it
+ * allocates nothing. */
+int skinny_qmm_w4g64_noalloc_errors(void* dst, void* stream);
 
 #ifdef __cplusplus
 }

@@ -35,8 +35,7 @@ SIGNATURES = {
     "skinny_qmm_workspace_bytes": (c_size_t, [c_int, c_int]),
     "skinny_qmm_w4g64": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                  c_void_p, c_size_t, c_void_p]),
-    "skinny_qmm_w4g64_simt": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int,
-                                      c_int, c_void_p]),
+    "skinny_qmm_launch_config": (c_int, [c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "skinny_qmm_w4g64_grouped": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                          c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "skinny_xq_bytes": (c_size_t, [c_int, c_int]),
@@ -66,6 +65,7 @@ SIGNATURES = {
                                     c_int, c_int, c_int, c_int, c_void_p]),
     "skinny_qmm_w4g64_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int,
                                          c_int, c_void_p]),
+    "skinny_qmm_w4g64_noalloc_errors": (c_int, [c_void_p, c_void_p]),
 }
 
 

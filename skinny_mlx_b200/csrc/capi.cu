@@ -16,8 +16,8 @@ cudaError_t qmm_tc_launch_grouped(int n, const void* const* x, const int* ldx, c
                                   void* ws, cudaStream_t stream, bool pdl);
 cudaError_t qmm_repack_launch(const uint32_t* w, const uint16_t* s, const uint16_t* b, void* w_tc,
                               int N, int K, cudaStream_t stream);
-cudaError_t qmm_simt_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
-                            int N, int K, cudaStream_t stream);
+cudaError_t qmm_launch_config(int M, int N, int K, int* token_cols, int* split, int* ctas);
+cudaError_t qmm_noalloc_error_copy(void* dst, cudaStream_t stream);
 cudaError_t qmm_dequant_launch(const void* w_tc, int N, int K, void* out, int ldo, cudaStream_t stream);
 bool qmm_noalloc_fits(int N, int K);
 size_t spec_accept_ws_bytes();
@@ -204,17 +204,6 @@ int skinny_dequant_w4g64(const void* w_tc, int N, int K, void* out, int ldo, voi
   return cuda_status(skinny::qmm_dequant_launch(w_tc, N, K, out, ldo, static_cast<cudaStream_t>(stream)));
 }
 
-int skinny_qmm_w4g64_simt(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
-                          int N, int K, void* stream) {
-  if (!x || !w_tc || !out) return SKINNY_ERR_INVALID_ARG;
-  int st = check_qmm_shape(N, K);
-  if (st != SKINNY_OK) return st;
-  if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
-  if (ldx < K || ldo < N) return SKINNY_ERR_INVALID_ARG;
-  return cuda_status(skinny::qmm_simt_launch(x, ldx, w_tc, out, ldo, M, N, K,
-                                             static_cast<cudaStream_t>(stream)));
-}
-
 int skinny_qmm_w4g64_noalloc(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
                              int N, int K, void* stream) {
   if (!x || !w_tc || !out) return SKINNY_ERR_INVALID_ARG;
@@ -226,6 +215,19 @@ int skinny_qmm_w4g64_noalloc(const void* x, int ldx, const void* w_tc, void* out
   if (!aligned16(x) || (ldx % 8) != 0 || !aligned16(w_tc)) return SKINNY_ERR_ALIGNMENT;
   return cuda_status(skinny::qmm_tc_launch_noalloc(x, ldx, w_tc, out, ldo, M, N, K,
                                                    static_cast<cudaStream_t>(stream)));
+}
+
+int skinny_qmm_w4g64_noalloc_errors(void* dst, void* stream) {
+  if (!dst) return SKINNY_ERR_INVALID_ARG;
+  return cuda_status(skinny::qmm_noalloc_error_copy(dst, static_cast<cudaStream_t>(stream)));
+}
+
+int skinny_qmm_launch_config(int M, int N, int K, int* token_cols, int* split, int* ctas) {
+  if (!token_cols || !split || !ctas) return SKINNY_ERR_INVALID_ARG;
+  const int st = check_qmm_shape(N, K);
+  if (st != SKINNY_OK) return st;
+  if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
+  return cuda_status(skinny::qmm_launch_config(M, N, K, token_cols, split, ctas));
 }
 
 // A peer-sync descriptor: absent, or a device epoch with an error word, 1..8 ranks, and for a

@@ -59,6 +59,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "peer.cuh"
@@ -807,54 +808,25 @@ __global__ void qmm_repack_kernel(const uint32_t* __restrict__ w, const uint16_t
   *reinterpret_cast<uint32_t*>(base + kUnitNibBytes + r * 4) = sbw;
 }
 
-// Plain CUDA-core cross-check of the relaid format: decodes the same units and computes
-// sum_g s * sum(x q) + b * sum(x) in f32 from x as given.  One thread per (row, token); tests only.
-__global__ void qmm_simt_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
-                                const uint8_t* __restrict__ w_tc, __nv_bfloat16* __restrict__ out,
-                                int ldo, int M, int N, int K) {
-  const int G = K / kGroup;
-  const int tile = blockIdx.x;
-  const int r = threadIdx.x;
-  const int tok = blockIdx.y;
-  const int n = tile * kTileRows + r;
-  if (n >= N || tok >= M) return;
-  float acc = 0.f;
-  for (int g = 0; g < G; ++g) {
-    const uint8_t* base = w_tc + (static_cast<long long>(tile) * G + g) * kUnitWBytes;
-    const uint32_t sbw = *reinterpret_cast<const uint32_t*>(base + kUnitNibBytes + r * 4);
-    const float sc = __uint_as_float(sbw << 16);
-    const float bi = __uint_as_float(sbw & 0xFFFF0000u);
-    const uint4 c0 = *reinterpret_cast<const uint4*>(base + r * 16);
-    const uint4 c1 = *reinterpret_cast<const uint4*>(base + 2048 + r * 16);
-    uint32_t a[16];
-    decode_i8(c0, c1, a);
-    float gs = 0.f, xsum = 0.f;
-    for (int col = 0; col < kGroup; ++col) {
-      const int q = (static_cast<int>(static_cast<int8_t>(a[col >> 2] >> (8 * (col & 3)))) >> 4) + 8;
-      const float xv = __bfloat162float(x[static_cast<size_t>(tok) * ldx + g * kGroup + col]);
-      gs = fmaf(static_cast<float>(q), xv, gs);
-      xsum += xv;
-    }
-    acc = fmaf(sc, gs, fmaf(bi, xsum, acc));
-  }
-  out[static_cast<size_t>(tok) * ldo + n] = __float2bfloat16_rn(acc);
-}
-
 // ---------------------------------------------------------------------------------------------
 // Host launchers (called from the C-ABI layer)
 // ---------------------------------------------------------------------------------------------
-static int g_num_sms[64] = {0};
-static bool g_attr_set[64][4] = {};
+// Per-device caches, filled on first use.  Several host threads may fill an entry at once; they
+// store the same value, and the entries are atomics so that this is not a data race.  They are
+// keyed by device index and so assume the device's primary context (the one the CUDA runtime
+// API uses); a host that switches between driver-API contexts on one device must not share them.
+static std::atomic<int> g_num_sms[64];
+static std::atomic<bool> g_attr_set[64][4];
 
 int device_sm_count(int dev) {
   if (dev < 0 || dev >= 64) return 148;
-  if (g_num_sms[dev] == 0) {
-    int v = 0;
+  int v = g_num_sms[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
       v = 148;
-    g_num_sms[dev] = v;
+    g_num_sms[dev].store(v, std::memory_order_relaxed);
   }
-  return g_num_sms[dev];
+  return v;
 }
 
 static void pdl_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, bool pdl) {
@@ -867,12 +839,12 @@ static void pdl_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, bool 
 template <int NT>
 static cudaError_t set_smem_attr(int dev) {
   constexpr int slot = NT == 2 ? 0 : NT == 4 ? 1 : NT == 8 ? 2 : 3;
-  if (dev >= 0 && dev < 64 && !g_attr_set[dev][slot]) {
+  if (dev >= 0 && dev < 64 && !g_attr_set[dev][slot].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(qmm_w4g64_tc_kernel<NT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(qmm_smem_bytes(NT)));
     if (e != cudaSuccess) return e;
-    g_attr_set[dev][slot] = true;
+    g_attr_set[dev][slot].store(true, std::memory_order_release);
   }
   return cudaSuccess;
 }
@@ -901,7 +873,7 @@ static cudaError_t launch_tc(const QmmParams& prm, int dev, cudaStream_t stream,
 // Clusters of S CTAs of the qmm kernel that can be resident at once on device `dev`: the
 // minimum over the four token-count variants, so that the split chosen from it is the same for
 // every M (the per-token results stay independent of M).  Cached per (device, S).
-static int g_max_clusters[64][9] = {};
+static std::atomic<int> g_max_clusters[64][9];
 
 template <int NT>
 static int clusters_of(int S) {
@@ -926,7 +898,8 @@ static int clusters_of(int S) {
 
 static int max_active_clusters(int dev, int S) {
   if (dev < 0 || dev >= 64 || S < 2 || S > 8) return 0;
-  if (g_max_clusters[dev][S] == 0) {
+  int cached = g_max_clusters[dev][S].load(std::memory_order_relaxed);
+  if (cached == 0) {
     if (set_smem_attr<2>(dev) != cudaSuccess || set_smem_attr<4>(dev) != cudaSuccess ||
         set_smem_attr<8>(dev) != cudaSuccess || set_smem_attr<16>(dev) != cudaSuccess)
       return 0;
@@ -934,9 +907,10 @@ static int max_active_clusters(int dev, int S) {
     n = std::min(n, clusters_of<4>(S));
     n = std::min(n, clusters_of<8>(S));
     n = std::min(n, clusters_of<16>(S));
-    g_max_clusters[dev][S] = n > 0 ? n : -1;
+    cached = n > 0 ? n : -1;
+    g_max_clusters[dev][S].store(cached, std::memory_order_relaxed);
   }
-  return g_max_clusters[dev][S];
+  return cached;
 }
 
 // Work split of a single-matrix call with `tiles` 128-row tiles of G groups on C CTAs.
@@ -951,6 +925,22 @@ static int choose_split(int dev, int tiles, int G, int C) {
   for (; S > 1; --S)
     if (max_active_clusters(dev, S) >= tiles) return S;
   return 1;
+}
+
+// What a single-matrix call (skinny_qmm_w4g64) launches for M tokens on the current device: the
+// token columns read back per unit, the split (0 = persistent stream-K over all units, S >= 1 =
+// S CTAs per 128-row tile) and the qmm grid size.
+cudaError_t qmm_launch_config(int M, int N, int K, int* token_cols, int* split, int* ctas) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const int C = device_sm_count(dev);
+  const QmmShape sh = qmm_shape(N, K);
+  const int S = choose_split(dev, static_cast<int>(sh.T), sh.G, C);
+  *token_cols = M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16;
+  *split = S;
+  *ctas = S > 0 ? static_cast<int>(sh.T) * S : static_cast<int>(sh.U < C ? sh.U : C);
+  return cudaSuccess;
 }
 
 static cudaError_t launch_xprep(const XPrepParams& xp, cudaStream_t stream, bool pdl) {
@@ -1171,6 +1161,18 @@ cudaError_t qmm_tc_launch_noalloc(const void* x, int ldx, const void* w_tc, void
                            scratch + kNoAllocXqOff, kNoAllocMaxGroups, C_cap, dev, stream, false);
 }
 
+// Copies the static scratch's error word (the device error bits of the latest no-alloc call
+// ordered before it on `stream`) to `dst` (device, pinned or pageable host memory), stream-ordered.
+cudaError_t qmm_noalloc_error_copy(void* dst, cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  uint8_t* scratch = nullptr;
+  e = noalloc_scratch(dev, &scratch);
+  if (e != cudaSuccess) return e;
+  return cudaMemcpyAsync(dst, scratch, sizeof(uint32_t), cudaMemcpyDefault, stream);
+}
+
 cudaError_t qmm_tc_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M, int N,
                           int K, void* ws, int /*C*/, cudaStream_t stream, bool pdl) {
   void* o = out;
@@ -1226,16 +1228,6 @@ cudaError_t qmm_dequant_launch(const void* w_tc, int N, int K, void* out, int ld
   const QmmShape sh = qmm_shape(N, K);
   qmm_dequant_kernel<<<static_cast<unsigned>(sh.U), 256, 0, stream>>>(static_cast<const uint8_t*>(w_tc), N, K,
                                                                     static_cast<__nv_bfloat16*>(out), ldo);
-  return cudaGetLastError();
-}
-
-cudaError_t qmm_simt_launch(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
-                            int N, int K, cudaStream_t stream) {
-  const QmmShape sh = qmm_shape(N, K);
-  dim3 grid(sh.T, M);
-  qmm_simt_kernel<<<grid, kTileRows, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), ldx,
-                                                   static_cast<const uint8_t*>(w_tc),
-                                                   static_cast<__nv_bfloat16*>(out), ldo, M, N, K);
   return cudaGetLastError();
 }
 

@@ -12,8 +12,9 @@
 // (chunk, row).  Each CTA reduces its chunk to (max value, lowest index attaining it) and publishes
 // it; the CTA that arrives last (global counter in the workspace) reduces the partials of every
 // row in chunk order, runs the prefix comparison, writes the result and re-arms the counter.
-// Ties resolve to the lowest vocabulary index (first occurrence, as numpy/MLX argmax); a NaN
-// logit never wins a comparison.
+// Ties resolve to the lowest vocabulary index (first occurrence), and a NaN counts as larger than
+// every number, so the first NaN of a row wins: the order numpy's argmax uses (the reference's
+// `.tolist()` of mx.argmax is compared with numpy's in its own checks).
 #include <cstdint>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -36,8 +37,11 @@ struct SpecWs {
 
 size_t spec_accept_ws_bytes() { return sizeof(SpecWs); }
 
-// (a, ia) better than (b, ib): larger value, or equal value and lower index.  NaN never wins.
+// (a, ia) better than (b, ib): larger value, or equal value and lower index; NaN above every
+// number, the lower index among NaNs.
 __device__ __forceinline__ bool better(float a, int ia, float b, int ib) {
+  const bool an = a != a, bn = b != b;
+  if (an || bn) return an && (!bn || ia < ib);
   return a > b || (a == b && ia < ib);
 }
 

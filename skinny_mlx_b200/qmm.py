@@ -4,9 +4,12 @@ Mirrors skinny_mlx/qmm.py (rachittshah/skinny-mlx):
 
 * ``repack_for_skinny`` (qmm.py:96) relays MLX 4-bit packs once at load, here into the
   tcgen05 unit order (128 rows x 64 columns per 4608-byte unit, scales and biases folded in).
-* ``skinny_qmm`` (qmm.py:132) runs the sm_100a kernel: x [M, K] @ dequant(W)[N, K]^T -> [M, N],
-  computing sum_g s * sum(x q) + b * sum(x) per 64-group in f32 (the affine identity of
-  qmm.py:8-9); the tensor-core products use bf16 x as given and exact nibbles, in f32.
+* ``skinny_qmm`` (qmm.py:132) runs the sm_100a kernel: x [M, K] @ dequant(W)[N, K]^T -> [M, N]
+  in x's dtype, computing sum_g s * sum(x q) + b * sum(x) per 64-group in f32 (the affine
+  identity of qmm.py:8-9).  The tensor-core products are exact integer dot products (tcgen05
+  kind::i8): the nibbles as int8 16 (q - 8), x as two int8 digits of 16-bit fixed point per
+  (token, group) with a power-of-two scale, so the only rounding before the f32 accumulation is
+  x to 16 significant bits relative to its group maximum.
 * ``qmm`` is the drop-in ``mx.quantized_matmul(x, w, scales, biases, transpose=True,
   group_size=64, bits=4)`` entry: MLX packing in, relayout cached per weight.
 * ``quantize`` produces MLX's packing with the affine rule scale = (max - min) / 15,
@@ -166,21 +169,26 @@ def reset_workspaces() -> None:
             ws.zero_()
 
 
-def config_for(m: int, n: int, k: int) -> dict:
-    """Launch configuration the library picks (mirrors skinny_mlx/qmm.py:118 config_for).
+def config_for(m: int, k: int, n: int = 9728) -> tuple[int, int]:
+    """The launch choice for M tokens of an N x K weight on the current device, as the pair the
+    reference's heuristic returns (skinny_mlx/qmm.py:118 config_for(m, k) -> (RF, SK): row
+    fragments per simdgroup, K-splits per threadgroup of the Metal kernel).  Here the two knobs
+    are (token columns read back per 128 x 64 unit: 2, 4, 8 or 16; K-split per 128-row tile: 0 =
+    the persistent stream-K grid, S >= 1 = S CTAs per tile summing S K-slices in a cluster).  The
+    split depends on N and the device (how many tiles, how many clusters fit), so N is an argument
+    (default: config 1's 9728).  Read from the library (skinny_qmm_launch_config), so it is what
+    skinny_qmm actually launches; the reference's CONFIG_OVERRIDE has no B200 counterpart."""
+    import ctypes
 
-    ``token_slots``: token columns each CTA reads back from TMEM (2, 4, 8 or 16);
-    ``units``: 128-row x 64-column units; ``ctas``: stream-K CTAs (one per SM, at most units).
-    """
-    t = (n + 127) // 128
-    units = t * (k // GROUP)
-    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    slots = 2 if m <= 2 else 4 if m <= 4 else 8 if m <= 8 else 16
-    return {"token_slots": slots, "units": units, "ctas": min(sms, units)}
+    tc, sp, ctas = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    _lib.call("skinny_qmm_launch_config", m, n, k, ctypes.byref(tc), ctypes.byref(sp), ctypes.byref(ctas))
+    return tc.value, sp.value
 
 
 def skinny_qmm(x: torch.Tensor, w: SkinnyWeight, out: torch.Tensor | None = None) -> torch.Tensor:
-    """x [..., K] (bf16) @ dequant(W)^T -> [..., N] bf16 through the tcgen05 kernel.
+    """x [..., K] @ dequant(W)^T -> [..., N] through the tcgen05 kernel, in x's dtype (as the
+    reference returns; the kernel reads bf16 activations and writes bf16, so other dtypes are cast
+    on the way in and out).  `out`, when given, is a bf16 [M, N] buffer and is returned as is.
 
     Token counts above 16 are processed in 16-token chunks by the same kernel (each token's
     result does not depend on the chunking); from PREFILL_TOKENS tokens (a prompt) the weight is
@@ -198,8 +206,9 @@ def skinny_qmm(x: torch.Tensor, w: SkinnyWeight, out: torch.Tensor | None = None
     if not x2.is_contiguous() or x2.data_ptr() % 16:
         x2 = x2.contiguous()
     m = x2.shape[0]
+    cast = x.dtype if out is None and x.dtype != torch.bfloat16 else None
     if m == 0:
-        return x.new_empty(*lead, w.N, dtype=torch.bfloat16)
+        return x.new_empty(*lead, w.N, dtype=cast or torch.bfloat16)
     dev = x2.device
     if out is None:
         out = torch.empty(m, w.N, dtype=torch.bfloat16, device=dev)
@@ -212,7 +221,8 @@ def skinny_qmm(x: torch.Tensor, w: SkinnyWeight, out: torch.Tensor | None = None
             _lib.check("skinny_dequant_w4g64", L.skinny_dequant_w4g64(
                 w.w_tc.data_ptr(), w.N, w.K, wd.data_ptr(), w.K, _stream_handle(dev)))
             torch.matmul(x2, wd.t(), out=out)
-        return out.reshape(*lead, w.N)
+        y = out.reshape(*lead, w.N)
+        return y if cast is None else y.to(cast)
     with torch.cuda.device(dev):
         need = L.skinny_qmm_workspace_bytes(w.N, w.K)
         ws = get_workspace(dev, need)
@@ -223,7 +233,8 @@ def skinny_qmm(x: torch.Tensor, w: SkinnyWeight, out: torch.Tensor | None = None
             _lib.check("skinny_qmm_w4g64", L.skinny_qmm_w4g64(
                 xs.data_ptr(), w.K, w.w_tc.data_ptr(), out[c0].data_ptr(), w.N, mc, w.N, w.K,
                 ws.data_ptr(), ws.numel(), stream))
-    return out.reshape(*lead, w.N)
+    y = out.reshape(*lead, w.N)
+    return y if cast is None else y.to(cast)
 
 
 MAX_GROUP = 192
@@ -271,20 +282,6 @@ def skinny_qmm_grouped(xs, weights, outs=None):
     return outs
 
 
-def skinny_qmm_simt(x: torch.Tensor, w: SkinnyWeight) -> torch.Tensor:
-    """CUDA-core cross-check of the relaid format (tests only)."""
-    _require_cuda(x, "x")
-    x2 = x.reshape(-1, w.K).to(torch.bfloat16).contiguous()
-    m = x2.shape[0]
-    out = torch.empty(m, w.N, dtype=torch.bfloat16, device=x2.device)
-    with torch.cuda.device(x2.device):
-        for c0 in range(0, m, MAX_TOKENS):
-            mc = min(MAX_TOKENS, m - c0)
-            _lib.call("skinny_qmm_w4g64_simt", x2[c0].data_ptr(), w.K, w.w_tc.data_ptr(),
-                      out[c0].data_ptr(), w.N, mc, w.N, w.K, _stream_handle(x2.device))
-    return out.reshape(*x.shape[:-1], w.N)
-
-
 # ---------------------------------------------------------------------------------------------
 # MLX-style drop-in entry
 # ---------------------------------------------------------------------------------------------
@@ -303,7 +300,7 @@ def qmm(x: torch.Tensor, w_packed: torch.Tensor, scales: torch.Tensor, biases: t
     bits=4)`` (the call skinny_mlx/patch.py:35 and qmm.py:183 make) on MLX-packed weights.
 
     The relayout is done on first use and cached per (w, scales, biases) storage and version.
-    Returns bf16 (x of another dtype is cast to bf16 first).
+    Returns x's dtype, as mx.quantized_matmul does.
     """
     if group_size != GROUP or bits != BITS:
         raise ValueError("skinny qmm supports group_size=64, bits=4 only")
@@ -318,5 +315,5 @@ def qmm(x: torch.Tensor, w_packed: torch.Tensor, scales: torch.Tensor, biases: t
 
 
 __all__ = ["GROUP", "BITS", "MAX_TOKENS", "quantize", "dequantize", "SkinnyWeight",
-           "repack_for_skinny", "skinny_qmm", "skinny_qmm_grouped", "skinny_qmm_simt", "qmm", "config_for",
+           "repack_for_skinny", "skinny_qmm", "skinny_qmm_grouped", "qmm", "config_for",
            "device_errors", "reset_workspaces", "workspace_bytes"]

@@ -13,6 +13,15 @@ from skinny_mlx_b200.dense import DenseModel, small_dense
 IDS = [5, 17, 300, 4000, 9, 2222, 123, 77]
 
 
+def _free_port() -> int:
+    """A TCP port on 127.0.0.1 that nothing listens on now (rendezvous of the spawned ranks)."""
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
 def _rank(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import datetime
@@ -38,7 +47,8 @@ def test_column_parallel_equals_unsharded_on_cpu():
     ref = ref_m(torch.tensor(IDS[5:]), caches).float()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, 29517, q)) for r in range(2)]
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
     got = q.get(timeout=300)
@@ -111,7 +121,8 @@ def test_column_parallel_nccl_two_gpus(cuda_lib, dev):
     ref = m(torch.tensor(IDS[5:], device=dev), caches).float().cpu()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_gpu_rank, args=(r, 2, 29617, q)) for r in range(2)]
+    port = _free_port()
+    procs = [ctx.Process(target=_gpu_rank, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
     got = q.get(timeout=300)
@@ -197,7 +208,7 @@ def test_dense_fused_step_two_gpus(cuda_lib, dev, exchange):
             for ids in (IDS[:5], IDS[5:], IDS[:1], (IDS * 2)[:16])]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29657 if exchange == "peer" else 29667
+    port = _free_port()
     procs = [ctx.Process(target=_gpu_fused_rank, args=(r, 2, port, q, exchange)) for r in range(2)]
     for p in procs:
         p.start()

@@ -87,17 +87,34 @@ def test_qmm_shapes_and_tails(cuda_lib, dev, n, k, m):
     assert quant.rel_err(quant.qmm_ref(xf, packed, s, b), y) <= TIGHT
 
 
-def test_qmm_tc_matches_simt_crosscheck(cuda_lib, dev):
-    from skinny_mlx_b200.qmm import repack_for_skinny, skinny_qmm, skinny_qmm_simt
+def test_config_for_is_the_launch_and_output_dtype_follows_x(cuda_lib, dev):
+    """config_for (the reference's (RF, SK) heuristic, skinny_mlx/qmm.py:118) reports the launch
+    the library makes: token columns by M, a K-split per tile for matrices with fewer tiles than
+    SMs (S CTAs per tile, S <= 8) and the persistent stream-K grid (split 0) for larger ones.
+    skinny_qmm and qmm return x's dtype (skinny_mlx/qmm.py:135,151)."""
+    from skinny_mlx_b200.qmm import config_for, qmm, repack_for_skinny, skinny_qmm
 
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    for m, cols in ((1, 2), (2, 2), (3, 4), (4, 4), (6, 8), (8, 8), (12, 16), (16, 16)):
+        assert config_for(m, 2560)[0] == cols
+    for n, k in ((9728, 2560), (2560, 9728), (5120, 2560), (2560, 2048)):
+        tiles = (n + 127) // 128
+        _, split = config_for(8, k, n)
+        assert 1 <= split <= min(8, max(1, sms // tiles)), (n, k, split)
+    assert config_for(8, 2560, 151936)[1] == 0  # more tiles than SMs: stream-K
+    with pytest.raises(Exception):
+        config_for(17, 2560)
     (packed, s, b), (tw, ts, tb) = make_weight(1024, 1024, 9, dev)
     sw = repack_for_skinny(tw, ts, tb)
-    xf, x = make_x(16, 1024, 10, dev)
-    a = skinny_qmm(x, sw).float()
-    c = skinny_qmm_simt(x, sw).float()
+    xf, x = make_x(8, 1024, 10, dev)
     ref = quant.qmm_ref(xf, packed, s, b)
-    assert quant.rel_err(ref, c.cpu().numpy()) <= TIGHT
-    assert quant.rel_err(c.cpu().numpy(), a.cpu().numpy()) <= TIGHT
+    for dt in (torch.float16, torch.float32):
+        y = skinny_qmm(x.to(dt), sw)
+        assert y.dtype == dt
+        assert quant.rel_err(ref, y.float().cpu().numpy()) <= TIGHT
+        y2 = qmm(x.to(dt), tw, ts, tb)
+        assert y2.dtype == dt
+        assert torch.equal(y2, y)
 
 
 def test_qmm_token_count_invariance(cuda_lib, dev):

@@ -17,6 +17,8 @@ def test_oracle_acceptance_rule():
     lg[0, 1] = 2.0  # tie between 1 and 3: first occurrence wins
     assert ospec.accept(lg, [1, 5, 7])[0] == 3
     assert ospec.accept(lg[:1], [])[1] == [1]
+    lg[1, 8] = np.nan  # a NaN is above every number (numpy's argmax)
+    assert ospec.accept(lg, [1, 8, 7]) == (3, [1, 8, 7, 9], [1, 8, 7, 9])
 
 
 def _case(rng, rows, v, n_match, tie=False):
@@ -65,5 +67,12 @@ def test_device_acceptance_special_values(cuda_lib, dev):
     x[2, :5] = np.nan
     lg = torch.from_numpy(quant.f32_to_bf16_bits(x).view(np.int16)).view(torch.bfloat16).to(dev)
     draft = [17, 0]
-    n, toks, _ = ospec.accept(quant.bf16_bits_to_f32(quant.f32_to_bf16_bits(x)), draft)
+    n, toks, pred = ospec.accept(quant.bf16_bits_to_f32(quant.f32_to_bf16_bits(x)), draft)
+    assert pred == [17, 0, 0]  # numpy's order: the first NaN of a row wins
+    assert accept(lg, torch.tensor(draft, dtype=torch.int32, device=dev)) == (n, toks)
+    x[2, :5] = -np.inf
+    x[2, 100] = np.nan
+    lg = torch.from_numpy(quant.f32_to_bf16_bits(x).view(np.int16)).view(torch.bfloat16).to(dev)
+    n, toks, pred = ospec.accept(quant.bf16_bits_to_f32(quant.f32_to_bf16_bits(x)), draft)
+    assert pred == [17, 0, 100]
     assert accept(lg, torch.tensor(draft, dtype=torch.int32, device=dev)) == (n, toks)

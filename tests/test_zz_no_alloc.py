@@ -79,3 +79,30 @@ def test_noalloc_rejects_shapes_over_the_scratch(cuda_lib, dev):
         ctypes.c_void_p(out.data_ptr()), 64, 1, 64, kbig,
         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert st == SCRATCH_LIMIT
+
+
+def test_noalloc_shape_switch_and_error_word(cuda_lib, dev):
+    """Different shapes back to back on one stream, sharing the scratch: a cluster split-K shape
+    (fewer tiles than SMs), a stream-K shape whose tiles straddle CTAs (it uses the scratch's
+    per-tile arrival counters, which every call clears first), a tail shape, then the first shape
+    again.  Each result equals the oracle; after each call the error word, copied out by
+    skinny_qmm_w4g64_noalloc_errors into device memory and into pinned host memory, is 0."""
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    err_dev = torch.full((1,), -1, dtype=torch.int32, device=dev)
+    err_host = torch.full((1,), -1, dtype=torch.int32).pin_memory()
+    for i, (n, k, m) in enumerate([(2560, 9728, 8), (20000, 256, 16), (200, 192, 3), (2560, 9728, 8)]):
+        (packed, s, b), sw = _weight(n, k, 90 + i % 3, dev)
+        rng = np.random.default_rng(900 + i)
+        xb = quant.f32_to_bf16_bits(rng.standard_normal((m, k)).astype(np.float32))
+        x = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).to(dev)
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        assert _noalloc(cuda_lib, x, sw, out) == 0
+        assert cuda_lib.skinny_qmm_w4g64_noalloc_errors(ctypes.c_void_p(err_dev.data_ptr()), stream) == 0
+        assert cuda_lib.skinny_qmm_w4g64_noalloc_errors(ctypes.c_void_p(err_host.data_ptr()), stream) == 0
+        torch.cuda.synchronize()
+        assert int(err_dev.item()) == 0 and int(err_host.item()) == 0
+        ref = quant.qmm_ref(quant.bf16_bits_to_f32(xb), packed, s, b)
+        assert quant.rel_err(ref, out.float().cpu().numpy()) <= TOL, (n, k, m)
+        err_dev.fill_(-1)
+        err_host.fill_(-1)
+    assert cuda_lib.skinny_qmm_w4g64_noalloc_errors(None, stream) == -1
