@@ -42,6 +42,7 @@ import torch  # noqa: E402
 
 FALLBACK_HBM_GBS = 6650.0
 M_STACK = 8
+WORKLOAD = "config 2: 129-projection hybrid stack (hidden 2560, 32 layers, 4-bit g64) at M=8"
 KERNELS_PER_CALL = 2  # every qmm call (single or grouped) launches the x-prep and the qmm kernel
 
 
@@ -425,7 +426,8 @@ def config4_spec(model, dev, n_tokens=256, prompt_len=512, fwd=None):
     GraphedStep; every run reuses one cache, and each configuration runs once untimed first."""
     from skinny_mlx_b200.mtp import MTPHead
     from skinny_mlx_b200.patch import patch_model
-    from skinny_mlx_b200.spec import GraphedMTPDrafter, PromptLookupDrafter, ScriptedDrafter, greedy, speculative
+    from skinny_mlx_b200.spec import (GraphedMTPDrafter, MTPDrafter, PromptLookupDrafter, ScriptedDrafter,
+                                      ScriptedTreeDrafter, greedy, speculative, speculative_tree)
 
     g = torch.Generator().manual_seed(512)
     prompt = torch.randint(0, model.cfg.vocab, (prompt_len,), generator=g).tolist()
@@ -448,9 +450,9 @@ def config4_spec(model, dev, n_tokens=256, prompt_len=512, fwd=None):
     out = {"greedy_tok_s": round(n_tokens / t_g, 1), "tokens": n_tokens, "prompt": prompt_len,
            "greedy_identical": got_g == ref}
 
-    def record(name, k, mk):
+    def record(name, k, mk, loop=speculative):
         st, d = {}, mk()  # one drafter for the untimed and the timed run (its state resets in begin)
-        got, t = timed(lambda n: speculative(step, prompt, n, d, k, st, cache=cache))
+        got, t = timed(lambda n: loop(step, prompt, n, d, k, st, cache=cache))
         j = next((i for i, (a, b) in enumerate(zip(ref, got)) if a != b), None)
         out[name] = {"tok_s": round(n_tokens / t, 1), "tokens_per_step": round(st["tokens_per_step"], 3),
                      "identical_first": n_tokens if j is None else j,
@@ -460,6 +462,15 @@ def config4_spec(model, dev, n_tokens=256, prompt_len=512, fwd=None):
         record(f"K{k}", k, lambda: GraphedMTPDrafter(model, head, vocab=32768, seed=3))
     record("K2_scripted_p0.81", 2, lambda: ScriptedDrafter(ref, 0.81, model.cfg.vocab, dev, seed=5))
     record("K3_prompt_lookup", 3, lambda: PromptLookupDrafter(3, dev))
+    # draft trees verified in one pass (top-2 at every chain position: M = 2K + 1 rows) beside
+    # chains of the same depth at the same per-token acceptance
+    record("K3_scripted_p0.81", 3, lambda: ScriptedDrafter(ref, 0.81, model.cfg.vocab, dev, seed=5))
+    record("K3_tree_scripted_p0.81", 3, lambda: ScriptedTreeDrafter(ref, 0.81, model.cfg.vocab, dev, seed=5),
+           speculative_tree)
+    record("K3_tree_scripted_p0.6", 3, lambda: ScriptedTreeDrafter(ref, 0.6, model.cfg.vocab, dev, seed=6),
+           speculative_tree)
+    record("K3_scripted_p0.6", 3, lambda: ScriptedDrafter(ref, 0.6, model.cfg.vocab, dev, seed=6))
+    record("K3_mtp_tree", 3, lambda: MTPDrafter(model, head, vocab=32768, seed=3), speculative_tree)
     return out
 
 
@@ -578,7 +589,7 @@ def run_reference(args, world, rank):
         "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(2024755200 / bps * 1e3, 1), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config 2: 129-projection hybrid stack, M=8", "tokens": M_STACK},
+        "config": {"workload": WORKLOAD, "tokens": M_STACK},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": per_step[0]["cores"],
                          "kind": "port",
                          "sample": "oracle f32 dequant+GEMM over consecutive stack projections, ~4 s of "
@@ -667,8 +678,7 @@ def run_skinny(args, world, rank, local):
             "scaling": "weak", "vs_baseline": None, "data": "synthetic",
             "dtype": "s8 x s8 -> s32 tensor-core products (4-bit weights as int8, activations as two int8 "
                      "digits of 16-bit fixed point), f32 scale/bias and accumulation",
-            "config": {"workload": "config 2: 129-projection hybrid stack (hidden 2560, 32 layers, 4-bit g64) at M=8",
-                       "tokens": M_STACK, "weight_bytes_per_step": 2024755200,
+            "config": {"workload": WORKLOAD, "tokens": M_STACK, "weight_bytes_per_step": 2024755200,
                        "algorithmic_bytes_per_step": per_step_bytes, "l2": "inputs larger than L2 (2.0 GB of weights)",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -692,6 +702,10 @@ def run_skinny(args, world, rank, local):
             "config3_verify_step_ms_module_path": c3m,
             "config4_spec": c4,
             "config5_dense_tp": c5,
+            # the sharded workload's own step time at this rank count (the headline value above is
+            # replica throughput at N > 1), for the per-N scaling records
+            "config5_m8_ms": c5["M8"]["ms_per_step"] if c5 else None,
+            "config5_m16_ms": c5["M16"]["ms_per_step"] if c5 else None,
             "device_error_bits": errs,
         }
         print(json.dumps(line), flush=True)

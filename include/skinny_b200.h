@@ -203,6 +203,19 @@ int skinny_gdn_fused(const void* proj, int ldp, void* conv, void* conv_full, con
                      float* ckpt, void* xq, void* o_out, int T, int Hv, int Hk, int W, void* err_word,
                      void* stream);
 
+/* skinny_gdn_fused over a token TREE of T nodes in topological order: parent (device int32 [T])
+ * with parent[0] = -1 and parent[t] in [0, t).  Node t's conv window is the W inputs before it on
+ * its ancestor path (the cached window above the root) and its recurrence starts from its
+ * parent's state.  ckpt [T, Hv, 128, 128] (required) receives the state after EVERY node and
+ * conv_full (required) the conv input [W + T, C]; state and conv are only read (the rollback,
+ * skinny_gdn_rollback_tree, selects the accepted path).  A malformed parent array sets
+ * kErrBitBadInput in err_word and is read as a chain.  Builds the branch-aware recurrence the
+ * reference names for tree drafts verified in one pass (docs/flatspec-design.md:64-69). */
+int skinny_gdn_fused_tree(const void* proj, int ldp, void* conv, void* conv_full, const float* conv_w,
+                          const float* A_log, const float* dt_bias, const float* norm_w, float eps, const float* state,
+                          float* ckpt, void* xq, void* o_out, int T, int Hv, int Hk, int W, void* err_word,
+                          const int32_t* parent, void* stream);
+
 /* Bytes of the workspace skinny_attn_fused needs for a KV cache of max_len positions (0 when the
  * shape is not supported).  It holds per-chunk partial results between the call's two launches
  * and no state between calls. */
@@ -233,6 +246,16 @@ int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const fl
                       const int32_t* length_dev, int T, int n_heads, int n_kv_heads, int max_len, void* workspace,
                       size_t workspace_bytes, void* xq, void* o_out, const skinny_peer_sync* sync, void* stream);
 
+/* skinny_attn_fused over a token TREE (parent as for skinny_gdn_fused_tree): node t is rotated
+ * at position L0 + depth(t), attends to the cached positions 0 .. L0-1 and to the new keys of its
+ * ancestors and itself, and its key / value are appended at slot L0 + t (after acceptance the
+ * caller moves the accepted path's slots to L0 + depth). */
+int skinny_attn_fused_tree(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
+                           const float* inv_freq, int rot, int gated, float eps, void* k_cache, void* v_cache, int L0,
+                           const int32_t* length_dev, int T, int n_heads, int n_kv_heads, int max_len,
+                           void* workspace, size_t workspace_bytes, void* xq, void* o_out, const int32_t* parent,
+                           void* stream);
+
 /* skinny_qmm_w4g64 on an input prepared by skinny_prep (same result as passing the bf16
  * activation itself), launched without the x-prep kernel.  Sharded step: with xq_ranks != NULL
  * the digit blocks of groups [r * xq_groups_per_rank, (r+1) * xq_groups_per_rank) are read from
@@ -247,7 +270,8 @@ size_t skinny_spec_accept_workspace_bytes(void);
 
 /* Greedy acceptance of a verified draft, fused on the device: for the rows = K+1 verified
  * positions, pred[i] = argmax over the V logits of row i (bf16, leading dimension ld; ties to the
- * lowest index, NaN never wins); n = the longest prefix with draft[i] == pred[i] (i < K); then
+ * lowest index, a NaN above every number: numpy's order); n = the longest prefix with
+ * draft[i] == pred[i] (i < K); then
  * result[0] = n, result[1 .. n+1] = draft[:n] + [pred[n]], result[n+2 .. rows] = -1.  pred (may be
  * NULL) receives the rows predictions.  rows <= 17, V <= 524,288; logits and ld*2 16-byte aligned.
  * Replaces the verify tail of skinny_mlx/spec.py:136-147 (argmax, the host sync of pred and
@@ -255,6 +279,16 @@ size_t skinny_spec_accept_workspace_bytes(void);
 int skinny_spec_accept(const void* logits, int ld, int rows, int V, const int32_t* draft,
                        int32_t* result, int32_t* pred, void* workspace, size_t workspace_bytes,
                        void* stream);
+
+/* Greedy acceptance of a verified draft TREE of `rows` nodes (node 0 = the last emitted token;
+ * tokens int32 [rows] the node tokens, parent int32 [rows] as for skinny_gdn_fused_tree, both
+ * device memory): pred as above; from the root, move repeatedly to the first child (lowest index)
+ * whose token equals the current node's prediction.  result int32 [2 rows + 1]: result[0] = n
+ * accepted nodes, result[1 .. rows] = their tokens + [pred[last]] then -1, result[rows+1 ..
+ * 2 rows] = the path 0, p1 .. pn then -1.  The tree form of skinny_mlx/spec.py:136-147. */
+int skinny_spec_accept_tree(const void* logits, int ld, int rows, int V, const int32_t* tokens,
+                            const int32_t* parent, int32_t* result, int32_t* pred, void* workspace,
+                            size_t workspace_bytes, void* stream);
 
 /* Gated DeltaNet verify recurrence with per-token state checkpoints (the B200 form of the
  * recurrence that skinny_mlx/rollback.py:39-42 records and re-runs).  Per value head h and token t
@@ -278,6 +312,13 @@ int skinny_gdn_recurrent(const void* q, const void* k, const void* v, const floa
 int skinny_gdn_rollback(int n_layers, float* const* state, const float* const* ckpt,
                         void* const* conv, const void* const* conv_full, long long state_elems,
                         int keep, int fed, int W, int C, void* stream);
+
+/* Rollback of all GDN layers after a TREE verify of `fed` nodes whose accepted path ends at node
+ * `node`: state[l] <- ckpt[l][node], conv[l] row q <- conv_full[l] row rows[q] for q < W (rows: a
+ * HOST array, the last W conv inputs along the path: window rows 0 .. W-1, node t at W + t). */
+int skinny_gdn_rollback_tree(int n_layers, float* const* state, const float* const* ckpt, void* const* conv,
+                             const void* const* conv_full, long long state_elems, int node, const int32_t* rows,
+                             int fed, int W, int C, void* stream);
 
 /* skinny_qmm_w4g64 without a workspace argument and without allocating anything: no cudaMalloc,
  * no cudaFree, no allocating library routine.  It has NO counterpart in the reference; it exists

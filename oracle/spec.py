@@ -26,3 +26,23 @@ def accept(logits: np.ndarray, draft) -> tuple[int, list[int], list[int]]:
     while n < len(draft) and draft[n] == pred[n]:
         n += 1
     return n, draft[:n] + [pred[n]], pred
+
+
+def accept_tree(logits: np.ndarray, tokens, parent) -> tuple[int, list[int], list[int]]:
+    """The tree form of the acceptance (the draft tree the reference proposes for flat verify,
+    docs/flatspec-design.md:64-69): logits [M, V] of the M nodes (node 0 = the last emitted
+    token), tokens [M], parent [M] (parent[0] = -1, parent[t] < t).  From the root, move to the
+    first child (lowest index) whose token equals the current node's prediction while one
+    exists.  Returns (n, the accepted tokens + [pred of the last node], the path 0, p1 .. pn)."""
+    pred = [int(v) for v in argmax_rows(np.asarray(logits))]
+    tokens = [int(t) for t in tokens]
+    parent = [int(p) for p in parent]
+    cur, path = 0, [0]
+    if parent[0] == -1:
+        while True:
+            nxt = next((c for c in range(cur + 1, len(parent)) if parent[c] == cur and tokens[c] == pred[cur]), None)
+            if nxt is None:
+                break
+            path.append(nxt)
+            cur = nxt
+    return len(path) - 1, [tokens[c] for c in path[1:]] + [pred[cur]], path

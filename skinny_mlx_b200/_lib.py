@@ -66,6 +66,16 @@ SIGNATURES = {
     "skinny_qmm_w4g64_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int,
                                          c_int, c_void_p]),
     "skinny_qmm_w4g64_noalloc_errors": (c_int, [c_void_p, c_void_p]),
+    "skinny_gdn_fused_tree": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                      ctypes.c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                      c_int, c_void_p, c_void_p, c_void_p]),
+    "skinny_attn_fused_tree": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, ctypes.c_float,
+                                       c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
+                                       c_size_t, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "skinny_spec_accept_tree": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                                        c_void_p, c_size_t, c_void_p]),
+    "skinny_gdn_rollback_tree": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_longlong, c_int,
+                                         c_void_p, c_int, c_int, c_int, c_void_p]),
 }
 
 

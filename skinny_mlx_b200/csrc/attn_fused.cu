@@ -17,6 +17,10 @@
 //                      chunks never race).
 //   attn_merge_kernel  CTA (one query row, KV head): merges the chunks (a fixed order:
 //                      deterministic), applies the gate and writes the digits.
+// Token trees: with parent != NULL the T new tokens are the nodes of a draft tree in topological
+// order (parent[0] = -1, parent[t] < t).  Node t sits at position L0 + depth(t) (RoPE of its q
+// and k) and sees the cached keys plus the new keys of its ancestors and itself; its key and
+// value are appended at slot L0 + t (the rollback moves the accepted path's slots into place).
 // No CTA waits on another; the merge launch waits for the chunk launch through programmatic
 // dependent launch, like every launch of the step (the next launch may start at once; a kernel
 // waits for the previous grid before its first global read).
@@ -58,6 +62,7 @@ struct AttnParams {
   int T, L0, nh, nkv, rot, nchunks, nrg, max_len;
   int gated;                  // 1: per head [q | gate] and o *= sigmoid(gate); 0: q heads only
   const int* len_dev;         // if set: the cache length is read here (grid sized for max_len)
+  const int32_t* parent;      // [T] tree of the new tokens, or null (a chain)
   float* part;                // [nkv, nrg, nchunks, 16, kAtPart]: per row m, l, -, -, o[128]
   uint8_t* xq;                // o_proj input digits (K = nh * 128)
   __nv_bfloat16* o_out;       // [T, nh * 128] or null
@@ -78,6 +83,8 @@ struct AttnSmem {
   __nv_bfloat16 pr[kAtPassRows][kAtStride];  // probabilities (bf16, as a flash kernel rounds them)
   float redm[kAtWarps][kAtPassRows];         // per (warp = 16-key block, row): max of the block
   float redl[kAtWarps][kAtPassRows];         //                                sum of its probabilities
+  int dep[kAtMaxT];                          // tree: depth of every new token
+  uint32_t anc[kAtMaxT];                     //       its ancestors and itself (bit per token)
 };
 
 __device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
@@ -251,13 +258,38 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_chunk_kernel(const __grid_
     }
     if (tid < kAtD) sm.qw[tid] = nwv;
     else sm.kw[tid - kAtD] = nwv;
+    if (p.parent) {  // tree: depth and ancestor set of every node (warp 0, by shuffles)
+      if (warp == 0) {
+        int par = lane - 1;
+        if (lane < p.T) {
+          const int v = p.parent[lane];
+          if (lane == 0 ? v == -1 : (v >= 0 && v < lane)) par = v;  // else read as a chain
+        }
+        int cur = lane, d = 0;
+        uint32_t m = lane < p.T ? 1u << lane : 0u;
+#pragma unroll
+        for (int it = 0; it < kAtMaxT; ++it) {
+          const int pc = __shfl_sync(0xFFFFFFFFu, par, cur & 31);
+          if (cur >= 0 && pc >= 0) {
+            m |= 1u << pc;
+            ++d;
+          }
+          cur = cur >= 0 ? pc : -1;
+        }
+        if (lane < p.T) {
+          sm.dep[lane] = d;
+          sm.anc[lane] = m;
+        }
+      }
+      __syncthreads();
+    }
 #pragma unroll
     for (int u = 0; u < kTabPer; ++u) {
       const int i = tid + u * kAtThreads;
       if (half > 0 && i < p.T * half) {
         const int t = i / half, j = i - t * half;
         float sn, c;
-        sincosf(static_cast<float>(L0 + t) * fr[u], &sn, &c);
+        sincosf(static_cast<float>(L0 + (p.parent ? sm.dep[t] : t)) * fr[u], &sn, &c);
         sm.cs[t][j][0] = c;
         sm.cs[t][j][1] = sn;
       }
@@ -343,13 +375,15 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_chunk_kernel(const __grid_
         for (int hf = 0; hf < 2; ++hf) {
           const int rr = rt * kAtRG + g + 8 * hf;
           const int t = min((rbase + rr) / rep, p.T - 1);
+          const uint32_t anc = p.parent ? sm.anc[t] : (2u << t) - 1u;  // new keys row t sees
           float m = -INFINITY;
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const int j = 16 * warp + 8 * nt + 2 * cq + e;
-              const bool vis = j < nk && k0 + j <= L0 + t;
+              const int rel = k0 + j - L0;  // < 0: a cached key
+              const bool vis = j < nk && (rel < 0 || ((anc >> rel) & 1u));
               const float v = vis ? c[rt][nt][2 * hf + e] * sc : -INFINITY;
               c[rt][nt][2 * hf + e] = v;
               m = fmaxf(m, v);
@@ -598,7 +632,7 @@ bool attn_fits(int T, int nh, int nkv) {
 cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, const float* kn_w,
                               const float* inv_freq, int rot, int gated, float eps, void* kc, void* vc, int L0,
                               const int* len_dev, int max_len, int T, int nh, int nkv, void* ws, void* xq,
-                              void* o_out, const skinny_peer_sync* sync, cudaStream_t stream) {
+                              void* o_out, const skinny_peer_sync* sync, const int32_t* parent, cudaStream_t stream) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -626,6 +660,7 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
   prm.rot = rot;
   prm.gated = gated;
   prm.len_dev = len_dev;
+  prm.parent = parent;
   prm.max_len = max_len;
   // chunk grid (and the partials' chunk stride): the largest chunk count this cache can need
   // with a device length, else the exact count

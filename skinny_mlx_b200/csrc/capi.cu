@@ -44,6 +44,7 @@ struct GdnFusedParamsHost {
   void* xq;
   void* o_out;
   uint32_t* err;
+  const int32_t* parent;
   int T, Hv, Hk, W;
 };
 cudaError_t gdn_fused_call(const GdnFusedParamsHost& prm, cudaStream_t stream);
@@ -64,7 +65,13 @@ bool attn_fits(int T, int nh, int nkv);
 cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, const float* kn_w,
                               const float* inv_freq, int rot, int gated, float eps, void* kc, void* vc, int L0,
                               const int* len_dev, int max_len, int T, int nh, int nkv, void* ws, void* xq,
-                              void* o_out, const skinny_peer_sync* sync, cudaStream_t stream);
+                              void* o_out, const skinny_peer_sync* sync, const int32_t* parent, cudaStream_t stream);
+cudaError_t spec_accept_tree_launch(const void* logits, int ld, int rows, int V, const int32_t* tokens,
+                                    const int32_t* parent, int32_t* result, int32_t* pred, void* ws,
+                                    cudaStream_t stream);
+cudaError_t gdn_rollback_tree_call(int n_layers, float* const* state, const float* const* ckpt, void* const* conv,
+                                  const void* const* conv_full, long long state_elems, int node, const int* rows,
+                                  int W, int C, cudaStream_t stream);
 }  // namespace skinny
 
 namespace {
@@ -317,22 +324,41 @@ int skinny_prep(int mode, const void* x, int ldx, const void* d, int ldd, int ds
                                          static_cast<cudaStream_t>(stream)));
 }
 
-int skinny_gdn_fused(const void* proj, int ldp, void* conv, void* conv_full, const float* conv_w,
-                     const float* A_log, const float* dt_bias, const float* norm_w, float eps, float* state,
-                     float* ckpt, void* xq, void* o_out, int T, int Hv, int Hk, int W, void* err_word,
-                     void* stream) {
+static int gdn_fused_common(const void* proj, int ldp, void* conv, void* conv_full, const float* conv_w,
+                            const float* A_log, const float* dt_bias, const float* norm_w, float eps, float* state,
+                            float* ckpt, void* xq, void* o_out, int T, int Hv, int Hk, int W, void* err_word,
+                            const int32_t* parent, void* stream) {
   if (!proj || !conv || !conv_w || !A_log || !dt_bias || !norm_w || !state || !xq || !err_word)
     return SKINNY_ERR_INVALID_ARG;
   if (T < 1 || T > skinny::kMaxTokens || Hv < 1 || Hk != Hv || W < 1 || W > 4) return SKINNY_ERR_SHAPE;
   const int C = 3 * Hv * 128;
   if (ldp < C + Hv * 128 + 2 * Hv) return SKINNY_ERR_INVALID_ARG;
+  if (parent && (!ckpt || !conv_full || !aligned4(parent))) return SKINNY_ERR_INVALID_ARG;
   // conv window and projection rows are read as 16-byte vectors
   if (!aligned16(state) || (ckpt && !aligned16(ckpt)) || !aligned16(xq) || (ldp % 8) || !aligned16(proj) ||
       !aligned16(conv) || !aligned16(conv_full) || !aligned4(o_out) || !aligned4(err_word))
     return SKINNY_ERR_ALIGNMENT;
   skinny::GdnFusedParamsHost prm{proj, ldp, conv, conv_full, conv_w, A_log, dt_bias, norm_w, eps, state,
-                             T > 1 ? ckpt : nullptr, xq, o_out, static_cast<uint32_t*>(err_word), T, Hv, Hk, W};
+                             (parent || T > 1) ? ckpt : nullptr, xq, o_out, static_cast<uint32_t*>(err_word),
+                             parent, T, Hv, Hk, W};
   return cuda_status(skinny::gdn_fused_call(prm, static_cast<cudaStream_t>(stream)));
+}
+
+int skinny_gdn_fused(const void* proj, int ldp, void* conv, void* conv_full, const float* conv_w,
+                     const float* A_log, const float* dt_bias, const float* norm_w, float eps, float* state,
+                     float* ckpt, void* xq, void* o_out, int T, int Hv, int Hk, int W, void* err_word,
+                     void* stream) {
+  return gdn_fused_common(proj, ldp, conv, conv_full, conv_w, A_log, dt_bias, norm_w, eps, state, ckpt, xq, o_out,
+                          T, Hv, Hk, W, err_word, nullptr, stream);
+}
+
+int skinny_gdn_fused_tree(const void* proj, int ldp, void* conv, void* conv_full, const float* conv_w,
+                          const float* A_log, const float* dt_bias, const float* norm_w, float eps, const float* state,
+                          float* ckpt, void* xq, void* o_out, int T, int Hv, int Hk, int W, void* err_word,
+                          const int32_t* parent, void* stream) {
+  if (!parent) return SKINNY_ERR_INVALID_ARG;
+  return gdn_fused_common(proj, ldp, conv, conv_full, conv_w, A_log, dt_bias, norm_w, eps, const_cast<float*>(state),
+                          ckpt, xq, o_out, T, Hv, Hk, W, err_word, parent, stream);
 }
 
 size_t skinny_attn_workspace_bytes(int T, int n_heads, int n_kv_heads, int max_len) {
@@ -340,10 +366,11 @@ size_t skinny_attn_workspace_bytes(int T, int n_heads, int n_kv_heads, int max_l
   return skinny::attn_ws_bytes(T, n_heads, n_kv_heads, max_len);
 }
 
-int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
-                      const float* inv_freq, int rot, int gated, float eps, void* k_cache, void* v_cache, int L0,
-                      const int32_t* length_dev, int T, int n_heads, int n_kv_heads, int max_len, void* workspace,
-                      size_t workspace_bytes, void* xq, void* o_out, const skinny_peer_sync* sync, void* stream) {
+static int attn_fused_common(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
+                             const float* inv_freq, int rot, int gated, float eps, void* k_cache, void* v_cache,
+                             int L0, const int32_t* length_dev, int T, int n_heads, int n_kv_heads, int max_len,
+                             void* workspace, size_t workspace_bytes, void* xq, void* o_out,
+                             const skinny_peer_sync* sync, const int32_t* parent, void* stream) {
   if (!proj || !q_norm_w || !k_norm_w || !k_cache || !v_cache || !xq || (rot > 0 && !inv_freq))
     return SKINNY_ERR_INVALID_ARG;
   if (T < 1 || T > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
@@ -355,14 +382,34 @@ int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const fl
   if ((gated != 0 && gated != 1) || ldp < ((1 + gated) * n_heads + 2 * n_kv_heads) * 128 || !sync_ok(sync))
     return SKINNY_ERR_INVALID_ARG;
   if (!aligned16(xq) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned4(o_out) || !aligned16(proj) ||
-      (ldp % 8) || !aligned4(length_dev))
+      (ldp % 8) || !aligned4(length_dev) || !aligned4(parent))
     return SKINNY_ERR_ALIGNMENT;
   if (!workspace || workspace_bytes < skinny::attn_ws_bytes(T, n_heads, n_kv_heads, max_len) ||
       !aligned16(workspace))
     return SKINNY_ERR_WORKSPACE;
   return cuda_status(skinny::attn_fused_launch(proj, ldp, q_norm_w, k_norm_w, inv_freq, rot, gated, eps, k_cache,
                                                v_cache, L0, length_dev, max_len, T, n_heads, n_kv_heads,
-                                               workspace, xq, o_out, sync, static_cast<cudaStream_t>(stream)));
+                                               workspace, xq, o_out, sync, parent, static_cast<cudaStream_t>(stream)));
+}
+
+int skinny_attn_fused(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
+                      const float* inv_freq, int rot, int gated, float eps, void* k_cache, void* v_cache, int L0,
+                      const int32_t* length_dev, int T, int n_heads, int n_kv_heads, int max_len, void* workspace,
+                      size_t workspace_bytes, void* xq, void* o_out, const skinny_peer_sync* sync, void* stream) {
+  return attn_fused_common(proj, ldp, q_norm_w, k_norm_w, inv_freq, rot, gated, eps, k_cache, v_cache, L0, length_dev,
+                           T, n_heads, n_kv_heads, max_len, workspace, workspace_bytes, xq, o_out, sync, nullptr,
+                           stream);
+}
+
+int skinny_attn_fused_tree(const void* proj, int ldp, const float* q_norm_w, const float* k_norm_w,
+                           const float* inv_freq, int rot, int gated, float eps, void* k_cache, void* v_cache, int L0,
+                           const int32_t* length_dev, int T, int n_heads, int n_kv_heads, int max_len,
+                           void* workspace, size_t workspace_bytes, void* xq, void* o_out, const int32_t* parent,
+                           void* stream) {
+  if (!parent) return SKINNY_ERR_INVALID_ARG;
+  return attn_fused_common(proj, ldp, q_norm_w, k_norm_w, inv_freq, rot, gated, eps, k_cache, v_cache, L0, length_dev,
+                           T, n_heads, n_kv_heads, max_len, workspace, workspace_bytes, xq, o_out, nullptr, parent,
+                           stream);
 }
 
 int skinny_qmm_w4g64_prepared(const void* xq, const void* w_tc, void* out, int ldo, int M, int N, int K,
@@ -432,6 +479,18 @@ int skinny_spec_accept(const void* logits, int ld, int rows, int V, const int32_
                                                 static_cast<cudaStream_t>(stream)));
 }
 
+int skinny_spec_accept_tree(const void* logits, int ld, int rows, int V, const int32_t* tokens,
+                            const int32_t* parent, int32_t* result, int32_t* pred, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (!logits || !result || !tokens || !parent) return SKINNY_ERR_INVALID_ARG;
+  if (!skinny::spec_accept_fits(rows, V) || ld < V) return SKINNY_ERR_SHAPE;
+  if (!aligned16(logits) || (ld % 8) != 0 || !aligned4(tokens) || !aligned4(parent)) return SKINNY_ERR_ALIGNMENT;
+  if (!workspace || workspace_bytes < skinny::spec_accept_ws_bytes() || !aligned16(workspace))
+    return SKINNY_ERR_WORKSPACE;
+  return cuda_status(skinny::spec_accept_tree_launch(logits, ld, rows, V, tokens, parent, result, pred, workspace,
+                                                     static_cast<cudaStream_t>(stream)));
+}
+
 int skinny_gdn_recurrent(const void* q, const void* k, const void* v, const float* g,
                          const float* beta, float* state, void* y, float* ckpt, int T, int Hv, int Hk,
                          int Dk, int Dv, void* stream) {
@@ -455,6 +514,23 @@ int skinny_gdn_rollback(int n_layers, float* const* state, const float* const* c
   }
   return cuda_status(skinny::gdn_rollback_call(n_layers, state, ckpt, conv, conv_full, state_elems,
                                                keep, fed, W, C, static_cast<cudaStream_t>(stream)));
+}
+
+int skinny_gdn_rollback_tree(int n_layers, float* const* state, const float* const* ckpt, void* const* conv,
+                             const void* const* conv_full, long long state_elems, int node, const int32_t* rows,
+                             int fed, int W, int C, void* stream) {
+  if (n_layers < 1 || n_layers > SKINNY_GDN_MAX_LAYERS || !state || !ckpt || !conv || !conv_full || !rows)
+    return SKINNY_ERR_INVALID_ARG;
+  if (node < 0 || node >= fed || state_elems < 4 || state_elems % 4 != 0 || W < 1 || W > 4 || C < 1)
+    return SKINNY_ERR_SHAPE;
+  for (int q = 0; q < W; ++q)
+    if (rows[q] < 0 || rows[q] >= W + fed) return SKINNY_ERR_SHAPE;
+  for (int l = 0; l < n_layers; ++l) {
+    if (!state[l] || !ckpt[l] || !conv[l] || !conv_full[l]) return SKINNY_ERR_INVALID_ARG;
+    if (!aligned16(state[l]) || !aligned16(ckpt[l])) return SKINNY_ERR_ALIGNMENT;
+  }
+  return cuda_status(skinny::gdn_rollback_tree_call(n_layers, state, ckpt, conv, conv_full, state_elems, node, rows,
+                                                    W, C, static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

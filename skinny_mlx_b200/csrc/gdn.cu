@@ -137,6 +137,56 @@ __global__ void __launch_bounds__(256) gdn_rollback_kernel(const __grid_constant
   }
 }
 
+// Tree rollback: the accepted path ends at node `node`; state[l] <- ckpt[l][node] and conv[l] row
+// q <- conv_full[l] row rows[q] (q < W): the last W conv inputs along the path.
+struct GdnRollbackTreeParams {
+  float* state[kGdnMaxLayers];
+  const float* ckpt[kGdnMaxLayers];
+  __nv_bfloat16* conv[kGdnMaxLayers];
+  const __nv_bfloat16* conv_full[kGdnMaxLayers];
+  long long state_elems;
+  int rows[4];
+  int n_layers, node, W, C;
+};
+
+__global__ void __launch_bounds__(256) gdn_rollback_tree_kernel(const __grid_constant__ GdnRollbackTreeParams p) {
+  const int l = blockIdx.y;
+  const float4* src = reinterpret_cast<const float4*>(p.ckpt[l] + static_cast<size_t>(p.node) * p.state_elems);
+  float4* dst = reinterpret_cast<float4*>(p.state[l]);
+  const long long n4 = p.state_elems / 4;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    dst[i] = src[i];
+  const long long n = static_cast<long long>(p.W) * p.C;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int q = static_cast<int>(i / p.C);
+    const long long c = i - static_cast<long long>(q) * p.C;
+    p.conv[l][i] = p.conv_full[l][static_cast<size_t>(p.rows[q]) * p.C + c];
+  }
+}
+
+cudaError_t gdn_rollback_tree_call(int n_layers, float* const* state, const float* const* ckpt, void* const* conv,
+                                  const void* const* conv_full, long long state_elems, int node, const int* rows,
+                                  int W, int C, cudaStream_t stream) {
+  static thread_local GdnRollbackTreeParams prm;
+  prm.n_layers = n_layers;
+  prm.node = node;
+  prm.W = W;
+  prm.C = C;
+  prm.state_elems = state_elems;
+  for (int q = 0; q < 4; ++q) prm.rows[q] = q < W ? rows[q] : 0;
+  for (int l = 0; l < n_layers; ++l) {
+    prm.state[l] = state[l];
+    prm.ckpt[l] = ckpt[l];
+    prm.conv[l] = static_cast<__nv_bfloat16*>(conv[l]);
+    prm.conv_full[l] = static_cast<const __nv_bfloat16*>(conv_full[l]);
+  }
+  dim3 grid(32, n_layers);
+  gdn_rollback_tree_kernel<<<grid, 256, 0, stream>>>(prm);
+  return cudaGetLastError();
+}
+
 cudaError_t gdn_rollback_call(int n_layers, float* const* state, const float* const* ckpt,
                              void* const* conv, const void* const* conv_full, long long state_elems,
                              int keep, int fed, int W, int C, cudaStream_t stream) {

@@ -19,6 +19,14 @@
 // 64-row groups of y, so each CTA pushes its y rows into the shared memory of every CTA
 // of the head (distributed shared memory), and rank r finishes tokens r and r + 8.
 //
+// Token trees (speculative verify of a draft tree in one pass).  With parent != NULL the T inputs
+// are the nodes of a tree in topological order (parent[0] = -1, parent[t] < t): node t's conv
+// window is the W inputs before it on its ancestor path (the cached window above the root), and
+// its recurrence starts from its parent's state -- carried in registers when the parent is node
+// t - 1, else reloaded from the parent's checkpoint (which this thread itself wrote).  The state
+// after EVERY node goes to ckpt[t]; neither `state` nor the conv window is written (the rollback
+// selects the accepted path's last node and gathers the window along the path).
+//
 // Rounding points follow the unfused model (skinny_mlx_b200/model.py): q, k, v and y to bf16,
 // the norm output to bf16, o to bf16.  Launched with programmatic dependent launch: the next
 // launch may start at once (it streams weights) and this one waits for the previous grid before
@@ -58,7 +66,8 @@ struct GdnFusedParams {
   float* ckpt;                // [T - 1, Hv, 128, 128] or null
   uint8_t* xq;                // out_proj input digits (K = Hv * 128)
   __nv_bfloat16* o_out;       // [T, Hv * 128] bf16 copy of o, or null
-  uint32_t* err;              // error word (kErrBitWaitCluster)
+  uint32_t* err;              // error word (kErrBitWaitCluster, kErrBitBadInput)
+  const int32_t* parent;      // [T] tree of the T inputs, or null (a chain)
   int T, Hv, Hk;
 };
 
@@ -95,6 +104,8 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
   __shared__ __align__(16) float yl[kGfMaxT][kGfRows];
   __shared__ __align__(16) float yall[kGfMaxT][kGfD];  // the head's y, pushed by every rank
   __shared__ float gs[kGfMaxT], bs[kGfMaxT], kq[kGfMaxT];  // gates; k_t . q_t
+  __shared__ int8_t rsel[kGfMaxT][W + 1];  // rows of fw that form node t's conv window
+  __shared__ int8_t par_s[kGfMaxT];        // parent node (-1: the root)
   __shared__ __align__(8) uint64_t ybar;
   __shared__ int abort_flag;
   // dynamic: the per-thread partials of S q for every token (summed after the recurrence) and u
@@ -114,6 +125,7 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
   }
   pdl_launch_dependents();
   pdl_wait_prior_grid();
+  const bool tree = p.parent != nullptr;
 
   // ---- every global load, issued together
   const int row = tid / kGfTpr, sub = tid % kGfTpr;  // recurrence: (state row, column phase)
@@ -171,6 +183,30 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
       }
     }
   }
+  // Conv window rows and parents of every node.  fw rows: [0, W) the cached window, W + t node
+  // t.  The row before node t's row is its parent's row (the last window row for the root), the
+  // row before a window row the previous one.  A malformed tree (parent[0] != -1, parent[t] >= t
+  // or < 0 for t > 0) is recorded and read as a chain.
+  if (tid < T) {
+    int pt = tid - 1;
+    if (tree) {
+      const int v = p.parent[tid];
+      const bool ok = tid == 0 ? v == -1 : (v >= 0 && v < tid);
+      if (!ok && rank == 0 && (blockIdx.x / kGfRanks) == 0) atomicOr(p.err, kErrBitBadInput);
+      if (ok) pt = v;
+    }
+    par_s[tid] = static_cast<int8_t>(pt);
+  }
+  __syncthreads();
+  if (tid < T) {
+    int r = W + tid;
+    rsel[tid][W] = static_cast<int8_t>(r);
+#pragma unroll
+    for (int q = W - 1; q >= 0; --q) {
+      r = r >= W ? (par_s[r - W] >= 0 ? W + par_s[r - W] : W - 1) : r - 1;
+      rsel[tid][q] = static_cast<int8_t>(r);
+    }
+  }
   __syncthreads();
   // Arrive once this CTA's mbarrier exists and its reads of the conv window are complete: a peer
   // writes its share of the new window, and stores into this CTA's shared memory, only after the
@@ -186,7 +222,7 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
     for (int t = 0; t < T; ++t) {
       float acc = 0.f;
 #pragma unroll
-      for (int q = 0; q <= W; ++q) acc = fmaf(__bfloat162float(fw[t + q][tid]), cw[q], acc);
+      for (int q = 0; q <= W; ++q) acc = fmaf(__bfloat162float(fw[rsel[t][q]][tid]), cw[q], acc);
       const float sv = __fdividef(acc, 1.f + __expf(-acc));
       if (part == 0) qs[t][j] = sv;
       else ks[t][j] = sv;
@@ -195,7 +231,7 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
     if (tv < T) {
       float acc = 0.f;
 #pragma unroll
-      for (int q = 0; q <= W; ++q) acc = fmaf(__bfloat162float(fw[tv + q][2 * kGfD + jv]), cwv[q], acc);
+      for (int q = 0; q <= W; ++q) acc = fmaf(__bfloat162float(fw[rsel[tv][q]][2 * kGfD + jv]), cwv[q], acc);
       vs[tv][jv] = bf16rf(__fdividef(acc, 1.f + __expf(-acc)));
     }
   }
@@ -264,6 +300,11 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
       qq[i] = qn[i];
     }
     if (t + 1 < T) load_tok(t + 1);
+    if (tree && t > 0 && par_s[t] != t - 1) {  // a branch: start from the parent's checkpoint
+      const float* cp = p.ckpt + static_cast<size_t>(par_s[t]) * p.Hv * kGfD * kGfD + srow;
+#pragma unroll
+      for (int i = 0; i < kGfCols; ++i) S[i] = cp[kGfTpr * i];
+    }
     float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
     for (int i = 0; i < kGfCols; i += 2) {
@@ -280,14 +321,16 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
 #pragma unroll
     for (int i = 0; i < kGfCols; ++i) S[i] = fmaf(u, kk[i], gt * S[i]);
     if (sub == 0) ust[t * kGfRows + row] = u;
-    if (p.ckpt && t + 1 < T) {
+    if (p.ckpt && (tree || t + 1 < T)) {
       float* cp = p.ckpt + static_cast<size_t>(t) * p.Hv * kGfD * kGfD + srow;
 #pragma unroll
       for (int i = 0; i < kGfCols; ++i) cp[kGfTpr * i] = S[i];
     }
   }
+  if (!tree) {
 #pragma unroll
-  for (int i = 0; i < kGfCols; ++i) p.state[srow + kGfTpr * i] = S[i];
+    for (int i = 0; i < kGfCols; ++i) p.state[srow + kGfTpr * i] = S[i];
+  }
   __syncthreads();
   // y = g b + u c per (token, row): b summed from the 16 column partials in the order of the
   // lane butterfly (pairs, then pairs of pairs, ...), which is the same value in every lane
@@ -323,7 +366,8 @@ __global__ void __launch_bounds__(kGfThreads) gdn_fused_kernel(const __grid_cons
     const int runs = (h % rep) == 0 ? 3 : 1;  // 8-channel vectors per row: 2 per run
     const int per_row = 2 * runs;
     const int n_full = p.conv_full ? (W + T) * per_row : 0;
-    for (int e = tid; e < n_full + W * per_row; e += kGfThreads) {
+    const int n_win = tree ? 0 : W * per_row;  // (a tree's window is gathered by the rollback)
+    for (int e = tid; e < n_full + n_win; e += kGfThreads) {
       const bool full = e < n_full;
       const int e2 = full ? e : e - n_full;
       const int r = e2 / per_row, v = e2 - r * per_row;
@@ -386,6 +430,7 @@ struct GdnFusedParamsHost {
   void* xq;
   void* o_out;
   uint32_t* err;
+  const int32_t* parent;
   int T, Hv, Hk, W;
 };
 
@@ -424,7 +469,7 @@ cudaError_t gdn_fused_call(const GdnFusedParamsHost& h, cudaStream_t stream) {
   GdnFusedParams prm{static_cast<const __nv_bfloat16*>(h.proj), h.ldp, static_cast<__nv_bfloat16*>(h.conv),
                      static_cast<__nv_bfloat16*>(h.conv_full), h.conv_w, h.A_log, h.dt_bias, h.norm_w, h.eps,
                      h.state, h.ckpt, static_cast<uint8_t*>(h.xq), static_cast<__nv_bfloat16*>(h.o_out),
-                     h.err, h.T, h.Hv, h.Hk};
+                     h.err, h.parent, h.T, h.Hv, h.Hk};
   switch (h.W) {
     case 1: return launch_gdn_fused<1>(prm, stream);
     case 2: return launch_gdn_fused<2>(prm, stream);

@@ -52,10 +52,47 @@ __device__ __forceinline__ void consider(float v, int i, float& bv, int& bi) {
   }
 }
 
+// The acceptance after the argmax of every row.  Chain (parent == null): n = the longest prefix
+// with draft[i] == pred[i]; result = [n, draft[:n] + [pred[n]], -1 ...].  Tree (parent != null,
+// tokens[i] the token of node i, node 0 the last emitted token): from the root, repeatedly move to
+// the first child (lowest index) whose token equals the current node's prediction; result = [n,
+// the n accepted tokens + [pred[last]], -1 ... (rows entries), the path 0, p1 .. pn, -1 ... (rows
+// entries)].  A malformed tree (parent[0] != -1 or parent[i] outside [0, i)) has no children.
+__device__ void accept_tail(const int* pred, int rows, const int32_t* draft, const int32_t* tokens,
+                            const int32_t* parent, int32_t* result) {
+  if (!parent) {
+    int n = 0;
+    while (n < rows - 1 && draft[n] == pred[n]) ++n;
+    result[0] = n;
+    for (int i = 0; i < rows; ++i) result[1 + i] = i < n ? draft[i] : (i == n ? pred[n] : -1);
+    return;
+  }
+  const bool root_ok = parent[0] == -1;
+  int cur = 0, n = 0;
+  int path[kSpecMaxRows];
+  path[0] = 0;
+  while (root_ok) {
+    int next = -1;
+    for (int c = cur + 1; c < rows; ++c)
+      if (parent[c] == cur && tokens[c] == pred[cur]) {
+        next = c;
+        break;
+      }
+    if (next < 0) break;
+    path[++n] = next;
+    cur = next;
+  }
+  result[0] = n;
+  for (int i = 0; i < rows; ++i) {
+    result[1 + i] = i < n ? tokens[path[i + 1]] : (i == n ? pred[cur] : -1);
+    result[1 + rows + i] = i <= n ? path[i] : -1;
+  }
+}
+
 __global__ void __launch_bounds__(kSpecThreads) spec_accept_kernel(
     const __nv_bfloat16* __restrict__ logits, int ld, int rows, int V, int chunks,
-    const int32_t* __restrict__ draft, int32_t* __restrict__ result, int32_t* __restrict__ pred_out,
-    SpecWs* __restrict__ ws) {
+    const int32_t* __restrict__ draft, const int32_t* __restrict__ tokens, const int32_t* __restrict__ parent,
+    int32_t* __restrict__ result, int32_t* __restrict__ pred_out, SpecWs* __restrict__ ws) {
   const int chunk = blockIdx.x;
   const int row = blockIdx.y;
   const int tid = threadIdx.x;
@@ -114,10 +151,7 @@ __global__ void __launch_bounds__(kSpecThreads) spec_accept_kernel(
   }
   __syncthreads();
   if (tid == 0) {
-    int n = 0;
-    while (n < rows - 1 && draft[n] == pred[n]) ++n;
-    result[0] = n;
-    for (int i = 0; i < rows; ++i) result[1 + i] = i < n ? draft[i] : (i == n ? pred[n] : -1);
+    accept_tail(pred, rows, draft, tokens, parent, result);
     if (pred_out)
       for (int i = 0; i < rows; ++i) pred_out[i] = pred[i];
     ws->counter = 0u;
@@ -129,7 +163,18 @@ cudaError_t spec_accept_launch(const void* logits, int ld, int rows, int V, cons
   const int chunks = (V + kSpecChunk - 1) / kSpecChunk;
   dim3 grid(chunks, rows);
   spec_accept_kernel<<<grid, kSpecThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), ld,
-                                                        rows, V, chunks, draft, result, pred,
+                                                        rows, V, chunks, draft, nullptr, nullptr, result, pred,
+                                                        static_cast<SpecWs*>(ws));
+  return cudaGetLastError();
+}
+
+cudaError_t spec_accept_tree_launch(const void* logits, int ld, int rows, int V, const int32_t* tokens,
+                                    const int32_t* parent, int32_t* result, int32_t* pred, void* ws,
+                                    cudaStream_t stream) {
+  const int chunks = (V + kSpecChunk - 1) / kSpecChunk;
+  dim3 grid(chunks, rows);
+  spec_accept_kernel<<<grid, kSpecThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), ld,
+                                                        rows, V, chunks, nullptr, tokens, parent, result, pred,
                                                         static_cast<SpecWs*>(ws));
   return cudaGetLastError();
 }

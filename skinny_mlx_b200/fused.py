@@ -73,9 +73,10 @@ class FusedOps:
         land in one place (skinny_mlx_b200.qmm.device_errors reads it)."""
         return get_workspace(dev, int(_lib.lib().skinny_qmm_workspace_bytes(128, 64)))
 
-    def _attention(self, ent, proj, c: AttnCache, m: int, xq, stream, len_dev=None):
+    def _attention(self, ent, proj, c: AttnCache, m: int, xq, stream, len_dev=None, tree=None):
         """len_dev: a device int32 holding c.length when the launch runs (graph replay); the
-        caller then advances the host length itself."""
+        caller then advances the host length itself.  tree: device int32 parents of the m
+        tokens (a draft tree) or None."""
         cfg = self.cfg
         max_len = c.k.shape[0]
         ws = self._attn_ws.get(max_len)
@@ -83,9 +84,14 @@ class FusedOps:
             n = int(_lib.lib().skinny_attn_workspace_bytes(16, cfg.n_heads, cfg.n_kv_heads, max_len))
             ws = self._attn_ws[max_len] = torch.zeros(n, dtype=torch.uint8, device=proj.device)
         L0 = c.length
-        _lib.call("skinny_attn_fused", _p(proj), proj.stride(0), _p(ent["qn"]), _p(ent["kn"]), _p(ent["inv"]),
-                  cfg.rotary_dim, 1, cfg.rms_eps, _p(c.k), _p(c.v), L0, _p(len_dev), m, cfg.n_heads, cfg.n_kv_heads,
-                  max_len, _p(ws), ws.numel(), _p(xq), None, None, stream)
+        if tree is None:
+            _lib.call("skinny_attn_fused", _p(proj), proj.stride(0), _p(ent["qn"]), _p(ent["kn"]), _p(ent["inv"]),
+                      cfg.rotary_dim, 1, cfg.rms_eps, _p(c.k), _p(c.v), L0, _p(len_dev), m, cfg.n_heads,
+                      cfg.n_kv_heads, max_len, _p(ws), ws.numel(), _p(xq), None, None, stream)
+        else:
+            _lib.call("skinny_attn_fused_tree", _p(proj), proj.stride(0), _p(ent["qn"]), _p(ent["kn"]),
+                      _p(ent["inv"]), cfg.rotary_dim, 1, cfg.rms_eps, _p(c.k), _p(c.v), L0, _p(len_dev), m,
+                      cfg.n_heads, cfg.n_kv_heads, max_len, _p(ws), ws.numel(), _p(xq), None, _p(tree), stream)
         if len_dev is None:
             c.length = L0 + m
 
@@ -111,10 +117,22 @@ class FusedStep(FusedOps):
         self.final_norm = model.norm.weight
         self._bufs: dict[int, dict] = {}
         self._attn_ws: dict[int, torch.Tensor] = {}
+        self._tree_bufs: dict[int, torch.Tensor] = {}
 
     @property
     def device(self):
         return self.model.device
+
+    def _tree_dev(self, tree, m: int):
+        """The parents of a draft tree as a device int32 [m] tensor (copied there if given on the
+        host), or None for a chain."""
+        if tree is None or (isinstance(tree, torch.Tensor) and tree.is_cuda):
+            return tree
+        buf = self._tree_bufs.get(m)
+        if buf is None:
+            buf = self._tree_bufs[m] = torch.empty(m, dtype=torch.int32, device=self.model.device)
+        buf.copy_(torch.as_tensor(tree, dtype=torch.int32))
+        return buf
 
     def make_cache(self, *a, **k):
         return self.model.make_cache(*a, **k)
@@ -145,15 +163,20 @@ class FusedStep(FusedOps):
 
     # ---------------------------------------------------------------- the step
     @torch.no_grad()
-    def __call__(self, ids: torch.Tensor, cache, lens_dev: torch.Tensor | None = None
+    def __call__(self, ids: torch.Tensor, cache, lens_dev: torch.Tensor | None = None, tree=None
                  ) -> tuple[torch.Tensor, torch.Tensor]:
         """Same contract as HybridModel.forward for 1 <= len(ids) <= 16: (final normed hidden,
         logits) as bf16 [T, H] and [T, V] (views of reused buffers: copy to keep).  lens_dev
         (int32, one entry per attention layer): the attention kernels read the cache lengths there
-        and the host lengths are left to the caller (see GraphedStep)."""
+        and the host lengths are left to the caller (see GraphedStep).  tree: the parents of the
+        tokens (host list or device int32 tensor) for a draft-tree verify, which needs recording
+        GDN caches (HybridRollback.record) and is followed by HybridRollback.rollback_tree."""
         cfg, m = self.cfg, ids.shape[0]
         if m > 16:  # prefill: the module-by-module forward (qmm in 16-token chunks)
+            if tree is not None:
+                raise ValueError("a tree verify takes at most 16 tokens")
             return self.model(ids, cache)
+        tree = self._tree_dev(tree, m)
         b = self._buffers(m)
         stream = ctypes.c_void_p(torch.cuda.current_stream(self.model.device).cuda_stream)
         emb = self.model.embed_tokens
@@ -184,14 +207,22 @@ class FusedStep(FusedOps):
                 rec = c.recording
                 if rec:
                     c.fed = m
-                _lib.call("skinny_gdn_fused", _p(proj), proj.stride(0), _p(c.conv),
-                          _p(c.conv_full if rec else None), _p(ent["conv_w"]), _p(ent["A_log"]), _p(ent["dt_bias"]),
-                          _p(ent["norm_w"]), cfg.rms_eps, _p(c.state), _p(c.ckpt if rec and m > 1 else None),
-                          _p(b["xq_o"]), None, m, cfg.gdn_v_heads, cfg.gdn_k_heads, cfg.conv_kernel - 1,
-                          _p(self._err_word(proj.device)), stream)
+                if tree is not None:
+                    if not rec:
+                        raise ValueError("a tree verify needs recording GDN caches (HybridRollback.record)")
+                    _lib.call("skinny_gdn_fused_tree", _p(proj), proj.stride(0), _p(c.conv), _p(c.conv_full),
+                              _p(ent["conv_w"]), _p(ent["A_log"]), _p(ent["dt_bias"]), _p(ent["norm_w"]),
+                              cfg.rms_eps, _p(c.state), _p(c.ckpt), _p(b["xq_o"]), None, m, cfg.gdn_v_heads,
+                              cfg.gdn_k_heads, cfg.conv_kernel - 1, _p(self._err_word(proj.device)), _p(tree), stream)
+                else:
+                    _lib.call("skinny_gdn_fused", _p(proj), proj.stride(0), _p(c.conv),
+                              _p(c.conv_full if rec else None), _p(ent["conv_w"]), _p(ent["A_log"]),
+                              _p(ent["dt_bias"]), _p(ent["norm_w"]), cfg.rms_eps, _p(c.state),
+                              _p(c.ckpt if rec and m > 1 else None), _p(b["xq_o"]), None, m, cfg.gdn_v_heads,
+                              cfg.gdn_k_heads, cfg.conv_kernel - 1, _p(self._err_word(proj.device)), stream)
             else:
                 self._attention(ent, proj, c, m, b["xq_o"], stream,
-                                None if lens_dev is None else lens_dev[ai:ai + 1])
+                                None if lens_dev is None else lens_dev[ai:ai + 1], tree)
                 ai += 1
             self._qmm(b["xq_o"], ent["out"], b["mix"], m, stream)
             # h = x_l + mixer; digits of post_attention_layernorm(h)
@@ -231,10 +262,12 @@ class GraphedStep:
             cache._lens_host = torch.zeros(max(len(attn), 1), dtype=torch.int32).pin_memory()
         return cache._attn, cache._lens_dev, cache._lens_host
 
-    def _capture(self, cache, m: int):
+    def _capture(self, cache, m: int, tree: bool = False):
         f, dev = self.fused, self.fused.device
         attn, lens_dev, _ = self._lens(cache)
         ids_buf = torch.zeros(m, dtype=torch.long, device=dev)
+        # a tree graph reads the parents from a device buffer filled before every replay
+        par_buf = torch.tensor([-1] + list(range(m - 1)), dtype=torch.int32, device=dev) if tree else None
         gdn = [c for c in cache.layers if isinstance(c, GDNCache)]
         # warm-up on a scratch cache of the same shape, on the capture stream (buffers, the
         # stream's qmm workspace and kernel attributes exist before capture)
@@ -245,34 +278,39 @@ class GraphedStep:
         _, slens, _ = self._lens(scratch)
         self._stream.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(self._stream):
-            f(ids_buf, scratch, slens)
+            f(ids_buf, scratch, slens, par_buf)
         self._stream.synchronize()
         del scratch
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=self._stream):
-            f(ids_buf, cache, lens_dev)
+            f(ids_buf, cache, lens_dev, par_buf)
         # the entry keeps the cache alive: its id (the key) can then not be reused by another
         # cache while the graph, which holds its buffers' addresses, exists
-        ent = (ids_buf, g, cache)
-        self._graphs[(id(cache), m, tuple(c.recording for c in gdn))] = ent
+        par_host = torch.zeros(m, dtype=torch.int32).pin_memory() if tree else None
+        ent = (ids_buf, g, cache, par_buf, par_host)
+        self._graphs[(id(cache), m, tuple(c.recording for c in gdn), tree)] = ent
         return ent
 
     @torch.no_grad()
-    def __call__(self, ids: torch.Tensor, cache):
+    def __call__(self, ids: torch.Tensor, cache, tree=None):
+        """tree: parents of the tokens (host list) for a draft-tree verify, else None."""
         m = ids.shape[0]
         if m > 16:
-            return self.fused(ids, cache)
+            return self.fused(ids, cache, tree=tree)
         gdn = [c for c in cache.layers if isinstance(c, GDNCache)]
-        key = (id(cache), m, tuple(c.recording for c in gdn))
-        ent = self._graphs.get(key) or self._capture(cache, m)
-        ids_buf, g, _ = ent
+        key = (id(cache), m, tuple(c.recording for c in gdn), tree is not None)
+        ent = self._graphs.get(key) or self._capture(cache, m, tree is not None)
+        ids_buf, g, _, par_buf, par_host = ent
         attn, lens_dev, lens_host = self._lens(cache)
         if hasattr(cache, "_lens_evt"):
-            cache._lens_evt.synchronize()  # the previous copy out of the pinned buffer is done
+            cache._lens_evt.synchronize()  # the previous copy out of the pinned buffers is done
         for i, c in enumerate(attn):
             lens_host[i] = c.length
         ids_buf.copy_(ids, non_blocking=True)
         lens_dev.copy_(lens_host, non_blocking=True)
+        if tree is not None:
+            par_host.copy_(torch.as_tensor(tree, dtype=torch.int32))
+            par_buf.copy_(par_host, non_blocking=True)
         if not hasattr(cache, "_lens_evt"):
             cache._lens_evt = torch.cuda.Event()
         cache._lens_evt.record()

@@ -3,8 +3,9 @@
 
 `recurrent` runs the verify pass of one GDN layer and, given a checkpoint buffer, keeps the
 state after every token but the last; `rollback` then restores the state after token keep-1 and
-re-slices the conv window for every layer in one launch.  Attention KV caches need no device
-work: trimming them is a length update (`KVLength.trim`).
+re-slices the conv window for every layer in one launch; `rollback_tree` does the same after a
+tree verify (the state of the accepted path's last node, the window gathered along the path).
+Attention KV caches need no device work for a chain: trimming them is a length update.
 """
 
 from __future__ import annotations
@@ -60,20 +61,18 @@ def rollback(states: list[torch.Tensor], ckpts: list[torch.Tensor], keep: int, f
               _stream(states[0].device))
 
 
-class KVLength:
-    """Attention KV cache bookkeeping: the cache tensors stay in place, rollback trims the length
-    (the reference's KVCache.trim(fed - keep), skinny_mlx/rollback.py:72-73)."""
-
-    def __init__(self, length: int = 0):
-        self.length = length
-
-    def advance(self, n: int) -> None:
-        self.length += n
-
-    def trim(self, n: int) -> int:
-        n = min(n, self.length)
-        self.length -= n
-        return n
+def rollback_tree(states: list[torch.Tensor], ckpts: list[torch.Tensor], node: int, rows: list[int], fed: int,
+                  convs: list[torch.Tensor], conv_fulls: list[torch.Tensor]) -> None:
+    """After a tree verify of `fed` nodes whose accepted path ends at `node`: every GDN layer's
+    state <- its checkpoint of `node`, its conv window <- conv_full rows `rows` (one launch)."""
+    n = len(states)
+    arr = ctypes.c_void_p * n
+    W, C = convs[0].shape
+    if len(rows) != W:
+        raise ValueError("one conv_full row per window row")
+    _lib.call("skinny_gdn_rollback_tree", n, arr(*[s.data_ptr() for s in states]), arr(*[c.data_ptr() for c in ckpts]),
+              arr(*[c.data_ptr() for c in convs]), arr(*[c.data_ptr() for c in conv_fulls]), states[0].numel(), node,
+              (ctypes.c_int32 * W)(*rows), fed, W, C, _stream(states[0].device))
 
 
-__all__ = ["recurrent", "rollback", "KVLength"]
+__all__ = ["recurrent", "rollback", "rollback_tree"]

@@ -184,7 +184,8 @@ class GDNCache:
         W = cfg.conv_kernel - 1
         self.conv = torch.zeros(W, cfg.conv_dim, dtype=torch.bfloat16, device=dev)
         self.state = torch.zeros(cfg.gdn_v_heads, cfg.gdn_dim, cfg.gdn_dim, dtype=torch.float32, device=dev)
-        self.ckpt = torch.zeros(max(max_verify - 1, 1), cfg.gdn_v_heads, cfg.gdn_dim, cfg.gdn_dim,
+        # the state after every verified token (a chain uses the first T - 1, a tree all T)
+        self.ckpt = torch.zeros(max_verify, cfg.gdn_v_heads, cfg.gdn_dim, cfg.gdn_dim,
                                 dtype=torch.float32, device=dev)
         self.conv_full = torch.zeros(W + max_verify, cfg.conv_dim, dtype=torch.bfloat16, device=dev)
         self.max_verify = max_verify
@@ -218,6 +219,21 @@ class Cache:
 
 
 # ---------------------------------------------------------------------------------------------
+# token trees (a speculative draft tree verified in one forward)
+# ---------------------------------------------------------------------------------------------
+def tree_paths(parent) -> list[list[int]]:
+    """parent[t] of every node (parent[0] = -1, parent[t] < t) -> each node's path from the root
+    (root first, the node last).  A chain is parent = [-1, 0, 1, ...]."""
+    parent = [int(v) for v in parent]
+    if not parent or parent[0] != -1 or any(not 0 <= parent[t] < t for t in range(1, len(parent))):
+        raise ValueError("a token tree needs parent[0] = -1 and 0 <= parent[t] < t")
+    paths = [[0]]
+    for t in range(1, len(parent)):
+        paths.append(paths[parent[t]] + [t])
+    return paths
+
+
+# ---------------------------------------------------------------------------------------------
 # layers
 # ---------------------------------------------------------------------------------------------
 # Backends for the module path's attention: the memory-efficient kernel takes the explicit
@@ -248,27 +264,38 @@ class Attention(nn.Module):
         self.q_norm = RMSNorm(D, cfg.rms_eps)
         self.k_norm = RMSNorm(D, cfg.rms_eps)
 
-    def forward(self, x: torch.Tensor, cache: AttnCache) -> torch.Tensor:
-        return self.o_proj(self.attend(self.q_proj(x), self.k_proj(x), self.v_proj(x), cache))
+    def forward(self, x: torch.Tensor, cache: AttnCache, tree=None) -> torch.Tensor:
+        return self.o_proj(self.attend(self.q_proj(x), self.k_proj(x), self.v_proj(x), cache, tree))
 
-    def attend(self, qg: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cache: AttnCache) -> torch.Tensor:
+    def attend(self, qg: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cache: AttnCache, tree=None) -> torch.Tensor:
         """Everything between the projections and o_proj: q/k norm, partial RoPE, KV append,
-        causal GQA attention over the cache, output gate.  Returns o bf16 [T, n_heads * D]."""
+        causal GQA attention over the cache, output gate.  Returns o bf16 [T, n_heads * D].
+        tree (parents of the T tokens, see tree_paths): token t sits at position L0 + depth(t)
+        and sees the cache and its ancestors; its key / value go to slot L0 + t."""
         cfg = self.cfg
         T, D, nh, nkv = qg.shape[0], cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
         qg = qg.reshape(T, nh, 2 * D)
         q, gate = qg[..., :D], qg[..., D:]
         k = k.reshape(T, nkv, D)
         v = v.reshape(T, nkv, D)
-        pos = torch.arange(cache.length, cache.length + T, device=qg.device)
+        L0 = cache.length
+        if tree is None:
+            pos = torch.arange(L0, L0 + T, device=qg.device)
+        else:
+            paths = tree_paths(tree)
+            pos = torch.tensor([L0 + len(pt) - 1 for pt in paths], device=qg.device)
         q = _rope(self.q_norm(q).float(), pos, cfg.rotary_dim, cfg.rope_theta)
         k = _rope(self.k_norm(k).float(), pos, cfg.rotary_dim, cfg.rope_theta)
-        L0 = cache.length
         cache.k[L0:L0 + T] = k.to(torch.bfloat16)
         cache.v[L0:L0 + T] = v
         cache.length = L0 + T
-        # queries sit at positions L0 .. L0+T-1 after L0 cached keys: bottom-right causal mask
-        causal = pos[:, None] >= torch.arange(L0 + T, device=qg.device)[None, :]
+        if tree is None:  # queries at positions L0 .. L0+T-1 after L0 cached keys: bottom-right causal
+            causal = pos[:, None] >= torch.arange(L0 + T, device=qg.device)[None, :]
+        else:
+            causal = torch.zeros(T, L0 + T, dtype=torch.bool, device=qg.device)
+            causal[:, :L0] = True
+            for t, pt in enumerate(paths):
+                causal[t, [L0 + j for j in pt]] = True
         with sdpa_kernel(_SDPA_BACKENDS):
             o = F.scaled_dot_product_attention(
                 q.to(torch.bfloat16).transpose(0, 1)[None], cache.k[:L0 + T].transpose(0, 1)[None],
@@ -298,25 +325,34 @@ class GatedDeltaNet(nn.Module):
         self.norm = RMSNorm(cfg.gdn_dim, cfg.rms_eps)
         self.out_proj = _qlinear(H, cfg.gdn_value_dim, gen, std, dev)
 
-    def forward(self, x: torch.Tensor, cache: GDNCache) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, cache: GDNCache, tree=None) -> torch.Tensor:
         return self.out_proj(self.mix(self.in_proj_qkv(x), self.in_proj_z(x), self.in_proj_b(x),
-                                      self.in_proj_a(x), cache))
+                                      self.in_proj_a(x), cache, tree))
 
-    def mix(self, qkv, z, b, a, cache: GDNCache) -> torch.Tensor:
+    def mix(self, qkv, z, b, a, cache: GDNCache, tree=None) -> torch.Tensor:
         """Everything between the input projections and out_proj (conv, gates, recurrence, gated
-        norm).  Returns o bf16 [T, value_dim]."""
+        norm).  Returns o bf16 [T, value_dim].  tree (parents, see tree_paths; needs a recording
+        cache): each token's conv window and recurrence follow its ancestor path, the state after
+        every token goes to the checkpoints, and the live state and window are left for the
+        rollback to select."""
         cfg = self.cfg
         T, W, dk = qkv.shape[0], cfg.conv_kernel - 1, cfg.gdn_dim
         z = z.reshape(T, cfg.gdn_v_heads, dk)
         b = b.float()
         a = a.float()
         full = torch.cat([cache.conv, qkv], dim=0)                     # [W + T, C]
+        if tree is not None and not cache.recording:
+            raise ValueError("a tree verify needs a recording cache (HybridRollback.record)")
         if cache.recording:
             cache.conv_full[:W + T] = full
             cache.fed = T
-        cache.conv.copy_(full[T:])
-        # depthwise causal conv: out[t] = sum_j w[:, j] * full[t + j], then SiLU
-        win = full.float().unfold(0, cfg.conv_kernel, 1)                # [T, C, kernel]
+        if tree is None:
+            cache.conv.copy_(full[T:])
+            # depthwise causal conv: out[t] = sum_j w[:, j] * full[t + j], then SiLU
+            win = full.float().unfold(0, cfg.conv_kernel, 1)            # [T, C, kernel]
+        else:
+            rows = torch.tensor([tree_rows(tree, t, W) for t in range(T)], device=qkv.device)
+            win = full.float()[rows].permute(0, 2, 1)                     # [T, C, kernel]
         conv = F.silu((win * self.conv_weight.float()[None]).sum(-1))
         q, k, v = torch.split(conv, [cfg.gdn_key_dim, cfg.gdn_key_dim, cfg.gdn_value_dim], dim=-1)
         q = F.normalize(q.view(T, cfg.gdn_k_heads, dk), dim=-1) / math.sqrt(dk)
@@ -325,7 +361,9 @@ class GatedDeltaNet(nn.Module):
         g = torch.exp(-torch.exp(self.A_log.float()) * F.softplus(a + self.dt_bias.float()))
         beta = torch.sigmoid(b)
         qb, kb, vb = (t.to(torch.bfloat16).contiguous() for t in (q, k, v))
-        if qkv.is_cuda and not GatedDeltaNet.torch_recurrence:  # CPU runs (tests) use torch
+        if tree is not None:  # (the module path's tree recurrence runs in torch)
+            y = _recurrent_torch(qb, kb, vb, g, beta, cache, tree)
+        elif qkv.is_cuda and not GatedDeltaNet.torch_recurrence:  # CPU runs (tests) use torch
             from .gdn import recurrent
 
             y = recurrent(qb, kb, vb, g.contiguous(), beta.contiguous(), cache.state,
@@ -336,19 +374,31 @@ class GatedDeltaNet(nn.Module):
         return o.reshape(T, cfg.gdn_value_dim).to(torch.bfloat16)
 
 
-def _recurrent_torch(q, k, v, g, beta, cache: GDNCache) -> torch.Tensor:
-    """The same gated delta rule in torch (CPU runs and cross-checks)."""
-    S = cache.state
+def tree_rows(tree, t: int, W: int) -> list[int]:
+    """Rows of [conv window (W rows); the T inputs] that form input t's causal conv window along
+    its ancestor path (the cached window above the root), oldest first, t's own row last."""
+    path = tree_paths(tree)[t]
+    seq = list(range(W)) + [W + j for j in path]
+    return seq[-(W + 1):]
+
+
+def _recurrent_torch(q, k, v, g, beta, cache: GDNCache, tree=None) -> torch.Tensor:
+    """The same gated delta rule in torch (CPU runs and cross-checks).  tree: each token starts
+    from its parent's state; the state after every token is checkpointed, the live state kept."""
     rep = v.shape[1] // q.shape[1]
+    parent = [int(p) for p in tree] if tree is not None else None
+    S = cache.state if tree is None else cache.state.clone()
     ys = []
     for t in range(q.shape[0]):
+        if parent is not None and t > 0 and parent[t] != t - 1:
+            S = cache.ckpt[parent[t]].clone()
         kt = k[t].float().repeat_interleave(rep, 0)
         qt = q[t].float().repeat_interleave(rep, 0)
         S.mul_(g[t][:, None, None])
         sk = torch.einsum("hvk,hk->hv", S, kt)
         S.add_(torch.einsum("hv,hk->hvk", beta[t][:, None] * (v[t].float() - sk), kt))
         ys.append(torch.einsum("hvk,hk->hv", S, qt))
-        if cache.recording and t + 1 < q.shape[0]:
+        if cache.recording and (tree is not None or t + 1 < q.shape[0]):
             cache.ckpt[t].copy_(S)
     return torch.stack(ys).to(torch.bfloat16)
 
@@ -377,9 +427,9 @@ class DecoderLayer(nn.Module):
         self.input_layernorm = RMSNorm(cfg.hidden, cfg.rms_eps)
         self.post_attention_layernorm = RMSNorm(cfg.hidden, cfg.rms_eps)
 
-    def forward(self, x, cache):
+    def forward(self, x, cache, tree=None):
         mixer = self.linear_attn if self.is_linear else self.self_attn
-        h = (x.float() + mixer(self.input_layernorm(x), cache).float()).to(torch.bfloat16)
+        h = (x.float() + mixer(self.input_layernorm(x), cache, tree).float()).to(torch.bfloat16)
         return (h.float() + self.mlp(self.post_attention_layernorm(h)).float()).to(torch.bfloat16)
 
 
@@ -406,13 +456,15 @@ class HybridModel(nn.Module):
         return Cache(self, max_len, max_verify)
 
     @torch.no_grad()
-    def forward(self, ids: torch.Tensor, cache: Cache):
+    def forward(self, ids: torch.Tensor, cache: Cache, tree=None):
+        """tree: parents of the input tokens (a draft tree, see tree_paths), or None (a chain)."""
         x = self.embed_tokens(ids)
         for layer, c in zip(self.layers, cache.layers):
-            x = layer(x, c)
+            x = layer(x, c, tree)
         h = self.norm(x)
         return h, self.embed_tokens.as_linear(h)
 
 
-__all__ = ["ModelConfig", "config3", "SMALL", "HybridModel", "QuantizedLinear", "QuantizedEmbedding",
+__all__ = ["ModelConfig", "config3", "SMALL", "HybridModel", "QuantizedLinear", "QuantizedEmbedding", "tree_paths",
+           "tree_rows",
            "Cache", "AttnCache", "GDNCache", "RMSNorm", "DecoderLayer", "Attention", "GatedDeltaNet", "MLP"]

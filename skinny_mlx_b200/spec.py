@@ -53,12 +53,49 @@ def accept(logits: torch.Tensor, draft: torch.Tensor) -> tuple[int, list[int]]:
     return n, r[1:n + 2]
 
 
-__all__ = ["accept", "accept_device"]
+def accept_tree(logits: torch.Tensor, tokens: torch.Tensor, parent: torch.Tensor) -> tuple[int, list[int], list[int]]:
+    """Greedy acceptance of a verified draft tree (one launch, one small D2H): logits bf16
+    [M, V] of the M nodes, tokens int32 [M] (node 0 = the last emitted token), parent int32 [M]
+    (parent[0] = -1, parent[t] < t), all on the device.  From the root, move to the first child
+    whose token equals the current node's prediction while one exists.  Returns (n accepted
+    nodes, emitted tokens: theirs + the last node's prediction, the path 0, p1 .. pn)."""
+    if logits.dtype != torch.bfloat16 or logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be a bf16 [M, V] tensor with unit column stride")
+    rows, v = logits.shape
+    if tokens.numel() != rows or parent.numel() != rows or tokens.dtype != torch.int32 or parent.dtype != torch.int32:
+        raise ValueError("tokens and parent must be int32 with one entry per node")
+    dev = logits.device
+    result = torch.empty(2 * rows + 1, dtype=torch.int32, device=dev)
+    ws = _workspace(dev)
+    _lib.call("skinny_spec_accept_tree", ctypes.c_void_p(logits.data_ptr()), logits.stride(0), rows, v,
+              ctypes.c_void_p(tokens.data_ptr()), ctypes.c_void_p(parent.data_ptr()), ctypes.c_void_p(result.data_ptr()),
+              None, ctypes.c_void_p(ws.data_ptr()), ws.numel(), ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+    r = result.cpu().tolist()
+    n = r[0]
+    return n, r[1:n + 2], r[1 + rows:2 + rows + n]
+
+
+__all__ = ["accept", "accept_device", "accept_tree"]
 
 
 # ---------------------------------------------------------------------------------------------
 # decode loops (skinny_mlx/spec.py:54-156 on B200)
 # ---------------------------------------------------------------------------------------------
+def _accept_tree_any(logits: torch.Tensor, tokens: torch.Tensor, parent: list[int]) -> tuple[int, list[int], list[int]]:
+    if logits.is_cuda:
+        return accept_tree(logits, tokens.to(torch.int32), torch.tensor(parent, dtype=torch.int32, device=logits.device))
+    pred = torch.argmax(logits.float(), dim=-1).tolist()  # CPU runs of the model (tests)
+    tok = tokens.tolist()
+    cur, path = 0, [0]
+    while True:
+        nxt = next((c for c in range(cur + 1, len(parent)) if parent[c] == cur and tok[c] == pred[cur]), None)
+        if nxt is None:
+            break
+        path.append(nxt)
+        cur = nxt
+    return len(path) - 1, [tok[c] for c in path[1:]] + [pred[cur]], path
+
+
 def _accept_any(logits: torch.Tensor, draft: torch.Tensor) -> tuple[int, list[int]]:
     if logits.is_cuda:
         return accept(logits, draft)
@@ -103,6 +140,51 @@ class HybridRollback:
         for c in cache.layers:
             if isinstance(c, AttnCache):
                 c.trim(fed - keep)
+
+    def rollback_tree(self, cache, fed: int, path: list[int]) -> None:
+        """After a tree verify of `fed` nodes, keep the accepted path (node indices, root 0
+        first): GDN state <- the checkpoint of the path's last node, conv window <- the last W
+        conv inputs along the path; attention caches keep the path's keys and values, moved to
+        the slots of their positions (L0 + depth), and drop the rest."""
+        from .model import AttnCache, GDNCache
+
+        gdn = [c for c in cache.layers if isinstance(c, GDNCache)]
+        for c in gdn:
+            c.recording = False
+        node, n = path[-1], len(path) - 1
+        if gdn:
+            W = gdn[0].conv.shape[0]
+            rows = ([*range(W)] + [W + j for j in path])[-W:]
+            if gdn[0].state.is_cuda:
+                from .gdn import rollback_tree
+
+                rollback_tree([c.state for c in gdn], [c.ckpt for c in gdn], node, rows, fed, [c.conv for c in gdn],
+                              [c.conv_full for c in gdn])
+            else:
+                for c in gdn:
+                    c.state.copy_(c.ckpt[node])
+                    c.conv.copy_(c.conv_full[rows])
+        moved = path[1:] != list(range(1, n + 1))
+        for c in cache.layers:
+            if isinstance(c, AttnCache):
+                L0 = c.length - fed
+                if moved:
+                    src = torch.tensor([L0 + j for j in path[1:]], device=c.k.device)
+                    c.k[L0 + 1:L0 + 1 + n] = c.k[src]
+                    c.v[L0 + 1:L0 + 1 + n] = c.v[src]
+                c.length = L0 + 1 + n
+
+
+def chain_tree(k: int) -> list[int]:
+    """Parents of the top-2 chain tree of depth k: node 0 the last emitted token, then per depth
+    i = 1 .. k the chain's token c_i (node 2i - 1) and its runner-up s_i (node 2i), both children
+    of c_{i-1} (of the root for i = 1).  M = 2k + 1 nodes: the drafter's best guess at every
+    position plus the alternative that a chain drafter throws away."""
+    par = [-1]
+    for i in range(1, k + 1):
+        p = 0 if i == 1 else 2 * i - 3
+        par += [p, p]
+    return par
 
 
 class MTPDrafter:
@@ -164,6 +246,20 @@ class MTPDrafter:
         self.cache.trim(self.n_spec)
         self.h_last = self._step(torch.tensor(new_tokens, device=self.model.device), h_kept)[-1:]
         self.n_spec = 0
+
+    def draft_tree(self, k: int) -> tuple[torch.Tensor, list[int]]:
+        """The top-2 chain tree (chain_tree): the K chained head steps of draft(), keeping each
+        step's runner-up as a sibling of its chain token.  Returns (tokens of nodes 1 .. 2k,
+        int32 on the device, parents of all 2k + 1 nodes)."""
+        toks, h = [], self.h_last
+        for i in range(k):
+            top = torch.topk(self._logits(h[-1:]).float(), 2, dim=-1).indices[0]
+            t2 = self.ids[top]
+            toks.append(t2)
+            if i < k - 1:
+                h = self._step(t2[:1], h[-1:])
+        self.n_spec = k - 1
+        return torch.cat(toks).to(torch.int32), chain_tree(k)
 
 
 class GraphedMTPDrafter(MTPDrafter):
@@ -263,6 +359,9 @@ class GraphedMTPDrafter(MTPDrafter):
         self.cache.length += m
         self.n_spec = 0
 
+    def draft_tree(self, k: int):
+        raise NotImplementedError("tree drafts use the eager MTPDrafter (the graphs replay a chain)")
+
 
 class PromptLookupDrafter:
     """Model-free drafter (skinny_mlx/spec.py:32-51): proposes the up to K tokens that followed the
@@ -333,6 +432,35 @@ class ScriptedDrafter:
         self.pos += len(new_tokens)
 
 
+class ScriptedTreeDrafter:
+    """The top-2 chain tree (chain_tree) over a known greedy continuation `ref`: each chain token
+    is right with probability p (seeded); where it is wrong, its sibling is right with
+    probability p, else both are wrong.  Speculative decoding with a tree at a chosen acceptance
+    rate; compare ScriptedDrafter at the same p (the chain alone)."""
+
+    def __init__(self, ref: list[int], p: float, vocab: int, device, seed: int = 0):
+        self.ref, self.p, self.vocab, self.device = ref, p, vocab, device
+        self.rng = torch.Generator().manual_seed(seed)
+
+    def begin(self, prompt, h, first) -> None:
+        self.pos = 1
+
+    def draft_tree(self, k: int) -> tuple[torch.Tensor, list[int]]:
+        toks = []
+        for i in range(k):
+            j = self.pos + i
+            t = self.ref[j] if j < len(self.ref) else 0
+            chain_ok = float(torch.rand((), generator=self.rng)) < self.p
+            sib_ok = not chain_ok and float(torch.rand((), generator=self.rng)) < self.p
+            c = t if chain_ok else (t + 1) % self.vocab
+            sib = t if sib_ok else (t + 2) % self.vocab
+            toks += [c, sib]
+        return torch.tensor(toks, dtype=torch.int32).to(self.device, non_blocking=True), chain_tree(k)
+
+    def update(self, h_kept, new_tokens) -> None:
+        self.pos += len(new_tokens)
+
+
 def _fresh_cache(model, cache):
     if cache is None:
         return model.make_cache()
@@ -391,5 +519,35 @@ def speculative(model, prompt: list[int], max_tokens: int, drafter, k: int, stat
     return out[:max_tokens]
 
 
-__all__ += ["HybridRollback", "MTPDrafter", "GraphedMTPDrafter", "PromptLookupDrafter", "ScriptedDrafter", "greedy",
-            "speculative"]
+def speculative_tree(model, prompt: list[int], max_tokens: int, drafter, k: int, stats: dict | None = None,
+                     cache=None) -> list[int]:
+    """Greedy-exact speculative decoding with a draft TREE verified in one forward (the wider
+    drafts the reference proposes to fill the flat-verify budget, docs/flatspec-design.md:64-69):
+    each step the drafter proposes tree nodes (draft_tree(k) -> node tokens, parents), the model
+    verifies [last token] + nodes with tree attention and a branch-aware GDN recurrence, the
+    device walks the tree along the model's own predictions, and the cache keeps the accepted
+    path.  `model` is a HybridModel (module path) or its FusedStep / GraphedStep."""
+    cache = _fresh_cache(model, cache)
+    rb = HybridRollback()
+    h, logits = model(torch.tensor(prompt, device=model.device), cache)
+    out = [int(torch.argmax(logits[-1].float()))]
+    drafter.begin(prompt, h, out[0])
+    steps = accepted = 0
+    while len(out) < max_tokens:
+        nodes, parent = drafter.draft_tree(k)
+        x = torch.cat([torch.tensor([out[-1]], dtype=torch.int32, device=model.device), nodes])
+        rb.record(cache)
+        h, logits = model(x.long(), cache, tree=parent)
+        n, new, path = _accept_tree_any(logits, x, parent)
+        rb.rollback_tree(cache, fed=x.numel(), path=path)
+        drafter.update(h[torch.tensor(path, device=h.device)], new)
+        out += new
+        steps += 1
+        accepted += n
+    if stats is not None:
+        stats.update(steps=steps, tokens_per_step=len(out) / max(steps, 1), accepted=accepted)
+    return out[:max_tokens]
+
+
+__all__ += ["HybridRollback", "MTPDrafter", "GraphedMTPDrafter", "PromptLookupDrafter", "ScriptedDrafter",
+            "ScriptedTreeDrafter", "chain_tree", "greedy", "speculative", "speculative_tree"]

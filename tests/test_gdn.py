@@ -80,7 +80,7 @@ def test_recurrent_matches_oracle(cuda_lib, dev, T, Hv, Hk):
 
 @pytest.mark.gpu
 def test_rollback_restores_prefix_state_and_conv(cuda_lib, dev):
-    from skinny_mlx_b200.gdn import recurrent, rollback, KVLength
+    from skinny_mlx_b200.gdn import recurrent, rollback
 
     rng = np.random.default_rng(7)
     T, Hv, W, C, L = 6, 16, 3, 256, 3
@@ -106,5 +106,28 @@ def test_rollback_restores_prefix_state_and_conv(cuda_lib, dev):
             assert np.array_equal(conv.float().cpu().numpy(), c_want)
         for (s, c), x in zip(snap, layers):  # restore the after-verify state for the next keep
             x[0].copy_(s)
-    kv = KVLength(100)
-    assert kv.trim(6 - 4) == 2 and kv.length == 98
+
+
+@pytest.mark.gpu
+def test_rollback_tree_selects_node_state_and_path_window(cuda_lib, dev):
+    """Tree rollback: every layer's state becomes its checkpoint of the accepted path's last node
+    and its conv window the given conv_full rows, bit for bit, in one launch."""
+    from skinny_mlx_b200.gdn import rollback_tree
+    from skinny_mlx_b200.model import tree_rows
+
+    torch.manual_seed(3)
+    T, Hv, W, C, L = 7, 4, 3, 192, 2
+    parent = [-1, 0, 0, 1, 1, 3, 3]
+    states = [torch.randn(Hv, 128, 128, device=dev) for _ in range(L)]
+    ckpts = [torch.randn(T, Hv, 128, 128, device=dev) for _ in range(L)]
+    convs = [torch.zeros(W, C, dtype=torch.bfloat16, device=dev) for _ in range(L)]
+    fulls = [torch.randn(W + T, C, device=dev).to(torch.bfloat16) for _ in range(L)]
+    for path in ([0], [0, 2], [0, 1, 4], [0, 1, 3, 6]):
+        node = path[-1]
+        rows = tree_rows(parent, node, W)[1:]  # the window after the node: its last W inputs
+        assert rows == ([*range(W)] + [W + j for j in path])[-W:]
+        rollback_tree(states, ckpts, node, rows, T, convs, fulls)
+        torch.cuda.synchronize()
+        for s, ck, cv, cf in zip(states, ckpts, convs, fulls):
+            assert torch.equal(s, ck[node])
+            assert torch.equal(cv, cf[rows])

@@ -171,3 +171,108 @@ def test_cpu_mtp_head_matches_oracle():
     for a, b in ((0, 20), (20, 21), (21, 24)):
         ref = oh(emb[a:b].float().numpy()[None], hid[a:b].float().numpy()[None], oc)[0]
         assert rel_err(ref, head(emb[a:b], hid[a:b], c).float().numpy()) <= 1.5e-2
+
+
+def _tree_vs_paths(model, cache_factory, ids_prompt, nodes, parent, dev):
+    """Logits of a tree verify, and for every node t the logits of a chain verify of t's path
+    from the same cache (the reference for tree attention and the branch-aware recurrence)."""
+    from skinny_mlx_b200.model import tree_paths
+    from skinny_mlx_b200.spec import HybridRollback
+
+    rb = HybridRollback()
+    c = cache_factory()
+    model(ids_prompt, c)
+    rb.record(c)
+    tree_logits = model(nodes, c, tree=parent)[1].float().cpu().clone()
+    rows = []
+    for t, path in enumerate(tree_paths(parent)):
+        c = cache_factory()
+        model(ids_prompt, c)
+        rb.record(c)
+        rows.append(model(nodes[path], c)[1][-1].float().cpu().clone())
+    return tree_logits, torch.stack(rows)
+
+
+def test_cpu_tree_verify_equals_path_verifies():
+    """Module path on the CPU: each node's logits in a tree verify (tree mask, positions by depth,
+    branch-aware conv and recurrence) equal those of verifying its ancestor path as a chain."""
+    from oracle.checks import rel_err
+    from skinny_mlx_b200.spec import chain_tree
+
+    m = _model("cpu")
+    parent = chain_tree(3)
+    nodes = torch.tensor(G["greedy"][:7])
+    got, want = _tree_vs_paths(m, m.make_cache, torch.tensor(PROMPT), nodes, parent, "cpu")
+    assert rel_err(want.numpy(), got.numpy()) <= 1e-2
+
+
+def test_cpu_tree_speculation_matches_reference_stream():
+    """speculative_tree (top-2 chain trees from a scripted drafter; host acceptance and tree
+    rollback) on the CPU module path reproduces the reference's greedy stream."""
+    from skinny_mlx_b200.spec import ScriptedTreeDrafter, speculative_tree
+
+    m = _model("cpu")
+    for k, p in ((2, 0.5), (3, 0.7)):
+        st = {}
+        got = speculative_tree(m, PROMPT, N, ScriptedTreeDrafter(G["greedy"], p, m.cfg.vocab, "cpu", seed=k), k, st)
+        _check(f"tree k{k}", got)
+        assert st["accepted"] > 0
+
+
+@pytest.mark.gpu
+def test_gpu_tree_verify_equals_path_verifies(cuda_lib, dev):
+    """Fused kernels (tree attention, branch-aware GDN mixer), eager and graph-replayed: each
+    node's logits in one tree verify equal the logits of verifying its ancestor path as a chain
+    on the same kernels (a token's arithmetic does not depend on its batch), and equal the torch
+    module path's tree verify within the bf16 tolerance."""
+    from oracle.checks import argmax_violations, rel_err
+    from skinny_mlx_b200.fused import FusedStep, GraphedStep
+    from skinny_mlx_b200.patch import patch_model
+    from skinny_mlx_b200.spec import chain_tree
+
+    m = _model(dev)
+    patch_model(m)
+    f = FusedStep(m)
+    gs = GraphedStep(f)
+    ids = torch.tensor(PROMPT, device=dev)
+    for k, parent in ((3, chain_tree(3)), (2, [-1, 0, 0, 1, 1]), (7, [-1, 0, 1, 1, 0, 4, 2, 3, 7, 8, 6, 10, 11, 12, 9])):
+        nodes = torch.tensor(G["greedy"][:len(parent)], device=dev)
+        got, want = _tree_vs_paths(f, f.make_cache, ids, nodes, parent, dev)
+        assert rel_err(want.numpy(), got.numpy()) <= 1.5e-2, k
+        assert not argmax_violations(want.numpy(), got.numpy())
+        gcache = gs.make_cache()
+        got_g, _ = _tree_vs_paths(gs, lambda: (gcache.reset(), gcache)[1], ids, nodes, parent, dev)
+        assert torch.equal(got_g, got)
+        mod, _ = _tree_vs_paths(m, m.make_cache, ids, nodes, parent, dev)
+        assert rel_err(mod.numpy(), got.numpy()) <= 1.5e-2
+    from skinny_mlx_b200.qmm import device_errors
+
+    assert device_errors(dev) == 0
+
+
+@pytest.mark.gpu
+def test_gpu_tree_speculation_matches_reference_stream(cuda_lib, dev):
+    """speculative_tree on the fused step (eager and graph-replayed) with scripted top-2 trees and
+    the MTP head's top-2 chain tree reproduces the reference's greedy stream."""
+    from skinny_mlx_b200.fused import FusedStep, GraphedStep
+    from skinny_mlx_b200.mtp import MTPHead
+    from skinny_mlx_b200.patch import patch_model
+    from skinny_mlx_b200.spec import MTPDrafter, ScriptedTreeDrafter, speculative_tree
+
+    m = _model(dev)
+    head = MTPHead(m, seed=13, init_device="cpu")
+    patch_model(m)
+    patch_model(head)
+    f = FusedStep(m)
+    gs = GraphedStep(f)
+    cache = gs.make_cache()
+    for k, p in ((2, 0.5), (3, 0.7), (4, 0.8)):
+        for label, model, kw in (("fused", f, {}), ("graphed", gs, {"cache": cache})):
+            st = {}
+            d = ScriptedTreeDrafter(G["greedy"], p, m.cfg.vocab, dev, seed=k)
+            _check(f"tree k{k} {label}", speculative_tree(model, PROMPT, N, d, k, st, **kw))
+            assert st["accepted"] > 0
+    _check("mtp tree", speculative_tree(gs, PROMPT, N, MTPDrafter(m, head, vocab=None), 3, cache=cache))
+    from skinny_mlx_b200.qmm import device_errors
+
+    assert device_errors(dev) == 0
