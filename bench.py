@@ -18,7 +18,7 @@ MTP, prompt-lookup and scripted drafters); at every N, config 5 (the 64-layer de
 over the ranks).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl skinny|reference]
-    python bench.py --case head|verify|attn ...   (small cases for profilers)
+    python bench.py --case head|verify|attn|gdn ...   (small cases for profilers)
 
 With N > 1 (torchrun) every rank runs an independent replica of the stack (the path has no
 exchange step at this configuration): value = bytes of all ranks / max-over-ranks time.
@@ -660,7 +660,9 @@ def run_skinny(args, world, rank, local):
         r = cpu_baseline.time_stack(cshapes, M_STACK, budget_s=12.0)
         cpu = {"value": round(r["bytes_per_s"] / 1e9, 3), "unit": "GB/s", "cores": r["cores"], "kind": "port",
                "sample": f"{r['calls']} consecutive stack projections at M=8 through the oracle's f32 "
-                         f"dequant+GEMM ({r['seconds']:.1f} s of CPU work), scaled to bytes/s"}
+                         f"dequant+GEMM ({r['seconds']:.1f} s of CPU work), scaled to bytes/s",
+               # the other configs' CPU rows (same port, about 16 s more of CPU work)
+               "rows": cpu_baseline.baseline_rows(cshapes)}
 
     traffic = None
     tp = ROOT / "profiles" / "qmm_traffic.json"
@@ -771,6 +773,57 @@ def run_attn_case(args):
                       "GBps": round(kv / (us * 1e-6) / 1e9, 1)}), flush=True)
 
 
+def run_gdn_case(args):
+    """--case gdn: the fused GDN mixer of the config-3 model (16 value heads of 128, conv window 3)
+    at --m tokens with checkpoints recorded, 24 layers' states back to back per step: a small case
+    for profilers (about 60 MB on the device)."""
+    import ctypes
+
+    from skinny_mlx_b200 import _lib
+    from skinny_mlx_b200.model import GDNCache, config3
+
+    dev = torch.device("cuda", 0)
+    cfg = config3()
+    T, layers, Hv = args.m, 24, cfg.gdn_v_heads
+    g = torch.Generator(device=dev).manual_seed(3)
+    width = 4 * cfg.gdn_value_dim + 2 * Hv
+    proj = (torch.randn(T, width, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+    caches = []
+    for _ in range(layers):
+        c = GDNCache(cfg, 17, dev)
+        c.state.normal_(generator=g).mul_(0.05)
+        caches.append(c)
+    conv_w = (torch.randn(cfg.conv_dim, cfg.conv_kernel, device=dev, generator=g) * 0.3).contiguous()
+    A_log = torch.log(torch.rand(Hv, device=dev, generator=g) * 15 + 1)
+    dt_bias = torch.randn(Hv, device=dev, generator=g) * 0.1
+    norm_w = torch.zeros(cfg.gdn_dim, device=dev)
+    xq = torch.empty(int(_lib.lib().skinny_xq_bytes(T, cfg.gdn_value_dim)), dtype=torch.uint8, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+
+    def step():
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        for c in caches:
+            _lib.call("skinny_gdn_fused", P(proj), proj.stride(0), P(c.conv), P(c.conv_full), P(conv_w), P(A_log),
+                      P(dt_bias), P(norm_w), cfg.rms_eps, P(c.state), P(c.ckpt) if T > 1 else None, P(xq), None, T,
+                      Hv, Hv, cfg.conv_kernel - 1, P(err), stream)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps / layers
+    state = Hv * cfg.gdn_dim * cfg.gdn_dim * 4
+    moved = 2 * state + (T - 1) * state  # state read and written, T - 1 checkpoints written
+    print(json.dumps({"case": "gdn", "tokens": T, "us_per_layer": round(us, 2), "state_bytes": moved,
+                      "GBps": round(moved / (us * 1e-6) / 1e9, 1), "errors": int(err.item())}), flush=True)
+
+
 def run_verify_case(args):
     """--case verify: the config-3 fused verify step at M = 1 and M = 8 (2048 cached tokens,
     checkpoints recorded), each captured in a CUDA graph; after warm replays, one replay of each
@@ -841,11 +894,11 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the config-3/4 model measurements")
     ap.add_argument("--no-dense", action="store_true", help="skip the config-5 column-parallel model")
-    ap.add_argument("--case", default="stack", choices=["stack", "head", "verify", "attn"],
+    ap.add_argument("--case", default="stack", choices=["stack", "head", "verify", "attn", "gdn"],
                     help="head: single-matrix profiling case; verify: the config-3 step at M = 1 and 8 "
-                         "in NVTX ranges; attn: the dense model's attention at --m tokens; all instead "
-                         "of the bench line")
-    ap.add_argument("--m", type=int, default=M_STACK, help="tokens for --case head and --case attn")
+                         "in NVTX ranges; attn: the dense model's attention at --m tokens; gdn: the "
+                         "config-3 GDN mixer at --m tokens; all instead of the bench line")
+    ap.add_argument("--m", type=int, default=M_STACK, help="tokens for --case head, attn and gdn")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.case == "head":
@@ -856,6 +909,9 @@ def main():
         return
     if args.case == "attn":
         run_attn_case(args)
+        return
+    if args.case == "gdn":
+        run_gdn_case(args)
         return
     world, rank, local = init_dist()
     try:

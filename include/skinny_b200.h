@@ -313,6 +313,14 @@ int skinny_gdn_rollback(int n_layers, float* const* state, const float* const* c
                         void* const* conv, const void* const* conv_full, long long state_elems,
                         int keep, int fed, int W, int C, void* stream);
 
+/* Attention caches after a TREE verify (skinny_attn_fused_tree appends node t at slot L0 + t):
+ * in each of n_layers K and V caches ([max_len, ...] rows of row_bytes, 16-byte aligned) rows
+ * L0[l] + path[j] move to rows L0[l] + j for j = 1 .. n_path - 1 (path: HOST array, the accepted
+ * path 0, p1 .. pn, strictly increasing).  One launch; the caller then sets each length to
+ * L0 + n_path.  The tree counterpart of KVCache.trim in skinny_mlx/rollback.py:72-73. */
+int skinny_kv_compact(int n_layers, void* const* k_caches, void* const* v_caches, int row_bytes, const int32_t* L0,
+                      const int32_t* path, int n_path, int max_len, void* stream);
+
 /* Rollback of all GDN layers after a TREE verify of `fed` nodes whose accepted path ends at node
  * `node`: state[l] <- ckpt[l][node], conv[l] row q <- conv_full[l] row rows[q] for q < W (rows: a
  * HOST array, the last W conv inputs along the path: window rows 0 .. W-1, node t at W + t). */

@@ -63,6 +63,32 @@ def time_stack(shapes, m: int, budget_s: float = 12.0, seed: int = 0) -> dict:
             "cores": threads(), "host_cpus": os.cpu_count()}
 
 
+def baseline_rows(stack_shapes, budget_s: float = 16.0) -> dict:
+    """CPU rows beside the B200 numbers, all through qmm_cpu on the host cores, about budget_s of
+    work: config 1 (one 9728 x 2560 matrix) at M = 1, 8, 16; the config-2 stack at M = 1 and 8,
+    from which the config-3 step's projection cost at M = 1 and 8 and the config-4 greedy rate
+    follow (the step's 129 projections only: the mixers' recurrence and attention are left out,
+    so these CPU step times are lower bounds)."""
+    out = {"config1_gbs": {}}
+    for m in (1, 8, 16):
+        r = time_stack([(9728, 2560)], m, budget_s=budget_s * 0.08)
+        out["config1_gbs"][str(m)] = round(r["bytes_per_s"] / 1e9, 3)
+    stack_bytes = sum(n * k // 2 + n * (k // 64) * 4 for n, k in stack_shapes)
+    steps = {}
+    for m, frac in ((1, 0.3), (8, 0.46)):
+        r = time_stack(stack_shapes, m, budget_s=budget_s * frac, seed=m)
+        w_bytes_s = r["bytes_per_s"] * stack_bytes / (stack_bytes + 2 * m * sum(n + k for n, k in stack_shapes))
+        steps[str(m)] = round(stack_bytes / w_bytes_s * 1e3, 1)
+        if m == 8:
+            out["config2_stack_gbs"] = round(r["bytes_per_s"] / 1e9, 3)
+    out["config3_projection_ms"] = steps
+    out["config3_cost_m8_vs_m1"] = round(steps["8"] / steps["1"], 3)
+    out["config4_greedy_tok_s"] = round(1e3 / steps["1"], 3)
+    out["cores"] = threads()
+    out["host_cpus"] = os.cpu_count()
+    return out
+
+
 if __name__ == "__main__":
     print(time_stack([(9728, 2560)], 8, budget_s=3.0))
     _ = np

@@ -74,6 +74,7 @@ SIGNATURES = {
                                        c_size_t, c_void_p, c_void_p, c_void_p, c_void_p]),
     "skinny_spec_accept_tree": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_size_t, c_void_p]),
+    "skinny_kv_compact": (c_int, [c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "skinny_gdn_rollback_tree": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_longlong, c_int,
                                          c_void_p, c_int, c_int, c_int, c_void_p]),
 }

@@ -618,6 +618,63 @@ __global__ void __launch_bounds__(kAtThreads) attn_merge_kernel(const __grid_con
   peer_signal_done(p.sync, &sync_flag);  // (sharded step) this rank's digit groups are ready
 }
 
+// KV slot compaction after a tree verify: in every layer's K and V cache, rows L0 + path[j] move
+// to rows L0 + j (j = 1 .. n; path[0] = 0 stays).  One CTA per (layer, K or V): every source row
+// is loaded before any destination row is written (a destination may be another copy's source).
+constexpr int kKvMaxLayers = 64;
+struct KvCompactParams {
+  uint8_t* cache[2 * kKvMaxLayers];  // k of layer l at 2l, v at 2l + 1
+  int L0[kKvMaxLayers];
+  int path[kAtMaxT];
+  int n, row_bytes;
+};
+
+__global__ void __launch_bounds__(256) kv_compact_kernel(const __grid_constant__ KvCompactParams p) {
+  constexpr int kPer = 8;  // 16-byte pieces per thread: 256 * 8 * 16 = 32 KB >= 15 rows of 2 KB
+  uint8_t* base = p.cache[blockIdx.x];
+  const int L0 = p.L0[blockIdx.x >> 1];
+  const int pieces_row = p.row_bytes / 16, total = p.n * pieces_row;
+  uint4 v[kPer];
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int e = threadIdx.x + u * 256;
+    if (e < total) {
+      const int j = e / pieces_row + 1, q = e - (j - 1) * pieces_row;
+      v[u] = *reinterpret_cast<const uint4*>(base + static_cast<size_t>(L0 + p.path[j]) * p.row_bytes + 16 * q);
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int e = threadIdx.x + u * 256;
+    if (e < total) {
+      const int j = e / pieces_row + 1, q = e - (j - 1) * pieces_row;
+      *reinterpret_cast<uint4*>(base + static_cast<size_t>(L0 + j) * p.row_bytes + 16 * q) = v[u];
+    }
+  }
+}
+
+bool kv_compact_fits(int n_layers, int n, int row_bytes) {
+  return n_layers >= 1 && n_layers <= kKvMaxLayers && n >= 0 && n < kAtMaxT && row_bytes >= 16 &&
+         row_bytes % 16 == 0 && static_cast<long long>(n) * (row_bytes / 16) <= 256 * 8;
+}
+
+cudaError_t kv_compact_launch(int n_layers, void* const* k, void* const* v, const int* L0, const int* path, int n,
+                              int row_bytes, cudaStream_t stream) {
+  static thread_local KvCompactParams prm;
+  for (int l = 0; l < n_layers; ++l) {
+    prm.cache[2 * l] = static_cast<uint8_t*>(k[l]);
+    prm.cache[2 * l + 1] = static_cast<uint8_t*>(v[l]);
+    prm.L0[l] = L0[l];
+  }
+  for (int j = 0; j < kAtMaxT; ++j) prm.path[j] = j <= n ? path[j] : 0;
+  prm.n = n;
+  prm.row_bytes = row_bytes;
+  if (n == 0) return cudaSuccess;
+  kv_compact_kernel<<<2 * n_layers, 256, 0, stream>>>(prm);
+  return cudaGetLastError();
+}
+
 size_t attn_ws_bytes(int T, int nh, int nkv, int max_len) {
   const int rep = nh / nkv;
   const int nrg = (T * rep + kAtRG - 1) / kAtRG;

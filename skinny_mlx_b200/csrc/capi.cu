@@ -69,6 +69,9 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
 cudaError_t spec_accept_tree_launch(const void* logits, int ld, int rows, int V, const int32_t* tokens,
                                     const int32_t* parent, int32_t* result, int32_t* pred, void* ws,
                                     cudaStream_t stream);
+bool kv_compact_fits(int n_layers, int n, int row_bytes);
+cudaError_t kv_compact_launch(int n_layers, void* const* k, void* const* v, const int* L0, const int* path, int n,
+                              int row_bytes, cudaStream_t stream);
 cudaError_t gdn_rollback_tree_call(int n_layers, float* const* state, const float* const* ckpt, void* const* conv,
                                   const void* const* conv_full, long long state_elems, int node, const int* rows,
                                   int W, int C, cudaStream_t stream);
@@ -514,6 +517,21 @@ int skinny_gdn_rollback(int n_layers, float* const* state, const float* const* c
   }
   return cuda_status(skinny::gdn_rollback_call(n_layers, state, ckpt, conv, conv_full, state_elems,
                                                keep, fed, W, C, static_cast<cudaStream_t>(stream)));
+}
+
+int skinny_kv_compact(int n_layers, void* const* k_caches, void* const* v_caches, int row_bytes, const int32_t* L0,
+                      const int32_t* path, int n_path, int max_len, void* stream) {
+  if (!k_caches || !v_caches || !L0 || !path || n_path < 1) return SKINNY_ERR_INVALID_ARG;
+  if (!skinny::kv_compact_fits(n_layers, n_path - 1, row_bytes) || path[0] != 0) return SKINNY_ERR_SHAPE;
+  for (int j = 1; j < n_path; ++j)
+    if (path[j] < j || path[j] <= path[j - 1]) return SKINNY_ERR_SHAPE;  // a root-to-node path in a topological tree
+  for (int l = 0; l < n_layers; ++l) {
+    if (!k_caches[l] || !v_caches[l]) return SKINNY_ERR_INVALID_ARG;
+    if (!aligned16(k_caches[l]) || !aligned16(v_caches[l])) return SKINNY_ERR_ALIGNMENT;
+    if (L0[l] < 0 || L0[l] + path[n_path - 1] >= max_len) return SKINNY_ERR_SHAPE;
+  }
+  return cuda_status(skinny::kv_compact_launch(n_layers, k_caches, v_caches, L0, path, n_path - 1, row_bytes,
+                                               static_cast<cudaStream_t>(stream)));
 }
 
 int skinny_gdn_rollback_tree(int n_layers, float* const* state, const float* const* ckpt, void* const* conv,

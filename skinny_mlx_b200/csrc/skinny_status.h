@@ -22,7 +22,6 @@ constexpr unsigned kErrBitWaitAEmpty = 1u << 3;
 constexpr unsigned kErrBitWaitDFull = 1u << 4;
 constexpr unsigned kErrBitWaitDEmpty = 1u << 5;
 constexpr unsigned kErrBitWaitDrain = 1u << 6;
-constexpr unsigned kErrBitXOverflow = 1u << 8;  // an activation exceeded the f16 range
 constexpr unsigned kErrBitBadInput = 1u << 9;   // e.g. a token id outside the vocabulary
 constexpr unsigned kErrBitWaitCluster = 1u << 10;  // a CTA's wait for its cluster peers' data
 constexpr unsigned kErrBitWaitPeer = 1u << 11;     // a launch's wait for the other ranks' flags

@@ -164,15 +164,24 @@ class HybridRollback:
                 for c in gdn:
                     c.state.copy_(c.ckpt[node])
                     c.conv.copy_(c.conv_full[rows])
-        moved = path[1:] != list(range(1, n + 1))
-        for c in cache.layers:
-            if isinstance(c, AttnCache):
-                L0 = c.length - fed
-                if moved:
-                    src = torch.tensor([L0 + j for j in path[1:]], device=c.k.device)
-                    c.k[L0 + 1:L0 + 1 + n] = c.k[src]
-                    c.v[L0 + 1:L0 + 1 + n] = c.v[src]
-                c.length = L0 + 1 + n
+        attn = [c for c in cache.layers if isinstance(c, AttnCache)]
+        if attn and path[1:] != list(range(1, n + 1)):  # the path's keys / values to slots L0 + depth
+            L0 = [c.length - fed for c in attn]
+            if attn[0].k.is_cuda:
+                import ctypes
+
+                arr = ctypes.c_void_p * len(attn)
+                _lib.call("skinny_kv_compact", len(attn), arr(*[c.k.data_ptr() for c in attn]),
+                          arr(*[c.v.data_ptr() for c in attn]), attn[0].k[0].numel() * attn[0].k.element_size(),
+                          (ctypes.c_int32 * len(attn))(*L0), (ctypes.c_int32 * len(path))(*path), len(path),
+                          attn[0].k.shape[0], ctypes.c_void_p(torch.cuda.current_stream(attn[0].k.device).cuda_stream))
+            else:
+                for c, l0 in zip(attn, L0):
+                    src = torch.tensor([l0 + j for j in path[1:]])
+                    c.k[l0 + 1:l0 + 1 + n] = c.k[src]
+                    c.v[l0 + 1:l0 + 1 + n] = c.v[src]
+        for c in attn:
+            c.length = c.length - fed + 1 + n
 
 
 def chain_tree(k: int) -> list[int]:
@@ -540,7 +549,7 @@ def speculative_tree(model, prompt: list[int], max_tokens: int, drafter, k: int,
         h, logits = model(x.long(), cache, tree=parent)
         n, new, path = _accept_tree_any(logits, x, parent)
         rb.rollback_tree(cache, fed=x.numel(), path=path)
-        drafter.update(h[torch.tensor(path, device=h.device)], new)
+        drafter.update(h[path[0]:path[0] + 1] if n == 0 else h[torch.tensor(path, device=h.device)], new)
         out += new
         steps += 1
         accepted += n

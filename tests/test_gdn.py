@@ -131,3 +131,34 @@ def test_rollback_tree_selects_node_state_and_path_window(cuda_lib, dev):
         for s, ck, cv, cf in zip(states, ckpts, convs, fulls):
             assert torch.equal(s, ck[node])
             assert torch.equal(cv, cf[rows])
+
+
+@pytest.mark.gpu
+def test_kv_compaction_moves_the_path_rows(cuda_lib, dev):
+    """After a tree verify, rows L0 + path[j] of every K and V cache move to L0 + j (a moved row
+    may be another move's source), one launch for all layers; other rows are untouched."""
+    from skinny_mlx_b200.model import AttnCache, SMALL
+    from skinny_mlx_b200.spec import HybridRollback
+
+    torch.manual_seed(5)
+    caches = [AttnCache(SMALL, 64, dev) for _ in range(3)]
+    for c in caches:
+        c.k.normal_()
+        c.v.normal_()
+    for path, fed in (([0, 2, 3], 7), ([0, 1, 4, 6], 7), ([0, 1, 2], 5), ([0], 3)):
+        for c in caches:
+            c.length = 20 + fed
+        before = [(c.k.clone(), c.v.clone()) for c in caches]
+
+        class C:
+            layers = caches
+
+        HybridRollback().rollback_tree(C(), fed, path)
+        torch.cuda.synchronize()
+        for c, (k0, v0) in zip(caches, before):
+            n = len(path)
+            assert c.length == 20 + n
+            want_k, want_v = k0.clone(), v0.clone()
+            want_k[20:20 + n] = k0[[20 + j for j in path]]
+            want_v[20:20 + n] = v0[[20 + j for j in path]]
+            assert torch.equal(c.k, want_k) and torch.equal(c.v, want_v)
