@@ -730,33 +730,50 @@ def run_head_case(args):
 
 
 def run_attn_case(args):
-    """--case attn: the fused attention of the config-5 dense model (40 query heads, 8 KV heads,
-    rotary on all 128 dims, no gate) at --m tokens against 4096 cached tokens, 8 layers' caches
-    back to back per step: a small case for profilers (about 0.3 GB on the device)."""
+    """--case attn: the fused attention at --m tokens, 8 layers' caches back to back per step,
+    replayed as one CUDA graph (device time, no host launch cost in the timed region): by default
+    the config-5 dense model's layer (40 query heads, 8 KV heads, rotary on all 128 dims, no gate)
+    against 4096 cached tokens; --attn-shape hybrid: the config-3 layer (16 query heads with a
+    gate, 4 KV heads, rotary on 32 dims) against 2048.  A small case for profilers (about 0.3 GB
+    on the device)."""
     import ctypes
 
     from skinny_mlx_b200 import _lib
 
     dev = torch.device("cuda", 0)
-    D, nh, nkv, L0, layers, T = 128, 40, 8, 4096, 8, args.m
+    hybrid = getattr(args, "attn_shape", "dense") == "hybrid"
+    D, layers, T = 128, 8, args.m
+    nh, nkv, L0, rot, gated = (16, 4, 2048, 32, 1) if hybrid else (40, 8, 4096, 128, 0)
     max_len = L0 + 32
     g = torch.Generator(device=dev).manual_seed(3)
-    proj = torch.randn(T, (nh + 2 * nkv) * D, device=dev, generator=g).to(torch.bfloat16)
+    proj = torch.randn(T, ((1 + gated) * nh + 2 * nkv) * D, device=dev, generator=g).to(torch.bfloat16)
     caches = [(torch.randn(max_len, nkv, D, device=dev, generator=g).to(torch.bfloat16),
                torch.randn(max_len, nkv, D, device=dev, generator=g).to(torch.bfloat16)) for _ in range(layers)]
     qn = torch.zeros(D, device=dev)
     kn = torch.zeros(D, device=dev)
-    inv = (1e6 ** (-torch.arange(0, 64, device=dev, dtype=torch.float32) / 64)).contiguous()
+    inv = (1e6 ** (-torch.arange(0, rot // 2, device=dev, dtype=torch.float32) / (rot // 2))).contiguous()
     L = _lib.lib()
     ws = torch.zeros(int(L.skinny_attn_workspace_bytes(16, nh, nkv, max_len)), dtype=torch.uint8, device=dev)
     xq = torch.zeros(int(L.skinny_xq_bytes(16, nh * D)), dtype=torch.uint8, device=dev)
     P = lambda t: ctypes.c_void_p(t.data_ptr())
 
-    def step():
+    def launches():
         stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
         for kc, vc in caches:
-            _lib.call("skinny_attn_fused", P(proj), proj.stride(0), P(qn), P(kn), P(inv), 128, 0, 1e-6, P(kc), P(vc), L0,
-                      None, T, nh, nkv, max_len, P(ws), ws.numel(), P(xq), None, None, stream)
+            _lib.call("skinny_attn_fused", P(proj), proj.stride(0), P(qn), P(kn), P(inv), rot, gated, 1e-6, P(kc),
+                      P(vc), L0, None, T, nh, nkv, max_len, P(ws), ws.numel(), P(xq), None, None, stream)
+
+    launches()  # (eager once: library set-up outside the capture)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side), torch.cuda.graph(graph, stream=side):
+        launches()
+    torch.cuda.current_stream(dev).wait_stream(side)
+
+    def step():
+        graph.replay()
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -769,8 +786,9 @@ def run_attn_case(args):
     e1.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / args.steps / layers
     kv = L0 * nkv * D * 2 * 2
-    print(json.dumps({"case": "attn", "tokens": T, "us_per_layer": round(us, 2), "kv_bytes": kv,
-                      "GBps": round(kv / (us * 1e-6) / 1e9, 1)}), flush=True)
+    print(json.dumps({"case": "attn", "shape": "hybrid" if hybrid else "dense", "tokens": T,
+                      "us_per_layer": round(us, 2), "kv_bytes": kv, "GBps": round(kv / (us * 1e-6) / 1e9, 1)}),
+          flush=True)
 
 
 def run_gdn_case(args):
@@ -899,6 +917,8 @@ def main():
                          "in NVTX ranges; attn: the dense model's attention at --m tokens; gdn: the "
                          "config-3 GDN mixer at --m tokens; all instead of the bench line")
     ap.add_argument("--m", type=int, default=M_STACK, help="tokens for --case head, attn and gdn")
+    ap.add_argument("--attn-shape", default="dense", choices=["dense", "hybrid"],
+                    help="--case attn: the config-5 dense layer or the config-3 hybrid layer")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.case == "head":
