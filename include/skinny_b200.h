@@ -166,7 +166,7 @@ size_t skinny_xq_bytes(int M, int K);
  * qmm's input format, so a step's elementwise work and its next matmul need no x-prep launch or
  * activation round trip (the B200 form of the glue between the reference model's projections).
  *   mode 0: h = x (+ d if d != NULL; h written to h_out when given), a = bf16(h / rms(h) * (1 + w))
- *           with w f32 [K] (zero-centred RMSNorm, eps); K <= 16384, x and d (or every shard)
+ *           with w f32 [K] (zero-centred RMSNorm, eps); K <= 8192 (else SKINNY_ERR_SHAPE), x and d (or every shard)
  *           16-byte aligned with leading dimensions multiples of 8
  *   mode 1: a = bf16(silu(g) * u), x = [g | u] with 2K columns (SwiGLU)
  *   mode 2: a = x

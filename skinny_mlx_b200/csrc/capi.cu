@@ -27,6 +27,7 @@ cudaError_t qmm_tc_launch_prepared(const void* xq, const void* w_tc, void* out, 
 cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd, int dseg_cols,
                         const void* const* dseg, void* h_out, int ldh, const float* w, float eps, int K, int M,
                         void* xq, void* a_out, const skinny_peer_sync* sync, cudaStream_t stream);
+int prep_max_k();
 cudaError_t embed_launch(const int64_t* ids, int M, const void* w, const void* sc, const void* bi, int V, int K,
                          void* out, int ldo, cudaStream_t stream);
 struct GdnFusedParamsHost {
@@ -279,7 +280,7 @@ int skinny_prep(int mode, const void* x, int ldx, const void* d, int ldd, int ds
                 const skinny_peer_sync* sync, void* stream) {
   if (!x || !xq || mode < 0 || mode > 2 || (mode == 0 && !w)) return SKINNY_ERR_INVALID_ARG;
   if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
-  if (K < skinny::kGroup || K % skinny::kGroup) return SKINNY_ERR_SHAPE;
+  if (K < skinny::kGroup || K % skinny::kGroup || (mode == 0 && K > skinny::prep_max_k())) return SKINNY_ERR_SHAPE;
   if (!sync_ok(sync)) return SKINNY_ERR_INVALID_ARG;
   const int need = mode == 1 ? 2 * K : K;
   if (ldx < need || (h_out && ldh < K)) return SKINNY_ERR_INVALID_ARG;

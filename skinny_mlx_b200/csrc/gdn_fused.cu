@@ -436,22 +436,22 @@ struct GdnFusedParamsHost {
 
 constexpr size_t kGfDynBytes = (kGfMaxT * kGfThreads + kGfMaxT * kGfRows) * sizeof(float);
 
+// One or two CTAs per SM.  Under programmatic dependent launch this kernel's CTAs become resident while
+// the previous launch (a qmm of one CTA per SM) still holds most SMs, and the block scheduler
+// packs them onto the few free SMs, up to four per SM: those CTAs then take about 1.6x as long
+// (measured in a verify step with per-CTA %smid / %globaltimer records).  Asking for more than
+// half (a third) of an SM's shared memory keeps at most one (two) CTAs on an SM; the padding is
+// used only where the GPU can hold every cluster of the launch at once (else the launch would
+// run in waves).
 template <int W>
 static cudaError_t launch_gdn_fused(const GdnFusedParams& prm, cudaStream_t stream) {
-  static bool attr_set[64] = {};
+  static int dyn_for[64][65] = {};  // per device and value-head count: the dynamic shared memory used
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!attr_set[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(gdn_fused_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(kGfDynBytes));
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(prm.Hv * kGfRanks);
   cfg.blockDim = dim3(kGfThreads);
-  cfg.dynamicSmemBytes = kGfDynBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -462,6 +462,37 @@ static cudaError_t launch_gdn_fused(const GdnFusedParams& prm, cudaStream_t stre
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
+  int& dyn = dyn_for[dev][min(prm.Hv, 64)];
+  if (dyn == 0) {
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaFuncGetAttributes(&fa, gdn_fused_kernel<W>);
+    int smem_sm = 0;
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    if (e != cudaSuccess) return e;
+    // at most one, else at most two CTAs per SM (more than a half, a third of its shared memory)
+    dyn = static_cast<int>(kGfDynBytes);
+    for (int per_sm = 1; per_sm <= 2; ++per_sm) {
+      const int padded = max(static_cast<int>(kGfDynBytes),
+                             smem_sm / (per_sm + 1) + 1024 - static_cast<int>(fa.sharedSizeBytes));
+      e = cudaFuncSetAttribute(gdn_fused_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, padded);
+      if (e != cudaSuccess) return e;
+      int clusters = 0;
+      cfg.dynamicSmemBytes = padded;
+      if (cudaOccupancyMaxActiveClusters(&clusters, gdn_fused_kernel<W>, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        clusters = 0;
+      }
+      if (clusters >= prm.Hv) {
+        dyn = padded;
+        break;
+      }
+    }
+    if (dyn == static_cast<int>(kGfDynBytes)) {
+      e = cudaFuncSetAttribute(gdn_fused_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+      if (e != cudaSuccess) return e;
+    }
+  }
+  cfg.dynamicSmemBytes = dyn;
   return cudaLaunchKernelEx(&cfg, gdn_fused_kernel<W>, prm);
 }
 

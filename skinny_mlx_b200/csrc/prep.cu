@@ -37,9 +37,13 @@
 
 namespace skinny {
 
-constexpr int kPrepThreads = 256;
-constexpr int kPrepWarps = kPrepThreads / 32;
-constexpr int kPrepMaxK = 8 * 8 * kPrepThreads;  // mode 0 row length: 16-byte vectors per thread <= 8
+// CTAs of 64 threads and at most 64 registers (4096 per CTA): a prep CTA fits on an SM beside a
+// qmm CTA (640 threads x 96 registers = 61440 of the SM's 65536), so the next qmm's CTAs become
+// resident and stream their weights while the prep runs.  (An RMSNorm row longer than 2560
+// columns takes 128-thread CTAs without that bound.)
+constexpr int kPrepThreads = 128;                  // the embedding gather's CTA
+constexpr int kPrepLeanThreads = 64;
+constexpr int kPrepMaxK = 8 * 8 * 128;             // mode 0 row length: 16-byte vectors per thread <= 8
 
 __device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
@@ -61,9 +65,10 @@ __device__ __forceinline__ const __nv_bfloat16* d_at(const __nv_bfloat16* d, con
   return segs.p[sh] + static_cast<size_t>(t) * ldd + (c - sh * seg_cols);
 }
 
-// mode 0: rmsnorm (optional residual add), 1: swiglu, 2: plain.
-template <int MODE>
-__global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
+// mode 0: rmsnorm (optional residual add), 1: swiglu, 2: plain.  NTHR threads; LEAN: at most
+// 4096 registers per CTA.
+template <int MODE, int NTHR, bool LEAN>
+__global__ void __launch_bounds__(NTHR, LEAN ? 65536 / 4096 : 1) prep_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                                                             const __nv_bfloat16* __restrict__ d, int ldd,
                                                             int dseg_cols, const __grid_constant__ DSegs segs,
                                                             __nv_bfloat16* __restrict__ h_out, int ldh,
@@ -74,9 +79,10 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16*
   const int t = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = K / 64;
-  const int g = blockIdx.x * kPrepWarps + warp;
+  constexpr int kWarps = NTHR / 32;
+  const int g = blockIdx.x * kWarps + warp;
   const bool live = t < M;
-  __shared__ float red[kPrepWarps];
+  __shared__ float red[kWarps];
   __shared__ int sync_flag;
   pdl_launch_dependents();
   pdl_wait_prior_grid();  // x, d (and the buffers written below) belong to earlier launches
@@ -89,12 +95,12 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16*
   float* hrow = reinterpret_cast<float*>(prep_smem);
   float rstd = 1.f;
   if (MODE == 0 && live) {
-    constexpr int kMaxPer = 8;  // 16-byte vectors per thread and tensor: K <= 8 * 8 * 256
+    constexpr int kMaxPer = LEAN ? 5 : 8;  // 16-byte vectors per thread and tensor: K <= kMaxPer * 8 * NTHR
     const int nvec = K / 8;
     uint4 xv[kMaxPer], dv[kMaxPer];
 #pragma unroll
     for (int u = 0; u < kMaxPer; ++u) {
-      const int v = tid + u * kPrepThreads;
+      const int v = tid + u * NTHR;
       if (v < nvec) {
         xv[u] = *reinterpret_cast<const uint4*>(xr + 8 * v);
         if (has_d) dv[u] = *reinterpret_cast<const uint4*>(d_at(d, segs, t, 8 * v, ldd, dseg_cols));
@@ -103,7 +109,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16*
     float ss = 0.f;
 #pragma unroll
     for (int u = 0; u < kMaxPer; ++u) {
-      const int v = tid + u * kPrepThreads;
+      const int v = tid + u * NTHR;
       if (v < nvec) {
         const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv[u]);
         const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&dv[u]);
@@ -127,7 +133,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16*
     __syncthreads();
     float tot = 0.f;
 #pragma unroll
-    for (int i = 0; i < kPrepWarps; ++i) tot += red[i];  // fixed order, the same in every chunk
+    for (int i = 0; i < kWarps; ++i) tot += red[i];  // fixed order, the same in every chunk
     rstd = rsqrtf(tot / static_cast<float>(K) + eps);
   }
   if (g < G) {
@@ -160,13 +166,13 @@ __global__ void __launch_bounds__(kPrepThreads) prep_kernel(const __nv_bfloat16*
 static cudaError_t launch_pdl(void (*kern)(const __nv_bfloat16*, int, const __nv_bfloat16*, int, int, DSegs,
                                            __nv_bfloat16*, int, const float*, float, int, int, int, uint8_t*,
                                            __nv_bfloat16*, PeerSync),
-                              dim3 grid, size_t smem, cudaStream_t stream, const __nv_bfloat16* x, int ldx,
+                              int nthr, dim3 grid, size_t smem, cudaStream_t stream, const __nv_bfloat16* x, int ldx,
                               const __nv_bfloat16* d, int ldd, int dseg_cols, const DSegs& segs, __nv_bfloat16* h,
                               int ldh, const float* w, float eps, int K, int M, int mpad, uint8_t* xq,
                               __nv_bfloat16* a_out, const PeerSync& sync) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(kPrepThreads);
+  cfg.blockDim = dim3(nthr);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -177,12 +183,16 @@ static cudaError_t launch_pdl(void (*kern)(const __nv_bfloat16*, int, const __nv
   return cudaLaunchKernelEx(&cfg, kern, x, ldx, d, ldd, dseg_cols, segs, h, ldh, w, eps, K, M, mpad, xq, a_out, sync);
 }
 
+int prep_max_k() { return kPrepMaxK; }
+
 cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd, int dseg_cols,
                         const void* const* dseg, void* h_out, int ldh, const float* w, float eps, int K, int M,
                         void* xq, void* a_out, const skinny_peer_sync* sync, cudaStream_t stream) {
   const int mpad = M <= 8 ? 8 : 16;
   const int G = K / 64;
-  const dim3 grid((G + kPrepWarps - 1) / kPrepWarps, mpad);
+  const bool lean = mode != 0 || K <= 5 * 8 * kPrepLeanThreads;
+  const int nthr = lean ? kPrepLeanThreads : 128;
+  const dim3 grid((G + nthr / 32 - 1) / (nthr / 32), mpad);
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   auto* q = static_cast<uint8_t*>(xq);
   DSegs segs{};
@@ -190,24 +200,25 @@ cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd
     for (int i = 0; i < K / dseg_cols && i < kMaxPeers; ++i) segs.p[i] = static_cast<const __nv_bfloat16*>(dseg[i]);
   const PeerSync ps = peer_sync_from(sync);
   if (mode == 0) {
-    static bool attr_set[64] = {};
+    const auto kern = lean ? prep_kernel<0, kPrepLeanThreads, true> : prep_kernel<0, 128, false>;
+    static bool attr_set[2][64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-      const cudaError_t e = cudaFuncSetAttribute(prep_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (dev >= 0 && dev < 64 && !attr_set[lean][dev]) {
+      const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  static_cast<int>(kPrepMaxK * sizeof(float)));
       if (e != cudaSuccess) return e;
-      attr_set[dev] = true;
+      attr_set[lean][dev] = true;
     }
-    return launch_pdl(prep_kernel<0>, grid, static_cast<size_t>(K) * sizeof(float), stream, xb, ldx,
+    return launch_pdl(kern, nthr, grid, static_cast<size_t>(K) * sizeof(float), stream, xb, ldx,
                       static_cast<const __nv_bfloat16*>(d), ldd, dseg_cols, segs, static_cast<__nv_bfloat16*>(h_out),
                       ldh, w, eps, K, M, mpad, q, static_cast<__nv_bfloat16*>(a_out), ps);
   }
   if (mode == 1)
-    return launch_pdl(prep_kernel<1>, grid, 0, stream, xb, ldx, nullptr, 0, 0, segs, nullptr, 0, nullptr, 0.f, K, M,
-                      mpad, q, nullptr, ps);
-  return launch_pdl(prep_kernel<2>, grid, 0, stream, xb, ldx, nullptr, 0, 0, segs, nullptr, 0, nullptr, 0.f, K, M,
-                    mpad, q, nullptr, ps);
+    return launch_pdl(prep_kernel<1, kPrepLeanThreads, true>, nthr, grid, 0, stream, xb, ldx, nullptr, 0, 0, segs,
+                      nullptr, 0, nullptr, 0.f, K, M, mpad, q, nullptr, ps);
+  return launch_pdl(prep_kernel<2, kPrepLeanThreads, true>, nthr, grid, 0, stream, xb, ldx, nullptr, 0, 0, segs,
+                    nullptr, 0, nullptr, 0.f, K, M, mpad, q, nullptr, ps);
 }
 
 // Token embedding rows of a 4-bit group-64 table (MLX packing: word j of a row holds columns
