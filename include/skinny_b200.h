@@ -256,6 +256,17 @@ int skinny_attn_fused_tree(const void* proj, int ldp, const float* q_norm_w, con
                            void* workspace, size_t workspace_bytes, void* xq, void* o_out, const int32_t* parent,
                            void* stream);
 
+/* The gate|up projection of a SwiGLU MLP with its activation in the epilogue: xq is a prepared
+ * input (skinny_prep, M tokens, K columns), w_tc a relaid weight of N = 2I rows whose 128-row
+ * tile j holds gate rows 64j .. 64j+63 then up rows 64j .. 64j+63 (I % 64 == 0).  Instead of the
+ * [M, N] product it writes a = bf16(silu(bf16(g)) bf16(u)) for the I output columns as a prepared
+ * input of K = I columns (skinny_xq_bytes(M, I) bytes at xq_out, 16-byte aligned): the same digits
+ * as skinny_prep mode 1 on the product's bf16 output, without that launch or the output's round
+ * trip.  Workspace as for skinny_qmm_w4g64_prepared.  No counterpart in the reference's own code
+ * (its MLP runs gate/up, the activation and down as separate MLX operations). */
+int skinny_qmm_w4g64_swiglu(const void* xq, const void* w_tc, void* xq_out, int M, int N, int K, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* skinny_qmm_w4g64 on an input prepared by skinny_prep (same result as passing the bf16
  * activation itself), launched without the x-prep kernel.  Sharded step: with xq_ranks != NULL
  * the digit blocks of groups [r * xq_groups_per_rank, (r+1) * xq_groups_per_rank) are read from

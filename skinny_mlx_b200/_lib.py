@@ -77,6 +77,8 @@ SIGNATURES = {
     "skinny_kv_compact": (c_int, [c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "skinny_gdn_rollback_tree": (c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_longlong, c_int,
                                          c_void_p, c_int, c_int, c_int, c_void_p]),
+    "skinny_qmm_w4g64_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t,
+                                        c_void_p]),
 }
 
 

@@ -23,7 +23,7 @@ bool qmm_noalloc_fits(int N, int K);
 size_t spec_accept_ws_bytes();
 cudaError_t qmm_tc_launch_prepared(const void* xq, const void* w_tc, void* out, int ldo, int M, int N, int K,
                                    void* ws, const void* const* xq_ranks, int xq_gpr, const skinny_peer_sync* sync,
-                                   cudaStream_t stream);
+                                   cudaStream_t stream, void* swiglu_xq = nullptr);
 cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd, int dseg_cols,
                         const void* const* dseg, void* h_out, int ldh, const float* w, float eps, int K, int M,
                         void* xq, void* a_out, const skinny_peer_sync* sync, cudaStream_t stream);
@@ -438,6 +438,20 @@ int skinny_qmm_w4g64_prepared(const void* xq, const void* w_tc, void* out, int l
   if (!workspace || workspace_bytes < wl.total || !aligned16(workspace)) return SKINNY_ERR_WORKSPACE;
   return cuda_status(skinny::qmm_tc_launch_prepared(xq, w_tc, out, ldo, M, N, K, workspace, xq_ranks,
                                                     xq_groups_per_rank, sync, static_cast<cudaStream_t>(stream)));
+}
+
+int skinny_qmm_w4g64_swiglu(const void* xq, const void* w_tc, void* xq_out, int M, int N, int K, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (!xq || !w_tc || !xq_out) return SKINNY_ERR_INVALID_ARG;
+  const int st = check_qmm_shape(N, K);
+  if (st != SKINNY_OK) return st;
+  if (N % (2 * skinny::kGroup) != 0) return SKINNY_ERR_SHAPE;
+  if (M < 1 || M > skinny::kMaxTokens) return SKINNY_ERR_TOKENS;
+  if (!aligned16(xq) || !aligned16(w_tc) || !aligned16(xq_out)) return SKINNY_ERR_ALIGNMENT;
+  const skinny::WsLayout wl = skinny::ws_layout(skinny::device_sm_count(current_device()));
+  if (!workspace || workspace_bytes < wl.total || !aligned16(workspace)) return SKINNY_ERR_WORKSPACE;
+  return cuda_status(skinny::qmm_tc_launch_prepared(xq, w_tc, nullptr, N, M, N, K, workspace, nullptr, 0, nullptr,
+                                                    static_cast<cudaStream_t>(stream), xq_out));
 }
 
 // ---- peer memory (CUDA IPC) ----

@@ -62,6 +62,7 @@
 #include <atomic>
 #include <mutex>
 
+#include "digits.cuh"
 #include "peer.cuh"
 #include "ptx.cuh"
 #include "qmm_layout.cuh"
@@ -124,6 +125,10 @@ struct QmmParams {
   const uint8_t* xq_rank[kMaxPeers];
   int xq_gpr;
   PeerSync sync;
+  // SwiGLU epilogue (one-matrix prepared calls): with swiglu_xq set, the weight's tile j holds the
+  // gate rows 64j .. 64j+63 then the up rows 64j .. 64j+63, and instead of the bf16 output a
+  // finished tile writes group j of the qmm input digits of a = bf16(silu(g) u) to swiglu_xq.
+  uint8_t* swiglu_xq;
   QmmMat mats[kMaxMats];
 };
 
@@ -324,10 +329,42 @@ __device__ __forceinline__ void copy_x_blocks(const QmmParams& p, uint32_t dst, 
   }
 }
 
+// The finished tile lt of an interleaved gate|up weight, as the 128 threads of one epilogue lane
+// hold it (thread r: row r's sum for every token): g = bf16(rows 0-63), u = bf16(rows 64-127),
+// a = bf16(silu(g) u) for output columns 64 lt .. 64 lt + 63 (the rounding of a gate|up output
+// followed by the SwiGLU producer), written as x-prep group lt of swiglu_xq (tokens >= M zero).
+// sc: 2 * NT * 64 floats of shared scratch; bar: the lane's named barrier.
+template <int NT>
+__device__ __forceinline__ void swiglu_digits(const QmmParams& p, int lt, int r, int lane, int wq, int bar,
+                                              const float (&val)[NT], float* sc) {
+  constexpr int MP = mpad_of(NT);
+  float* us = sc;            // [NT][64] up values
+  float* as = sc + NT * 64;  // [NT][64] outputs
+  if (r >= 64) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) us[t * 64 + (r - 64)] = __bfloat162float(__float2bfloat16_rn(val[t]));
+  }
+  named_bar_sync(bar, kEpiThreads);
+  if (r < 64) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const float g = __bfloat162float(__float2bfloat16_rn(val[t]));
+      as[t * 64 + r] = __bfloat162float(__float2bfloat16_rn(g / (1.f + __expf(-g)) * us[t * 64 + r]));
+    }
+  }
+  named_bar_sync(bar, kEpiThreads);
+  for (int t = wq; t < MP; t += 4) {
+    const bool live = t < NT && t < p.M;
+    const float a0 = live ? as[t * 64 + 2 * lane] : 0.f, a1 = live ? as[t * 64 + 2 * lane + 1] : 0.f;
+    write_digits(p.swiglu_xq, MP, t, lt, lane, a0, a1);
+  }
+  named_bar_sync(bar, kEpiThreads);  // the scratch is the lanes' exchange buffer
+}
+
 // ---------------------------------------------------------------------------------------------
 // The qmm kernel.  NT: token columns read back per unit (2, 4, 8 or 16).
 // ---------------------------------------------------------------------------------------------
-template <int NT>
+template <int NT, bool SWIGLU = false>
 __global__ void __launch_bounds__(kThreads, 1)
     qmm_w4g64_tc_kernel(const __grid_constant__ QmmParams p) {
   constexpr int MP = mpad_of(NT);
@@ -670,7 +707,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             dep_waited = true;
           }
           if (full_tile) {
-            if (live && row_g < mt.N) {
+            if constexpr (SWIGLU) {
+              swiglu_digits<NT>(p, wk.lt, r, lane, warp & 3, 4 + L, acc, xb);  // (barriers: every thread)
+            } else if (live && row_g < mt.N) {
 #pragma unroll
               for (int t = 0; t < NT; ++t)
                 if (t < p.M) mt.out[static_cast<size_t>(t) * mt.ldo + row_g] = __float2bfloat16_rn(acc[t]);
@@ -702,7 +741,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int t = 0; t < NT; ++t) v[t] += __ldcg(src + t * kTileRows + r);
               }
-              if (row_g < mt.N) {
+              if constexpr (SWIGLU) {
+                swiglu_digits<NT>(p, wk.lt, r, lane, warp & 3, bar, v, xb);
+              } else if (row_g < mt.N) {
 #pragma unroll
                 for (int t = 0; t < NT; ++t)
                   if (t < p.M) mt.out[static_cast<size_t>(t) * mt.ldo + row_g] = __float2bfloat16_rn(v[t]);
@@ -816,7 +857,7 @@ __global__ void qmm_repack_kernel(const uint32_t* __restrict__ w, const uint16_t
 // keyed by device index and so assume the device's primary context (the one the CUDA runtime
 // API uses); a host that switches between driver-API contexts on one device must not share them.
 static std::atomic<int> g_num_sms[64];
-static std::atomic<bool> g_attr_set[64][4];
+static std::atomic<bool> g_attr_set[64][8];  // per device: [token-column variant + 4 for the SwiGLU epilogue]
 
 int device_sm_count(int dev) {
   if (dev < 0 || dev >= 64) return 148;
@@ -836,11 +877,11 @@ static void pdl_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, bool 
   cfg.numAttrs = 1;
 }
 
-template <int NT>
+template <int NT, bool SWIGLU = false>
 static cudaError_t set_smem_attr(int dev) {
-  constexpr int slot = NT == 2 ? 0 : NT == 4 ? 1 : NT == 8 ? 2 : 3;
+  constexpr int slot = (NT == 2 ? 0 : NT == 4 ? 1 : NT == 8 ? 2 : 3) + (SWIGLU ? 4 : 0);
   if (dev >= 0 && dev < 64 && !g_attr_set[dev][slot].load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(qmm_w4g64_tc_kernel<NT>,
+    cudaError_t e = cudaFuncSetAttribute(qmm_w4g64_tc_kernel<NT, SWIGLU>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(qmm_smem_bytes(NT)));
     if (e != cudaSuccess) return e;
@@ -849,9 +890,9 @@ static cudaError_t set_smem_attr(int dev) {
   return cudaSuccess;
 }
 
-template <int NT>
+template <int NT, bool SWIGLU = false>
 static cudaError_t launch_tc(const QmmParams& prm, int dev, cudaStream_t stream, bool pdl) {
-  const cudaError_t e = set_smem_attr<NT>(dev);
+  const cudaError_t e = set_smem_attr<NT, SWIGLU>(dev);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(prm.C);
@@ -867,7 +908,7 @@ static cudaError_t launch_tc(const QmmParams& prm, int dev, cudaStream_t stream,
     attr[1].val.clusterDim.z = 1;
     cfg.numAttrs = 2;
   }
-  return cudaLaunchKernelEx(&cfg, qmm_w4g64_tc_kernel<NT>, prm);
+  return cudaLaunchKernelEx(&cfg, qmm_w4g64_tc_kernel<NT, SWIGLU>, prm);
 }
 
 // Clusters of S CTAs of the qmm kernel that can be resident at once on device `dev`: the
@@ -977,6 +1018,7 @@ static cudaError_t launch_grouped_on(int n, const void* const* x, const int* ldx
   prm.n_mats = n;
   prm.xq_gpr = 0;
   prm.sync = PeerSync{};
+  prm.swiglu_xq = nullptr;
   xp.xq = xq;
   xp.M = M;
   xp.mpad = mpad;
@@ -1028,7 +1070,7 @@ static cudaError_t launch_grouped_on(int n, const void* const* x, const int* ldx
 // (prep.cu): no x-prep launch.  xq holds K/64 blocks for mpad(M) token rows.
 cudaError_t qmm_tc_launch_prepared(const void* xq, const void* w_tc, void* out, int ldo, int M, int N, int K,
                                    void* ws, const void* const* xq_ranks, int xq_gpr, const skinny_peer_sync* sync,
-                                   cudaStream_t stream) {
+                                   cudaStream_t stream, void* swiglu_xq) {
   int dev = 0;
   cudaGetDevice(&dev);
   const int C_dev = device_sm_count(dev);
@@ -1058,6 +1100,14 @@ cudaError_t qmm_tc_launch_prepared(const void* xq, const void* w_tc, void* out, 
   mt.ldo = ldo;
   prm.U = static_cast<int>(sh.U);
   prm.C = static_cast<int>(sh.U < C_dev ? sh.U : C_dev);
+  prm.swiglu_xq = static_cast<uint8_t*>(swiglu_xq);
+  if (swiglu_xq) {  // (a separate kernel variant; its epilogue finishes tiles in the stream-K paths only)
+    prm.split = 0;
+    if (M <= 2) return launch_tc<2, true>(prm, dev, stream, true);
+    if (M <= 4) return launch_tc<4, true>(prm, dev, stream, true);
+    if (M <= 8) return launch_tc<8, true>(prm, dev, stream, true);
+    return launch_tc<16, true>(prm, dev, stream, true);
+  }
   prm.split = choose_split(dev, static_cast<int>(sh.T), sh.G, C_dev);
   if (prm.split > 0) prm.C = static_cast<int>(sh.T) * prm.split;
   if (M <= 2) return launch_tc<2>(prm, dev, stream, true);

@@ -38,7 +38,7 @@ def layer_entry(layer, cfg) -> dict:
 
     mlp = layer.mlp
     assert isinstance(mlp.gate_proj, FusedSliceLinear) and isinstance(mlp.down_proj, SkinnyQuantizedLinear)
-    ent = {"gate_up": mlp.gate_proj._group.rw, "down": mlp.down_proj.rweight,
+    ent = {"gate_up": mlp.gate_proj._group.rw, "swiglu": mlp.gate_proj._group.interleaved, "down": mlp.down_proj.rweight,
            "in_norm": layer.input_layernorm.weight, "post_norm": layer.post_attention_layernorm.weight}
     if layer.is_linear:
         g = layer.linear_attn
@@ -99,6 +99,18 @@ class FusedOps:
         ws = get_workspace(out.device, int(_lib.lib().skinny_qmm_workspace_bytes(w.N, w.K)))
         _lib.call("skinny_qmm_w4g64_prepared", _p(xq), _p(w.w_tc), _p(out), out.stride(0), m, w.N, w.K,
                   _p(ws), ws.numel(), None, 0, None, stream)
+
+    def _gate_up(self, ent, xq_h, gu, xq_i, m: int, stream):
+        """gate|up projection and SwiGLU -> down_proj digits: one launch (activation in the qmm
+        epilogue) for an interleaved gate|up weight, else the product and skinny_prep mode 1."""
+        w = ent["gate_up"]
+        if ent.get("swiglu"):
+            ws = get_workspace(xq_i.device, int(_lib.lib().skinny_qmm_workspace_bytes(w.N, w.K)))
+            _lib.call("skinny_qmm_w4g64_swiglu", _p(xq_h), _p(w.w_tc), _p(xq_i), m, w.N, w.K, _p(ws), ws.numel(),
+                      stream)
+        else:
+            self._qmm(xq_h, w, gu, m, stream)
+            self._prep(1, gu, m, w.N // 2, xq_i, stream)
 
     def _prep(self, mode, x, m, k, xq, stream, d=None, h_out=None, w=None, a_out=None):
         _lib.call("skinny_prep", mode, _p(x), x.stride(0), _p(d), d.stride(0) if d is not None else 0, 0, None,
@@ -227,8 +239,7 @@ class FusedStep(FusedOps):
             self._qmm(b["xq_o"], ent["out"], b["mix"], m, stream)
             # h = x_l + mixer; digits of post_attention_layernorm(h)
             add_norm(b["mix"], ent["post_norm"])
-            self._qmm(b["xq_h"], ent["gate_up"], b["gu"], m, stream)
-            self._prep(1, b["gu"], m, cfg.intermediate, b["xq_i"], stream)
+            self._gate_up(ent, b["xq_h"], b["gu"], b["xq_i"], m, stream)
             self._qmm(b["xq_i"], ent["down"], b["down"], m, stream)
             d = b["down"]
         add_norm(d, self.final_norm, a_out=b["a"])

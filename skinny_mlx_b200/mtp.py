@@ -120,8 +120,7 @@ class FusedMTPHead(FusedOps):
         self._attention(ent, b["proj"], cache, m, b["xq_o"], stream, len_dev)
         self._qmm(b["xq_o"], ent["out"], b["mix"], m, stream)
         self._prep(0, b["x"], m, H, b["xq_h"], stream, d=b["mix"], h_out=b["h2"], w=ent["post_norm"])
-        self._qmm(b["xq_h"], ent["gate_up"], b["gu"], m, stream)
-        self._prep(1, b["gu"], m, cfg.intermediate, b["xq_i"], stream)
+        self._gate_up(ent, b["xq_h"], b["gu"], b["xq_i"], m, stream)
         self._qmm(b["xq_i"], ent["down"], b["down"], m, stream)
         self._prep(0, b["h2"], m, H, b["xq_h"], stream, d=b["down"], h_out=b["h3"], w=head.norm.weight,
                    a_out=b["out"])

@@ -53,12 +53,32 @@ class SkinnyQuantizedLinear(nn.Module):
         return _qmm(x, self.rweight)
 
 
-class _FusedGroup:
-    """Concatenated weights of same-input projections + a one-entry result cache (patch.py:52-68)."""
+def _interleave64(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Rows of a and b (same shape, rows % 64 == 0) in blocks of 64: a[0:64], b[0:64], a[64:128], ..."""
+    n = a.shape[0]
+    return torch.stack([a.reshape(n // 64, 64, *a.shape[1:]), b.reshape(n // 64, 64, *b.shape[1:])], 1).reshape(
+        2 * n, *a.shape[1:])
 
-    def __init__(self, qls: list[QuantizedLinear]):
-        self.rw = repack_for_skinny(torch.cat([q.weight for q in qls]), torch.cat([q.scales for q in qls]),
-                                    torch.cat([q.biases for q in qls]))
+
+class _FusedGroup:
+    """Concatenated weights of same-input projections + a one-entry result cache (patch.py:52-68).
+
+    A SwiGLU pair (gate_proj, up_proj of equal size, a multiple of 64 rows) is stored with its rows
+    interleaved in blocks of 64 (gate 0-63, up 0-63, gate 64-127, ...): each 128-row tile of the
+    relaid weight then holds matching gate and up rows, so the fused step's gate|up launch can
+    apply the activation in its epilogue (skinny_qmm_w4g64_swiglu).  The slices return the
+    projections' outputs in their own column order either way."""
+
+    def __init__(self, qls: list[QuantizedLinear], swiglu: bool = False):
+        self.interleaved = (swiglu and len(qls) == 2 and qls[0].weight.shape == qls[1].weight.shape
+                            and qls[0].weight.shape[0] % 64 == 0)
+        if self.interleaved:
+            g, u = qls
+            self.rw = repack_for_skinny(_interleave64(g.weight, u.weight), _interleave64(g.scales, u.scales),
+                                        _interleave64(g.biases, u.biases))
+        else:
+            self.rw = repack_for_skinny(torch.cat([q.weight for q in qls]), torch.cat([q.scales for q in qls]),
+                                        torch.cat([q.biases for q in qls]))
         sizes = [q.weight.shape[0] for q in qls]
         self.bounds = [(sum(sizes[:i]), sum(sizes[: i + 1])) for i in range(len(sizes))]
         self.x = self.y = None
@@ -68,14 +88,22 @@ class _FusedGroup:
             self.x, self.y = x, _qmm(x, self.rw)
         return self.y
 
+    def slice(self, x: torch.Tensor, idx: int) -> torch.Tensor:
+        y = self.output(x)
+        if self.interleaved:  # [..., I / 64, (gate | up), 64] -> projection idx
+            return y.unflatten(-1, (-1, 2, 64))[..., idx, :].flatten(-2)
+        lo, hi = self.bounds[idx]
+        return y[..., lo:hi]
+
 
 class FusedSliceLinear(nn.Module):
     def __init__(self, group: _FusedGroup, idx: int):
         super().__init__()
-        self._group, (self._lo, self._hi) = group, group.bounds[idx]
+        self._group, self._idx = group, idx
+        self._lo, self._hi = group.bounds[idx]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return self._group.output(x)[..., self._lo: self._hi]
+        return self._group.slice(x, self._idx)
 
 
 def _ok(m) -> bool:
@@ -98,7 +126,7 @@ def patch_model(model: nn.Module, fuse: bool = True) -> dict:
             children = dict(parent.named_children())
             for names in FUSE_GROUPS:
                 if all(_ok(children.get(n)) for n in names):
-                    group = _FusedGroup([children[n] for n in names])
+                    group = _FusedGroup([children[n] for n in names], swiglu=names == ("gate_proj", "up_proj"))
                     for i, n in enumerate(names):
                         fused_ids.add(id(children[n]))
                         setattr(parent, n, FusedSliceLinear(group, i))

@@ -40,6 +40,44 @@ def test_prep_plain_is_the_xprep_format(cuda_lib, dev, m):
     assert np.array_equal(xq.cpu().numpy().reshape(10, -1), quant.xq_blocks(x, mpad))
 
 
+@pytest.mark.parametrize("m", [1, 3, 8, 13, 16])
+@pytest.mark.parametrize("K,I", [(2560, 9728), (512, 256)])
+def test_swiglu_epilogue_equals_product_then_swiglu_prep(cuda_lib, dev, m, K, I):
+    """skinny_qmm_w4g64_swiglu on an interleaved gate|up weight writes byte for byte the digits that
+    the prepared product (same weight) followed by skinny_prep mode 1 on the de-interleaved bf16
+    output writes.  (2560, 9728): the config-3 MLP, whole tiles and stream-K partial tiles;
+    (512, 256): 32 units on 32 CTAs, every tile finished by the fix-up."""
+    from skinny_mlx_b200.patch import _interleave64
+    from skinny_mlx_b200.qmm import get_workspace, quantize, repack_for_skinny
+
+    torch.manual_seed(7 * m + K)
+    wq, sq, bq = quantize(torch.randn(2 * I, K, device=dev) * 0.03)
+    g, u = (wq[:I], sq[:I], bq[:I]), (wq[I:], sq[I:], bq[I:])
+    w = repack_for_skinny(*(_interleave64(a, b) for a, b in zip(g, u)))
+    ws = get_workspace(dev, int(cuda_lib.skinny_qmm_workspace_bytes(2 * I, K)))
+    x = (torch.randn(m, K, device=dev) * 2).to(torch.bfloat16)
+    xq = torch.zeros(int(cuda_lib.skinny_xq_bytes(m, K)), dtype=torch.uint8, device=dev)
+    assert cuda_lib.skinny_prep(2, _p(x), K, None, 0, 0, None, None, 0, None, ctypes.c_float(0), m, K, _p(xq), None,
+                                None, _stream()) == 0
+    got = torch.full((int(cuda_lib.skinny_xq_bytes(m, I)),), 0x5A, dtype=torch.uint8, device=dev)
+    assert cuda_lib.skinny_qmm_w4g64_swiglu(_p(xq), _p(w.w_tc), _p(got), m, 2 * I, K, _p(ws), ws.numel(), _stream()) == 0
+    gu = torch.empty(m, 2 * I, dtype=torch.bfloat16, device=dev)
+    assert cuda_lib.skinny_qmm_w4g64_prepared(_p(xq), _p(w.w_tc), _p(gu), 2 * I, m, 2 * I, K, _p(ws), ws.numel(),
+                                              None, 0, None, _stream()) == 0
+    gu = gu.unflatten(-1, (-1, 2, 64)).transpose(1, 2).reshape(m, 2 * I).contiguous()  # [gate | up]
+    ref = torch.full_like(got, 0x5A)
+    assert cuda_lib.skinny_prep(1, _p(gu), 2 * I, None, 0, 0, None, None, 0, None, ctypes.c_float(0), m, I, _p(ref),
+                                None, None, _stream()) == 0
+    torch.cuda.synchronize()
+    assert int(ws[:4].view(torch.int32).item()) == 0
+    assert torch.equal(got, ref)
+    # argument checks: N not a whole number of 128-row tiles; misaligned output
+    assert cuda_lib.skinny_qmm_w4g64_swiglu(_p(xq), _p(w.w_tc), _p(got), m, 2 * I - 64, K, _p(ws), ws.numel(),
+                                            _stream()) == -2
+    assert cuda_lib.skinny_qmm_w4g64_swiglu(_p(xq), _p(w.w_tc), ctypes.c_void_p(got.data_ptr() + 4), m, 2 * I, K,
+                                            _p(ws), ws.numel(), _stream()) == -4
+
+
 @pytest.mark.parametrize("m", [1, 8, 16])
 def test_prep_norm_and_swiglu_feed_the_prepared_qmm(cuda_lib, dev, m):
     from skinny_mlx_b200.qmm import get_workspace, quantize, repack_for_skinny, skinny_qmm
