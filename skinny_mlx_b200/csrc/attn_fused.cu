@@ -24,6 +24,7 @@
 // No CTA waits on another; the merge launch waits for the chunk launch through programmatic
 // dependent launch, like every launch of the step (the next launch may start at once; a kernel
 // waits for the previous grid before its first global read).
+#include <algorithm>
 #include <cfloat>
 #include <cstdint>
 #include <cuda_bf16.h>
@@ -686,6 +687,13 @@ bool attn_fits(int T, int nh, int nkv) {
   return nkv >= 1 && nkv <= 64 && nh % nkv == 0 && T * (nh / nkv) <= kAtRG * kAtMaxRG;
 }
 
+static int device_sm_count_attn(int dev) {
+  static int n[64] = {};
+  if (dev < 0 || dev >= 64) return 0;
+  if (n[dev] == 0) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev];
+}
+
 cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, const float* kn_w,
                               const float* inv_freq, int rot, int gated, float eps, void* kc, void* vc, int L0,
                               const int* len_dev, int max_len, int T, int nh, int nkv, void* ws, void* xq,
@@ -727,13 +735,32 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
   prm.xq = static_cast<uint8_t*>(xq);
   prm.o_out = static_cast<__nv_bfloat16*>(o_out);
   prm.sync = peer_sync_from(sync);
+  // One CTA per SM where the grid fits the GPU: launched early (programmatic dependent launch),
+  // CTAs otherwise pile onto the few SMs the previous launch leaves free, two to four per SM.
+  // Asking for more than half an SM's shared memory spreads them.
+  static int padded[64][2] = {};  // per device: dynamic bytes of the chunk / merge launch (0: unset)
+  if (padded[dev][0] == 0) {
+    int smem_sm = 0;
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, attn_merge_kernel);
+    if (e != cudaSuccess) return e;
+    const int chunk = std::max(static_cast<int>(sizeof(AttnSmem)), smem_sm / 2 + 1024);
+    const int merge = smem_sm / 2 + 1024 - static_cast<int>(fa.sharedSizeBytes);
+    e = cudaFuncSetAttribute(attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, chunk);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, merge);
+    if (e != cudaSuccess) return e;
+    padded[dev][0] = chunk;
+    padded[dev][1] = merge;
+  }
+  const int n_sm = device_sm_count_attn(dev);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(prm.nchunks, nkv);
   cfg.blockDim = dim3(kAtThreads);
-  cfg.dynamicSmemBytes = sizeof(AttnSmem);
+  cfg.dynamicSmemBytes = prm.nchunks * nkv <= n_sm ? padded[dev][0] : sizeof(AttnSmem);
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
@@ -742,7 +769,7 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
   cudaLaunchConfig_t mcfg = {};
   mcfg.gridDim = dim3(prm.nrg * (kAtRG / kAtMergeRows), nkv);  // (rows, row group) x KV head
   mcfg.blockDim = dim3(kAtThreads);
-  mcfg.dynamicSmemBytes = 0;
+  mcfg.dynamicSmemBytes = mcfg.gridDim.x * mcfg.gridDim.y <= static_cast<unsigned>(n_sm) ? padded[dev][1] : 0;
   mcfg.stream = stream;
   mcfg.attrs = attr;
   mcfg.numAttrs = 1;

@@ -469,13 +469,15 @@ static cudaError_t launch_gdn_fused(const GdnFusedParams& prm, cudaStream_t stre
     int smem_sm = 0;
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
     if (e != cudaSuccess) return e;
-    // at most one, else at most two CTAs per SM (more than a half, a third of its shared memory)
+    // at most one, else at most two CTAs per SM (more than a half, a third of its shared memory);
+    // the kernel's limit stays at the largest size any launch may use
+    const int pad1 = max(static_cast<int>(kGfDynBytes), smem_sm / 2 + 1024 - static_cast<int>(fa.sharedSizeBytes));
+    e = cudaFuncSetAttribute(gdn_fused_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, pad1);
+    if (e != cudaSuccess) return e;
     dyn = static_cast<int>(kGfDynBytes);
     for (int per_sm = 1; per_sm <= 2; ++per_sm) {
       const int padded = max(static_cast<int>(kGfDynBytes),
                              smem_sm / (per_sm + 1) + 1024 - static_cast<int>(fa.sharedSizeBytes));
-      e = cudaFuncSetAttribute(gdn_fused_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, padded);
-      if (e != cudaSuccess) return e;
       int clusters = 0;
       cfg.dynamicSmemBytes = padded;
       if (cudaOccupancyMaxActiveClusters(&clusters, gdn_fused_kernel<W>, &cfg) != cudaSuccess) {
@@ -486,10 +488,6 @@ static cudaError_t launch_gdn_fused(const GdnFusedParams& prm, cudaStream_t stre
         dyn = padded;
         break;
       }
-    }
-    if (dyn == static_cast<int>(kGfDynBytes)) {
-      e = cudaFuncSetAttribute(gdn_fused_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
-      if (e != cudaSuccess) return e;
     }
   }
   cfg.dynamicSmemBytes = dyn;
