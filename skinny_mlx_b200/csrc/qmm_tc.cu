@@ -353,7 +353,8 @@ __device__ __forceinline__ void swiglu_digits(const QmmParams& p, int lt, int r,
     }
   }
   named_bar_sync(bar, kEpiThreads);
-  for (int t = wq; t < MP; t += 4) {
+#pragma unroll
+  for (int t = wq; t < MP; t += 4) {  // (unrolled: the warp's token jobs are independent chains)
     const bool live = t < NT && t < p.M;
     const float a0 = live ? as[t * 64 + 2 * lane] : 0.f, a1 = live ? as[t * 64 + 2 * lane + 1] : 0.f;
     write_digits(p.swiglu_xq, MP, t, lt, lane, a0, a1);
@@ -716,25 +717,45 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           } else {
             const int bar = 4 + L;
-            float* mine = p.part + (static_cast<size_t>(c) * 2 + (first_seg ? 0 : 1)) * kMaxTokens * kTileRows;
-#pragma unroll
-            for (int t = 0; t < NT; ++t) mine[t * kTileRows + r] = acc[t];
-            __threadfence();
-            named_bar_sync(bar, kEpiThreads);
             const long long cf = cta_of_unit(tile_u0, p.U, p.C);
             const long long cl = cta_of_unit(tile_u0 + mt.G - 1, p.U, p.C);
+            const unsigned n_contrib = static_cast<unsigned>(cl - cf + 1);
+            // A CTA whose last segment this is usually arrives last (the others published the
+            // tile's other parts early in their ranges): it peeks at the counter first and, when
+            // every other contributor has arrived, finishes the tile from its own registers and
+            // their partials without publishing its own (one write, fence and atomic fewer on
+            // the launch's critical path).  Otherwise: publish, count, and the last arriver sums.
             if (e == 0) {
-              const unsigned n_contrib = static_cast<unsigned>(cl - cf + 1);
-              const unsigned old = live ? atomicAdd(&p.cnt[tile], 1u) : 0u;
-              sb->last_flag[L] = live && (old == n_contrib - 1);
+              unsigned seen = 0u;
+              if (live && wk.u + n == u1)
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(p.cnt + tile) : "memory");
+              sb->last_flag[L] = (live && wk.u + n == u1 && seen == n_contrib - 1) ? 2 : 0;
             }
             named_bar_sync(bar, kEpiThreads);
+            const bool early = sb->last_flag[L] == 2;
+            if (!early) {
+              float* mine = p.part + (static_cast<size_t>(c) * 2 + (first_seg ? 0 : 1)) * kMaxTokens * kTileRows;
+#pragma unroll
+              for (int t = 0; t < NT; ++t) mine[t * kTileRows + r] = acc[t];
+              __threadfence();
+              named_bar_sync(bar, kEpiThreads);
+              if (e == 0) {
+                const unsigned old = live ? atomicAdd(&p.cnt[tile], 1u) : 0u;
+                sb->last_flag[L] = live && (old == n_contrib - 1);
+              }
+              named_bar_sync(bar, kEpiThreads);
+            }
             if (sb->last_flag[L]) {
               __threadfence();
               float v[NT];
 #pragma unroll
               for (int t = 0; t < NT; ++t) v[t] = 0.f;
-              for (long long cc = cf; cc <= cl; ++cc) {
+              for (long long cc = cf; cc <= cl; ++cc) {  // contributor order, whoever finishes
+                if (early && cc == c) {
+#pragma unroll
+                  for (int t = 0; t < NT; ++t) v[t] += acc[t];
+                  continue;
+                }
                 const long long cu0 = u_begin(cc, p.U, p.C);
                 const int cs = (cu0 >= tile_u0) ? 0 : 1;  // the tile is this contributor's first segment
                 const float* src = p.part + (static_cast<size_t>(cc) * 2 + cs) * kMaxTokens * kTileRows;
