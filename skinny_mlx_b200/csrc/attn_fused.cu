@@ -25,6 +25,7 @@
 // dependent launch, like every launch of the step (the next launch may start at once; a kernel
 // waits for the previous grid before its first global read).
 #include <algorithm>
+#include <atomic>
 #include <cfloat>
 #include <cstdint>
 #include <cuda_bf16.h>
@@ -688,25 +689,27 @@ bool attn_fits(int T, int nh, int nkv) {
 }
 
 static int device_sm_count_attn(int dev) {
-  static int n[64] = {};
+  static std::atomic<int> n[64];
   if (dev < 0 || dev >= 64) return 0;
-  if (n[dev] == 0) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
-  return n[dev];
+  int v = n[dev].load(std::memory_order_relaxed);
+  if (v == 0 && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+    n[dev].store(v, std::memory_order_relaxed);
+  return v;
 }
 
 cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, const float* kn_w,
                               const float* inv_freq, int rot, int gated, float eps, void* kc, void* vc, int L0,
                               const int* len_dev, int max_len, int T, int nh, int nkv, void* ws, void* xq,
                               void* o_out, const skinny_peer_sync* sync, const int32_t* parent, cudaStream_t stream) {
-  static bool attr_set[64] = {};
+  static std::atomic<bool> attr_set[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!attr_set[dev]) {
+  if (!attr_set[dev].load(std::memory_order_acquire)) {
     const cudaError_t e = cudaFuncSetAttribute(attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(sizeof(AttnSmem)));
     if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+    attr_set[dev].store(true, std::memory_order_release);
   }
   const int rep = nh / nkv;
   AttnParams prm;
@@ -738,8 +741,8 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
   // One CTA per SM where the grid fits the GPU: launched early (programmatic dependent launch),
   // CTAs otherwise pile onto the few SMs the previous launch leaves free, two to four per SM.
   // Asking for more than half an SM's shared memory spreads them.
-  static int padded[64][2] = {};  // per device: dynamic bytes of the chunk / merge launch (0: unset)
-  if (padded[dev][0] == 0) {
+  static std::atomic<int> padded[64][2];  // per device: dynamic bytes of the chunk / merge launch (0: unset)
+  if (padded[dev][1].load(std::memory_order_acquire) == 0) {
     int smem_sm = 0;
     cudaFuncAttributes fa{};
     cudaError_t e = cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
@@ -750,8 +753,8 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
     e = cudaFuncSetAttribute(attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, chunk);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, merge);
     if (e != cudaSuccess) return e;
-    padded[dev][0] = chunk;
-    padded[dev][1] = merge;
+    padded[dev][0].store(chunk, std::memory_order_relaxed);
+    padded[dev][1].store(merge, std::memory_order_release);
   }
   const int n_sm = device_sm_count_attn(dev);
   cudaLaunchAttribute attr[1];
@@ -760,7 +763,7 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(prm.nchunks, nkv);
   cfg.blockDim = dim3(kAtThreads);
-  cfg.dynamicSmemBytes = prm.nchunks * nkv <= n_sm ? padded[dev][0] : sizeof(AttnSmem);
+  cfg.dynamicSmemBytes = prm.nchunks * nkv <= n_sm ? padded[dev][0].load(std::memory_order_relaxed) : sizeof(AttnSmem);
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
@@ -769,7 +772,8 @@ cudaError_t attn_fused_launch(const void* proj, int ldp, const float* qn_w, cons
   cudaLaunchConfig_t mcfg = {};
   mcfg.gridDim = dim3(prm.nrg * (kAtRG / kAtMergeRows), nkv);  // (rows, row group) x KV head
   mcfg.blockDim = dim3(kAtThreads);
-  mcfg.dynamicSmemBytes = mcfg.gridDim.x * mcfg.gridDim.y <= static_cast<unsigned>(n_sm) ? padded[dev][1] : 0;
+  mcfg.dynamicSmemBytes =
+      mcfg.gridDim.x * mcfg.gridDim.y <= static_cast<unsigned>(n_sm) ? padded[dev][1].load(std::memory_order_relaxed) : 0;
   mcfg.stream = stream;
   mcfg.attrs = attr;
   mcfg.numAttrs = 1;

@@ -31,6 +31,7 @@
 // the norm output to bf16, o to bf16.  Launched with programmatic dependent launch: the next
 // launch may start at once (it streams weights) and this one waits for the previous grid before
 // its first global read.
+#include <atomic>
 #include <cfloat>
 #include <cstdint>
 #include <cuda_bf16.h>
@@ -445,7 +446,7 @@ constexpr size_t kGfDynBytes = (kGfMaxT * kGfThreads + kGfMaxT * kGfRows) * size
 // run in waves).
 template <int W>
 static cudaError_t launch_gdn_fused(const GdnFusedParams& prm, cudaStream_t stream) {
-  static int dyn_for[64][65] = {};  // per device and value-head count: the dynamic shared memory used
+  static std::atomic<int> dyn_for[64][65];  // per device and value-head count: the dynamic shared memory used
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
@@ -462,7 +463,7 @@ static cudaError_t launch_gdn_fused(const GdnFusedParams& prm, cudaStream_t stre
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  int& dyn = dyn_for[dev][min(prm.Hv, 64)];
+  int dyn = dyn_for[dev][min(prm.Hv, 64)].load(std::memory_order_acquire);
   if (dyn == 0) {
     cudaFuncAttributes fa{};
     cudaError_t e = cudaFuncGetAttributes(&fa, gdn_fused_kernel<W>);
@@ -490,6 +491,7 @@ static cudaError_t launch_gdn_fused(const GdnFusedParams& prm, cudaStream_t stre
       }
     }
   }
+  dyn_for[dev][min(prm.Hv, 64)].store(dyn, std::memory_order_release);  // (the same value from any thread)
   cfg.dynamicSmemBytes = dyn;
   return cudaLaunchKernelEx(&cfg, gdn_fused_kernel<W>, prm);
 }

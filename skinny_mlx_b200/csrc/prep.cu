@@ -25,6 +25,7 @@
 // Launched with programmatic dependent launch: a CTA allows the next launch to start at once
 // (the next qmm then streams its weights during this kernel) and waits for the previous grid
 // before its first global read.
+#include <atomic>
 #include <cfloat>
 #include <cstdint>
 #include <cuda_bf16.h>
@@ -201,14 +202,14 @@ cudaError_t prep_launch(int mode, const void* x, int ldx, const void* d, int ldd
   const PeerSync ps = peer_sync_from(sync);
   if (mode == 0) {
     const auto kern = lean ? prep_kernel<0, kPrepLeanThreads, true> : prep_kernel<0, 128, false>;
-    static bool attr_set[2][64] = {};
+    static std::atomic<bool> attr_set[2][64];
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[lean][dev]) {
+    if (dev >= 0 && dev < 64 && !attr_set[lean][dev].load(std::memory_order_acquire)) {
       const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  static_cast<int>(kPrepMaxK * sizeof(float)));
       if (e != cudaSuccess) return e;
-      attr_set[lean][dev] = true;
+      attr_set[lean][dev].store(true, std::memory_order_release);
     }
     return launch_pdl(kern, nthr, grid, static_cast<size_t>(K) * sizeof(float), stream, xb, ldx,
                       static_cast<const __nv_bfloat16*>(d), ldd, dseg_cols, segs, static_cast<__nv_bfloat16*>(h_out),
