@@ -164,6 +164,7 @@ struct __align__(16) QmmSmem {
   uint32_t tmem_base;
   int abort_flag;
   int last_flag[2];
+  int pre_xg[kMaxStages], pre_n[kMaxStages];  // producer: the prefetched stages' x-prep groups and unit counts
 };
 // followed by the epilogue's partial-sum exchange, float [2][NT][128]
 
@@ -442,17 +443,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint8_t* w_tc = p.mats[cmi].w_tc;
       int xg_off = p.mats[cmi].xg_off;
       int k = 0;
-      // first stages: weights before griddepcontrol.wait, x blocks after
+      // First stages: weights before griddepcontrol.wait, x blocks after.  Each stage's x-prep
+      // group and unit count are noted (in shared memory) as its weights are issued, so that
+      // after the wait only the x copies are issued: the walk's kernel-parameter reads, about a
+      // microsecond for a full ring, stay off the dependency's critical path.
       while (wk.u < u1 && k < kStages) {
         if (wk.mi != cmi) {
           cmi = wk.mi;
           w_tc = p.mats[cmi].w_tc;
+          xg_off = p.mats[cmi].xg_off;
         }
         const int n = wk.stage_n(u1);
         mbar_arrive_expect_tx(smem_u32(&sb->full[k]), static_cast<uint32_t>(n) * (kUnitWBytes + XB));
         bulk_g2s_hint(smem_u32(wring + k * kWStageBytes),
                       w_tc + static_cast<size_t>(wk.u - wk.uoff) * kUnitWBytes,
                       static_cast<uint32_t>(n) * kUnitWBytes, smem_u32(&sb->full[k]), pol_w);
+        sb->pre_xg[k] = xg_off + wk.g;
+        sb->pre_n[k] = n;
         wk.advance(p, n);
         ++k;
       }
@@ -461,18 +468,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         peer_wait_flags(p.sync);
         fence_proxy_async_global();  // the bulk copies below read what the acquire made visible
       }
-      {
-        UnitWalk w2;
-        w2.init(p, u0);
-        for (int f = 0; f < k; ++f) {
-          const int n = w2.stage_n(u1);
-          copy_x_blocks(p, smem_u32(xring + f * XSTAGE), p.mats[w2.mi].xg_off + w2.g, n, XB, smem_u32(&sb->full[f]));
-          w2.advance(p, n);
-        }
-        cmi = wk.mi;
-        w_tc = p.mats[cmi].w_tc;
-        xg_off = p.mats[cmi].xg_off;
-      }
+      for (int f = 0; f < k; ++f)
+        copy_x_blocks(p, smem_u32(xring + f * XSTAGE), sb->pre_xg[f], sb->pre_n[f], XB, smem_u32(&sb->full[f]));
+      cmi = wk.mi;
+      w_tc = p.mats[cmi].w_tc;
+      xg_off = p.mats[cmi].xg_off;
       while (wk.u < u1) {
         const int s = k % kStages;
         if (!mbar_wait(smem_u32(&sb->empty[s]), ((k / kStages) - 1) & 1, p.err, kErrBitWaitEmpty,
