@@ -709,6 +709,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (full_tile) {
             if constexpr (SWIGLU) {
+              // The scratch overlaps the exchange slots this warpgroup's other threads may still
+              // be reading for the lane combine above: every thread's read first.
+              named_bar_sync(4 + L, kEpiThreads);
               swiglu_digits<NT>(p, wk.lt, r, lane, warp & 3, 4 + L, acc, xb);  // (barriers: every thread)
             } else if (live && row_g < mt.N) {
 #pragma unroll
