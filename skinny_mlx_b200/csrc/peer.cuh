@@ -2,9 +2,15 @@
 // per rank, peers' buffers mapped with CUDA IPC over NVLink; plain loads and stores only).
 //
 // A producer launch (a kernel that writes this rank's slice of a buffer the other ranks read)
-// ends with peer_signal_done: every CTA fences its writes at system scope and counts itself on a
-// local counter; the last one resets the counter and stores the step's epoch into this rank's
-// flag word in every rank's flag array.  A consumer launch (one that reads other ranks' slices)
+// ends with peer_signal_done: every CTA counts itself on a local counter with a GPU-scope
+// acquire-release atomic (releasing the CTA's writes, its local ones and those into the other
+// ranks' buffers alike); the last one, which thereby acquired every CTA's writes, resets the
+// counter, issues ONE system-scope fence and stores the step's epoch into this rank's flag word
+// in every rank's flag array.  By the PTX memory model's causality order (release / acquire at
+// GPU scope between the CTAs, then the system-scope fence and flag store, then the consumer's
+// system-scope acquire) every write of the launch is visible to a consumer that saw the flag.
+// A system-scope fence costs microseconds: one per CTA (the earlier form of this protocol) made
+// the 2-GPU config-5 step 8.92 ms against 7.25 ms with the fences of the counting removed.  A consumer launch (one that reads other ranks' slices)
 // starts with peer_wait_all: one thread waits, bounded, until every rank's flag for this launch
 // holds the epoch, and the CTA proceeds (or records an error and skips its reads).
 //
@@ -51,8 +57,13 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
 
 // Called by one thread.  True when every rank's flag reached the epoch; false (error bit set)
@@ -83,19 +94,18 @@ __device__ __forceinline__ bool peer_wait_all(const PeerSync& s, int* flag_smem)
 // Every thread of the CTA, after its last write of the launch.
 __device__ __forceinline__ void peer_signal_done(const PeerSync& s, int* flag_smem) {
   if (!s.epoch || !s.counter) return;
-  __syncthreads();
+  __syncthreads();  // the CTA's writes, observed by thread 0 through the barrier
   if (threadIdx.x == 0) {
-    __threadfence_system();  // this CTA's writes (ordered before by the barrier) reach every rank
     const uint32_t n = gridDim.x * gridDim.y * gridDim.z;
-    const uint32_t prev = atomicAdd(s.counter, 1u);
+    const uint32_t prev = atom_add_acq_rel_gpu(s.counter, 1u);  // release ours, acquire the earlier CTAs'
     *flag_smem = prev == n - 1;
   }
   __syncthreads();
   if (*flag_smem && threadIdx.x == 0) {
-    *s.counter = 0u;
-    __threadfence_system();  // every CTA's writes: they fenced before counting
+    *s.counter = 0u;  // (the next launch's atomics come after this kernel in stream order)
+    asm volatile("fence.acq_rel.sys;" ::: "memory");  // with the relaxed stores: a system-scope release
     const uint32_t e = *s.epoch;
-    for (int r = 0; r < s.n_ranks; ++r) st_release_sys(s.signal_flags[r], e);
+    for (int r = 0; r < s.n_ranks; ++r) st_relaxed_sys(s.signal_flags[r], e);
   }
 }
 
