@@ -477,10 +477,9 @@ def config4_spec(model, dev, n_tokens=256, prompt_len=512, fwd=None):
 def config5_steps(world: int, rank: int, dev, kv_len=4096, ms=(8, 16), steps=5, cfg=None):
     """the 64-layer dense model, column-parallel over the job's ranks, one
     verify step at M tokens with `kv_len` cached tokens: the fused step (DenseFusedStep with its
-    default exchange for this many ranks: peer memory over NVLink at 2, NCCL all-gathers from 4),
-    and at the first M, for comparison, the fused step with the other exchange (more than one
-    rank) and the module-by-module forward; each captured with its collectives in one CUDA graph
-    when possible; max over ranks."""
+    default exchange, peer memory over NVLink), and at the first M, for comparison, the fused step
+    with NCCL all-gathers (more than one rank) and the module-by-module forward; each captured
+    with its collectives in one CUDA graph when possible; max over ranks."""
     from skinny_mlx_b200.configs import DENSE_64L, packed_bytes
     from skinny_mlx_b200.dense import DenseModel
     from skinny_mlx_b200.patch import patch_model
@@ -491,9 +490,9 @@ def config5_steps(world: int, rank: int, dev, kv_len=4096, ms=(8, 16), steps=5, 
     t0 = time.perf_counter()
     model = DenseModel(cfg, rank, world, seed=21, device=dev)
     patch_model(model)
-    fused = DenseFusedStep(model)  # the default exchange for this many ranks
-    # the other exchange beside it, for the rank counts where both were validated (2 and 4)
-    other = {"peer": "nccl", "nccl": "peer"}.get(fused.exchange) if world <= 4 else None
+    fused = DenseFusedStep(model)  # the default exchange (peer memory)
+    # the other exchange beside it (both validated on 2, 4 and 8 B200s)
+    other = {"peer": "nccl", "nccl": "peer"}.get(fused.exchange)
     fused_alt = DenseFusedStep(model, exchange=other) if other else None
     torch.cuda.empty_cache()
     build_s = time.perf_counter() - t0

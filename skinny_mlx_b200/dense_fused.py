@@ -16,7 +16,7 @@ Per layer, rank g of G:
 
 Two exchanges (G > 1):
 
-* "peer" (the default for 2 ranks): each rank keeps a buffer the other ranks map through CUDA IPC (NVLink peer
+* "peer" (the default): each rank keeps a buffer the other ranks map through CUDA IPC (NVLink peer
   memory).  The digit producers (attention, SwiGLU prep) write their digit blocks into every
   rank's buffer (skinny_peer_sync mirrors), so each qmm reads its whole input from local memory
   however often its tiles re-read it; the output shards of o_proj and down are read in place
@@ -24,7 +24,7 @@ Two exchanges (G > 1):
   after a bounded wait on per-(layer, kind) flags that each producer launch sets on every rank
   when its last CTA finishes.  No collective runs inside a layer; one NCCL all-gather of the
   logits ends the step.
-* "nccl" (the default from 4 ranks): an all_gather_into_tensor after each of the four producers.
+* "nccl": an all_gather_into_tensor after each of the four producers (the comparison arm).
 
 With G = 1 there is no exchange.  The logits come back as [G, M, V/G] (rank-major shards).
 """
@@ -52,9 +52,9 @@ def _align(n: int, a: int = 256) -> int:
 
 
 class DenseFusedStep:
-    """exchange: "peer", "nccl", or "auto" (peer memory for 2 ranks, NCCL from 4: measured on B200,
-    the peer exchange ties NCCL's all-gathers at 2 ranks and trails them at 4, where every
-    producer writes its digit blocks to three other GPUs and every consumer polls four flags)."""
+    """exchange: "peer", "nccl", or "auto" (= "peer": measured on B200, config 5 at M = 8, the
+    peer exchange takes 6.54 / 5.93 / 6.26 ms per step at 2 / 4 / 8 ranks against 8.67 / 8.29 /
+    9.39 ms with NCCL's all-gathers, since its producers issue one system-scope fence per launch)."""
 
     def __init__(self, model: DenseModel, exchange: str = "auto"):
         from .patch import SkinnyQuantizedLinear
@@ -62,7 +62,7 @@ class DenseFusedStep:
         self.model, self.cfg, self.G, self.rank = model, model.cfg, model.world, model.rank
         self.group = model.ex.group
         if exchange == "auto":
-            exchange = "peer" if self.G == 2 else "nccl"
+            exchange = "peer"
         self.exchange = exchange if self.G > 1 else "none"
         assert self.exchange in ("none", "peer", "nccl")
         cfg = self.cfg

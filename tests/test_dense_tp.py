@@ -192,13 +192,15 @@ def _gpu_fused_rank(rank, world, port, q, exchange):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("exchange", ["peer", "nccl"])
-def test_dense_fused_step_two_gpus(cuda_lib, dev, exchange):
-    """2 ranks (skipped on a 1-GPU box): the fused sharded step against the unsharded patched
-    module path, with the peer-memory exchange (other ranks' digit blocks and output shards read
-    in place over NVLink after per-layer flags) and with NCCL all-gathers."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def test_dense_fused_step_multi_gpu(cuda_lib, dev, exchange, world):
+    """2, 4 and 8 ranks (skipped on a box with fewer GPUs): the fused sharded step against the
+    unsharded patched module path, with the peer-memory exchange (digit blocks pushed into every
+    rank's buffer, output shards read in place over NVLink, per-layer flags) and with NCCL
+    all-gathers."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from skinny_mlx_b200.patch import patch_model
 
     m = DenseModel(small_dense(), 0, 1, seed=3, device=dev)
@@ -209,7 +211,7 @@ def test_dense_fused_step_two_gpus(cuda_lib, dev, exchange):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_gpu_fused_rank, args=(r, 2, port, q, exchange)) for r in range(2)]
+    procs = [ctx.Process(target=_gpu_fused_rank, args=(r, world, port, q, exchange)) for r in range(world)]
     for p in procs:
         p.start()
     got, errs = q.get(timeout=300)
