@@ -348,7 +348,9 @@ int skinny_gdn_rollback_tree(int n_layers, float* const* state, const float* con
  * and K <= 32,768 columns; larger shapes return SKINNY_ERR_SCRATCH_LIMIT before anything is
  * launched.  The first call on a
  * device does the set-up (scratch address lookup, kernel attributes) and should come before any
- * stream capture.  Calls that may overlap on one device (other streams or threads without
+ * stream capture; what it looks up is cached per device index, i.e. for the device's primary
+ * context (the runtime API's): a host that switches driver-API contexts or resets the device
+ * between calls is not supported.  Calls that may overlap on one device (other streams or threads without
  * ordering) race on the shared scratch; order them.  Each call clears the scratch's counters on
  * `stream` and then launches, without programmatic dependent launch. */
 int skinny_qmm_w4g64_noalloc(const void* x, int ldx, const void* w_tc, void* out, int ldo, int M,
