@@ -11,8 +11,8 @@
 // system-scope acquire) every write of the launch is visible to a consumer that saw the flag.
 // A system-scope fence costs microseconds: one per CTA (the earlier form of this protocol) made
 // the 2-GPU config-5 step 8.92 ms against 7.25 ms with the fences of the counting removed.  A consumer launch (one that reads other ranks' slices)
-// starts with peer_wait_all: one thread waits, bounded, until every rank's flag for this launch
-// holds the epoch, and the CTA proceeds (or records an error and skips its reads).
+// starts with peer_wait_all: warp 0 waits, bounded, until every rank's flag for this launch holds
+// the epoch (one lane per rank), and the CTA proceeds (or records an error and skips its reads).
 //
 // The epoch is a device counter the caller advances once per step, so one captured graph serves
 // every step; flags only grow, so a flag is never reset while a peer may still read it.
@@ -66,27 +66,37 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v
   return old;
 }
 
-// Called by one thread.  True when every rank's flag reached the epoch; false (error bit set)
-// after SKINNY_WAIT_NS.
-__device__ __forceinline__ bool peer_wait_flags(const PeerSync& s) {
+// Called by all 32 lanes of one warp: lane r < n_ranks waits (bounded) until rank r's flag
+// reached the epoch, with system-scope acquire loads; the ranks' flags are thus polled in
+// parallel, not one acquire after another.  The warp then synchronises, which orders every lane's
+// acquire before the warp's later reads.  True when every flag reached the epoch; false (error
+// bit set) after SKINNY_WAIT_NS.
+__device__ __forceinline__ bool peer_wait_flags_warp(const PeerSync& s, int lane) {
   if (!s.epoch || !s.wait_flags) return true;
-  const uint32_t e = *s.epoch;
-  const uint64_t t0 = globaltimer_ns();
-  for (int r = 0; r < s.n_ranks; ++r) {
-    while (static_cast<int32_t>(ld_acquire_sys(s.wait_flags + r) - e) < 0) {
+  bool ok = true;
+  if (lane < s.n_ranks) {
+    const uint32_t e = *s.epoch;
+    const uint64_t t0 = globaltimer_ns();
+    while (static_cast<int32_t>(ld_acquire_sys(s.wait_flags + lane) - e) < 0) {
       if (globaltimer_ns() - t0 > SKINNY_WAIT_NS) {
         atomicOr(s.err, kErrBitWaitPeer);
-        return false;
+        ok = false;
+        break;
       }
     }
   }
-  return true;
+  ok = __all_sync(0xFFFFFFFFu, ok);
+  __syncwarp();
+  return ok;
 }
 
-// Every thread of the CTA: thread 0 waits, the CTA learns the outcome.
+// Every thread of the CTA: warp 0 waits, the CTA learns the outcome.
 __device__ __forceinline__ bool peer_wait_all(const PeerSync& s, int* flag_smem) {
   if (!s.epoch || !s.wait_flags) return true;
-  if (threadIdx.x == 0) *flag_smem = peer_wait_flags(s) ? 1 : 0;
+  if (threadIdx.x < 32) {
+    const bool ok = peer_wait_flags_warp(s, threadIdx.x);
+    if (threadIdx.x == 0) *flag_smem = ok ? 1 : 0;
+  }
   __syncthreads();
   return *flag_smem != 0;
 }

@@ -434,15 +434,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   if (warp == 0) {
+    // ------------------------------ TMA producer (lane 0) ------------------------------
+    // (the whole warp waits for the other ranks' flags of a sharded step, a lane per rank)
+    uint64_t pol_w = 0;
+    UnitWalk wk;
+    int cmi = 0;  // matrix whose weight pointer and x-prep offset are cached
+    const uint8_t* w_tc = nullptr;
+    int xg_off = 0;
+    int k = 0;
     if (lane == 0) {
-      // ------------------------------ TMA producer ------------------------------
-      const uint64_t pol_w = policy_evict_first();
-      UnitWalk wk;
+      pol_w = policy_evict_first();
       wk.init(p, u0);
-      int cmi = wk.mi;  // matrix whose weight pointer and x-prep offset are cached
-      const uint8_t* w_tc = p.mats[cmi].w_tc;
-      int xg_off = p.mats[cmi].xg_off;
-      int k = 0;
+      cmi = wk.mi;
+      w_tc = p.mats[cmi].w_tc;
+      xg_off = p.mats[cmi].xg_off;
       // First stages: weights before griddepcontrol.wait, x blocks after.  Each stage's x-prep
       // group and unit count are noted (in shared memory) as its weights are issued, so that
       // after the wait only the x copies are issued: the walk's kernel-parameter reads, about a
@@ -463,11 +468,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         wk.advance(p, n);
         ++k;
       }
-      pdl_wait_prior_grid();  // the x-prep blocks are written by the previous kernel
-      if (p.sync.wait_flags) {  // (sharded step) and by the other ranks; a timeout is recorded
-        peer_wait_flags(p.sync);
-        fence_proxy_async_global();  // the bulk copies below read what the acquire made visible
-      }
+    }
+    __syncwarp();
+    if (lane == 0 || p.sync.wait_flags) pdl_wait_prior_grid();  // the x-prep blocks are written by the previous kernel
+    if (p.sync.wait_flags) {  // (sharded step) and by the other ranks; a timeout is recorded
+      peer_wait_flags_warp(p.sync, lane);
+      if (lane == 0) fence_proxy_async_global();  // the bulk copies below read what the acquires made visible
+    }
+    if (lane == 0) {
       for (int f = 0; f < k; ++f)
         copy_x_blocks(p, smem_u32(xring + f * XSTAGE), sb->pre_xg[f], sb->pre_n[f], XB, smem_u32(&sb->full[f]));
       cmi = wk.mi;
