@@ -53,7 +53,7 @@ def _align(n: int, a: int = 256) -> int:
 
 class DenseFusedStep:
     """exchange: "peer", "nccl", or "auto" (= "peer": measured on B200, config 5 at M = 8, the
-    peer exchange takes 6.54 / 5.93 / 6.26 ms per step at 2 / 4 / 8 ranks against 8.67 / 8.29 /
+    peer exchange takes 6.54 / 5.82 / 6.26 ms per step at 2 / 4 / 8 ranks against 8.67 / 8.29 /
     9.39 ms with NCCL's all-gathers, since its producers issue one system-scope fence per launch)."""
 
     def __init__(self, model: DenseModel, exchange: str = "auto"):
