@@ -127,9 +127,10 @@ int skinny_ipc_free(void* ptr);
 /* Synchronisation of one launch with the other ranks (all pointers device memory):
  *   wait_flags  != NULL: before reading other ranks' data, wait (bounded, error bit 11) until
  *                        wait_flags[0 .. n_ranks) >= *epoch;
- *   counter     != NULL: after its last write, the launch's last CTA stores *epoch into
- *                        signal_flags[r] for every rank r (this rank's word in each rank's
- *                        flags), after a system-scope fence; the counter is zero between launches.
+ *   counter     != NULL: after its last write each CTA counts itself on counter (a GPU-scope
+ *                        acquire-release atomic), and the last one, after one system-scope fence,
+ *                        stores *epoch into signal_flags[r] for every rank r (this rank's word in
+ *                        each rank's flags); the counter is zero between launches.
  *   n_mirror > 0:        a launch that writes qmm input digits (skinny_prep, skinny_attn_fused)
  *                        also writes them to mirror[0 .. n_mirror): other ranks' buffers, each
  *                        the address that corresponds to xq there (same block offsets), so that
